@@ -1,0 +1,538 @@
+#!/usr/bin/env python
+"""Benchmark of the Q8_0 quantized linear hot path on B200.
+
+Workload: the decode-step linear stack of a random-init
+Qwen3-1.7B-shaped Q8_0 model at batch 1 - 28 layers of [qkv 4096x2048,
+o 2048x2048, gate/up 12288x2048, down 2048x6144] plus the tied lm_head
+151936x2048 - with int8 weights U[-127, 127] and fp16-drawn block scales
+U[0.001, 0.01] widened to f32 (the reference's Q8 layout, 36 bytes per
+block). One step is one token through all 113 projections; every
+projection quantizes its input activation to Q8_0 inside the GEMV.
+
+On N GPUs every matrix is split by output rows; each rank computes its row
+slice and an NCCL all-gather over NVLink rebuilds the full activation for
+the next projection (strong scaling: the model is fixed, rows are divided).
+Outputs are bit-identical for every N: a row's result does not depend on the
+split (lab_native.c:550-552).
+
+Metric: tokens/s of the whole job (value), plus HBM GB/s of the weight
+stream. `e2e` is the same token loop driven through the reference-facing
+C-ABI (lab_gemm_q8) with host activations and outputs, one synchronous call
+per projection as dianoia's NativeQ8Matrix.apply does. `--impl reference`
+times the reference's own CPU kernels (lab_native.c, compiled unmodified
+into oracle/_ref) on this host's cores on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, HEADS, KV_HEADS, HEAD_DIM, INTER, LAYERS, VOCAB = 2048, 16, 8, 128, 6144, 28, 151936
+# (name, rows, cols, input) per layer; qkv and gate/up are stored row-concatenated.
+LAYER_MATS = [("qkv", (HEADS + 2 * KV_HEADS) * HEAD_DIM, HIDDEN),
+              ("o", HEADS * HEAD_DIM, HEADS * HEAD_DIM),
+              ("gate_up", 2 * INTER, HIDDEN),
+              ("down", HIDDEN, INTER)]
+Q8_BLOCK_BYTES_REF = 36   # reference layout: 32 int8 + f32 scale
+Q8_BLOCK_BYTES_ALG = 34   # algorithmic credit: 32 int8 + fp16 scale (GGUF Q8_0)
+METRIC = "quantized-linear HBM GB/s (GEMV), int8 TOPS (GEMM), tokens/s at 1/2/4/8 B200"
+CHUNKS = 8                # weights are generated per 1/8 row chunk so any N in {1,2,4,8} shards alike
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def matrices():
+    """All projections of one token, in order: (layer, name, rows, cols)."""
+    out = []
+    for layer in range(LAYERS):
+        for name, rows, cols in LAYER_MATS:
+            out.append((layer, name, rows, cols))
+    out.append((LAYERS, "lm_head", VOCAB, HIDDEN))
+    return out
+
+
+def step_bytes(block_bytes: int) -> int:
+    """Weight + activation bytes one token must move through HBM."""
+    total = 0
+    for _, _, rows, cols in matrices():
+        total += rows * (cols // 32) * block_bytes + cols * 4 + rows * 4
+    return total
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ model
+
+class Stack:
+    """This rank's row slices of every projection, resident in HBM."""
+
+    def __init__(self, torch, rank: int, world: int, device):
+        self.torch = torch
+        self.rank, self.world, self.device = rank, world, device
+        self.mats = []
+        for idx, (layer, name, rows, cols) in enumerate(matrices()):
+            r0, r1 = rows * rank // world, rows * (rank + 1) // world
+            qs, sc = self._weights(idx, rows, cols, r0, r1)
+            self.mats.append(dict(layer=layer, name=name, rows=rows, cols=cols, r0=r0, r1=r1,
+                                  qs=qs, scales=sc))
+        t = torch
+        self.x0 = t.empty(HIDDEN, dtype=t.float32, device=device)
+        gen = t.Generator(device=device)
+        gen.manual_seed(12345)
+        self.x0.normal_(generator=gen)
+        self.bufs = {n: t.zeros(r, dtype=t.float32, device=device)
+                     for n, r, _ in [("qkv", LAYER_MATS[0][1], 0), ("o", LAYER_MATS[1][1], 0),
+                                     ("gate_up", LAYER_MATS[2][1], 0), ("down", HIDDEN, 0),
+                                     ("lm_head", VOCAB, 0)]}
+
+    def _weights(self, idx, rows, cols, r0, r1):
+        t = self.torch
+        blocks = cols // 32
+        qs = t.empty((r1 - r0) * cols, dtype=t.int8, device=self.device)
+        sc = t.empty((r1 - r0) * blocks, dtype=t.float32, device=self.device)
+        step = rows // CHUNKS
+        gen = t.Generator(device=self.device)
+        for c in range(CHUNKS):
+            c0, c1 = c * step, (c + 1) * step
+            lo, hi = max(c0, r0), min(c1, r1)
+            if lo >= hi:
+                continue
+            gen.manual_seed(1_000_003 * idx + c)
+            chunk_q = t.randint(-127, 128, ((c1 - c0) * cols,), dtype=t.int8, device=self.device,
+                                generator=gen)
+            chunk_s = t.empty((c1 - c0) * blocks, dtype=t.float32, device=self.device)
+            chunk_s.uniform_(0.001, 0.01, generator=gen)
+            chunk_s = chunk_s.half().float()
+            qs[(lo - r0) * cols:(hi - r0) * cols] = chunk_q[(lo - c0) * cols:(hi - c0) * cols]
+            sc[(lo - r0) * blocks:(hi - r0) * blocks] = chunk_s[(lo - c0) * blocks:(hi - c0) * blocks]
+        return qs, sc
+
+    def inputs_of(self, m, x):
+        """The input activation of projection m given the running hidden state x."""
+        name = m["name"]
+        if name == "qkv" or name == "lm_head":
+            return x
+        if name == "o":
+            return self.bufs["qkv"][:HEADS * HEAD_DIM]
+        if name == "gate_up":
+            return self.bufs["o"]
+        return self.bufs["gate_up"][:INTER]  # down reads the gate half
+
+
+def run_step(stack, L, stream_handle, gather, flags=1):
+    """One token through all projections on the current stream. Returns launches."""
+    x = stack.x0
+    launches = 0
+    for m in stack.mats:
+        xin = stack.inputs_of(m, x)
+        out = stack.bufs[m["name"]] if m["name"] != "down" else stack.bufs["down"]
+        rows_local = m["r1"] - m["r0"]
+        rc = L.dn_linear(0, m["qs"].data_ptr(), m["scales"].data_ptr(), xin.data_ptr(), None, None,
+                         out.data_ptr() + 4 * m["r0"], rows_local, m["cols"], 1, rows_local, 1,
+                         -1, flags, stream_handle)
+        if rc != 0:
+            raise RuntimeError(f"dn_linear failed: {L.dn_error_string(rc).decode()}")
+        launches += 1
+        if gather is not None:
+            gather(out)
+        if m["name"] == "down":
+            x = stack.bufs["down"]
+    return launches
+
+
+# -------------------------------------------------------------- CPU legs
+
+def host_weights(stack):
+    return [(m["qs"].cpu().numpy(), m["scales"].cpu().numpy(), m["rows"], m["cols"])
+            for m in stack.mats]
+
+
+def cpu_reference_tokens(ref, hw, x0, threads: int, tokens: int):
+    """Runs `tokens` decode steps of the stack through the reference's
+    lab_gemm_q8 (mode 1) on the host; returns seconds per token and the logits."""
+    maxc = max(c for _, _, _, c in hw)
+    xq = np.zeros(maxc, np.int8)
+    xsc = np.zeros(maxc // 32 + 1, np.float32)
+    outs = {n: np.zeros(r, np.float32) for n, r in [("qkv", 4096), ("o", 2048), ("gate_up", 12288),
+                                                   ("down", 2048), ("lm_head", VOCAB)]}
+    names = [m[1] for m in matrices()]
+    t0 = time.perf_counter()
+    for _ in range(tokens):
+        x = x0
+        for (qs, sc, rows, cols), name in zip(hw, names):
+            xin = {"qkv": x, "lm_head": x, "o": outs["qkv"][:2048], "gate_up": outs["o"],
+                   "down": outs["gate_up"][:INTER]}[name]
+            xin = np.ascontiguousarray(xin)
+            ref.gemm("q8", qs, sc, xin, rows, cols, 1, mode=1, threads=threads,
+                     out=(outs[name], xq, xsc))
+            if name == "down":
+                x = outs["down"]
+    return (time.perf_counter() - t0) / tokens, outs["lm_head"].copy()
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference_arm(args, rank, world):
+    """--impl reference: the reference's CPU kernels on this host's cores."""
+    if rank != 0:
+        return None
+    from oracle import oracle as orc
+    try:
+        ref = orc.Reference()
+    except FileNotFoundError as e:
+        return {"impl": "reference", "unavailable": str(e)}
+    rng = np.random.default_rng(0)
+    # The same shapes and distributions as our arm; generated on the host.
+    hw = []
+    for _, _, rows, cols in matrices():
+        qs, sc = orc.q8_weights(rng, rows, cols)
+        hw.append((qs, sc, rows, cols))
+    x0 = orc.activations(rng, 1, HIDDEN)
+    threads = host_threads()
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    for _ in range(args.warmup):
+        cpu_reference_tokens(ref, hw, x0, threads, 1)
+    times = []
+    for _ in range(args.steps):
+        s, _ = cpu_reference_tokens(ref, hw, x0, threads, 1)
+        times.append(s)
+    total = sum(times)
+    value = args.steps / total
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} full decode-step linear stacks (113 lab_gemm_q8 calls each)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "hbm_gbs": step_bytes(Q8_BLOCK_BYTES_REF) * value / 1e9,
+    }
+
+
+def workload_config(world):
+    return {"workload": "config3: Qwen3-1.7B-shaped Q8_0 decode-step linear stack, batch 1 "
+                        "(28 x [qkv 4096x2048, o 2048x2048, gate/up 12288x2048, down 2048x6144] "
+                        "+ lm_head 151936x2048)",
+            "global_batch": 1, "parallelism": f"row-sharded x{world} + all-gather",
+            "weights_bytes_per_token_ref_layout": step_bytes(Q8_BLOCK_BYTES_REF),
+            "l2": "inputs larger than L2 (1.94 GB of weights streamed per step)"}
+
+
+# ------------------------------------------------------------------ main
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--cpu-tokens", type=int, default=3)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference_arm(args, rank, world)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from dianoia_b200 import _lib
+    L = _lib.lib()
+    if L.lab_cpu_supported() != 1:
+        raise SystemExit("no sm_100 device visible to libdianoia_b200")
+
+    stack = Stack(torch, rank, world, device)
+    torch.cuda.synchronize()
+
+    gather = None
+    if world > 1:
+        def gather(out):
+            n = out.numel() // world
+            dist.all_gather_into_tensor(out, out[rank * n:(rank + 1) * n])
+
+    stream = torch.cuda.Stream(device=device)
+    graph = None
+    launches_per_step = len(stack.mats)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            run_step(stack, L, stream.cuda_stream, gather)
+        torch.cuda.synchronize()
+        if not args.no_graph:
+            try:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    run_step(stack, L, torch.cuda.current_stream().cuda_stream, gather)
+                torch.cuda.synchronize()
+            except Exception as e:  # eager launches if capture is not possible
+                log("graph capture failed, running eagerly:", repr(e))
+                graph = None
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            run_step(stack, L, stream.cuda_stream, gather)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                step()
+            end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    status = L.dn_device_status(1)
+    if status != 0:
+        raise SystemExit(f"kernel bounded wait timed out (status {status})")
+
+    ms_per_step = ms_max / args.steps
+    tokens_per_s = 1e3 / ms_per_step
+    alg_bytes = step_bytes(Q8_BLOCK_BYTES_ALG)
+    ref_bytes = step_bytes(Q8_BLOCK_BYTES_REF)
+
+    # Dominant kernel: the fused quantize + GEMV (every launch in the step).
+    # Achieved = algorithmic bytes per step / step time on the launching
+    # stream (inter-kernel gaps included, so this is a lower bound of the
+    # kernel's own bandwidth); on N GPUs, bytes per rank.
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    per_rank_bytes = alg_bytes / world
+    achieved = per_rank_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # Checksum of the logits: identical for every N (rows do not depend on the split).
+    logits = stack.bufs["lm_head"].double()
+    checksum = float(logits.sum().item())
+
+    # End to end through the C-ABI with host buffers (rank-local shards; on
+    # N > 1 the slices are all-gathered through device copies).
+    e2e = run_e2e(args, stack, L, torch, rank, world, gather, device)
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and args.cpu_tokens > 0:
+        cpu_baseline = run_cpu_baseline(args, stack)
+
+    if rank == 0:
+        res = {
+            "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random-init Q8_0 weights, N(0,1) activations, seeded)",
+            "config": workload_config(world),
+            "hbm_gbs_per_gpu": ref_bytes / world / (ms_per_step * 1e-3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
+                         "algorithmic_bytes_per_step_per_gpu": per_rank_bytes,
+                         "traffic": None},
+            "e2e": e2e,
+            "cpu_baseline": cpu_baseline,
+            "gpu_launches": launches_per_step * args.steps,
+            "graph": graph is not None,
+            "clocks": clocks.summary(),
+            "logits_checksum": checksum,
+        }
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, stack, L, torch, rank, world, gather, device):
+    """Token loop through lab_gemm_q8 with host activations / outputs."""
+    steps = args.e2e_steps
+    if steps <= 0:
+        return None
+    maxc = max(m["cols"] for m in stack.mats)
+    xq = np.zeros(maxc, np.int8)
+    xsc = np.zeros(maxc // 32 + 1, np.float32)
+    host = {n: np.zeros(b.numel(), np.float32) for n, b in stack.bufs.items()}
+    x0 = stack.x0.cpu().numpy()
+    dev_tmp = {n: b.clone() for n, b in stack.bufs.items()} if world > 1 else None
+    h2d = d2h = 0
+
+    def one_token():
+        nonlocal h2d, d2h
+        x = x0
+        h2d = d2h = 0
+        for m in stack.mats:
+            name = m["name"]
+            xin = {"qkv": x, "lm_head": x, "o": host["qkv"][:2048], "gate_up": host["o"],
+                   "down": host["gate_up"][:INTER]}[name]
+            xin = np.ascontiguousarray(xin)
+            out = host[name]
+            rl = m["r1"] - m["r0"]
+            ys = out[m["r0"]:m["r1"]]
+            L.lab_gemm_q8(m["qs"].data_ptr(), m["scales"].data_ptr(), xin.ctypes.data,
+                          xq.ctypes.data, xsc.ctypes.data, ys.ctypes.data, rl, m["cols"], 1, 1, 1)
+            h2d += xin.nbytes
+            d2h += ys.nbytes + m["cols"] + m["cols"] // 32 * 4
+            if world > 1:
+                d = dev_tmp[name]
+                n = d.numel() // world
+                d[rank * n:(rank + 1) * n].copy_(torch.from_numpy(ys))
+                gather(d)
+                out[:] = d.cpu().numpy()
+            if name == "down":
+                x = host["down"]
+        if L.dn_last_error() != 0:
+            raise RuntimeError("lab_gemm_q8 failed")
+
+    for _ in range(2):
+        one_token()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_token()
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    # Same logits as the device-resident run.
+    same = bool(np.array_equal(host["lm_head"], stack.bufs["lm_head"].cpu().numpy()))
+    return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "api": "lab_gemm_q8 (host x / y, device weights)",
+            "steps": steps, "logits_match_device_run": same}
+
+
+def run_cpu_baseline(args, stack):
+    from oracle import oracle as orc
+    try:
+        ref = orc.Reference()
+        kind = "reference"
+    except FileNotFoundError:
+        return None
+    hw = host_weights(stack)
+    x0 = stack.x0.cpu().numpy()
+    threads = host_threads()
+    cpu_reference_tokens(ref, hw, x0, threads, 1)  # warm-up (page-in, OpenMP pool)
+    sec, logits = cpu_reference_tokens(ref, hw, x0, threads, args.cpu_tokens)
+    same = bool(np.array_equal(logits, stack.bufs["lm_head"].cpu().numpy()))
+    return {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{args.cpu_tokens} tokens of the full stack (113 lab_gemm_q8 mode-1 calls "
+                      f"each, OpenMP, OMP_PROC_BIND={os.environ.get('OMP_PROC_BIND', 'unset')})",
+            "logits_bit_identical_to_gpu": same}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,78 @@
+"""Loads libdianoia_b200.so (the CUDA kernels behind the C-ABI) with ctypes.
+
+There is no fallback: if the library is missing, importing the product path
+fails loudly. Build it with ``python dianoia_b200/build.py`` (or
+``__graft_entry__.build()``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libdianoia_b200.so")
+HEADER = os.path.join(os.path.dirname(PKG), "include", "dianoia_b200.h")
+
+_i64 = ctypes.c_int64
+_p = ctypes.c_void_p
+
+# Every exported function with its ctypes signature (restype, argtypes).
+SIGNATURES = {
+    "lab_alloc": (_p, [_i64]),
+    "lab_free": (None, [_p]),
+    "lab_cpu_supported": (_i64, []),
+    "lab_quantize_q8": (None, [_p, _p, _p, _i64, _i64]),
+    "lab_quantize_q4": (None, [_p, _p, _p, _i64, _i64]),
+    "lab_gemm_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
+    "lab_gemm_q4": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
+    "lab_gemv_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
+    "dn_linear": (_i64, [_i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
+    "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
+    "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),
+    "dn_quantize_q4": (_i64, [_p, _p, _p, _i64, _i64, _p]),
+    "dn_last_error": (_i64, []),
+    "dn_device_status": (_i64, [_i64]),
+    "dn_error_string": (ctypes.c_char_p, [_i64]),
+}
+
+# Status codes (include/dianoia_b200.h).
+DN_OK, DN_ERR_ARGS, DN_ERR_CUDA, DN_ERR_NO_DEVICE, DN_ERR_UNSUPPORTED, DN_ERR_TOO_LARGE = 0, -1, -2, -3, -4, -5
+DN_Q8, DN_Q4 = 0, 1
+DN_PATH_AUTO, DN_PATH_GEMV, DN_PATH_TC, DN_PATH_GENERIC = -1, 0, 1, 2
+DN_FLAG_PDL = 1
+
+_lib = None
+
+
+class LibraryMissing(ImportError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library, with argument types set; raises if it is not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise LibraryMissing(
+                f"{LIB_PATH} is not built; run `python dianoia_b200/build.py` (nvcc, sm_100a)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def header_functions(path: str = HEADER) -> list[str]:
+    """Names of the functions include/dianoia_b200.h declares."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b((?:lab|dn)_\w+)\s*\(", text)))
+
+
+def check(code: int, what: str = "dianoia_b200") -> None:
+    if code != DN_OK:
+        msg = lib().dn_error_string(code).decode()
+        raise RuntimeError(f"{what}: {msg} ({code})")

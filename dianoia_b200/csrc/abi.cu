@@ -1,0 +1,471 @@
+// The C-ABI of libdianoia_b200.so: dianoia's lab_* kernel symbols served by
+// the GPU, and the library's own device-resident dn_* API. See
+// include/dianoia_b200.h for the contract of each function.
+//
+// Host side of a lab_* call: every pointer is classified once per call
+// (cudaPointerGetAttributes). Managed (lab_alloc) and device memory is used
+// in place; host memory is staged through per-thread pinned and device
+// buffers that grow on demand, so concurrent calls from different threads do
+// not share scratch. Each call runs on its thread's own stream and
+// synchronizes before it returns, like the reference's CPU kernels.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <new>
+#include <mutex>
+
+#include "dianoia_b200.h"
+#include "dn_launch.h"
+
+using dn::LinearArgs;
+
+namespace {
+
+thread_local int64_t tl_last_error = DN_OK;
+
+void set_error(int64_t e) {
+  if (e != DN_OK && tl_last_error == DN_OK) tl_last_error = e;
+}
+
+bool cuda_ok(cudaError_t e) {
+  if (e == cudaSuccess) return true;
+  static int reported = 0;
+  if (reported++ < 8) fprintf(stderr, "dianoia_b200: CUDA error: %s\n", cudaGetErrorString(e));
+  set_error(DN_ERR_CUDA);
+  return false;
+}
+
+// ---------------------------------------------------------------- devices
+
+struct DeviceState {
+  bool ready = false;
+  uint32_t* status_host = nullptr;  // pinned, mapped: kernels' bounded-wait status
+  uint32_t* status_dev = nullptr;
+};
+
+std::mutex g_mu;
+DeviceState g_devices[64];
+
+int device_count() {
+  static int count = -1;
+  if (count < 0) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    int usable = 0;
+    for (int d = 0; d < n; d++) {
+      cudaDeviceProp p;
+      if (cudaGetDeviceProperties(&p, d) == cudaSuccess && p.major == 10) usable++;
+    }
+    count = usable;
+  }
+  return count;
+}
+
+DeviceState* device_state() {
+  if (device_count() <= 0) return nullptr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceState& d = g_devices[dev & 63];
+  if (!d.ready) {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess)
+      return nullptr;
+    memset(h, 0, 64);
+    void* dp = nullptr;
+    if (cudaHostGetDevicePointer(&dp, h, 0) != cudaSuccess) {
+      cudaFreeHost(h);
+      return nullptr;
+    }
+    d.status_host = static_cast<uint32_t*>(h);
+    d.status_dev = static_cast<uint32_t*>(dp);
+    d.ready = true;
+  }
+  return &d;
+}
+
+// ---------------------------------------------------------- lab_alloc registry
+//
+// Allocations from lab_alloc, so that a weight matrix in managed memory is
+// prefetched to the GPU once, at its first use, instead of page-faulting in.
+
+struct Alloc {
+  size_t bytes;
+  int prefetched_to;  // device, or -1
+};
+std::map<uintptr_t, Alloc> g_allocs;
+
+void prefetch_once(const void* p, int dev, cudaStream_t st) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_allocs.upper_bound((uintptr_t)p);
+  if (it == g_allocs.begin()) return;
+  --it;
+  if ((uintptr_t)p >= it->first + it->second.bytes || it->second.prefetched_to == dev) return;
+  if (cudaMemPrefetchAsync((void*)it->first, it->second.bytes, dev, st) == cudaSuccess) {
+    it->second.prefetched_to = dev;
+  } else {
+    cudaGetLastError();
+  }
+}
+
+// ------------------------------------------------------------ call context
+
+struct Buf {
+  void* p = nullptr;
+  size_t cap = 0;
+  bool pinned = false;
+  bool grow(size_t bytes) {
+    if (bytes <= cap) return true;
+    release();
+    size_t want = bytes < 4096 ? 4096 : bytes + bytes / 4;
+    cudaError_t e = pinned ? cudaHostAlloc(&p, want, cudaHostAllocPortable) : cudaMalloc(&p, want);
+    if (!cuda_ok(e)) {
+      p = nullptr;
+      cap = 0;
+      return false;
+    }
+    cap = want;
+    return true;
+  }
+  void release() {
+    if (p != nullptr) {
+      if (pinned) cudaFreeHost(p); else cudaFree(p);
+    }
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+struct CallCtx {
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  Buf dw, ds, dx, dy, dxq, dxsc;  // device staging
+  Buf hx, hy, hxq, hxsc;          // pinned staging
+  CallCtx() { hx.pinned = hy.pinned = hxq.pinned = hxsc.pinned = true; }
+  ~CallCtx() {
+    // At process exit the runtime may already be gone; errors are ignored.
+    for (Buf* b : {&dw, &ds, &dx, &dy, &dxq, &dxsc, &hx, &hy, &hxq, &hxsc}) b->release();
+    if (stream != nullptr) cudaStreamDestroy(stream);
+    cudaGetLastError();
+  }
+};
+
+thread_local CallCtx tl_ctx;
+
+CallCtx* call_ctx() {
+  if (device_state() == nullptr) {
+    set_error(DN_ERR_NO_DEVICE);
+    return nullptr;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  CallCtx& c = tl_ctx;
+  if (c.device != dev) {
+    // A thread that moved to another device starts over there.
+    c.~CallCtx();
+    new (&c) CallCtx();
+    if (!cuda_ok(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking))) return nullptr;
+    c.device = dev;
+  }
+  return &c;
+}
+
+bool on_device(const void* p) {
+  if (p == nullptr) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// An input the kernels may read: itself when device-addressable, else a
+// device copy on the call's stream.
+const void* stage_in(CallCtx* c, Buf& dev, Buf* pinned, const void* p, size_t bytes) {
+  if (p == nullptr || bytes == 0) return p;
+  if (on_device(p)) {
+    prefetch_once(p, c->device, c->stream);
+    return p;
+  }
+  if (!dev.grow(bytes)) return nullptr;
+  const void* src = p;
+  if (pinned != nullptr) {  // small per-call inputs: pinned copy, asynchronous DMA
+    if (!pinned->grow(bytes)) return nullptr;
+    memcpy(pinned->p, p, bytes);
+    src = pinned->p;
+  }
+  if (!cuda_ok(cudaMemcpyAsync(dev.p, src, bytes, cudaMemcpyHostToDevice, c->stream))) return nullptr;
+  return dev.p;
+}
+
+// An output: itself when device-addressable, else device staging that
+// finish_out copies back after the kernels.
+struct Out {
+  void* user = nullptr;
+  void* dev = nullptr;
+  Buf* pinned = nullptr;
+  size_t bytes = 0;
+  bool staged = false;
+};
+
+bool stage_out(Buf& dev, Buf& pinned, void* p, size_t bytes, Out& o) {
+  o.user = p;
+  o.bytes = bytes;
+  o.dev = p;
+  if (p == nullptr || bytes == 0 || on_device(p)) return true;
+  if (!dev.grow(bytes) || !pinned.grow(bytes)) return false;
+  o.dev = dev.p;
+  o.pinned = &pinned;
+  o.staged = true;
+  return true;
+}
+
+bool copy_back(CallCtx* c, const Out& o) {
+  if (!o.staged) return true;
+  return cuda_ok(cudaMemcpyAsync(o.pinned->p, o.dev, o.bytes, cudaMemcpyDeviceToHost, c->stream));
+}
+
+void finish_out(const Out& o) {
+  if (o.staged) memcpy(o.user, o.pinned->p, o.bytes);
+}
+
+bool finish_call(CallCtx* c, DeviceState* d) {
+  if (!cuda_ok(cudaStreamSynchronize(c->stream))) return false;
+  if (d != nullptr && *(volatile uint32_t*)d->status_host != 0) set_error(DN_ERR_CUDA);
+  return true;
+}
+
+size_t q4_bytes(int64_t rows, int64_t cols) {
+  return rows <= 0 ? 0 : (size_t)(((rows - 1) * cols) / 2 + (cols / 32) * 16);
+}
+
+void gemm_entry(bool q4, const void* qs, const void* scales, const float* xs, int8_t* xq,
+                float* xsc, float* ys, int64_t rows, int64_t cols, int64_t n, int64_t mode) {
+  if (rows < 0 || cols < 0 || n < 0 || (mode != 0 && mode != 1)) {
+    set_error(DN_ERR_ARGS);
+    return;
+  }
+  if (n == 0) return;
+  CallCtx* c = call_ctx();
+  DeviceState* d = device_state();
+  if (c == nullptr || d == nullptr) return;
+  const int64_t blocks = cols / 32;
+  const size_t qbytes = q4 ? q4_bytes(rows, cols) : (size_t)(rows * cols);
+  const size_t sbytes = (size_t)(rows * blocks * (q4 ? 2 : 4));
+  const size_t xbytes = (size_t)(n * cols) * 4, ybytes = (size_t)(n * rows) * 4;
+  const size_t xqbytes = (size_t)(n * cols), xscbytes = (size_t)(n * blocks) * 4;
+
+  const void* dqs = rows > 0 && blocks > 0 ? stage_in(c, c->dw, nullptr, qs, qbytes) : qs;
+  const void* dsc = rows > 0 && blocks > 0 ? stage_in(c, c->ds, nullptr, scales, sbytes) : scales;
+  const float* dxs = static_cast<const float*>(stage_in(c, c->dx, &c->hx, xs, xbytes));
+  Out oy, oxq, oxsc;
+  bool ok = (dqs != nullptr || qbytes == 0) && (dsc != nullptr || sbytes == 0) &&
+            (dxs != nullptr || xbytes == 0);
+  ok = ok && stage_out(c->dy, c->hy, ys, ybytes, oy);
+  if (mode == 1) {
+    ok = ok && stage_out(c->dxq, c->hxq, xq, xqbytes, oxq) &&
+         stage_out(c->dxsc, c->hxsc, xsc, xscbytes, oxsc);
+  }
+  if (!ok) return;
+  LinearArgs a{q4,
+               dqs,
+               dsc,
+               dxs,
+               static_cast<int8_t*>(oxq.dev),
+               static_cast<float*>(oxsc.dev),
+               static_cast<float*>(oy.dev),
+               rows,
+               cols,
+               n,
+               rows,
+               mode,
+               d->status_dev};
+  int64_t r = DN_OK;
+  if (rows == 0) {
+    // No rows to multiply; mode 1 still leaves the quantized inputs behind.
+    if (mode == 1 && !cuda_ok(dn::launch_quantize_q8(dxs, a.xq, a.xsc, n, cols, c->stream))) return;
+  } else {
+    r = dn::launch_linear(a, c->stream);
+  }
+  if (r != DN_OK) {
+    set_error(r);
+    return;
+  }
+  if (!copy_back(c, oy) || !copy_back(c, oxq) || !copy_back(c, oxsc)) return;
+  if (!finish_call(c, d)) return;
+  finish_out(oy);
+  finish_out(oxq);
+  finish_out(oxsc);
+}
+
+template <typename QT, typename ST>
+void quantize_entry(bool q4, const float* w, QT* qs, ST* scales, int64_t rows, int64_t cols) {
+  if (rows < 0 || cols < 0) {
+    set_error(DN_ERR_ARGS);
+    return;
+  }
+  const int64_t blocks = cols / 32;
+  if (rows == 0 || blocks == 0) return;
+  CallCtx* c = call_ctx();
+  DeviceState* d = device_state();
+  if (c == nullptr || d == nullptr) return;
+  const size_t wbytes = (size_t)(rows * cols) * 4;
+  const size_t qbytes = q4 ? q4_bytes(rows, cols) : (size_t)(rows * cols);
+  const size_t sbytes = (size_t)(rows * blocks) * (q4 ? 2 : 4);
+  const float* dw = static_cast<const float*>(stage_in(c, c->dx, nullptr, w, wbytes));
+  Out oq, os;
+  if (dw == nullptr || !stage_out(c->dxq, c->hxq, qs, qbytes, oq) ||
+      !stage_out(c->dxsc, c->hxsc, scales, sbytes, os))
+    return;
+  cudaError_t e =
+      q4 ? dn::launch_quantize_q4(dw, static_cast<uint8_t*>(oq.dev), static_cast<uint16_t*>(os.dev),
+                                  rows, cols, c->stream)
+         : dn::launch_quantize_q8(dw, static_cast<int8_t*>(oq.dev), static_cast<float*>(os.dev),
+                                  rows, cols, c->stream);
+  if (!cuda_ok(e) || !copy_back(c, oq) || !copy_back(c, os) || !finish_call(c, d)) return;
+  finish_out(oq);
+  finish_out(os);
+}
+
+}  // namespace
+
+// ======================================================================= lab_*
+
+extern "C" {
+
+void* lab_alloc(int64_t bytes) {
+  if (bytes < 0 || device_state() == nullptr) return nullptr;
+  void* p = nullptr;
+  const size_t n = bytes == 0 ? 1 : (size_t)bytes;
+  if (cudaMallocManaged(&p, n, cudaMemAttachGlobal) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  memset(p, 0, n);
+  std::lock_guard<std::mutex> lock(g_mu);
+  g_allocs[(uintptr_t)p] = Alloc{n, -1};
+  return p;
+}
+
+void lab_free(void* p) {
+  if (p == nullptr) return;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_allocs.erase((uintptr_t)p) == 0) return;  // not ours
+  }
+  cudaFree(p);
+  cudaGetLastError();
+}
+
+int64_t lab_cpu_supported(void) { return device_count() > 0 ? 1 : 0; }
+
+void lab_quantize_q8(const float* w, int8_t* qs, float* scales, int64_t rows, int64_t cols) {
+  quantize_entry<int8_t, float>(false, w, qs, scales, rows, cols);
+}
+
+void lab_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t rows, int64_t cols) {
+  quantize_entry<uint8_t, uint16_t>(true, w, qs, scales, rows, cols);
+}
+
+void lab_gemm_q8(const int8_t* qs, const float* scales, const float* xs, int8_t* xq, float* xsc,
+                 float* ys, int64_t rows, int64_t cols, int64_t n, int64_t threads, int64_t mode) {
+  (void)threads;
+  gemm_entry(false, qs, scales, xs, xq, xsc, ys, rows, cols, n, mode);
+}
+
+void lab_gemm_q4(const uint8_t* qs, const uint16_t* scales, const float* xs, int8_t* xq,
+                 float* xsc, float* ys, int64_t rows, int64_t cols, int64_t n, int64_t threads,
+                 int64_t mode) {
+  (void)threads;
+  gemm_entry(true, qs, scales, xs, xq, xsc, ys, rows, cols, n, mode);
+}
+
+void lab_gemv_q8(const int8_t* qs, const float* scales, const float* x, int8_t* xq, float* xs,
+                 float* y, int64_t rows, int64_t cols, int64_t threads, int64_t mode) {
+  lab_gemm_q8(qs, scales, x, xq, xs, y, rows, cols, 1, threads, mode);
+}
+
+// ======================================================================= dn_*
+
+int64_t dn_linear(int64_t format, const void* qs, const void* scales, const float* xs, int8_t* xq,
+                  float* xsc, float* ys, int64_t rows, int64_t cols, int64_t n, int64_t ldy,
+                  int64_t mode, int64_t path, int64_t flags, void* stream) {
+  if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;
+  if (rows < 0 || cols < 0 || n < 0 || ldy < rows || (mode != 0 && mode != 1)) return DN_ERR_ARGS;
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  LinearArgs a{format == DN_Q4, qs, scales, xs, xq, xsc, ys, rows, cols, n, ldy, mode,
+               d->status_dev};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (path) {
+    case DN_PATH_AUTO:
+      if ((flags & DN_FLAG_PDL) && dn::path_for(a) == 0) return dn::launch_gemv(a, st, true);
+      return dn::launch_linear(a, st);
+    case DN_PATH_GEMV: return dn::launch_gemv(a, st, (flags & DN_FLAG_PDL) != 0);
+    case DN_PATH_TC: return dn::launch_gemm_tc(a, st);
+    case DN_PATH_GENERIC: return dn::launch_generic(a, st);
+    default: return DN_ERR_ARGS;
+  }
+}
+
+int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const float* xs,
+                       const int8_t* xq, int64_t rows, int64_t cols, int64_t n, int64_t mode) {
+  LinearArgs a{format == DN_Q4, qs, scales, xs, const_cast<int8_t*>(xq), nullptr, nullptr, rows,
+               cols, n, rows, mode, nullptr};
+  return dn::path_for(a);
+}
+
+int64_t dn_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
+                       void* stream) {
+  if (n < 0 || cols < 0) return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_quantize_q8(xs, xq, xsc, n, cols, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
+int64_t dn_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t rows, int64_t cols,
+                       void* stream) {
+  if (rows < 0 || cols < 0) return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_quantize_q4(w, qs, scales, rows, cols, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
+int64_t dn_last_error(void) {
+  const int64_t e = tl_last_error;
+  tl_last_error = DN_OK;
+  return e;
+}
+
+int64_t dn_device_status(int64_t clear) {
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  volatile uint32_t* s = d->status_host;
+  const int64_t v = *s;
+  if (clear) *s = 0;
+  return v;
+}
+
+const char* dn_error_string(int64_t code) {
+  switch (code) {
+    case DN_OK: return "ok";
+    case DN_ERR_ARGS: return "invalid arguments";
+    case DN_ERR_CUDA: return "CUDA runtime error";
+    case DN_ERR_NO_DEVICE: return "no usable sm_100 device";
+    case DN_ERR_UNSUPPORTED: return "unsupported combination";
+    case DN_ERR_TOO_LARGE: return "size beyond the stated maximum";
+    default: return "unknown error";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,159 @@
+// Shared device helpers of the Q4_0 / Q8_0 quantized linear kernels (sm_100a).
+//
+// Float arithmetic here is spelled with explicit round-to-nearest intrinsics
+// (__fmul_rn, __fadd_rn, __fmaf_rn, __fdiv_rn) wherever the reference rounds
+// an operation on its own, so that nvcc never contracts a multiply and an add
+// that dianoia's CPU kernels (built with -ffp-contract=off) keep apart.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dn {
+
+constexpr int kBlock = 32;  // weights per Q4_0 / Q8_0 block
+
+// Status bits a kernel leaves in the status word when a bounded wait gives up.
+enum : uint32_t {
+  kStatusTmaTimeout = 1u << 0,   // an mbarrier wait for a bulk copy ran out
+  kStatusPeerTimeout = 1u << 1,  // a wait on another GPU's flag ran out
+  kStatusMmaTimeout = 1u << 2,   // a wait for a tensor-core commit ran out
+};
+
+// How long a bounded wait spins before it records a timeout and returns.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// The status word lives in pinned host memory mapped into the device, so the
+// host reads it after a synchronize with no copy. Bits only ever get set, and
+// only on failure; a plain read-modify-write (PCIe atomics are not assumed)
+// may drop a concurrent bit but never turns a failure into zero.
+__device__ __forceinline__ void report(uint32_t* status, uint32_t bits) {
+  if (status != nullptr) {
+    volatile uint32_t* s = status;
+    *s = *s | bits;
+    __threadfence_system();
+  }
+}
+
+// --------------------------------------------------------------- exact math
+
+// The truncating (int) cast of the reference as x86-64 executes it
+// (cvttss2si): toward zero, and INT32_MIN for NaN or values outside int32.
+__device__ __forceinline__ int32_t trunc_i32_x86(float q) {
+  return (q >= -2147483648.0f && q < 2147483648.0f) ? __float2int_rz(q) : INT32_MIN;
+}
+
+// One element of lab_quantize_q8 (lab_native.c:420-425): q = x * inv,
+// rounded half away from zero by an f32 add of +-0.5 and a truncating cast,
+// clamped to [-127, 127].
+__device__ __forceinline__ int32_t quant_q8_elem(float x, float inv) {
+  float q = __fmul_rn(x, inv);
+  q = q < 0.0f ? __fsub_rn(q, 0.5f) : __fadd_rn(q, 0.5f);
+  const int32_t v = trunc_i32_x86(q);
+  return v > 127 ? 127 : (v < -127 ? -127 : v);
+}
+
+// scale = amax / 127 and inv = 1 / scale (0 when scale is 0), both IEEE
+// round-to-nearest divisions (lab_native.c:416-417).
+__device__ __forceinline__ void q8_scale(float amax, float& scale, float& inv) {
+  scale = __fdiv_rn(amax, 127.0f);
+  inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+}
+
+__device__ __forceinline__ uint32_t pack4(int32_t a, int32_t b, int32_t c, int32_t d) {
+  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) |
+         ((uint32_t)(d & 0xff) << 24);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+  return __half2float(__ushort_as_half(h));  // exact
+}
+
+// --------------------------------------------------------------- PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+// Makes barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for phase `parity` of an mbarrier to complete, for at most
+// kWaitLimitNs. Returns false (and records `bits`) if it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                                  uint32_t bits) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
+      report(status, bits);
+      return false;
+    }
+  }
+}
+
+// 1-D bulk copy global -> shared (TMA engine), completing on `bar` with
+// `bytes` transaction bytes. dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait until the previous kernel's writes are visible.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t lds_u32(const void* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+}  // namespace dn

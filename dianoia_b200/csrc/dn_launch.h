@@ -1,0 +1,50 @@
+// Host-side launchers of the quantized linear kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dn {
+
+// Status codes returned by the launchers and the dn_* entry points.
+enum : int64_t {
+  kOk = 0,
+  kErrArgs = -1,        // a shape, pointer or mode the entry point does not accept
+  kErrCuda = -2,        // a CUDA runtime call failed (see dn_last_cuda_error)
+  kErrNoDevice = -3,    // no usable sm_100 device
+  kErrUnsupported = -4, // a combination this build does not implement
+  kErrTooLarge = -5,    // a size beyond a stated maximum
+};
+
+struct LinearArgs {
+  bool q4;              // Q4_0 (uint8 nibbles + fp16 scales) or Q8_0 (int8 + f32 scales)
+  const void* qs;       // weights, [rows, cols] in the reference layout
+  const void* scales;   // per-block scales, [rows, cols / 32]
+  const float* xs;      // activations [n, cols]
+  int8_t* xq;           // quantized activations out [n, cols] (mode 1; may be null on the fast path)
+  float* xsc;           // their block scales out [n, cols / 32]
+  float* ys;            // outputs, ys[t * ldy + r]
+  int64_t rows, cols, n, ldy, mode;
+  uint32_t* status;     // device word for bounded-wait timeouts (may be null)
+};
+
+// Quantizes n rows of cols floats to Q8_0 (lab_quantize_q8 semantics).
+cudaError_t launch_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
+                               cudaStream_t stream);
+// Quantizes weights to Q4_0 (lab_quantize_q4 semantics).
+cudaError_t launch_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t rows,
+                               int64_t cols, cudaStream_t stream);
+
+// ys = W xs for all n tokens (lab_gemm_q8 / lab_gemm_q4 semantics). Picks the
+// decode GEMV, the tensor-core GEMM or the generic kernel.
+int64_t launch_linear(const LinearArgs& a, cudaStream_t stream);
+
+// Individual paths (exposed for tests and benchmarks through dn_* symbols).
+int64_t launch_gemv(const LinearArgs& a, cudaStream_t stream, bool pdl);
+int64_t launch_generic(const LinearArgs& a, cudaStream_t stream);
+int64_t launch_gemm_tc(const LinearArgs& a, cudaStream_t stream);
+
+// Which path launch_linear would pick (0 gemv, 1 tensor-core gemm, 2 generic).
+int path_for(const LinearArgs& a);
+
+}  // namespace dn

@@ -1,0 +1,138 @@
+/*
+ * dianoia_b200 - C-ABI of the B200 (sm_100a) Q4_0 / Q8_0 quantized linear path.
+ *
+ * libdianoia_b200.so exports the symbols dianoia's Dart code binds through
+ * dart:ffi for its quantized products (lib/src/native.dart:135-243), with
+ * the same signatures and meaning, so the package's NativeQ8Matrix /
+ * NativeQ4Matrix / NativeKernels drive CUDA kernels instead of
+ * src/c/lab_native.c. All shapes are int64; outputs are token-major,
+ * ys[t * rows + r]. Every call is synchronous: results are in place when it
+ * returns, as with the CPU kernels.
+ *
+ * Pointers may be host memory (pageable or pinned: copied to and from the
+ * GPU inside the call), memory from lab_alloc (CUDA managed memory; the GPU
+ * reads it in place, so weights allocated there stay in HBM between calls)
+ * or device memory.
+ *
+ * The reference's C functions report no errors; neither do these, but a
+ * failure is recorded per thread and returned by dn_last_error().
+ *
+ * The dn_* functions below the lab_* block are this library's own
+ * device-resident API (no counterpart in the reference): device pointers,
+ * an explicit CUDA stream, asynchronous, with a status code return.
+ */
+#ifndef DIANOIA_B200_H_
+#define DIANOIA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ lab_* (reference ABI) */
+
+/* Zeroed memory, at least 128-byte aligned, that both the host and the GPU
+ * can address (CUDA managed memory); NULL on failure.
+ * Replaces lab_alloc, src/c/lab_native.c:88-98; bound at lib/src/native.dart:135. */
+void* lab_alloc(int64_t bytes);
+
+/* Frees memory from lab_alloc. Replaces lab_free, lab_native.c:100-104;
+ * bound at native.dart:236. */
+void lab_free(void* p);
+
+/* 1 when the kernels can run here (a CUDA device of compute capability 10.x),
+ * else 0. Replaces lab_cpu_supported, lab_native.c:64-84; bound at native.dart:242. */
+int64_t lab_cpu_supported(void);
+
+/* Q8_0 quantization of rows x cols floats: per block of 32, scale = amax/127,
+ * q = round-half-away(x / scale) clamped to +-127; the trailing cols % 32
+ * values of a row are ignored. Replaces lab_quantize_q8, lab_native.c:407-429;
+ * bound at native.dart:137-148. */
+void lab_quantize_q8(const float* w, int8_t* qs, float* scales, int64_t rows, int64_t cols);
+
+/* Q4_0 quantization (llama.cpp's quantize_row_q4_0_ref) into split nibbles
+ * and fp16 scales. Replaces lab_quantize_q4, lab_native.c:928-955; bound at
+ * native.dart:177-188. */
+void lab_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t rows, int64_t cols);
+
+/* ys[t * rows + r] = (W xs[t])[r] for t < n, W in Q8_0 (qs int8[rows*cols],
+ * scales f32[rows*cols/32]). mode 1 quantizes xs into xq (n*cols bytes) and
+ * xsc (n*cols/32 floats) first and multiplies int8 by int8; mode 0 multiplies
+ * the floats. `threads` is accepted and ignored. Replaces lab_gemm_q8,
+ * lab_native.c:546-579; bound at native.dart:150-175. */
+void lab_gemm_q8(const int8_t* qs, const float* scales, const float* xs, int8_t* xq, float* xsc,
+                 float* ys, int64_t rows, int64_t cols, int64_t n, int64_t threads, int64_t mode);
+
+/* The same for Q4_0 weights (qs uint8[rows*cols/2], scales fp16 bits
+ * uint16[rows*cols/32]). Replaces lab_gemm_q4, lab_native.c:1057-1080; bound
+ * at native.dart:190-216. */
+void lab_gemm_q4(const uint8_t* qs, const uint16_t* scales, const float* xs, int8_t* xq,
+                 float* xsc, float* ys, int64_t rows, int64_t cols, int64_t n, int64_t threads,
+                 int64_t mode);
+
+/* lab_gemm_q8 with n = 1. Replaces lab_gemv_q8, lab_native.c:581-586 (the
+ * reference's stage-5a benchmark symbol; not bound in Dart). */
+void lab_gemv_q8(const int8_t* qs, const float* scales, const float* x, int8_t* xq, float* xs,
+                 float* y, int64_t rows, int64_t cols, int64_t threads, int64_t mode);
+
+/* ------------------------------------------------------------ dn_* (device API) */
+
+/* Status codes of the dn_* functions and of dn_last_error(). */
+#define DN_OK 0
+#define DN_ERR_ARGS (-1)        /* a shape, pointer or mode that is not accepted */
+#define DN_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define DN_ERR_NO_DEVICE (-3)   /* no usable sm_100 device */
+#define DN_ERR_UNSUPPORTED (-4) /* a combination this build does not implement */
+#define DN_ERR_TOO_LARGE (-5)   /* a size beyond a stated maximum */
+
+/* Weight formats and kernel paths for dn_linear. */
+#define DN_Q8 0
+#define DN_Q4 1
+#define DN_PATH_AUTO (-1)
+#define DN_PATH_GEMV 0    /* decode GEMV: bit-exact with lab_native.c */
+#define DN_PATH_TC 1      /* tcgen05 int8 GEMM */
+#define DN_PATH_GENERIC 2 /* any alignment / mode, slow */
+
+/* Flags for dn_linear. DN_FLAG_PDL launches with programmatic dependent
+ * launch: the kernel may start reading the weights before the previous kernel
+ * in the stream has finished, so it is only for weights no kernel in flight
+ * writes. */
+#define DN_FLAG_PDL 1
+
+/* ys[t * ldy + r] = (W xs[t])[r] on `stream` (a cudaStream_t; NULL = default
+ * stream), all pointers device-addressable. `format` DN_Q8 (qs int8, scales
+ * f32) or DN_Q4 (qs nibbles, scales fp16 bits). In mode 1, xq / xsc receive the
+ * quantized activations; the GEMV path accepts NULL for both. Returns DN_OK or
+ * a DN_ERR_* code. */
+int64_t dn_linear(int64_t format, const void* qs, const void* scales, const float* xs, int8_t* xq,
+                  float* xsc, float* ys, int64_t rows, int64_t cols, int64_t n, int64_t ldy,
+                  int64_t mode, int64_t path, int64_t flags, void* stream);
+
+/* Which path DN_PATH_AUTO picks for these arguments. */
+int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const float* xs,
+                       const int8_t* xq, int64_t rows, int64_t cols, int64_t n, int64_t mode);
+
+/* lab_quantize_q8 / lab_quantize_q4 on device memory, asynchronous. */
+int64_t dn_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
+                       void* stream);
+int64_t dn_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t rows, int64_t cols,
+                       void* stream);
+
+/* The calling thread's last error from a lab_* call (DN_OK if none), cleared
+ * by reading. */
+int64_t dn_last_error(void);
+
+/* Bits the kernels on the current device set when a bounded wait gave up
+ * (1: bulk copy, 2: peer flag, 4: tensor-core commit); cleared by reading
+ * when `clear` is non-zero. Call after synchronizing. */
+int64_t dn_device_status(int64_t clear);
+
+/* A short English description of a DN_* code. */
+const char* dn_error_string(int64_t code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIANOIA_B200_H_ */

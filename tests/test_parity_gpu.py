@@ -1,0 +1,238 @@
+"""CUDA path against the oracle, through the C-ABI (GPU only).
+
+The GEMV and generic paths must equal the reference bit for bit (f32 outputs
+included); the tensor-core GEMM must give bit-exact quantized activations and
+f32 outputs within the reference's 1e-5 relative bound
+(native_kernels_test.dart:146-180). Fixtures come from the reference library
+itself; larger shapes are checked against the oracle's C restatement, which
+tests/test_oracle.py pins to the reference.
+"""
+import numpy as np
+import pytest
+
+from conftest import golden_names, load_golden
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+TOL = 1e-5  # max |y - ref| / sum |w x|, the reference's own bound
+
+
+def host_gemm(L, fmt, qs, sc, xs, rows, cols, n, mode):
+    ys = np.full(n * rows, np.nan, np.float32)
+    xq = np.zeros(n * cols, np.int8)
+    xsc = np.zeros(n * (cols // 32) + 1, np.float32)
+    fn = L.lab_gemm_q4 if fmt == "q4" else L.lab_gemm_q8
+    fn(qs.ctypes.data, sc.ctypes.data, xs.ctypes.data, xq.ctypes.data, xsc.ctypes.data,
+       ys.ctypes.data, rows, cols, n, 4, mode)
+    assert L.dn_last_error() == 0
+    return ys, xq, xsc[: n * (cols // 32)]
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def dev_linear(L, fmt, qs, sc, xs, rows, cols, n, mode=1, path=-1, ldy=None, flags=0):
+    """dn_linear on device tensors; returns (ys [n, ldy], xq, xsc) as numpy."""
+    ldy = rows if ldy is None else ldy
+    ys = torch.full((n * ldy,), float("nan"), dtype=torch.float32, device="cuda")
+    xq = torch.zeros(n * cols, dtype=torch.int8, device="cuda")
+    xsc = torch.zeros(n * (cols // 32) + 1, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = L.dn_linear(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
+                     xq.data_ptr(), xsc.data_ptr(), ys.data_ptr(), rows, cols, n, ldy, mode,
+                     path, flags, st)
+    torch.cuda.synchronize()
+    assert rc == 0, L.dn_error_string(rc)
+    assert L.dn_device_status(1) == 0
+    return ys.cpu().numpy(), xq.cpu().numpy(), xsc.cpu().numpy()[: n * (cols // 32)]
+
+
+def same_bits(a, b):
+    return np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
+
+
+def weights(fmt, rng, rows, cols):
+    return orc.q4_weights(rng, rows, cols) if fmt == "q4" else orc.q8_weights(rng, rows, cols)
+
+
+# ----------------------------------------------------------------- fixtures
+
+
+@pytest.mark.parametrize("name", golden_names("linear"))
+@pytest.mark.parametrize("mode", [0, 1])
+def test_golden_through_lab_gemm(cuda_lib, name, mode):
+    g = load_golden(name)
+    fmt, rows, cols, n = str(g["fmt"]), int(g["rows"]), int(g["cols"]), int(g["n"])
+    ys, xq, xsc = host_gemm(cuda_lib, fmt, g["qs"], g["scales"], g["xs"], rows, cols, n, mode)
+    want = g[f"ys_mode{mode}"]
+    path = cuda_lib.dn_linear_path(1 if fmt == "q4" else 0, None, None, None, None, rows, cols, n,
+                                   mode)
+    if mode == 1:
+        assert np.array_equal(xq, g["xq"]) and same_bits(xsc, g["xsc"])
+    if path == 1:  # tensor-core GEMM: tolerance, not bits
+        ref, mag = orc.Oracle().reference_f64(fmt, g["qs"], g["scales"], g["xs"], rows, cols, n, mode)
+        assert orc.max_rel_err(ys, ref, mag) < TOL
+    else:
+        assert same_bits(ys, want)
+
+
+def test_quantizers_on_special_values(cuda_lib):
+    g = load_golden("quant_special")
+    rows, cols = int(g["rows"]), int(g["cols"])
+    x = g["x"]
+    xq = np.zeros(rows * cols, np.int8)
+    xsc = np.zeros(rows * cols // 32, np.float32)
+    cuda_lib.lab_quantize_q8(x.ctypes.data, xq.ctypes.data, xsc.ctypes.data, rows, cols)
+    assert np.array_equal(xq, g["xq"]) and same_bits(xsc, g["xsc"])
+    q4 = np.zeros(rows * cols // 2, np.uint8)
+    s4 = np.zeros(rows * cols // 32, np.uint16)
+    cuda_lib.lab_quantize_q4(x.ctypes.data, q4.ctypes.data, s4.ctypes.data, rows, cols)
+    assert np.array_equal(q4, g["q4"]) and np.array_equal(s4, g["s4"])
+    assert cuda_lib.dn_last_error() == 0
+
+
+# ------------------------------------------------------- configuration shapes
+
+CONFIG_SHAPES = [
+    ("q4", 6144, 2048),   # config 1: Qwen3-1.7B MLP up, Q4_0
+    ("q8", 2048, 2048),   # config 2: q / o
+    ("q8", 1024, 2048),   # config 2: k / v
+    ("q8", 6144, 2048),   # config 2: gate / up
+    ("q8", 2048, 6144),   # config 2: down
+    ("q4", 2048, 6144),   # config 4: down, Q4_0
+    ("q8", 3456, 1152),   # config 5: qkv
+    ("q8", 1152, 4320),   # config 5: fc2, K zero-padded from 4304
+    ("q4", 4304, 1152),   # config 5 fc1 shape in Q4 (K blocks not 16-byte aligned as fp16)
+]
+
+
+@pytest.mark.parametrize("fmt,rows,cols", CONFIG_SHAPES)
+@pytest.mark.parametrize("n", [1, 3, 8])
+def test_config_shapes_bit_exact(cuda_lib, oracle, fmt, rows, cols, n):
+    rng = np.random.default_rng(rows + cols + n)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    want, wq, wsc = oracle.gemm(fmt, qs, sc, xs, rows, cols, n, 1)
+    ys, xq, xsc = dev_linear(cuda_lib, fmt, dev(qs), dev(sc), dev(xs), rows, cols, n, path=0)
+    assert np.array_equal(xq, wq) and same_bits(xsc, wsc)
+    assert same_bits(ys, want)
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+def test_lm_head_bit_exact(cuda_lib, oracle, fmt):
+    rows, cols = 151936, 2048
+    rng = np.random.default_rng(151936)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, 1, cols)
+    want, _, _ = oracle.gemm(fmt, qs, sc, xs, rows, cols, 1, 1)
+    ys, _, _ = dev_linear(cuda_lib, fmt, dev(qs), dev(sc), dev(xs), rows, cols, 1)
+    assert same_bits(ys, want)
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+@pytest.mark.parametrize("rows", [1, 7, 8, 9, 37, 100, 1000, 4097])
+@pytest.mark.parametrize("n", [1, 2, 5, 11])
+def test_ragged_rows_and_tokens(cuda_lib, oracle, fmt, rows, n):
+    cols = 544  # 17 blocks: a partial last stage for both formats
+    rng = np.random.default_rng(rows * 31 + n)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    want, _, _ = oracle.gemm(fmt, qs, sc, xs, rows, cols, n, 1)
+    ys, _, _ = dev_linear(cuda_lib, fmt, dev(qs), dev(sc), dev(xs), rows, cols, n, path=0)
+    assert same_bits(ys, want)
+
+
+def test_strided_output_and_pdl(cuda_lib, oracle):
+    rows, cols, n, ldy = 300, 1024, 3, 1000
+    rng = np.random.default_rng(5)
+    qs, sc = weights("q8", rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    want, _, _ = oracle.gemm("q8", qs, sc, xs, rows, cols, n, 1)
+    ys, _, _ = dev_linear(cuda_lib, "q8", dev(qs), dev(sc), dev(xs), rows, cols, n, ldy=ldy,
+                          flags=1)
+    ys = ys.reshape(n, ldy)
+    assert same_bits(ys[:, :rows].reshape(-1), want)
+    assert np.isnan(ys[:, rows:]).all()  # nothing written past the rows
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_generic_path_unaligned(cuda_lib, oracle, fmt, mode):
+    rows, cols, n = 45, 640, 3
+    rng = np.random.default_rng(77)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    want, wq, wsc = oracle.gemm(fmt, qs, sc, xs, rows, cols, n, mode)
+    raw = torch.zeros(qs.nbytes + 16, dtype=torch.uint8, device="cuda")
+    raw[1: 1 + qs.nbytes] = dev(qs.view(np.uint8))
+    qs_odd = raw[1:]  # 1-byte misaligned: the GEMV's bulk copies cannot take it
+    assert cuda_lib.dn_linear_path(1 if fmt == "q4" else 0, qs_odd.data_ptr(), None, None, None,
+                                   rows, cols, n, mode) == 2
+    ys, xq, xsc = dev_linear(cuda_lib, fmt, qs_odd, dev(sc), dev(xs), rows, cols, n, mode=mode)
+    assert same_bits(ys, want)
+    if mode == 1:
+        assert np.array_equal(xq, wq) and same_bits(xsc, wsc)
+
+
+def test_zero_and_degenerate_shapes(cuda_lib):
+    L = cuda_lib
+    xs = np.ones(64, np.float32)
+    ys = np.full(4, np.nan, np.float32)
+    xq = np.zeros(64, np.int8)
+    xsc = np.zeros(4, np.float32)
+    w = np.zeros(4 * 16, np.int8)
+    s = np.zeros(4, np.float32)
+    # cols < 32: no blocks, every output is +0 as in the reference
+    L.lab_gemm_q8(w.ctypes.data, s.ctypes.data, xs.ctypes.data, xq.ctypes.data, xsc.ctypes.data,
+                  ys.ctypes.data, 4, 16, 1, 1, 1)
+    assert L.dn_last_error() == 0 and (ys == 0).all() and not np.signbit(ys).any()
+    # n = 0 and rows = 0 do nothing and report nothing
+    L.lab_gemm_q8(w.ctypes.data, s.ctypes.data, xs.ctypes.data, xq.ctypes.data, xsc.ctypes.data,
+                  ys.ctypes.data, 4, 32, 0, 1, 1)
+    L.lab_gemm_q8(w.ctypes.data, s.ctypes.data, xs.ctypes.data, xq.ctypes.data, xsc.ctypes.data,
+                  ys.ctypes.data, 0, 32, 2, 1, 1)
+    assert L.dn_last_error() == 0
+    assert xq[:64].any()  # rows = 0 still quantizes, like lab_gemm_q8
+    # bad arguments are reported, not run
+    assert L.dn_linear(0, None, None, None, None, None, None, 4, 32, 1, 2, 1, -1, 0, None) == -1
+    assert L.dn_linear(7, None, None, None, None, None, None, 4, 32, 1, 4, 1, -1, 0, None) == -1
+
+
+def test_native_matrix_mirror(cuda_lib, oracle):
+    from dianoia_b200 import NativeKernels, NativeQ4Matrix, NativeQ8Matrix, StateError
+    NativeKernels.load(None, threads=2)
+    rng = np.random.default_rng(11)
+    rows, cols, n = 37, 2048, 6
+    w = rng.uniform(-0.5, 0.5, rows * cols).astype(np.float32)
+    xs = rng.uniform(-1, 1, n * cols).astype(np.float32)
+    for cls, fmt in ((NativeQ8Matrix, "q8"), (NativeQ4Matrix, "q4")):
+        m = cls.quantize(w, rows, cols)
+        qs = np.array(m.qs_bytes)
+        sc = np.array(m.scale_bytes).view(np.uint16 if fmt == "q4" else np.float32)
+        wq, ws = oracle.quantize_q4(w, rows, cols) if fmt == "q4" else oracle.quantize_q8(w, rows, cols)
+        assert np.array_equal(qs, wq.view(np.uint8)) and np.array_equal(sc.view(np.uint8), ws.view(np.uint8))
+        for int8 in (True, False):
+            ys = np.zeros(n * rows, np.float32)
+            m.apply(xs, ys, n, int8_inputs=int8)
+            want, _, _ = oracle.gemm(fmt, wq, ws, xs, rows, cols, n, 1 if int8 else 0)
+            assert same_bits(ys, want)
+        if fmt == "q8":
+            assert m.weight_at(3, 100) == float(wq[3 * cols + 100]) * float(ws[(3 * cols + 100) // 32])
+        m.free()
+        m.free()  # a second free is a no-op
+        with pytest.raises(StateError):
+            m.apply(xs, np.zeros(n * rows, np.float32), n)
+
+
+def test_repeat_calls_identical(cuda_lib):
+    rng = np.random.default_rng(2)
+    rows, cols = 4096, 2048
+    qs, sc = weights("q4", rng, rows, cols)
+    xs = orc.activations(rng, 1, cols)
+    a = host_gemm(cuda_lib, "q4", qs, sc, xs, rows, cols, 1, 1)[0]
+    b = host_gemm(cuda_lib, "q4", qs, sc, xs, rows, cols, 1, 1)[0]
+    assert same_bits(a, b)
