@@ -31,6 +31,8 @@ SIGNATURES = {
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_quantize_q4": (_i64, [_p, _p, _p, _i64, _i64, _p]),
+    "dn_quantize_qa": (_i64, [_p, _p, _i64, _i64, _i64, _p]),
+    "dn_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_last_error": (_i64, []),
     "dn_device_status": (_i64, [_i64]),
     "dn_error_string": (ctypes.c_char_p, [_i64]),
@@ -41,6 +43,7 @@ DN_OK, DN_ERR_ARGS, DN_ERR_CUDA, DN_ERR_NO_DEVICE, DN_ERR_UNSUPPORTED, DN_ERR_TO
 DN_Q8, DN_Q4 = 0, 1
 DN_PATH_AUTO, DN_PATH_GEMV, DN_PATH_TC, DN_PATH_GENERIC = -1, 0, 1, 2
 DN_FLAG_PDL = 1
+QA_BYTES = 36  # QA activation block: 32 int8 + f32 scale
 
 _lib = None
 

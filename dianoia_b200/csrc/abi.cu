@@ -214,7 +214,11 @@ struct Out {
   bool staged = false;
 };
 
-bool stage_out(Buf& dev, Buf& pinned, void* p, size_t bytes, Out& o) {
+// With `preserve`, the staging starts as a copy of the user's buffer, for
+// outputs the kernels only partly write (xq when cols % 32 != 0: the
+// reference leaves each row's tail untouched).
+bool stage_out(CallCtx* c, Buf& dev, Buf& pinned, void* p, size_t bytes, Out& o,
+               bool preserve = false) {
   o.user = p;
   o.bytes = bytes;
   o.dev = p;
@@ -223,6 +227,11 @@ bool stage_out(Buf& dev, Buf& pinned, void* p, size_t bytes, Out& o) {
   o.dev = dev.p;
   o.pinned = &pinned;
   o.staged = true;
+  if (preserve) {
+    memcpy(pinned.p, p, bytes);
+    if (!cuda_ok(cudaMemcpyAsync(dev.p, pinned.p, bytes, cudaMemcpyHostToDevice, c->stream)))
+      return false;
+  }
   return true;
 }
 
@@ -267,10 +276,10 @@ void gemm_entry(bool q4, const void* qs, const void* scales, const float* xs, in
   Out oy, oxq, oxsc;
   bool ok = (dqs != nullptr || qbytes == 0) && (dsc != nullptr || sbytes == 0) &&
             (dxs != nullptr || xbytes == 0);
-  ok = ok && stage_out(c->dy, c->hy, ys, ybytes, oy);
+  ok = ok && stage_out(c, c->dy, c->hy, ys, ybytes, oy);
   if (mode == 1) {
-    ok = ok && stage_out(c->dxq, c->hxq, xq, xqbytes, oxq) &&
-         stage_out(c->dxsc, c->hxsc, xsc, xscbytes, oxsc);
+    ok = ok && stage_out(c, c->dxq, c->hxq, xq, xqbytes, oxq, cols % 32 != 0) &&
+         stage_out(c, c->dxsc, c->hxsc, xsc, xscbytes, oxsc);
   }
   if (!ok) return;
   LinearArgs a{q4,
@@ -320,8 +329,8 @@ void quantize_entry(bool q4, const float* w, QT* qs, ST* scales, int64_t rows, i
   const size_t sbytes = (size_t)(rows * blocks) * (q4 ? 2 : 4);
   const float* dw = static_cast<const float*>(stage_in(c, c->dx, nullptr, w, wbytes));
   Out oq, os;
-  if (dw == nullptr || !stage_out(c->dxq, c->hxq, qs, qbytes, oq) ||
-      !stage_out(c->dxsc, c->hxsc, scales, sbytes, os))
+  if (dw == nullptr || !stage_out(c, c->dxq, c->hxq, qs, qbytes, oq, cols % 32 != 0) ||
+      !stage_out(c, c->dxsc, c->hxsc, scales, sbytes, os))
     return;
   cudaError_t e =
       q4 ? dn::launch_quantize_q4(dw, static_cast<uint8_t*>(oq.dev), static_cast<uint16_t*>(os.dev),
@@ -416,7 +425,9 @@ int64_t dn_linear(int64_t format, const void* qs, const void* scales, const floa
 
 int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const float* xs,
                        const int8_t* xq, int64_t rows, int64_t cols, int64_t n, int64_t mode) {
-  LinearArgs a{format == DN_Q4, qs, scales, xs, const_cast<int8_t*>(xq), nullptr, nullptr, rows,
+  // Null pointers stand for "suitably aligned" in this query.
+  const float* x = xs != nullptr ? xs : reinterpret_cast<const float*>(256);
+  LinearArgs a{format == DN_Q4, qs, scales, x, const_cast<int8_t*>(xq), nullptr, nullptr, rows,
                cols, n, rows, mode, nullptr};
   return dn::path_for(a);
 }
@@ -439,6 +450,43 @@ int64_t dn_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t ro
                  cudaSuccess
              ? DN_OK
              : DN_ERR_CUDA;
+}
+
+int64_t dn_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols, int64_t xa_stride,
+                       void* stream) {
+  if (n < 0 || cols < 0 || xa_stride < (cols / 32) * dn::kQABytes) return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_quantize_qa(xs, xa, n, cols, xa_stride, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
+int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
+                     int64_t xa_stride, float* ys, int64_t ldy, uint8_t* ya, int64_t ya_stride,
+                     int64_t rows, int64_t cols, int64_t n, int64_t flags, void* stream) {
+  if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;
+  if (rows < 0 || cols < 0 || n < 0 || xa == nullptr || xa_stride < (cols / 32) * dn::kQABytes)
+    return DN_ERR_ARGS;
+  if (ys != nullptr && ldy < rows) return DN_ERR_ARGS;
+  if (ya != nullptr && ya_stride < (rows / 32) * dn::kQABytes) return DN_ERR_ARGS;
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  dn::GemvArgs g{};
+  g.q4 = format == DN_Q4;
+  g.qs = qs;
+  g.scales = scales;
+  g.xa = xa;
+  g.xa_stride = xa_stride;
+  g.ys = ys;
+  g.ldy = ldy;
+  g.ya = ya;
+  g.ya_stride = ya_stride;
+  g.rows = rows;
+  g.cols = cols;
+  g.n = n;
+  g.status = d->status_dev;
+  return dn::launch_gemv_ex(g, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
 }
 
 int64_t dn_last_error(void) {

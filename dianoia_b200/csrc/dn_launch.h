@@ -28,6 +28,35 @@ struct LinearArgs {
   uint32_t* status;     // device word for bounded-wait timeouts (may be null)
 };
 
+// Quantized activations ("QA" blocks): per 32 values, the 32 int8 of
+// lab_quantize_q8 followed by their f32 scale, 36 bytes. A decode chain hands
+// these from one GEMV's epilogue to the next GEMV's prologue.
+constexpr int kQABytes = 36;
+
+struct GemvArgs {
+  bool q4;
+  const void* qs;
+  const void* scales;
+  const float* xs;        // f32 activations [n, cols] (quantized in the CTA), or null
+  const uint8_t* xa;      // QA activations, token t at xa + t * xa_stride, or null
+  int64_t xa_stride;
+  int8_t* xq;             // with xs: lab_gemm's quantized inputs out (optional)
+  float* xsc;
+  float* ys;              // f32 outputs ys[t * ldy + r] (optional)
+  int64_t ldy;
+  uint8_t* ya;            // QA outputs, block r/32 of token t at ya + t * ya_stride (optional)
+  int64_t ya_stride;
+  int64_t rows, cols, n;
+  uint32_t* status;
+};
+
+// The decode GEMV on either activation form (gemv.cu).
+int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl);
+bool gemv_ex_supported(const GemvArgs& g);
+// f32 -> QA blocks (quantize.cu).
+cudaError_t launch_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols,
+                               int64_t xa_stride, cudaStream_t stream);
+
 // Quantizes n rows of cols floats to Q8_0 (lab_quantize_q8 semantics).
 cudaError_t launch_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
                                cudaStream_t stream);

@@ -54,6 +54,41 @@ __global__ void __launch_bounds__(kQuantThreads)
   if (sub == 0) xsc[t * blocks + b] = scale;
 }
 
+// The same quantization into QA blocks (32 int8, then the f32 scale):
+// token t's block b at xa + t * xa_stride + 36 * b.
+__global__ void __launch_bounds__(kQuantThreads)
+    quantize_qa_kernel(const float* __restrict__ xs, uint8_t* __restrict__ xa, int64_t n,
+                       int64_t cols, int64_t blocks, int64_t xa_stride, bool vec) {
+  const int64_t gid = (int64_t)blockIdx.x * kQuantThreads + threadIdx.x;
+  const int64_t blk = gid >> 3;
+  const int sub = (int)(gid & 7);
+  const bool active = blk < n * blocks;
+  const int64_t t = active ? blk / blocks : 0, b = active ? blk % blocks : 0;
+  const float* src = xs + t * cols + b * kBlock + sub * 4;
+  float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (active) {
+    if (vec) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(src));
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+      for (int i = 0; i < 4; i++) v[i] = __ldg(src + i);
+    }
+  }
+  float amax = 0.0f;
+  for (int i = 0; i < 4; i++) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  float scale, inv;
+  q8_scale(amax, scale, inv);
+  if (!active) return;
+  uint8_t* dst = xa + t * xa_stride + b * kQABytes;
+  *reinterpret_cast<uint32_t*>(dst + sub * 4) =
+      pack4(quant_q8_elem(v[0], inv), quant_q8_elem(v[1], inv), quant_q8_elem(v[2], inv),
+            quant_q8_elem(v[3], inv));
+  if (sub == 0) *reinterpret_cast<float*>(dst + 32) = scale;
+}
+
 // lab_quantize_q4 (lab_native.c:928-955): sixteen lanes per block, lane k
 // holds values k and k + 16, which share byte k of the block.
 __global__ void __launch_bounds__(kQuantThreads)
@@ -103,6 +138,17 @@ cudaError_t launch_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t 
   const int64_t grid = (threads + kQuantThreads - 1) / kQuantThreads;
   quantize_q8_kernel<<<(unsigned)grid, kQuantThreads, 0, stream>>>(xs, xq, xsc, n, cols, blocks,
                                                                    vec);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols,
+                               int64_t xa_stride, cudaStream_t stream) {
+  const int64_t blocks = cols / kBlock;
+  if (n <= 0 || blocks <= 0) return cudaSuccess;
+  const bool vec = cols % 4 == 0 && ((uintptr_t)xs & 15) == 0;
+  const int64_t grid = (n * blocks * 8 + kQuantThreads - 1) / kQuantThreads;
+  quantize_qa_kernel<<<(unsigned)grid, kQuantThreads, 0, stream>>>(xs, xa, n, cols, blocks,
+                                                                   xa_stride, vec);
   return cudaGetLastError();
 }
 

@@ -119,6 +119,22 @@ int64_t dn_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64
 int64_t dn_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t rows, int64_t cols,
                        void* stream);
 
+/* Quantized activations ("QA" blocks) for chains of products: per 32 values,
+ * the 32 int8 that lab_quantize_q8 gives, then their f32 scale (36 bytes).
+ * Token t starts at xa + t * xa_stride. dn_quantize_qa writes them from f32
+ * activations [n, cols]. */
+int64_t dn_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols, int64_t xa_stride,
+                       void* stream);
+
+/* The decode GEMV on QA activations: ys[t * ldy + r] = (W x_t)[r] (ys may be
+ * NULL), and, when ya is not NULL, the outputs quantized again into QA blocks
+ * (block r / 32 of token t at ya + t * ya_stride; only whole 32-row blocks),
+ * ready to be the next product's input. Results equal lab_gemm_q8 /
+ * lab_gemm_q4 (mode 1) on the dequantized inputs, bit for bit. */
+int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
+                     int64_t xa_stride, float* ys, int64_t ldy, uint8_t* ya, int64_t ya_stride,
+                     int64_t rows, int64_t cols, int64_t n, int64_t flags, void* stream);
+
 /* The calling thread's last error from a lab_* call (DN_OK if none), cleared
  * by reading. */
 int64_t dn_last_error(void);

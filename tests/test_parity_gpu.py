@@ -236,3 +236,72 @@ def test_repeat_calls_identical(cuda_lib):
     a = host_gemm(cuda_lib, "q4", qs, sc, xs, rows, cols, 1, 1)[0]
     b = host_gemm(cuda_lib, "q4", qs, sc, xs, rows, cols, 1, 1)[0]
     assert same_bits(a, b)
+
+
+# ------------------------------------------------- quantized-activation chain
+
+
+def qa_pack(xq, xsc, n, cols):
+    """QA blocks (32 int8 + f32 scale per block) from separate xq / xsc."""
+    blocks = cols // 32
+    out = np.zeros((n, blocks, 36), np.uint8)
+    out[:, :, :32] = xq.reshape(n, blocks, 32).view(np.uint8)
+    out[:, :, 32:] = xsc.reshape(n, blocks, 1).view(np.uint8).reshape(n, blocks, 4)
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("fmt,rows,cols", [("q8", 4096, 2048), ("q4", 6144, 2048),
+                                           ("q8", 2048, 6144), ("q8", 1152, 4320),
+                                           ("q4", 96, 1152)])
+@pytest.mark.parametrize("n", [1, 4])
+def test_qa_linear_matches_lab_gemm(cuda_lib, oracle, fmt, rows, cols, n):
+    L = cuda_lib
+    rng = np.random.default_rng(rows ^ cols ^ n)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    want, wq, wsc = oracle.gemm(fmt, qs, sc, xs, rows, cols, n, 1)
+    st = torch.cuda.current_stream().cuda_stream
+    xs_d = dev(xs)
+    xa = torch.zeros(n * (cols // 32) * 36, dtype=torch.uint8, device="cuda")
+    assert L.dn_quantize_qa(xs_d.data_ptr(), xa.data_ptr(), n, cols, cols // 32 * 36, st) == 0
+    ys = torch.full((n * rows,), float("nan"), device="cuda")
+    ya = torch.zeros(n * (rows // 32) * 36, dtype=torch.uint8, device="cuda")
+    qs_d, sc_d = dev(qs), dev(sc)
+    rc = L.dn_linear_qa(1 if fmt == "q4" else 0, qs_d.data_ptr(), sc_d.data_ptr(), xa.data_ptr(),
+                        cols // 32 * 36, ys.data_ptr(), rows, ya.data_ptr(), rows // 32 * 36,
+                        rows, cols, n, 1, st)
+    torch.cuda.synchronize()
+    assert rc == 0 and L.dn_device_status(1) == 0
+    assert np.array_equal(xa.cpu().numpy(), qa_pack(wq, wsc, n, cols))
+    assert same_bits(ys.cpu().numpy(), want)
+    yq, ysc = oracle.quantize_q8(want, n, rows)
+    assert np.array_equal(ya.cpu().numpy(), qa_pack(yq, ysc, n, rows))
+
+
+def test_qa_chain_of_projections(cuda_lib, oracle):
+    """qkv -> o -> gate/up -> down as in the benchmark, against per-call oracle products."""
+    L = cuda_lib
+    rng = np.random.default_rng(42)
+    shapes = [("qkv", 4096, 2048), ("o", 2048, 2048), ("gu", 12288, 2048), ("down", 2048, 6144)]
+    mats = {name: weights("q8", rng, r, c) for name, r, c in shapes}
+    x0 = orc.activations(rng, 1, 2048)
+    st = torch.cuda.current_stream().cuda_stream
+    xa = torch.zeros(2048 // 32 * 36, dtype=torch.uint8, device="cuda")
+    assert L.dn_quantize_qa(dev(x0).data_ptr(), xa.data_ptr(), 1, 2048, 2048 // 32 * 36, st) == 0
+    x_host = x0
+    keep = []
+    for name, r, c in shapes:
+        qs, sc = mats[name]
+        want, _, _ = oracle.gemm("q8", qs, sc, x_host, r, c, 1, 1)
+        ys = torch.zeros(r, device="cuda")
+        ya = torch.zeros(r // 32 * 36, dtype=torch.uint8, device="cuda")
+        qd, sd = dev(qs), dev(sc)
+        keep += [qd, sd, ys, ya]
+        assert L.dn_linear_qa(0, qd.data_ptr(), sd.data_ptr(), xa.data_ptr(), c // 32 * 36,
+                              ys.data_ptr(), r, ya.data_ptr(), r // 32 * 36, r, c, 1, 1, st) == 0
+        torch.cuda.synchronize()
+        assert same_bits(ys.cpu().numpy(), want), name
+        nxt = {"qkv": 2048, "o": 2048, "gu": 6144, "down": 2048}[name]
+        x_host = want[:nxt].copy()
+        xa = ya  # the prefix of the QA output feeds the next product
+    assert L.dn_device_status(1) == 0
