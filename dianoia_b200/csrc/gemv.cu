@@ -17,69 +17,127 @@
 // nibbles go straight into dp4a and the "- 8" is folded in as -8 * (sum of the
 // lane's eight activations), precomputed once per token and block.
 //
-// Memory path: weights stream from HBM with 1-D TMA bulk copies
-// (cp.async.bulk) of one 512-byte row chunk each into a 4-stage shared-memory
-// ring, completing on an mbarrier per stage; rows sit 16 bytes apart in
-// shared memory beyond their 512 bytes so the lanes' 4-byte reads are free of
-// bank conflicts. Every CTA quantizes the activations itself (they are small
-// and L2-resident), which fuses the activation quantize into the GEMV; CTA
-// column 0 also writes xq / xsc out, as lab_gemm_* does.
+// Memory path: a persistent, warp-specialized kernel. Each CTA owns a set of
+// 32-row tiles (one Q8_0 block of the output each). A producer warp streams
+// the weights of all its tiles, chunk by chunk (512 bytes of each row plus
+// its scales), through a shared-memory ring with 2-D TMA tensor copies of
+// 32 rows x 128 bytes (4 KB boxes, 128-byte swizzle) that complete on a
+// "full" mbarrier per stage; four consumer warps compute and release each
+// stage on an "empty" mbarrier, so the next tile's weights are in flight
+// while the current one is computed. Few, large copies keep enough bytes in
+// flight per SM (many 512-byte copies capped the stream near 2 TB/s), and
+// the swizzle puts the eight rows a warp reads at once in eight different
+// bank groups. The activations are loaded once
+// per CTA: f32 inputs are bulk-copied and quantized in the CTA (which fuses
+// lab_gemm's input quantize; CTA 0 also writes xq / xsc out), QA inputs are
+// bulk-copied as they are. Each tile's 32 outputs per token can be quantized
+// again in the epilogue (QA output) for the next product of a chain.
+#include <string.h>
+
 #include <algorithm>
 
 #include "dn_common.cuh"
 #include "dn_launch.h"
+#include "dn_tmap.h"
 
 namespace dn {
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kWarps = 4;
-constexpr int kRows = 8 * kWarps;  // rows per CTA: one Q8_0 block of the output
-constexpr int kThreads = 32 * kWarps;
-constexpr int kRowPad = 16;        // bytes between consecutive rows of a stage
-constexpr int kChunkBytes = 512;   // weight bytes per row per stage
-constexpr int kMaxSmem = 227 * 1024;
+constexpr int kConsumerWarps = 4;
+constexpr int kRows = 8 * kConsumerWarps;   // rows per tile: one Q8_0 block of the output
+constexpr int kConsumers = 32 * kConsumerWarps;
+constexpr int kThreads = kConsumers + 32;   // + one producer warp
+constexpr int kChunkBytes = 512;            // weight bytes per row per stage
+constexpr int kBoxBytes = 128;              // inner box width (the 128-byte swizzle span)
+constexpr int kBox = kRows * kBoxBytes;     // 4 KB per box in shared memory
+constexpr int kWBoxes = kChunkBytes / kBoxBytes;
+constexpr int kScaleRow = 64;               // scale bytes per row per stage (16 f32 / 32 fp16)
+constexpr int kStageBytes = kWBoxes * kBox + kRows * kScaleRow;  // weight boxes + scale box
+constexpr int kMaxSmem = 226 * 1024;  // dynamic; leaves room for static smem
+constexpr int kSmemPerSM = 228 * 1024;
+constexpr int kSMs = 148;
+constexpr int kMaxStages = 16;
 
 template <bool Q4>
 struct Fmt {
   static constexpr int kWB = Q4 ? 16 : 32;          // weight bytes per block
   static constexpr int kSB = Q4 ? 2 : 4;            // scale bytes per block
-  static constexpr int kKC = kChunkBytes / kWB;     // blocks per stage
-  static constexpr int kWStride = kKC * kWB + kRowPad;
-  static constexpr int kSStride = kKC * kSB + kRowPad;
+  static constexpr int kKC = kChunkBytes / kWB;     // blocks per stage (scales: 64 bytes)
 };
 
 __host__ __device__ inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 struct SmemPlan {
-  int64_t w_off, s_off, bar_off, xa_off, xa_stride, xs8_off, yt_off, xf_off, total;
+  int64_t bar_off, xw_off, xw_stride, xs_off, xs_stride, yt_off, stg_off, stg_stride, total;
 };
 
-// bars: kStages weight stages, then two activation barriers.
+// Activations in shared memory, lane-interleaved: for block b, lane l's two
+// words (bytes 4l..4l+3 and 16+4l..16+4l+3 of the block) sit together, so a
+// lane reads its block operand with one 64-bit load (Q8). Q4 adds the lane's
+// -8 * sum term: 16 bytes per lane, one 128-bit load. Block scales are a
+// separate f32 array.
 template <bool Q4>
-__host__ __device__ inline SmemPlan plan(int nt, int64_t cols, bool f32_in) {
-  using F = Fmt<Q4>;
+struct XLayout {
+  static constexpr int kLaneBytes = Q4 ? 16 : 8;
+  static constexpr int kBlockBytes = 4 * kLaneBytes;
+  // Offset of word w (0..7) of a block.
+  __device__ static __forceinline__ int word_off(int w) { return (w & 3) * kLaneBytes + (w >> 2) * 4; }
+};
+
+// Layout from a 1024-byte aligned base: the stages, the barriers (`stages`
+// full, `stages` empty, two activation, two epilogue), the activations, the
+// epilogue's outputs and the input staging. `total` includes the slack to
+// align the base.
+template <bool Q4>
+__host__ __device__ inline SmemPlan plan(int stages, int nt, int64_t cols, bool f32_in) {
   const int64_t blocks = cols / kBlock;
   SmemPlan p;
-  p.w_off = 0;
-  p.s_off = p.w_off + (int64_t)kStages * kRows * F::kWStride;
-  p.bar_off = p.s_off + (int64_t)kStages * kRows * F::kSStride;
-  p.xa_off = round_up(p.bar_off + 8 * (kStages + 2), 128);
-  p.xa_stride = round_up(blocks * kQABytes, 16);
-  p.xs8_off = p.xa_off + nt * p.xa_stride;
-  p.yt_off = p.xs8_off + (Q4 ? (int64_t)nt * blocks * 16 : 0);
-  p.xf_off = round_up(p.yt_off + (int64_t)nt * kRows * 4, 128);
-  p.total = p.xf_off + (f32_in ? 2 * cols * 4 : 0);
+  p.bar_off = (int64_t)stages * kStageBytes;
+  p.xw_off = round_up(p.bar_off + 8 * (2 * stages + 4), 128);
+  p.xw_stride = blocks * XLayout<Q4>::kBlockBytes;
+  p.xs_off = p.xw_off + nt * p.xw_stride;
+  p.xs_stride = round_up(blocks, 4);
+  p.yt_off = p.xs_off + nt * p.xs_stride * 4;
+  p.stg_off = round_up(p.yt_off + 2 * (int64_t)nt * kRows * 4, 128);
+  p.stg_stride = f32_in ? cols * 4 : round_up(blocks * kQABytes, 16);
+  p.total = p.stg_off + (f32_in ? 2 : nt) * p.stg_stride + 1024;
   return p;
 }
 
-// Quantizes one token of f32 activations (in shared memory) into QA blocks in
-// shared memory, eight lanes per block (lab_quantize_q8 semantics). With
-// `xq`, also writes lab_gemm's xq / xsc outputs for that token.
-__device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xa, int64_t blocks,
-                                               int8_t* xq, float* xsc) {
+// In a 128-byte-swizzled box of 32 rows x 128 bytes, byte `col` of row r
+// sits at r * 128 + (((col / 16) ^ (r % 8)) * 16) + col % 16: the 16-byte
+// chunk index is XORed with r mod 8.
+// A bounded wait whose result is the same on every lane of the warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  const bool got = mbar_wait_bounded(bar, parity, status, kStatusTmaTimeout);
+  return __all_sync(0xffffffffu, got) != 0;
+}
+
+// Named barrier over the consumer warps only (the producer never joins);
+// used in the prologue, which every consumer thread always reaches.
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ T lds(const void* p) {
+  return *reinterpret_cast<const T*>(p);
+}
+
+// -8 * (sum of the eight int8 a lane multiplies in one block).
+__device__ __forceinline__ int32_t lane_sum8(uint32_t w0, uint32_t w1) {
+  return -8 * __dp4a((int32_t)w0, 0x01010101, __dp4a((int32_t)w1, 0x01010101, 0));
+}
+
+// Quantizes one token of f32 activations (in shared memory) into the
+// lane-interleaved layout, eight lanes per block (lab_quantize_q8
+// semantics). With `xq`, also writes lab_gemm's xq / xsc outputs.
+template <bool Q4>
+__device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xw, float* xs,
+                                               int64_t blocks, int8_t* xq, float* xsc) {
+  using X = XLayout<Q4>;
   const int tid = threadIdx.x, sub = tid & 7;
-  for (int64_t base = 0; base < blocks; base += kThreads / 8) {
+  for (int64_t base = 0; base < blocks; base += kConsumers / 8) {
     const int64_t b = base + (tid >> 3);
     const bool active = b < blocks;
     const float4 v = active ? *reinterpret_cast<const float4*>(xf + b * kBlock + sub * 4)
@@ -92,9 +150,12 @@ __device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xa, int
     q8_scale(amax, scale, inv);
     const uint32_t word = pack4(quant_q8_elem(v.x, inv), quant_q8_elem(v.y, inv),
                                 quant_q8_elem(v.z, inv), quant_q8_elem(v.w, inv));
+    const uint32_t hi_word = __shfl_down_sync(0xffffffffu, word, 4);  // sub < 4: word sub + 4
     if (active) {
-      *reinterpret_cast<uint32_t*>(xa + b * kQABytes + sub * 4) = word;
-      if (sub == 0) *reinterpret_cast<float*>(xa + b * kQABytes + 32) = scale;
+      uint8_t* blk = xw + b * X::kBlockBytes;
+      *reinterpret_cast<uint32_t*>(blk + X::word_off(sub)) = word;
+      if (Q4 && sub < 4) *reinterpret_cast<int32_t*>(blk + sub * 16 + 8) = lane_sum8(word, hi_word);
+      if (sub == 0) xs[b] = scale;
       if (xq != nullptr) {
         *reinterpret_cast<uint32_t*>(xq + b * kBlock + sub * 4) = word;
         if (sub == 0) xsc[b] = scale;
@@ -103,61 +164,111 @@ __device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xa, int
   }
 }
 
+// QA blocks (staged in shared memory) -> the lane-interleaved layout.
+template <bool Q4>
+__device__ __forceinline__ void unpack_qa(const uint8_t* qa, uint8_t* xw, float* xs, int64_t blocks) {
+  using X = XLayout<Q4>;
+  for (int64_t i = threadIdx.x; i < blocks * 4; i += kConsumers) {
+    const int64_t b = i >> 2;
+    const int ll = (int)(i & 3);
+    const uint8_t* src = qa + b * kQABytes;
+    const uint32_t w0 = lds<uint32_t>(src + 4 * ll), w1 = lds<uint32_t>(src + 16 + 4 * ll);
+    uint8_t* dst = xw + b * X::kBlockBytes + ll * X::kLaneBytes;
+    if (Q4) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w0, w1, (uint32_t)lane_sum8(w0, w1), 0u);
+    } else {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+    }
+    if (ll == 0) xs[b] = lds<float>(src + 32);
+  }
+}
+
 template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN>
-__global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads)
+    gemv_i8_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
+                   const __grid_constant__ CUtensorMap tsc) {
   using F = Fmt<Q4>;
-  extern __shared__ __align__(128) uint8_t smem[];
+  using X = XLayout<Q4>;
+  constexpr int kPerBox = kBoxBytes / F::kWB;  // blocks per weight box: 4 (Q8) or 8 (Q4)
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int r8 = lane >> 2, l = lane & 3;
   const int64_t blocks = a.cols / kBlock;
-  const int64_t row0 = (int64_t)blockIdx.x * kRows;
-  const int tile_rows = (int)min64(kRows, a.rows - row0);
+  const int64_t ntiles = (a.rows + kRows - 1) / kRows;
   const int64_t t0 = (int64_t)blockIdx.y * NT;
   const int nt = (int)min64(NT, a.n - t0);
-  const int nchunks = (int)((blocks + F::kKC - 1) / F::kKC);
-  const SmemPlan sp = plan<Q4>(NT, a.cols, F32_IN);
-  uint8_t* w_s = smem + sp.w_off;
-  uint8_t* s_s = smem + sp.s_off;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sp.bar_off);
-  uint64_t* xbars = bars + kStages;
-  uint8_t* xa_s = smem + sp.xa_off;
-  int32_t* xs8_s = reinterpret_cast<int32_t*>(smem + sp.xs8_off);
+  const int nch = (int)((blocks + F::kKC - 1) / F::kKC);
+  // This CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int64_t my_tiles = (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  const int64_t total = my_tiles * nch;
+  const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_off);
+  uint64_t* empty = full + stages;
+  uint64_t* xbars = empty + stages;
+  uint64_t* epi = xbars + 2;
+  uint8_t* xw_s = smem + sp.xw_off;
+  float* xs_s = reinterpret_cast<float*>(smem + sp.xs_off);
   float* yt_s = reinterpret_cast<float*>(smem + sp.yt_off);
-  float* xf_s = reinterpret_cast<float*>(smem + sp.xf_off);
+  uint8_t* stg_s = smem + sp.stg_off;
+  __shared__ volatile int abort_flag;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages + 2; s++) mbar_init(&bars[s], 1);
+    for (int s = 0; s < stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(&xbars[0], 1);
+    mbar_init(&xbars[1], 1);
+    mbar_init(&epi[0], kConsumers);
+    mbar_init(&epi[1], kConsumers);
+    abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
 
-  const uint8_t* qs = static_cast<const uint8_t*>(a.qs);
-  const uint8_t* sc = static_cast<const uint8_t*>(a.scales);
-  const int64_t wrow_bytes = blocks * F::kWB, srow_bytes = blocks * F::kSB;
-  // Warp 0 issues one stage: a bulk copy per row of its weight chunk (and of
-  // its scale chunk when those are 16-byte aligned).
-  auto issue = [&](int c) {
-    const int s = c % kStages;
-    const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-    const uint32_t wbytes = nb * F::kWB, sbytes = TMA_SCALES ? nb * F::kSB : 0;
-    if (lane == 0) mbar_arrive_expect_tx(&bars[s], (uint32_t)tile_rows * (wbytes + sbytes));
-    __syncwarp();
-    for (int r = lane; r < tile_rows; r += 32) {
-      bulk_g2s(w_s + (s * kRows + r) * F::kWStride,
-               qs + (row0 + r) * wrow_bytes + (int64_t)c * F::kKC * F::kWB, wbytes, &bars[s]);
-      if (TMA_SCALES)
-        bulk_g2s(s_s + (s * kRows + r) * F::kSStride,
-                 sc + (row0 + r) * srow_bytes + (int64_t)c * F::kKC * F::kSB, sbytes, &bars[s]);
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    // The weights do not depend on the previous kernel, so no PDL wait here.
+    if (lane == 0) {
+      prefetch_tmap(&tw);
+      if (TMA_SCALES) prefetch_tmap(&tsc);
     }
-  };
-  int issued = 0;
-  if (warp == 0) {
-    for (; issued < min(kStages, nchunks); issued++) issue(issued);
+    int64_t k = 0;
+    for (; k < total; k++) {
+      const int s = (int)(k % stages);
+      if (k >= stages) {
+        const bool got = mbar_wait_bounded(&empty[s], (uint32_t)((k / stages) - 1) & 1u, a.status,
+                                           kStatusTmaTimeout);
+        if (!got) abort_flag = 1;
+      }
+      if (abort_flag) break;
+      if (lane == 0) {
+        const int64_t tile = blockIdx.x + (k / nch) * gridDim.x;
+        const int c = (int)(k % nch);
+        const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
+        const int boxes = (nb * F::kWB + kBoxBytes - 1) / kBoxBytes;
+        uint8_t* stage = smem + (int64_t)s * kStageBytes;
+        // Boxes past the matrix edge are zero-filled and count in full.
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * kBox + (TMA_SCALES ? kRows * kScaleRow : 0)));
+        const int32_t y = (int32_t)(tile * kRows);
+        for (int j = 0; j < boxes; j++)
+          tma_load_2d(stage + j * kBox, &tw, c * kChunkBytes + j * kBoxBytes, y, &full[s]);
+        if (TMA_SCALES) tma_load_2d(stage + kWBoxes * kBox, &tsc, c * F::kKC, y, &full[s]);
+      }
+      __syncwarp();
+    }
+    if (abort_flag && lane == 0) {
+      // Let the copies still in flight land before the CTA's shared memory goes.
+      for (int64_t j = k - 1; j >= 0 && j >= k - stages; j--)
+        mbar_wait_bounded(&full[j % stages], (uint32_t)(j / stages) & 1u, a.status, kStatusTmaTimeout);
+    }
+    return;
   }
 
-  // The weights do not depend on the previous kernel; the activations do.
-  pdl_wait();
+  // -------------------------------------------------------------- consumers
+  const int r8 = lane >> 2, l = lane & 3;
+  pdl_wait();  // the activations may come from the previous kernel
   bool ok = true;
   if (F32_IN) {
     // Token by token through two f32 buffers: the bulk copy of token t+2
@@ -165,24 +276,31 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvArgs a) {
     const uint32_t xbytes = (uint32_t)(a.cols * 4);
     auto issue_x = [&](int tt) {
       mbar_arrive_expect_tx(&xbars[tt & 1], xbytes);
-      bulk_g2s(xf_s + (tt & 1) * a.cols, a.xs + (t0 + tt) * a.cols, xbytes, &xbars[tt & 1]);
+      bulk_g2s(stg_s + (tt & 1) * sp.stg_stride, a.xs + (t0 + tt) * a.cols, xbytes, &xbars[tt & 1]);
     };
     if (tid == 0) {
       for (int tt = 0; tt < min(2, nt); tt++) issue_x(tt);
     }
     const bool writer = blockIdx.x == 0 && a.xq != nullptr;
-    for (int tt = 0; tt < nt; tt++) {
-      const bool got = mbar_wait_bounded(&xbars[tt & 1], (uint32_t)(tt >> 1) & 1u, a.status,
-                                         kStatusTmaTimeout);
+    int tt = 0;
+    for (; tt < nt; tt++) {
+      const bool got = warp_wait(&xbars[tt & 1], (uint32_t)(tt >> 1) & 1u, a.status);
       if (got)
-        quantize_token(xf_s + (tt & 1) * a.cols, xa_s + tt * sp.xa_stride, blocks,
-                       writer ? a.xq + (t0 + tt) * a.cols : nullptr,
-                       writer ? a.xsc + (t0 + tt) * blocks : nullptr);
-      if (__syncthreads_or(!got)) {
+        quantize_token<Q4>(reinterpret_cast<const float*>(stg_s + (tt & 1) * sp.stg_stride),
+                           xw_s + tt * sp.xw_stride, xs_s + tt * sp.xs_stride, blocks,
+                           writer ? a.xq + (t0 + tt) * a.cols : nullptr,
+                           writer ? a.xsc + (t0 + tt) * blocks : nullptr);
+      if (!got) abort_flag = 1;
+      consumers_sync();
+      if (abort_flag) {
         ok = false;
         break;
       }
       if (tid == 0 && tt + 2 < nt) issue_x(tt + 2);
+    }
+    if (!ok && tid == 0) {
+      for (int j = tt + 1; j < min(nt, tt + 2); j++)
+        mbar_wait_bounded(&xbars[j & 1], (uint32_t)(j >> 1) & 1u, a.status, kStatusTmaTimeout);
     }
   } else {
     const int64_t row_bytes = blocks * kQABytes;
@@ -191,118 +309,195 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvArgs a) {
       if (tid == 0) {
         mbar_arrive_expect_tx(&xbars[0], (uint32_t)(nt * row_bytes));
         for (int tt = 0; tt < nt; tt++)
-          bulk_g2s(xa_s + tt * sp.xa_stride, a.xa + (t0 + tt) * a.xa_stride, (uint32_t)row_bytes,
+          bulk_g2s(stg_s + tt * sp.stg_stride, a.xa + (t0 + tt) * a.xa_stride, (uint32_t)row_bytes,
                    &xbars[0]);
       }
-      ok = mbar_wait_bounded(&xbars[0], 0, a.status, kStatusTmaTimeout);
+      if (!warp_wait(&xbars[0], 0, a.status)) abort_flag = 1;
     } else {
       for (int tt = 0; tt < nt; tt++) {
         const uint32_t* src = reinterpret_cast<const uint32_t*>(a.xa + (t0 + tt) * a.xa_stride);
-        uint32_t* dst = reinterpret_cast<uint32_t*>(xa_s + tt * sp.xa_stride);
-        for (int64_t i = tid; i < row_bytes / 4; i += kThreads) dst[i] = __ldg(src + i);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(stg_s + tt * sp.stg_stride);
+        for (int64_t i = tid; i < row_bytes / 4; i += kConsumers) dst[i] = __ldg(src + i);
       }
     }
-    ok = __syncthreads_or(!ok) == 0;
-  }
-  if (Q4 && ok) {
-    // -8 * (sum of lane l's eight activations) per token and block: the
-    // nibbles enter dp4a unsigned and this term subtracts the offset of 8.
-    for (int64_t i = tid; i < (int64_t)nt * blocks * 4; i += kThreads) {
-      const int64_t tt = i / (blocks * 4), rem = i % (blocks * 4), b = rem >> 2;
-      const int ll = (int)(rem & 3);
-      const uint8_t* xb = xa_s + tt * sp.xa_stride + b * kQABytes + 4 * ll;
-      xs8_s[i] = -8 * __dp4a((int32_t)lds_u32(xb), 0x01010101, __dp4a((int32_t)lds_u32(xb + 16), 0x01010101, 0));
+    consumers_sync();
+    if (!abort_flag) {
+      for (int tt = 0; tt < nt; tt++)
+        unpack_qa<Q4>(stg_s + tt * sp.stg_stride, xw_s + tt * sp.xw_stride,
+                      xs_s + tt * sp.xs_stride, blocks);
     }
-    __syncthreads();
+    consumers_sync();
+    ok = !abort_flag;
   }
   pdl_launch_dependents();
+  if (!ok) return;
 
   const int row_local = warp * 8 + r8;
-  const int64_t row = row0 + min(row_local, tile_rows - 1);
-  float acc[NT];
+  const uint32_t rowoff = (uint32_t)row_local * kBoxBytes;
+  const uint8_t* sc = static_cast<const uint8_t*>(a.scales);
+  const uint8_t* xw_l = xw_s + l * X::kLaneBytes;
+  int64_t k = 0;
+  uint32_t e = 0;  // epilogue barrier uses so far
+  for (int64_t i = 0; i < my_tiles; i++) {
+    const int64_t tile = blockIdx.x + i * gridDim.x;
+    const int64_t row0 = tile * kRows;
+    const int tile_rows = (int)min64(kRows, a.rows - row0);
+    const int64_t row = row0 + min(row_local, tile_rows - 1);
+    float acc[NT];
 #pragma unroll
-  for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+    for (int t = 0; t < NT; t++) acc[t] = 0.0f;
 
-  bool failed = !ok;
-  int c = 0;
-  for (; c < nchunks && !failed; c++) {
-    const int s = c % kStages;
-    const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-    const bool got = mbar_wait_bounded(&bars[s], (uint32_t)(c / kStages) & 1u, a.status,
-                                       kStatusTmaTimeout);
-    if (got) {
-      const uint8_t* wrow = w_s + (s * kRows + row_local) * F::kWStride + 4 * l;
-      const int64_t b0 = (int64_t)c * F::kKC;
-#pragma unroll 4
-      for (int bb = 0; bb < nb; bb++) {
-        const int64_t b = b0 + bb;
-        float sw;
-        if (TMA_SCALES) {
-          const uint8_t* srow = s_s + (s * kRows + row_local) * F::kSStride;
-          sw = Q4 ? half_bits_to_float(reinterpret_cast<const uint16_t*>(srow)[bb])
-                  : reinterpret_cast<const float*>(srow)[bb];
-        } else {
-          sw = Q4 ? half_bits_to_float(__ldg(reinterpret_cast<const uint16_t*>(sc) + row * blocks + b))
-                  : __ldg(reinterpret_cast<const float*>(sc) + row * blocks + b);
-        }
-        int32_t w0, w1;
+    // One block: weights w0 / w1 (as int8 for Q8, nibbles for Q4), its
+    // scale, and the activations of every token.
+    auto block_step = [&](int b, int32_t w0, int32_t w1, float sw, const float* xsc_b) {
+#pragma unroll
+      for (int t = 0; t < NT; t++) {
+        const uint8_t* xb = xw_l + t * sp.xw_stride + b * X::kBlockBytes;
+        int32_t d;
         if (Q4) {
-          const uint32_t wv = lds_u32(wrow + bb * 16);
-          w0 = (int32_t)(wv & 0x0f0f0f0fu);          // weights 4l..4l+3, as 0..15
-          w1 = (int32_t)((wv >> 4) & 0x0f0f0f0fu);   // weights 16+4l..16+4l+3
+          const uint4 xv = lds<uint4>(xb);
+          d = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, (int32_t)xv.z));
         } else {
-          w0 = (int32_t)lds_u32(wrow + bb * 32);
-          w1 = (int32_t)lds_u32(wrow + bb * 32 + 16);
+          const uint2 xv = lds<uint2>(xb);
+          d = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, 0));
+        }
+        acc[t] = __fmaf_rn(__int2float_rn(d), __fmul_rn(sw, xsc_b[t]), acc[t]);
+      }
+    };
+    auto weights_of = [&](const uint8_t* stage, int bb, int32_t& w0, int32_t& w1) {
+      if (Q4) {
+        const uint32_t wv = lds<uint32_t>(stage + (bb / 8) * kBox + rowoff +
+                                          ((((bb & 7) ^ r8) & 7) << 4) + 4 * l);
+        w0 = (int32_t)(wv & 0x0f0f0f0fu);          // weights 4l..4l+3, as 0..15
+        w1 = (int32_t)((wv >> 4) & 0x0f0f0f0fu);   // weights 16+4l..16+4l+3
+      } else {
+        const uint8_t* line = stage + (bb / 4) * kBox + rowoff;
+        w0 = (int32_t)lds<uint32_t>(line + (((((bb & 3) * 2) ^ r8) & 7) << 4) + 4 * l);
+        w1 = (int32_t)lds<uint32_t>(line + (((((bb & 3) * 2 + 1) ^ r8) & 7) << 4) + 4 * l);
+      }
+    };
+    auto scale_of = [&](const uint8_t* stage, int bb, int64_t b) -> float {
+      if (TMA_SCALES) {
+        const uint8_t* sline = stage + kWBoxes * kBox + row_local * kScaleRow;
+        return Q4 ? half_bits_to_float(lds<uint16_t>(sline + bb * 2)) : lds<float>(sline + bb * 4);
+      }
+      return Q4 ? half_bits_to_float(__ldg(reinterpret_cast<const uint16_t*>(sc) + row * blocks + b))
+                : __ldg(reinterpret_cast<const float*>(sc) + row * blocks + b);
+    };
+
+    for (int c = 0; c < nch; c++, k++) {
+      const int s = (int)(k % stages);
+      const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
+      if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+        abort_flag = 1;
+        return;  // the producer drains what it issued; every other wait is bounded
+      }
+      const uint8_t* stage = smem + (int64_t)s * kStageBytes;
+      const int b0 = c * F::kKC;
+      const int full_boxes = nb / kPerBox;
+      // A whole box: kPerBox consecutive blocks, their scales in one 16-byte
+      // load, the activation scales in 16-byte loads.
+      auto do_box = [&](int j) {
+        const uint8_t* line = stage + j * kBox + rowoff;
+        float sws[kPerBox];
+        if (TMA_SCALES) {
+          const uint4 sv = lds<uint4>(stage + kWBoxes * kBox + row_local * kScaleRow + 16 * j);
+          if (Q4) {
+            const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int q = 0; q < 8; q++) sws[q] = half_bits_to_float((uint16_t)(u[q >> 1] >> (16 * (q & 1))));
+          } else {
+            sws[0] = __uint_as_float(sv.x);
+            sws[1] = __uint_as_float(sv.y);
+            sws[2] = __uint_as_float(sv.z);
+            sws[3] = __uint_as_float(sv.w);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < kPerBox; q++) sws[q] = scale_of(stage, j * kPerBox + q, b0 + j * kPerBox + q);
         }
 #pragma unroll
-        for (int t = 0; t < NT; t++) {
-          const uint8_t* xb = xa_s + t * sp.xa_stride + b * kQABytes;
-          const int32_t base = Q4 ? xs8_s[((int64_t)t * blocks + b) * 4 + l] : 0;
-          const int32_t d = __dp4a(w0, (int32_t)lds_u32(xb + 4 * l),
-                                   __dp4a(w1, (int32_t)lds_u32(xb + 16 + 4 * l), base));
-          const float s2 = __fmul_rn(sw, *reinterpret_cast<const float*>(xb + 32));
-          acc[t] = __fmaf_rn(__int2float_rn(d), s2, acc[t]);
+        for (int q4 = 0; q4 < kPerBox; q4 += 4) {
+          const int bq = b0 + j * kPerBox + q4;
+          float xsc[4][NT];
+#pragma unroll
+          for (int t = 0; t < NT; t++) {
+            const float4 xv = lds<float4>(xs_s + t * sp.xs_stride + bq);
+            xsc[0][t] = xv.x;
+            xsc[1][t] = xv.y;
+            xsc[2][t] = xv.z;
+            xsc[3][t] = xv.w;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            int32_t w0, w1;
+            if (Q4) {
+              const uint32_t wv = lds<uint32_t>(line + ((((q4 + q) ^ r8) & 7) << 4) + 4 * l);
+              w0 = (int32_t)(wv & 0x0f0f0f0fu);
+              w1 = (int32_t)((wv >> 4) & 0x0f0f0f0fu);
+            } else {
+              w0 = (int32_t)lds<uint32_t>(line + (((2 * q ^ r8) & 7) << 4) + 4 * l);
+              w1 = (int32_t)lds<uint32_t>(line + ((((2 * q + 1) ^ r8) & 7) << 4) + 4 * l);
+            }
+            block_step(bq + q, w0, w1, sws[q4 + q], xsc[q]);
+          }
         }
+      };
+      if (full_boxes == kWBoxes) {
+        // A full stage as straight-line code: later blocks' loads and dot
+        // products can be scheduled under the serial FMA chain.
+#pragma unroll
+        for (int j = 0; j < kWBoxes; j++) do_box(j);
+      } else {
+        for (int j = 0; j < full_boxes; j++) do_box(j);
+      }
+      // Blocks after the last whole box (only when cols is not a multiple of
+      // the box: 128 weights for Q8, 256 for Q4).
+      for (int bb = full_boxes * kPerBox; bb < nb; bb++) {
+        int32_t w0, w1;
+        weights_of(stage, bb, w0, w1);
+        float xsc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) xsc[t] = xs_s[t * sp.xs_stride + b0 + bb];
+        block_step(b0 + bb, w0, w1, scale_of(stage, bb, b0 + bb), xsc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    float* yt = yt_s + (e & 1) * NT * kRows;
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      const float v = acc[t];
+      const float s01 = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
+      const float y = __fadd_rn(s01, __shfl_down_sync(0xffffffffu, s01, 2));
+      if (l == 0 && row_local < tile_rows && t < nt) {
+        if (a.ys != nullptr) a.ys[(t0 + t) * a.ldy + row0 + row_local] = y;
+        yt[t * kRows + row_local] = y;
       }
     }
-    failed = __syncthreads_or(!got) != 0;
-    if (!failed && warp == 0 && issued < nchunks) issue(issued++);
-  }
-  if (failed) {
-    // Let copies still in flight land before the CTA's shared memory goes.
-    if (tid == 0) {
-      for (int k = c; k < issued; k++)
-        mbar_wait_bounded(&bars[k % kStages], (uint32_t)(k / kStages) & 1u, a.status,
-                          kStatusTmaTimeout);
-    }
-    __syncthreads();
-    return;
-  }
-
+    if (a.ya != nullptr && tile_rows == kRows) {
+      // The tile's 32 outputs of a token are one Q8_0 block of the next
+      // projection's input: quantize them here (lab_quantize_q8 semantics).
+      // All consumers meet on a bounded epilogue barrier; its buffer
+      // alternates, and no warp can get two tiles ahead of another.
+      mbar_arrive(&epi[e & 1]);
+      if (!warp_wait(&epi[e & 1], (e >> 1) & 1u, a.status)) {
+        abort_flag = 1;
+        return;
+      }
+      for (int t = warp; t < nt; t += kConsumerWarps) {
+        const float v = yt[t * kRows + lane];
+        float amax = fmaxf(0.0f, fabsf(v));
 #pragma unroll
-  for (int t = 0; t < NT; t++) {
-    const float v = acc[t];
-    const float s01 = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
-    const float y = __fadd_rn(s01, __shfl_down_sync(0xffffffffu, s01, 2));
-    if (l == 0 && row_local < tile_rows && t < nt) {
-      if (a.ys != nullptr) a.ys[(t0 + t) * a.ldy + row0 + row_local] = y;
-      yt_s[t * kRows + row_local] = y;
-    }
-  }
-  if (a.ya != nullptr && tile_rows == kRows) {
-    // The CTA's 32 outputs of a token are one Q8_0 block of the next
-    // projection's input: quantize them here (lab_quantize_q8 semantics).
-    __syncthreads();
-    for (int t = warp; t < nt; t += kWarps) {
-      const float v = yt_s[t * kRows + lane];
-      float amax = fmaxf(0.0f, fabsf(v));
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-      float scale, inv;
-      q8_scale(amax, scale, inv);
-      uint8_t* dst = a.ya + (t0 + t) * a.ya_stride + (int64_t)blockIdx.x * kQABytes;
-      dst[lane] = (uint8_t)(int8_t)quant_q8_elem(v, inv);
-      if (lane == 0) *reinterpret_cast<float*>(dst + 32) = scale;
+        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        float scale, inv;
+        q8_scale(amax, scale, inv);
+        uint8_t* dst = a.ya + (t0 + t) * a.ya_stride + tile * kQABytes;
+        dst[lane] = (uint8_t)(int8_t)quant_q8_elem(v, inv);
+        if (lane == 0) *reinterpret_cast<float*>(dst + 32) = scale;
+      }
+      e++;
     }
   }
 }
@@ -313,11 +508,6 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvArgs a) {
 // both modes. Same lane-per-chain mapping; weights come straight from global
 // memory a byte at a time, so it is slow, but exact. Mode 1 reads the
 // activations already quantized into xq / xsc.
-
-__device__ __forceinline__ int32_t gather_word(const uint8_t* p) {
-  return (int32_t)((uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) |
-                   ((uint32_t)p[3] << 24));
-}
 
 __device__ __forceinline__ int q4_weight(const uint8_t* blk, int j) {
   return (j < 16 ? (blk[j] & 15) : (blk[j - 16] >> 4)) - 8;
@@ -365,20 +555,48 @@ __global__ void __launch_bounds__(128) generic_kernel(const LinearArgs a) {
 
 template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN>
 int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
-  const SmemPlan sp = plan<Q4>(NT, a.cols, F32_IN);
+  using F = Fmt<Q4>;
+  const int64_t ntiles = (a.rows + kRows - 1) / kRows;
+  const int64_t blocks = a.cols / kBlock;
+  // Two CTAs per SM when the ring still gets at least 3 stages that way.
+  const SmemPlan base = plan<Q4>(0, NT, a.cols, F32_IN);
+  int per_sm = 2;
+  int stages = (int)((kSmemPerSM / per_sm - 1024 - base.total) / (kStageBytes + 16));
+  if (stages < 3) {
+    per_sm = 1;
+    stages = (int)((kMaxSmem - base.total) / (kStageBytes + 16));
+  }
+  stages = stages > kMaxStages ? kMaxStages : stages;
+  if (stages < 2) return kErrTooLarge;
+  const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN);
   if (sp.total > kMaxSmem) return kErrTooLarge;
+  CUtensorMap tw, tsc;
+  memset(&tsc, 0, sizeof tsc);
+  const uint64_t row_bytes = (uint64_t)blocks * F::kWB;
+  if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, (uint64_t)a.rows,
+                      row_bytes, kBoxBytes, kRows, true))
+    return kErrUnsupported;
+  if (TMA_SCALES &&
+      !encode_tmap_2d(&tsc, a.scales, Q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                      (uint64_t)blocks, (uint64_t)a.rows, (uint64_t)blocks * F::kSB, F::kKC, kRows,
+                      false))
+    return kErrUnsupported;
   auto kern = gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN>;
   static bool configured[64] = {};  // per device: the opt-in smem limit is set
   int dev = 0;
   cudaGetDevice(&dev);
-  if (sp.total > 48 * 1024 && !configured[dev & 63]) {
+  if (!configured[dev & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
       return kErrCuda;
     configured[dev & 63] = true;
   }
+  // Persistent grid, balanced so every CTA gets the same number of tiles.
+  const int64_t slots = (int64_t)kSMs * per_sm;
+  const int64_t waves = (ntiles + slots - 1) / slots;
+  const int64_t grid = (ntiles + waves - 1) / waves;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.rows + kRows - 1) / kRows), (unsigned)((a.n + NT - 1) / NT), 1);
+  cfg.gridDim = dim3((unsigned)grid, (unsigned)((a.n + NT - 1) / NT), 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)sp.total;
   cfg.stream = stream;
@@ -387,7 +605,7 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? kOk : kErrCuda;
+  return cudaLaunchKernelEx(&cfg, kern, a, stages, tw, tsc) == cudaSuccess ? kOk : kErrCuda;
 }
 
 template <bool Q4, int NT>
@@ -406,7 +624,9 @@ int64_t launch_gemv_s(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 template <bool Q4>
 int64_t launch_gemv_q(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const bool f32_in = a.xs != nullptr;
-  auto fits = [&](int nt) { return plan<Q4>(nt, a.cols, f32_in).total <= kMaxSmem; };
+  auto fits = [&](int nt) {
+    return plan<Q4>(2, nt, a.cols, f32_in).total <= kMaxSmem;
+  };
   if (a.n <= 1 || !fits(2)) return fits(1) ? launch_gemv_s<Q4, 1>(a, stream, pdl) : kErrTooLarge;
   if (a.n <= 2 || !fits(4)) return launch_gemv_s<Q4, 2>(a, stream, pdl);
   if (a.n <= 4 || !fits(8)) return launch_gemv_s<Q4, 4>(a, stream, pdl);
@@ -424,8 +644,8 @@ bool gemv_ex_supported(const GemvArgs& g) {
     return false;
   if (g.xa != nullptr && (((uintptr_t)g.xa & 3) != 0 || (g.xa_stride & 3) != 0)) return false;
   if (g.ya != nullptr && (((uintptr_t)g.ya & 3) != 0 || (g.ya_stride & 3) != 0)) return false;
-  return (g.q4 ? plan<true>(1, g.cols, g.xs != nullptr).total
-               : plan<false>(1, g.cols, g.xs != nullptr).total) <= kMaxSmem;
+  return (g.q4 ? plan<true>(2, 1, g.cols, g.xs != nullptr).total
+               : plan<false>(2, 1, g.cols, g.xs != nullptr).total) <= kMaxSmem;
 }
 
 int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl) {

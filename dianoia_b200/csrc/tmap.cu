@@ -1,0 +1,41 @@
+// TMA tensor-map encoding (see dn_tmap.h).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "dn_tmap.h"
+
+namespace dn {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type, uint64_t row_elems,
+                    uint64_t rows, uint64_t row_bytes, uint32_t box_elems, uint32_t box_rows,
+                    bool swizzle128) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {row_elems, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_elems, box_rows};
+  const cuuint32_t estrides[2] = {1, 1};
+  return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estrides,
+            CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace dn
