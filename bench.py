@@ -331,7 +331,16 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--workload", choices=["stack", "gemv"], default="stack",
+                    help="stack: config 3 (the default bench line); gemv: one matrix "
+                         "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
+    ap.add_argument("--fmt", choices=["q8", "q4"], default="q8")
+    ap.add_argument("--rows", type=int, default=VOCAB)
+    ap.add_argument("--cols", type=int, default=HIDDEN)
+    ap.add_argument("--n", type=int, default=1, help="tokens per product")
     args = ap.parse_args()
+    if args.workload == "gemv":
+        return run_gemv_workload(args)
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -479,6 +488,88 @@ def main():
         del graph
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_gemv_workload(args):
+    """One quantized matrix times n tokens through dn_linear_qa, timed with CUDA
+    events on the launching stream; the weights rotate through enough copies
+    to exceed twice the L2, so every launch streams them from HBM."""
+    import torch
+    from dianoia_b200 import _lib
+    L = _lib.lib()
+    rows, cols, n, q4 = args.rows, args.cols, args.n, args.fmt == "q4"
+    blocks = cols // 32
+    wbytes = rows * blocks * (18 if q4 else 36)
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    copies = max(1, -(-2 * l2 // wbytes))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    mats = []
+    for _ in range(copies):
+        if q4:
+            qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
+            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen)
+            sc = sc.half().view(torch.int16)
+        else:
+            qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
+            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen)
+            sc = sc.half().float()
+        mats.append((qs, sc))
+    x = torch.randn(n * cols, device="cuda", generator=gen)
+    xa = torch.zeros(n * blocks * 36, dtype=torch.uint8, device="cuda")
+    ys = torch.zeros(n * rows, device="cuda")
+    ya = torch.zeros(n * (rows // 32) * 36, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    assert L.dn_quantize_qa(x.data_ptr(), xa.data_ptr(), n, cols, blocks * 36, h) == 0
+
+    def launch(i, handle):
+        qs, sc = mats[i % copies]
+        rc = L.dn_linear_qa(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xa.data_ptr(),
+                            blocks * 36, ys.data_ptr(), rows, ya.data_ptr(), (rows // 32) * 36,
+                            rows, cols, n, 1, handle)
+        if rc != 0:
+            raise RuntimeError(L.dn_error_string(rc).decode())
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 1)):
+            launch(i, h)
+        torch.cuda.synchronize()
+        graph = None
+        if not args.no_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(args.steps):
+                    launch(i, torch.cuda.current_stream().cuda_stream)
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                launch(i, h)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if L.dn_device_status(1) != 0:
+        raise SystemExit("kernel bounded wait timed out")
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    alg = rows * blocks * (18 if q4 else 34) + n * cols * 4 + n * rows * 4
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    res = {"metric": "quantized-linear GEMV HBM GB/s", "workload": f"{args.fmt} {rows}x{cols} n={n}",
+           "us_per_launch": us, "weight_bytes_ref_layout": wbytes,
+           "gbs_ref_layout": wbytes / us / 1e3, "gbs_algorithmic": alg / us / 1e3,
+           "roofline_frac": alg / us / 1e3 / peak, "peak_gbs": peak, "copies": copies,
+           "launches": args.steps, "graph": graph is not None,
+           "l2": f"{copies} rotating weight copies (> 2 x L2)"}
+    print(json.dumps(res), flush=True)
 
 
 def run_e2e(args, stack, L, torch, rank, world, gather, device):
