@@ -427,7 +427,8 @@ int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const
                        const int8_t* xq, int64_t rows, int64_t cols, int64_t n, int64_t mode) {
   // Null pointers stand for "suitably aligned" in this query.
   const float* x = xs != nullptr ? xs : reinterpret_cast<const float*>(256);
-  LinearArgs a{format == DN_Q4, qs, scales, x, const_cast<int8_t*>(xq), nullptr, nullptr, rows,
+  int8_t* q = xq != nullptr ? const_cast<int8_t*>(xq) : reinterpret_cast<int8_t*>(256);
+  LinearArgs a{format == DN_Q4, qs, scales, x, q, reinterpret_cast<float*>(256), nullptr, rows,
                cols, n, rows, mode, nullptr};
   return dn::path_for(a);
 }

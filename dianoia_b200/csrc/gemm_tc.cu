@@ -1,13 +1,400 @@
-// Prefill / vision GEMM on the tcgen05 tensor cores: placeholder until the
-// kind::i8 kernel lands; launch_linear never selects it while this returns
-// false.
+// Prefill / vision GEMM on the 5th-generation tensor cores (tcgen05, kind::i8)
+// for Q8_0 and Q4_0 weights times Q8_0 activations (lab_gemm_q8 / lab_gemm_q4
+// with many tokens, lab_native.c:553-579, 1059-1080).
+//
+// One tcgen05.mma of K = 32 int8 is exactly one Q8_0 block: D_b[r, t] =
+// sum_k W[r, k] * xq[t, k] over block b, in int32 in TMEM - bit-exact block
+// dots. Every block has its own scale product sw[r, b] * sx[t, b], so each
+// block's D tile must leave TMEM and be scaled and accumulated in f32 on the
+// CUDA cores (acc += f32(d) * f32(sw * sx), the reference's per-block
+// operations). The f32 sums therefore run over whole blocks rather than the
+// reference's four lanes, and match it within its own 1e-5 relative bound.
+//
+// Tile: 128 weight rows (MMA M, TMEM lanes) x 128 tokens (MMA N, TMEM
+// columns). Warp roles:
+//   warp 0      TMA producer: per stage, the weights (Q8: a 128 x 128-byte
+//               box, 128-byte swizzle = the UMMA K-major SW128 layout; Q4: the
+//               raw 128 x 64-byte nibbles) and the activations (128 tokens x
+//               128 bytes, SW128) for 4 blocks of K
+//   warp 1      MMA issuer: allocates 512 TMEM columns = four D slots of 128
+//               columns, one per block of a stage; issues one MMA per block
+//               into its slot and commits to the slot's "full" barrier
+//   warps 2-9   drain ("epilogue"): two warps per TMEM lane quarter, each
+//               owning one weight row per lane and 64 token columns; per
+//               block: tcgen05.ld, release the slot, scale and accumulate
+//   warps 10-11 (Q4) nibble expansion: raw nibbles -> int8 (q - 8) in the
+//               SW128 K-major layout the MMA reads
+// Every mbarrier wait is bounded; on a timeout the kernel records it, lets
+// its copies and MMAs finish (bounded), frees its TMEM and returns.
+#include <string.h>
+
 #include "dn_common.cuh"
 #include "dn_launch.h"
+#include "dn_tmap.h"
 
 namespace dn {
+namespace {
 
-bool gemm_tc_supported(const LinearArgs&) { return false; }
+constexpr int kTileRows = 128;                 // MMA M
+constexpr int kTileTok = 128;                  // MMA N
+constexpr int kStageK = 128;                   // int8 of K per stage = 4 blocks
+constexpr int kBlocksPerStage = kStageK / kBlock;
+constexpr int kABytes = kTileRows * kStageK;   // 16 KB
+constexpr int kBBytes = kTileTok * kStageK;    // 16 KB
+constexpr int kRawBytes = kTileRows * (kStageK / 2);  // Q4 nibbles: 8 KB
+constexpr int kEpiWarps = 8;
+constexpr int kConvWarps = 2;
+constexpr int kEpiCols = kTileTok / 2;         // columns per drain warp
+constexpr uint32_t kTmemCols = 512;
+constexpr int kMaxSmemTc = 226 * 1024;
 
-int64_t launch_gemm_tc(const LinearArgs&, cudaStream_t) { return kErrUnsupported; }
+template <bool Q4>
+struct TcShape {
+  static constexpr int kWarps = 2 + kEpiWarps + (Q4 ? kConvWarps : 0);
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kStageBytes = kABytes + kBBytes + (Q4 ? kRawBytes : 0);
+};
+
+struct TcArgs {
+  const void* scales;
+  const float* xsc;
+  float* ys;
+  int64_t rows, cols, n, ldy;
+  uint32_t* status;
+};
+
+// ----------------------------------------------------------- tcgen05 PTX
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] = A * B (accumulate = false): one K = 32 step of int8 x int8 -> s32.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
+      : "memory");
+}
+// The mbarrier arrives once every tcgen05 operation this thread issued so far
+// has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major, 128-byte-swizzled operand
+// tile whose rows are 128 bytes: 8-row groups 1024 bytes apart (SBO), version
+// 1, layout SWIZZLE_128B. `addr` may be advanced by 32 bytes within the
+// swizzle span to select a K = 32 step.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: s32 accumulator, signed int8 A and B, both K-major,
+// N = 128, M = 128.
+constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileTok >> 3) << 17) |
+                              ((uint32_t)(kTileRows >> 4) << 24);
+
+__device__ __forceinline__ bool wait_tc(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                        uint32_t bits, volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (!mbar_wait_bounded(bar, parity, status, bits)) {
+    *abort_flag = 1;
+    return false;
+  }
+  return true;
+}
+
+template <bool Q4>
+__global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
+    gemm_tc_kernel(const TcArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
+                   const __grid_constant__ CUtensorMap tx) {
+  using S = TcShape<Q4>;
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)stages * S::kStageBytes);
+  uint64_t* conv = full + stages;
+  uint64_t* empty = conv + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + kBlocksPerStage;
+  uint64_t* done = tempty + kBlocksPerStage;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t blocks = a.cols / kBlock;
+  const int nst = (int)((blocks + kBlocksPerStage - 1) / kBlocksPerStage);
+  const int64_t row0 = (int64_t)blockIdx.x * kTileRows;
+  const int64_t tok0 = (int64_t)blockIdx.y * kTileTok;
+  auto stage_a = [&](int s) { return smem + (int64_t)s * S::kStageBytes; };
+  auto stage_b = [&](int s) { return smem + (int64_t)s * S::kStageBytes + kABytes; };
+  auto stage_raw = [&](int s) { return smem + (int64_t)s * S::kStageBytes + kABytes + kBBytes; };
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kConvWarps * 32);
+      mbar_init(&empty[s], 1);
+    }
+    for (int q = 0; q < kBlocksPerStage; q++) {
+      mbar_init(&tfull[q], 1);
+      mbar_init(&tempty[q], kEpiWarps);
+    }
+    mbar_init(done, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int k = 0;
+    if (lane == 0) {
+      prefetch_tmap(&tw);
+      prefetch_tmap(&tx);
+      for (; k < nst; k++) {
+        const int s = k % stages;
+        if (k >= stages &&
+            !wait_tc(&empty[s], (uint32_t)((k / stages) - 1) & 1u, a.status, kStatusMmaTimeout,
+                     &abort_flag))
+          break;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)((Q4 ? kRawBytes : kABytes) + kBBytes));
+        if (Q4)
+          tma_load_2d(stage_raw(s), &tw, k * (kStageK / 2), (int32_t)row0, &full[s]);
+        else
+          tma_load_2d(stage_a(s), &tw, k * kStageK, (int32_t)row0, &full[s]);
+        tma_load_2d(stage_b(s), &tx, k * kStageK, (int32_t)tok0, &full[s]);
+      }
+      if (abort_flag) {
+        // Let the copies already issued land before the CTA's memory goes.
+        for (int j = k - 1; j >= 0 && j >= k - stages; j--)
+          mbar_wait_bounded(&full[j % stages], (uint32_t)(j / stages) & 1u, a.status,
+                            kStatusTmaTimeout);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      for (int k = 0; k < nst; k++) {
+        const int s = k % stages;
+        const uint32_t ph = (uint32_t)(k / stages) & 1u;
+        if (!wait_tc(Q4 ? &conv[s] : &full[s], ph, a.status, kStatusTmaTimeout, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(stage_a(s)), b_addr = smem_u32(stage_b(s));
+        bool ok = true;
+        for (int q = 0; q < kBlocksPerStage; q++) {
+          if ((int64_t)k * kBlocksPerStage + q >= blocks) break;
+          if (k > 0 && !wait_tc(&tempty[q], (uint32_t)(k - 1) & 1u, a.status, kStatusMmaTimeout,
+                                &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          mma_i8(tmem + (uint32_t)(q * kTileTok), sw128_desc(a_addr + q * 32),
+                 sw128_desc(b_addr + q * 32), kIdescI8);
+          mma_commit(&tfull[q]);
+        }
+        mma_commit(&empty[s]);
+        if (!ok) break;
+      }
+      // Every MMA issued has completed once `done` arrives.
+      mma_commit(done);
+      mbar_wait_bounded(done, 0, a.status, kStatusMmaTimeout);
+    }
+  } else if (warp < 2 + kEpiWarps) {
+    // ------------------------------------------------------------ drain
+    const int quarter = warp & 3;               // TMEM lanes this warp may access
+    const int half = (warp - 2) >> 2;           // which 64 token columns
+    const int64_t row = row0 + quarter * 32 + lane;
+    const bool row_ok = row < a.rows;
+    const int64_t t_base = tok0 + half * kEpiCols;
+    float acc[kEpiCols];
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j++) acc[j] = 0.0f;
+    for (int k = 0; k < nst && !abort_flag; k++) {
+      for (int q = 0; q < kBlocksPerStage; q++) {
+        const int64_t b = (int64_t)k * kBlocksPerStage + q;
+        if (b >= blocks) break;
+        // The tcgen05.ld below is warp-wide: every lane must agree on the wait.
+        bool got = !abort_flag && mbar_wait_bounded(&tfull[q], (uint32_t)k & 1u, a.status,
+                                                    kStatusMmaTimeout);
+        got = __all_sync(0xffffffffu, got) != 0;
+        if (!got) {
+          abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        int32_t d0[32], d1[32];
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) +
+                               (uint32_t)(q * kTileTok + half * kEpiCols);
+        tmem_ld32(taddr, d0);
+        tmem_ld32(taddr + 32, d1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[q]);
+        float sw = 0.0f;
+        if (row_ok)
+          sw = Q4 ? half_bits_to_float(__ldg(static_cast<const uint16_t*>(a.scales) + row * blocks + b))
+                  : __ldg(static_cast<const float*>(a.scales) + row * blocks + b);
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++) {
+          const int64_t t = t_base + j;
+          const float sx = t < a.n ? __ldg(a.xsc + t * blocks + b) : 0.0f;
+          const int32_t d = j < 32 ? d0[j] : d1[j - 32];
+          acc[j] = __fmaf_rn(__int2float_rn(d), __fmul_rn(sw, sx), acc[j]);
+        }
+      }
+    }
+    if (row_ok && !abort_flag) {
+#pragma unroll
+      for (int j = 0; j < kEpiCols; j++) {
+        const int64_t t = t_base + j;
+        if (t < a.n) a.ys[t * a.ldy + row] = acc[j];
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ Q4 expansion
+    const int ct = tid - (2 + kEpiWarps) * 32;  // 0 .. 63
+    for (int k = 0; k < nst; k++) {
+      const int s = k % stages;
+      if (!wait_tc(&full[s], (uint32_t)(k / stages) & 1u, a.status, kStatusTmaTimeout, &abort_flag))
+        break;
+      const uint8_t* raw = stage_raw(s);
+      uint8_t* dst = stage_a(s);
+      // One (row, block) per task: 16 nibble bytes -> two swizzled 16-byte
+      // chunks of int8 (q - 8): low nibbles are weights 0..15 of the block,
+      // high nibbles weights 16..31 (GGUF order).
+      for (int task = ct; task < kTileRows * kBlocksPerStage; task += kConvWarps * 32) {
+        const int r = task >> 2, q = task & 3;
+        const uint4 v = *reinterpret_cast<const uint4*>(raw + r * (kStageK / 2) + q * 16);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          // (n & 15) + 0x78, then ^ 0x80, is n - 8 as a two's-complement byte.
+          lo[i] = ((w[i] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+          hi[i] = (((w[i] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        }
+        uint8_t* line = dst + (r >> 3) * 1024 + (r & 7) * 128;
+        *reinterpret_cast<uint4*>(line + (((2 * q) ^ (r & 7)) << 4)) =
+            make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(line + (((2 * q + 1) ^ (r & 7)) << 4)) =
+            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
+      mbar_arrive(&conv[s]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <bool Q4>
+int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
+  using S = TcShape<Q4>;
+  const int64_t blocks = a.cols / kBlock;
+  const int64_t bar_bytes = 8 * (3 * 16 + 2 * kBlocksPerStage + 2) + 16;
+  int stages = (int)((kMaxSmemTc - 1024 - bar_bytes) / S::kStageBytes);
+  stages = stages > 8 ? 8 : stages;
+  if (stages < 2) return kErrTooLarge;
+  const size_t smem = 1024 + (size_t)stages * S::kStageBytes + (size_t)bar_bytes;
+  CUtensorMap tw, tx;
+  if (Q4) {
+    if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)blocks * 16,
+                        (uint64_t)a.rows, (uint64_t)blocks * 16, kStageK / 2, kTileRows, false))
+      return kErrUnsupported;
+  } else {
+    if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)blocks * 32,
+                        (uint64_t)a.rows, (uint64_t)blocks * 32, kStageK, kTileRows, true))
+      return kErrUnsupported;
+  }
+  if (!encode_tmap_2d(&tx, a.xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)a.cols, (uint64_t)a.n,
+                      (uint64_t)a.cols, kStageK, kTileTok, true))
+    return kErrUnsupported;
+  auto kern = gemm_tc_kernel<Q4>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemTc) !=
+        cudaSuccess)
+      return kErrCuda;
+    configured[dev & 63] = true;
+  }
+  TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status};
+  const dim3 grid((unsigned)((a.rows + kTileRows - 1) / kTileRows),
+                  (unsigned)((a.n + kTileTok - 1) / kTileTok), 1);
+  kern<<<grid, S::kThreads, smem, stream>>>(t, stages, tw, tx);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace
+
+// The tensor-core path needs 16-byte aligned weights and quantized
+// activations (TMA), cols a multiple of 32, and the quantized activations
+// written to device memory first (xq / xsc).
+bool gemm_tc_supported(const LinearArgs& a) {
+  return a.mode == 1 && a.cols % kBlock == 0 && a.cols > 0 && a.xq != nullptr &&
+         a.xsc != nullptr && ((uintptr_t)a.qs & 15) == 0 && ((uintptr_t)a.xq & 15) == 0 &&
+         ((uintptr_t)a.xs & 15) == 0 && ((uintptr_t)a.scales & (a.q4 ? 1 : 3)) == 0 &&
+         ((uintptr_t)a.xsc & 3) == 0;
+}
+
+int64_t launch_gemm_tc(const LinearArgs& a, cudaStream_t stream) {
+  if (!gemm_tc_supported(a)) return kErrUnsupported;
+  if (a.rows <= 0 || a.n <= 0) return kOk;
+  if (launch_quantize_q8(a.xs, a.xq, a.xsc, a.n, a.cols, stream) != cudaSuccess) return kErrCuda;
+  return a.q4 ? launch_tc<true>(a, stream) : launch_tc<false>(a, stream);
+}
 
 }  // namespace dn

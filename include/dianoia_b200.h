@@ -109,7 +109,8 @@ int64_t dn_linear(int64_t format, const void* qs, const void* scales, const floa
                   float* xsc, float* ys, int64_t rows, int64_t cols, int64_t n, int64_t ldy,
                   int64_t mode, int64_t path, int64_t flags, void* stream);
 
-/* Which path DN_PATH_AUTO picks for these arguments. */
+/* Which path DN_PATH_AUTO picks for these arguments; NULL pointers stand for
+ * suitably aligned buffers the caller will provide. */
 int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const float* xs,
                        const int8_t* xq, int64_t rows, int64_t cols, int64_t n, int64_t mode);
 

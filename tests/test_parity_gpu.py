@@ -305,3 +305,36 @@ def test_qa_chain_of_projections(cuda_lib, oracle):
         x_host = want[:nxt].copy()
         xa = ya  # the prefix of the QA output feeds the next product
     assert L.dn_device_status(1) == 0
+
+
+# ---------------------------------------------------------- tensor-core GEMM
+
+TC_SHAPES = [
+    ("q8", 6144, 2048, 512),   # config 4 gate/up shape, Q8
+    ("q4", 6144, 2048, 512),   # config 4: gate/up, Q4_0
+    ("q4", 2048, 6144, 512),   # config 4: down, Q4_0
+    ("q8", 4304, 1152, 256),   # config 5: fc1 (rows not a multiple of the 128-row tile)
+    ("q8", 1152, 4320, 100),   # config 5: fc2, K padded to 4320 (135 blocks), ragged tokens
+    ("q8", 3456, 1152, 64),    # config 5: qkv, lm_head-sweep-sized M
+    ("q4", 70, 96, 40),        # gpu_linear_test shape: a single partial tile
+    ("q8", 128, 128, 16),      # the GEMV/GEMM crossover
+]
+
+
+@pytest.mark.parametrize("fmt,rows,cols,n", TC_SHAPES)
+def test_tensor_core_gemm_within_tolerance(cuda_lib, oracle, fmt, rows, cols, n):
+    rng = np.random.default_rng(rows * 7 + cols + n)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    _, wq, wsc = oracle.gemm(fmt, qs[: 32 * (cols // 2 if fmt == "q4" else cols)], sc[: 32 * (cols // 32)],
+                             xs, 32, cols, n, 1)
+    ys, xq, xsc = dev_linear(cuda_lib, fmt, dev(qs), dev(sc), dev(xs), rows, cols, n, path=1)
+    assert np.array_equal(xq, wq) and same_bits(xsc, wsc)  # activations: bit-exact
+    ref, mag = oracle.reference_f64(fmt, qs, sc, xs, rows, cols, n, 1)
+    err = orc.max_rel_err(ys, ref, mag)
+    assert err < TOL, f"max relative error {err:.3e}"
+
+
+def test_auto_path_uses_tensor_cores_for_prefill(cuda_lib):
+    assert cuda_lib.dn_linear_path(0, None, None, None, None, 6144, 2048, 512, 1) == 1
+    assert cuda_lib.dn_linear_path(1, None, None, None, None, 6144, 2048, 1, 1) == 0
