@@ -331,7 +331,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--workload", choices=["stack", "gemv"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "gemv", "gemm"], default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
     ap.add_argument("--fmt", choices=["q8", "q4"], default="q8")
@@ -341,6 +341,8 @@ def main():
     args = ap.parse_args()
     if args.workload == "gemv":
         return run_gemv_workload(args)
+    if args.workload == "gemm":
+        return run_gemm_workload(args)
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -569,6 +571,81 @@ def run_gemv_workload(args):
            "roofline_frac": alg / us / 1e3 / peak, "peak_gbs": peak, "copies": copies,
            "launches": args.steps, "graph": graph is not None,
            "l2": f"{copies} rotating weight copies (> 2 x L2)"}
+    print(json.dumps(res), flush=True)
+
+
+def run_gemm_workload(args):
+    """One quantized matrix times n tokens through dn_linear (tensor-core path
+    when n is above the crossover): activation quantize + GEMM per launch,
+    timed with CUDA events; reports int8 TOPS (2 * n * rows * cols per launch)."""
+    import torch
+    from dianoia_b200 import _lib
+    L = _lib.lib()
+    rows, cols, n, q4 = args.rows, args.cols, args.n, args.fmt == "q4"
+    blocks = cols // 32
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    if q4:
+        qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
+        sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen).half().view(torch.int16)
+    else:
+        qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
+        sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen).half().float()
+    xs = torch.randn(n * cols, device="cuda", generator=gen)
+    xq = torch.zeros(n * cols, dtype=torch.int8, device="cuda")
+    xsc = torch.zeros(n * blocks + 4, device="cuda")
+    ys = torch.zeros(n * rows, device="cuda")
+    stream = torch.cuda.Stream()
+    path = L.dn_linear_path(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
+                            xq.data_ptr(), rows, cols, n, 1)
+
+    def launch(handle):
+        rc = L.dn_linear(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(), xq.data_ptr(),
+                         xsc.data_ptr(), ys.data_ptr(), rows, cols, n, rows, 1, -1, 0, handle)
+        if rc != 0:
+            raise RuntimeError(L.dn_error_string(rc).decode())
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            launch(stream.cuda_stream)
+        torch.cuda.synchronize()
+        graph = None
+        if not args.no_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(args.steps):
+                    launch(torch.cuda.current_stream().cuda_stream)
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(args.steps):
+                launch(stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if L.dn_device_status(1) != 0:
+        raise SystemExit("kernel bounded wait timed out")
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    ops = 2.0 * n * rows * cols
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    # int8 dense tensor peak: twice the measured bf16 dense figure (the
+    # nominal ratio, 4.5 vs 2.25 PFLOP/s).
+    int8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    res = {"metric": "quantized-linear int8 GEMM TOPS", "workload": f"{args.fmt} {rows}x{cols} n={n}",
+           "path": {0: "gemv", 1: "tcgen05", 2: "generic"}.get(path, path),
+           "us_per_launch": us, "tops": ops / us / 1e6, "int8_peak_tops": int8_peak,
+           "frac_of_int8_peak": ops / us / 1e6 / int8_peak,
+           "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops" if peaks else "2 x fallback 1590",
+           "launches": args.steps, "graph": graph is not None,
+           "includes": "activation quantize (f32 -> Q8_0) + GEMM"}
     print(json.dumps(res), flush=True)
 
 

@@ -10,18 +10,21 @@
 // operations). The f32 sums therefore run over whole blocks rather than the
 // reference's four lanes, and match it within its own 1e-5 relative bound.
 //
-// Tile: 128 weight rows (MMA M, TMEM lanes) x 128 tokens (MMA N, TMEM
-// columns). Warp roles:
-//   warp 0      TMA producer: per stage, the weights (Q8: a 128 x 128-byte
-//               box, 128-byte swizzle = the UMMA K-major SW128 layout; Q4: the
-//               raw 128 x 64-byte nibbles) and the activations (128 tokens x
-//               128 bytes, SW128) for 4 blocks of K
-//   warp 1      MMA issuer: allocates 512 TMEM columns = four D slots of 128
-//               columns, one per block of a stage; issues one MMA per block
-//               into its slot and commits to the slot's "full" barrier
+// Tile: 128 weight rows (MMA M, TMEM lanes) x 64 tokens (MMA N, TMEM
+// columns); TMEM holds 8 such D slots, so the MMA warp runs two stages (8
+// blocks) ahead of the drain. Warp roles:
+//   warp 0      producer: per stage, TMA copies of the weights (Q8: a 128 x
+//               128-byte box, 128-byte swizzle = the UMMA K-major SW128
+//               layout; Q4: the raw 128 x 64-byte nibbles) and the
+//               activations (64 tokens x 128 bytes, SW128) for 4 blocks of K;
+//               the other lanes stage the block scales into shared memory
+//   warp 1      MMA issuer: allocates 512 TMEM columns = eight D slots of 64
+//               columns; issues one MMA per block into the next slot and
+//               commits to the slot's "full" barrier
 //   warps 2-9   drain ("epilogue"): two warps per TMEM lane quarter, each
-//               owning one weight row per lane and 64 token columns; per
-//               block: tcgen05.ld, release the slot, scale and accumulate
+//               owning one weight row per lane and 32 token columns; the
+//               TMEM load of the next block is in flight while the current
+//               one is scaled and accumulated (packed f32x2 math)
 //   warps 10-11 (Q4) nibble expansion: raw nibbles -> int8 (q - 8) in the
 //               SW128 K-major layout the MMA reads
 // Every mbarrier wait is bounded; on a timeout the kernel records it, lets
@@ -36,7 +39,7 @@ namespace dn {
 namespace {
 
 constexpr int kTileRows = 128;                 // MMA M
-constexpr int kTileTok = 128;                  // MMA N
+constexpr int kTileTok = 64;                   // MMA N
 constexpr int kStageK = 128;                   // int8 of K per stage = 4 blocks
 constexpr int kBlocksPerStage = kStageK / kBlock;
 constexpr int kABytes = kTileRows * kStageK;   // 16 KB
@@ -44,15 +47,22 @@ constexpr int kBBytes = kTileTok * kStageK;    // 16 KB
 constexpr int kRawBytes = kTileRows * (kStageK / 2);  // Q4 nibbles: 8 KB
 constexpr int kEpiWarps = 8;
 constexpr int kConvWarps = 2;
-constexpr int kEpiCols = kTileTok / 2;         // columns per drain warp
+constexpr int kEpiCols = kTileTok / (kEpiWarps / 4);  // columns per drain warp
 constexpr uint32_t kTmemCols = 512;
+constexpr int kSlots = (int)kTmemCols / kTileTok;  // D slots: blocks in flight between MMA and drain
 constexpr int kMaxSmemTc = 226 * 1024;
+
+constexpr int kSxBytes = kBlocksPerStage * kTileTok * 4;   // activation scales, block-major
+constexpr int kSwBytes = kTileRows * kBlocksPerStage * 4;   // weight scales, row-major (f32)
 
 template <bool Q4>
 struct TcShape {
   static constexpr int kWarps = 2 + kEpiWarps + (Q4 ? kConvWarps : 0);
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kStageBytes = kABytes + kBBytes + (Q4 ? kRawBytes : 0);
+  static constexpr int kRawOff = kABytes + kBBytes;
+  static constexpr int kSxOff = kRawOff + (Q4 ? kRawBytes : 0);
+  static constexpr int kSwOff = kSxOff + kSxBytes;
+  static constexpr int kStageBytes = kSwOff + kSwBytes;
 };
 
 struct TcArgs {
@@ -100,8 +110,36 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// The same wait, tied to the registers an earlier tcgen05.ld writes, so the
+// compiler cannot move their reads above it.
+__device__ __forceinline__ void tmem_wait_ld_regs(int32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
+        "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]),
+        "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]),
+        "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]),
+        "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+      :
+      : "memory");
+}
+// Asynchronous global -> shared copy of `bytes` (4, 8 or 16); fewer source
+// bytes (`src_bytes`, possibly 0) zero-fill the rest without reading them.
+__device__ __forceinline__ void cp_async(void* dst, const void* src, int bytes, int src_bytes) {
+  if (bytes == 16)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes) : "memory");
+  else if (bytes == 8)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes) : "memory");
+}
+// Arrives on the mbarrier once this thread's earlier cp.async copies landed
+// (the arrival counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base + i).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
@@ -128,9 +166,37 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 }
 
 // Instruction descriptor: s32 accumulator, signed int8 A and B, both K-major,
-// N = 128, M = 128.
+// N = 64, M = 128.
 constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileTok >> 3) << 17) |
                               ((uint32_t)(kTileRows >> 4) << 24);
+
+// Packed f32x2 arithmetic (sm_100): two lanes of float math per instruction.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// Two int32 block dots (|d| < 2^22) as floats, exactly: the bits
+// 0x4B400000 + d are the float 1.5 * 2^23 + d, and subtracting 1.5 * 2^23 is
+// exact. One integer add per value and one packed float add per pair, instead
+// of the slower int-to-float conversion.
+__device__ __forceinline__ uint64_t i2_to_f2(int32_t d0, int32_t d1) {
+  const uint64_t bits = (uint64_t)(uint32_t)(d0 + 0x4B400000) | ((uint64_t)(uint32_t)(d1 + 0x4B400000) << 32);
+  return f2_add(bits, f2_pack(-12582912.0f, -12582912.0f));
+}
 
 __device__ __forceinline__ bool wait_tc(uint64_t* bar, uint32_t parity, uint32_t* status,
                                         uint32_t bits, volatile int* abort_flag) {
@@ -153,8 +219,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   uint64_t* conv = full + stages;
   uint64_t* empty = conv + stages;
   uint64_t* tfull = empty + stages;
-  uint64_t* tempty = tfull + kBlocksPerStage;
-  uint64_t* done = tempty + kBlocksPerStage;
+  uint64_t* tempty = tfull + kSlots;
+  uint64_t* done = tempty + kSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   __shared__ volatile int abort_flag;
 
@@ -165,15 +231,17 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   const int64_t tok0 = (int64_t)blockIdx.y * kTileTok;
   auto stage_a = [&](int s) { return smem + (int64_t)s * S::kStageBytes; };
   auto stage_b = [&](int s) { return smem + (int64_t)s * S::kStageBytes + kABytes; };
-  auto stage_raw = [&](int s) { return smem + (int64_t)s * S::kStageBytes + kABytes + kBBytes; };
+  auto stage_raw = [&](int s) { return smem + (int64_t)s * S::kStageBytes + S::kRawOff; };
+  auto stage_sx = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSxOff); };
+  auto stage_sw = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSwOff); };
 
   if (tid == 0) {
     for (int s = 0; s < stages; s++) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + 32);           // TMA bytes + the producer lanes' scale stores
       mbar_init(&conv[s], kConvWarps * 32);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 1 + kEpiWarps);   // MMA commit + every drain warp
     }
-    for (int q = 0; q < kBlocksPerStage; q++) {
+    for (int q = 0; q < kSlots; q++) {
       mbar_init(&tfull[q], 1);
       mbar_init(&tempty[q], kEpiWarps);
     }
@@ -192,16 +260,26 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    int k = 0;
+    // Lane 0 issues the TMA copies; all lanes stage the stage's scales into
+    // shared memory: activation scales block-major (so the drain reads four
+    // tokens in one 16-byte load), weight scales as f32 per row.
     if (lane == 0) {
       prefetch_tmap(&tw);
       prefetch_tmap(&tx);
-      for (; k < nst; k++) {
-        const int s = k % stages;
-        if (k >= stages &&
-            !wait_tc(&empty[s], (uint32_t)((k / stages) - 1) & 1u, a.status, kStatusMmaTimeout,
-                     &abort_flag))
+    }
+    int k = 0;
+    for (; k < nst; k++) {
+      const int s = k % stages;
+      if (k >= stages) {
+        bool got = !abort_flag && mbar_wait_bounded(&empty[s], (uint32_t)((k / stages) - 1) & 1u,
+                                                    a.status, kStatusMmaTimeout);
+        got = __all_sync(0xffffffffu, got) != 0;
+        if (!got) {
+          abort_flag = 1;
           break;
+        }
+      }
+      if (lane == 0) {
         mbar_arrive_expect_tx(&full[s], (uint32_t)((Q4 ? kRawBytes : kABytes) + kBBytes));
         if (Q4)
           tma_load_2d(stage_raw(s), &tw, k * (kStageK / 2), (int32_t)row0, &full[s]);
@@ -209,12 +287,62 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           tma_load_2d(stage_a(s), &tw, k * kStageK, (int32_t)row0, &full[s]);
         tma_load_2d(stage_b(s), &tx, k * kStageK, (int32_t)tok0, &full[s]);
       }
-      if (abort_flag) {
-        // Let the copies already issued land before the CTA's memory goes.
-        for (int j = k - 1; j >= 0 && j >= k - stages; j--)
-          mbar_wait_bounded(&full[j % stages], (uint32_t)(j / stages) & 1u, a.status,
-                            kStatusTmaTimeout);
+      float* sx = stage_sx(s);
+      float* sw = stage_sw(s);
+      const int64_t b0 = (int64_t)k * kBlocksPerStage;
+      // Asynchronous copies (cp.async), so the producer never waits for the
+      // scales' latency: activation scales transposed to block-major, one
+      // 4-byte copy each; weight scales 16 (f32) or 8 (fp16) bytes per row.
+      // Out-of-range tokens, rows or blocks are zero-filled.
+      for (int i = lane; i < kTileTok; i += 32) {
+        const int64_t t = tok0 + i;
+#pragma unroll
+        for (int q = 0; q < kBlocksPerStage; q++) {
+          const bool in = t < a.n && b0 + q < blocks;
+          cp_async(sx + q * kTileTok + i, in ? (const void*)(a.xsc + t * blocks + b0 + q) : (const void*)a.xsc,
+                   4, in ? 4 : 0);
+        }
       }
+      const bool vec_w = (blocks % kBlocksPerStage) == 0 && ((uintptr_t)a.scales & (Q4 ? 7 : 15)) == 0;
+      for (int i = lane; i < kTileRows; i += 32) {
+        const int64_t r = row0 + i;
+        if (Q4) {
+          uint16_t* sw16 = reinterpret_cast<uint16_t*>(sw) + i * kBlocksPerStage;
+          const uint16_t* src = static_cast<const uint16_t*>(a.scales) + r * blocks + b0;
+          if (vec_w) {
+            cp_async(sw16, r < a.rows ? (const void*)src : a.scales, 8, r < a.rows ? 8 : 0);
+          } else {
+#pragma unroll
+            for (int q = 0; q < kBlocksPerStage; q++)
+              sw16[q] = (r < a.rows && b0 + q < blocks) ? __ldg(src + q) : (uint16_t)0;
+          }
+        } else {
+          const float* src = static_cast<const float*>(a.scales) + r * blocks + b0;
+          if (vec_w) {
+            cp_async(sw + i * kBlocksPerStage, r < a.rows ? (const void*)src : a.scales, 16,
+                     r < a.rows ? 16 : 0);
+          } else {
+#pragma unroll
+            for (int q = 0; q < kBlocksPerStage; q++) {
+              const bool in = r < a.rows && b0 + q < blocks;
+              cp_async(sw + i * kBlocksPerStage + q, in ? (const void*)(src + q) : a.scales, 4, in ? 4 : 0);
+            }
+          }
+        }
+      }
+      if (Q4 && !vec_w) {
+        // The fp16 scales went through plain stores: arrive after everything landed.
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        mbar_arrive(&full[s]);
+      } else {
+        cp_async_arrive(&full[s]);
+      }
+    }
+    if (abort_flag && lane == 0) {
+      // Let the copies already issued land before the CTA's memory goes.
+      for (int j = k - 1; j >= 0 && j >= k - stages; j--)
+        mbar_wait_bounded(&full[j % stages], (uint32_t)(j / stages) & 1u, a.status,
+                          kStatusTmaTimeout);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
@@ -227,16 +355,18 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
         const uint32_t a_addr = smem_u32(stage_a(s)), b_addr = smem_u32(stage_b(s));
         bool ok = true;
         for (int q = 0; q < kBlocksPerStage; q++) {
-          if ((int64_t)k * kBlocksPerStage + q >= blocks) break;
-          if (k > 0 && !wait_tc(&tempty[q], (uint32_t)(k - 1) & 1u, a.status, kStatusMmaTimeout,
-                                &abort_flag)) {
+          const int blk = k * kBlocksPerStage + q;
+          if (blk >= blocks) break;
+          const int slot = blk % kSlots, use = blk / kSlots;
+          if (use > 0 && !wait_tc(&tempty[slot], (uint32_t)(use - 1) & 1u, a.status,
+                                  kStatusMmaTimeout, &abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          mma_i8(tmem + (uint32_t)(q * kTileTok), sw128_desc(a_addr + q * 32),
+          mma_i8(tmem + (uint32_t)(slot * kTileTok), sw128_desc(a_addr + q * 32),
                  sw128_desc(b_addr + q * 32), kIdescI8);
-          mma_commit(&tfull[q]);
+          mma_commit(&tfull[slot]);
         }
         mma_commit(&empty[s]);
         if (!ok) break;
@@ -248,53 +378,93 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ drain
     const int quarter = warp & 3;               // TMEM lanes this warp may access
-    const int half = (warp - 2) >> 2;           // which 64 token columns
-    const int64_t row = row0 + quarter * 32 + lane;
-    const bool row_ok = row < a.rows;
-    const int64_t t_base = tok0 + half * kEpiCols;
-    float acc[kEpiCols];
+    const int half = (warp - 2) >> 2;           // which group of kEpiCols token columns
+    const int row_local = quarter * 32 + lane;
+    const int64_t row = row0 + row_local;
+    const int col0 = half * kEpiCols;
+    uint64_t acc[kEpiCols / 2];                  // f32 pairs: tokens col0 + 2i, col0 + 2i + 1
 #pragma unroll
-    for (int j = 0; j < kEpiCols; j++) acc[j] = 0.0f;
-    for (int k = 0; k < nst && !abort_flag; k++) {
+    for (int j = 0; j < kEpiCols / 2; j++) acc[j] = 0;
+    // Blocks in order; the TMEM load of block b + 1 is in flight while block
+    // b is scaled and accumulated. Stage / slot indices and their phases
+    // are running counters (no division in the loop).
+    const int nblk = (int)blocks;
+    int32_t dn[32];
+    int slot = 0;
+    uint32_t tph = 0;
+    auto start_load = [&](int sl, uint32_t ph) -> bool {
+      bool got = !abort_flag && mbar_wait_bounded(&tfull[sl], ph, a.status, kStatusMmaTimeout);
+      if (!__all_sync(0xffffffffu, got)) {  // tcgen05.ld is warp-wide: all lanes agree
+        abort_flag = 1;
+        return false;
+      }
+      tc_fence_after();
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sl * kTileTok + col0), dn);
+      return true;
+    };
+    bool alive = nblk > 0 && start_load(0, 0);
+    int st = 0;
+    uint32_t sph = 0;
+    for (int blk = 0; blk < nblk && alive;) {
+      // This stage's scales (the producer's cp.async copies) have landed.
+      bool got = !abort_flag && mbar_wait_bounded(&full[st], sph, a.status, kStatusTmaTimeout);
+      if (!__all_sync(0xffffffffu, got)) {
+        abort_flag = 1;
+        break;
+      }
+      float sws[kBlocksPerStage];
+      if (Q4) {
+        const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(stage_sw(st)) +
+                                                        row_local * kBlocksPerStage);
+        sws[0] = half_bits_to_float((uint16_t)h.x);
+        sws[1] = half_bits_to_float((uint16_t)(h.x >> 16));
+        sws[2] = half_bits_to_float((uint16_t)h.y);
+        sws[3] = half_bits_to_float((uint16_t)(h.y >> 16));
+      } else {
+        const float4 f = *reinterpret_cast<const float4*>(stage_sw(st) + row_local * kBlocksPerStage);
+        sws[0] = f.x; sws[1] = f.y; sws[2] = f.z; sws[3] = f.w;
+      }
+      const float* sx_stage = stage_sx(st) + col0;
+#pragma unroll
       for (int q = 0; q < kBlocksPerStage; q++) {
-        const int64_t b = (int64_t)k * kBlocksPerStage + q;
-        if (b >= blocks) break;
-        // The tcgen05.ld below is warp-wide: every lane must agree on the wait.
-        bool got = !abort_flag && mbar_wait_bounded(&tfull[q], (uint32_t)k & 1u, a.status,
-                                                    kStatusMmaTimeout);
-        got = __all_sync(0xffffffffu, got) != 0;
-        if (!got) {
-          abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        int32_t d0[32], d1[32];
-        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) +
-                               (uint32_t)(q * kTileTok + half * kEpiCols);
-        tmem_ld32(taddr, d0);
-        tmem_ld32(taddr + 32, d1);
-        tmem_wait_ld();
+        if (blk >= nblk || !alive) break;
+        tmem_wait_ld_regs(dn);
+        int32_t d0[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) d0[j] = dn[j];
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[q]);
-        float sw = 0.0f;
-        if (row_ok)
-          sw = Q4 ? half_bits_to_float(__ldg(static_cast<const uint16_t*>(a.scales) + row * blocks + b))
-                  : __ldg(static_cast<const float*>(a.scales) + row * blocks + b);
-#pragma unroll
-        for (int j = 0; j < kEpiCols; j++) {
-          const int64_t t = t_base + j;
-          const float sx = t < a.n ? __ldg(a.xsc + t * blocks + b) : 0.0f;
-          const int32_t d = j < 32 ? d0[j] : d1[j - 32];
-          acc[j] = __fmaf_rn(__int2float_rn(d), __fmul_rn(sw, sx), acc[j]);
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+        if (++slot == kSlots) {
+          slot = 0;
+          tph ^= 1u;
         }
+        if (blk + 1 < nblk && !start_load(slot, tph)) alive = false;
+        const uint64_t sw2 = f2_pack(sws[q], sws[q]);
+        const float* sxq = sx_stage + q * kTileTok;
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4) {
+          const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
+          // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
+          acc[j / 2] = f2_fma(i2_to_f2(d0[j], d0[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
+          acc[j / 2 + 1] = f2_fma(i2_to_f2(d0[j + 2], d0[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
+                                  acc[j / 2 + 1]);
+        }
+        blk++;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == stages) {
+        st = 0;
+        sph ^= 1u;
       }
     }
-    if (row_ok && !abort_flag) {
+    if (row < a.rows && !abort_flag) {
 #pragma unroll
-      for (int j = 0; j < kEpiCols; j++) {
-        const int64_t t = t_base + j;
-        if (t < a.n) a.ys[t * a.ldy + row] = acc[j];
+      for (int j = 0; j < kEpiCols / 2; j++) {
+        const int64_t t = tok0 + col0 + 2 * j;
+        if (t < a.n) a.ys[t * a.ldy + row] = __uint_as_float((uint32_t)acc[j]);
+        if (t + 1 < a.n) a.ys[(t + 1) * a.ldy + row] = __uint_as_float((uint32_t)(acc[j] >> 32));
       }
     }
   } else {
@@ -343,9 +513,9 @@ template <bool Q4>
 int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   using S = TcShape<Q4>;
   const int64_t blocks = a.cols / kBlock;
-  const int64_t bar_bytes = 8 * (3 * 16 + 2 * kBlocksPerStage + 2) + 16;
+  const int64_t bar_bytes = 8 * (3 * 16 + 2 * kSlots + 2) + 16;  // up to 16 stages
   int stages = (int)((kMaxSmemTc - 1024 - bar_bytes) / S::kStageBytes);
-  stages = stages > 8 ? 8 : stages;
+  stages = stages > 12 ? 12 : stages;
   if (stages < 2) return kErrTooLarge;
   const size_t smem = 1024 + (size_t)stages * S::kStageBytes + (size_t)bar_bytes;
   CUtensorMap tw, tx;
