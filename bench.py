@@ -239,6 +239,61 @@ def run_step(stack, chain, L, stream_handle, gather, gather_qa, flags=1):
     return launches
 
 
+class DecodeChain:
+    """All projections of one token as ONE persistent kernel (dn_chain_run):
+    weights stream without a gap between dependent projections. The chain
+    keeps the model's order: each projection starts after the one before it
+    (qkv after the previous layer's down), so no layer runs ahead of the
+    last. Each op has its own QA output buffer; only the logits are kept in
+    f32. One GPU only: the row shards of N > 1 need an all-gather between
+    ops."""
+
+    def __init__(self, torch, stack, qa, L, device):
+        from dianoia_b200 import _lib
+        self.L = L
+        self.keep = []
+        ops, last = [], {}
+        for i, m in enumerate(stack.mats):
+            name = m["name"]
+            src = INPUT_OF[name]
+            if src is not None:
+                xa, dep = last[src]
+            else:
+                # qkv reads x0 (the stand-in for the norm output) but, as in the
+                # model, starts only after the previous layer's down.
+                xa, dep = qa.xa0.data_ptr(), (last["down"][1] if "down" in last else -1)
+            ys = ya = None
+            if name == "lm_head":
+                ys = stack.bufs["lm_head"].data_ptr()
+            else:
+                buf = torch.zeros(m["rows"] // 32 * 36, dtype=torch.uint8, device=device)
+                self.keep.append(buf)
+                ya = buf.data_ptr()
+                last[name] = (ya, i)
+            ops.append(_lib.ChainOp(m["qs"].data_ptr(), m["scales"].data_ptr(), xa, ys, ya,
+                                    m["rows"], m["cols"], dep))
+        arr = (_lib.ChainOp * len(ops))(*ops)
+        self.handle = ctypes.c_void_p()
+        _lib.check(L.dn_chain_create(0, arr, len(ops), ctypes.byref(self.handle)), "dn_chain_create")
+
+    def close(self):
+        if self.handle:
+            self.L.dn_chain_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+
+def run_step_chain(stack, qa, dchain, L, stream_handle, flags=1):
+    """One token: quantize x0, then every projection in one chain kernel."""
+    rc = L.dn_quantize_qa(stack.x0.data_ptr(), qa.xa0.data_ptr(), 1, HIDDEN,
+                          HIDDEN // 32 * 36, stream_handle)
+    if rc != 0:
+        raise RuntimeError(f"dn_quantize_qa failed: {L.dn_error_string(rc).decode()}")
+    rc = L.dn_chain_run(dchain.handle, flags, stream_handle)
+    if rc != 0:
+        raise RuntimeError(f"dn_chain_run failed: {L.dn_error_string(rc).decode()}")
+    return 2
+
+
 # -------------------------------------------------------------- CPU legs
 
 def host_weights(stack):
@@ -329,6 +384,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--path", choices=["chain", "ops"], default="ops",
+                    help="chain: one persistent kernel per token (1 GPU); ops: one GEMV "
+                         "launch per projection (always used for N > 1)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm"], default="stack",
@@ -380,19 +438,26 @@ def main():
             dist.all_gather_into_tensor(out, out[rank * n:(rank + 1) * n])
         gather_qa = gather
 
+    path = args.path if world == 1 else "ops"
+    dchain = DecodeChain(torch, stack, chain, L, device) if path == "chain" else None
+
+    def one_step(handle):
+        if dchain is not None:
+            return run_step_chain(stack, chain, dchain, L, handle)
+        return run_step(stack, chain, L, handle, gather, gather_qa)
+
     stream = torch.cuda.Stream(device=device)
     graph = None
-    launches_per_step = len(stack.mats) + 1
+    launches_per_step = 2 if dchain is not None else len(stack.mats) + 1
     with torch.cuda.stream(stream):
         for _ in range(2):
-            run_step(stack, chain, L, stream.cuda_stream, gather, gather_qa)
+            one_step(stream.cuda_stream)
         torch.cuda.synchronize()
         if not args.no_graph:
             try:
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph, stream=stream):
-                    run_step(stack, chain, L, torch.cuda.current_stream().cuda_stream, gather,
-                             gather_qa)
+                    one_step(torch.cuda.current_stream().cuda_stream)
                 torch.cuda.synchronize()
             except Exception as e:  # eager launches if capture is not possible
                 log("graph capture failed, running eagerly:", repr(e))
@@ -402,7 +467,7 @@ def main():
         if graph is not None:
             graph.replay()
         else:
-            run_step(stack, chain, L, stream.cuda_stream, gather, gather_qa)
+            one_step(stream.cuda_stream)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -438,10 +503,11 @@ def main():
     alg_bytes = step_bytes(Q8_BLOCK_BYTES_ALG)
     ref_bytes = step_bytes(Q8_BLOCK_BYTES_REF)
 
-    # Dominant kernel: the fused quantize + GEMV (every launch in the step).
-    # Achieved = algorithmic bytes per step / step time on the launching
-    # stream (inter-kernel gaps included, so this is a lower bound of the
-    # kernel's own bandwidth); on N GPUs, bytes per rank.
+    # Dominant kernel: the decode chain (1 GPU) or the fused quantize + GEMV
+    # launches (N GPUs). Achieved = algorithmic bytes per step / step time on
+    # the launching stream (the activation quantize and any gaps included,
+    # so this is a lower bound of the kernel's own bandwidth); on N GPUs,
+    # bytes per rank.
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -455,6 +521,16 @@ def main():
     # Checksum of the logits: identical for every N (rows do not depend on the split).
     logits = stack.bufs["lm_head"].double()
     checksum = float(logits.sum().item())
+    chain_matches_ops = None
+    if dchain is not None:
+        # The chain's logits equal the per-projection launches', bit for bit.
+        chain_logits = stack.bufs["lm_head"].clone()
+        with torch.cuda.stream(stream):
+            stack.bufs["lm_head"].fill_(float("nan"))
+            run_step(stack, chain, L, stream.cuda_stream, None, None)
+        torch.cuda.synchronize()
+        chain_matches_ops = bool(torch.equal(chain_logits.view(torch.int32),
+                                             stack.bufs["lm_head"].view(torch.int32)))
 
     # End to end through the C-ABI with host buffers (rank-local shards; on
     # N > 1 the slices are all-gathered through device copies).
@@ -480,12 +556,20 @@ def main():
             "e2e": e2e,
             "cpu_baseline": cpu_baseline,
             "gpu_launches": launches_per_step * args.steps,
-            "gpu_launches_note": "1 activation quantize + 113 fused GEMVs per step",
+            "gpu_launches_note": ("1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
+                                  if dchain is not None else
+                                  "1 activation quantize + 113 fused GEMVs per step"),
+            "path": path,
+            "chain_logits_match_per_op_launches": chain_matches_ops,
             "graph": graph is not None,
             "clocks": clocks.summary(),
             "logits_checksum": checksum,
         }
         print(json.dumps(res), flush=True)
+    if dchain is not None:
+        del graph
+        torch.cuda.synchronize()
+        dchain.close()
     if world > 1:
         del graph
         dist.barrier()

@@ -33,6 +33,10 @@ SIGNATURES = {
     "dn_quantize_q4": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_quantize_qa": (_i64, [_p, _p, _i64, _i64, _i64, _p]),
     "dn_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p]),
+    "dn_chain_create": (_i64, [_i64, _p, _i64, _p]),
+    "dn_chain_run": (_i64, [_p, _i64, _p]),
+    "dn_chain_reset": (_i64, [_p, _p]),
+    "dn_chain_destroy": (_i64, [_p]),
     "dn_last_error": (_i64, []),
     "dn_device_status": (_i64, [_i64]),
     "dn_error_string": (ctypes.c_char_p, [_i64]),
@@ -44,6 +48,12 @@ DN_Q8, DN_Q4 = 0, 1
 DN_PATH_AUTO, DN_PATH_GEMV, DN_PATH_TC, DN_PATH_GENERIC = -1, 0, 1, 2
 DN_FLAG_PDL = 1
 QA_BYTES = 36  # QA activation block: 32 int8 + f32 scale
+
+
+class ChainOp(ctypes.Structure):
+    """dn_chain_op (include/dianoia_b200.h)."""
+    _fields_ = [("qs", _p), ("scales", _p), ("xa", _p), ("ys", _p), ("ya", _p),
+                ("rows", _i64), ("cols", _i64), ("dep", _i64)]
 
 _lib = None
 

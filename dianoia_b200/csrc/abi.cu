@@ -490,6 +490,36 @@ int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const u
   return dn::launch_gemv_ex(g, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
 }
 
+int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, void** chain) {
+  if ((format != DN_Q8 && format != DN_Q4) || ops == nullptr || chain == nullptr || nops <= 0)
+    return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  static_assert(sizeof(dn_chain_op) == sizeof(dn::ChainOpSpec), "op layouts differ");
+  dn::ChainHost* h = nullptr;
+  const int64_t rc = dn::chain_create(reinterpret_cast<const dn::ChainOpSpec*>(ops), nops,
+                                      format == DN_Q4, &h);
+  *chain = rc == DN_OK ? h : nullptr;
+  return rc;
+}
+
+int64_t dn_chain_run(void* chain, int64_t flags, void* stream) {
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  if (chain == nullptr) return DN_ERR_ARGS;
+  return dn::chain_launch(static_cast<dn::ChainHost*>(chain), d->status_dev,
+                          static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
+}
+
+int64_t dn_chain_reset(void* chain, void* stream) {
+  if (chain == nullptr) return DN_ERR_ARGS;
+  return dn::chain_reset(static_cast<dn::ChainHost*>(chain), static_cast<cudaStream_t>(stream));
+}
+
+int64_t dn_chain_destroy(void* chain) {
+  dn::chain_destroy(static_cast<dn::ChainHost*>(chain));
+  return DN_OK;
+}
+
 int64_t dn_last_error(void) {
   const int64_t e = tl_last_error;
   tl_last_error = DN_OK;

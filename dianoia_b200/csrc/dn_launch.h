@@ -57,6 +57,22 @@ bool gemv_ex_supported(const GemvArgs& g);
 cudaError_t launch_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols,
                                int64_t xa_stride, cudaStream_t stream);
 
+// Decode chains (chain.cu): the ops of a token run by one persistent kernel.
+struct ChainOpSpec {
+  const void* qs;
+  const void* scales;
+  const uint8_t* xa;   // QA input
+  float* ys;           // f32 outputs or null
+  uint8_t* ya;         // QA outputs or null
+  int64_t rows, cols;
+  int64_t dep;         // index of the op whose QA output xa is, or -1
+};
+struct ChainHost;
+int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost** out);
+void chain_destroy(ChainHost* h);
+int64_t chain_launch(ChainHost* h, uint32_t* status, cudaStream_t stream, bool pdl);
+int64_t chain_reset(ChainHost* h, cudaStream_t stream);
+
 // Quantizes n rows of cols floats to Q8_0 (lab_quantize_q8 semantics).
 cudaError_t launch_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
                                cudaStream_t stream);

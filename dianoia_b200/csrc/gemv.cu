@@ -39,149 +39,12 @@
 #include "dn_common.cuh"
 #include "dn_launch.h"
 #include "dn_tmap.h"
+#include "gemv_core.cuh"
 
 namespace dn {
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kRows = 8 * kConsumerWarps;   // rows per tile: one Q8_0 block of the output
-constexpr int kConsumers = 32 * kConsumerWarps;
-constexpr int kThreads = kConsumers + 32;   // + one producer warp
-constexpr int kChunkBytes = 512;            // weight bytes per row per stage
-constexpr int kBoxBytes = 128;              // inner box width (the 128-byte swizzle span)
-constexpr int kBox = kRows * kBoxBytes;     // 4 KB per box in shared memory
-constexpr int kWBoxes = kChunkBytes / kBoxBytes;
-constexpr int kScaleRow = 64;               // scale bytes per row per stage (16 f32 / 32 fp16)
-constexpr int kStageBytes = kWBoxes * kBox + kRows * kScaleRow;  // weight boxes + scale box
-constexpr int kMaxSmem = 226 * 1024;  // dynamic; leaves room for static smem
-constexpr int kSmemPerSM = 228 * 1024;
-constexpr int kSMs = 148;
-constexpr int kMaxStages = 16;
-
-template <bool Q4>
-struct Fmt {
-  static constexpr int kWB = Q4 ? 16 : 32;          // weight bytes per block
-  static constexpr int kSB = Q4 ? 2 : 4;            // scale bytes per block
-  static constexpr int kKC = kChunkBytes / kWB;     // blocks per stage (scales: 64 bytes)
-};
-
-__host__ __device__ inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
-
-struct SmemPlan {
-  int64_t bar_off, xw_off, xw_stride, xs_off, xs_stride, yt_off, stg_off, stg_stride, total;
-};
-
-// Activations in shared memory, lane-interleaved: for block b, lane l's two
-// words (bytes 4l..4l+3 and 16+4l..16+4l+3 of the block) sit together, so a
-// lane reads its block operand with one 64-bit load (Q8). Q4 adds the lane's
-// -8 * sum term: 16 bytes per lane, one 128-bit load. Block scales are a
-// separate f32 array.
-template <bool Q4>
-struct XLayout {
-  static constexpr int kLaneBytes = Q4 ? 16 : 8;
-  static constexpr int kBlockBytes = 4 * kLaneBytes;
-  // Offset of word w (0..7) of a block.
-  __device__ static __forceinline__ int word_off(int w) { return (w & 3) * kLaneBytes + (w >> 2) * 4; }
-};
-
-// Layout from a 1024-byte aligned base: the stages, the barriers (`stages`
-// full, `stages` empty, two activation, two epilogue), the activations, the
-// epilogue's outputs and the input staging. `total` includes the slack to
-// align the base.
-template <bool Q4>
-__host__ __device__ inline SmemPlan plan(int stages, int nt, int64_t cols, bool f32_in) {
-  const int64_t blocks = cols / kBlock;
-  SmemPlan p;
-  p.bar_off = (int64_t)stages * kStageBytes;
-  p.xw_off = round_up(p.bar_off + 8 * (2 * stages + 4), 128);
-  p.xw_stride = blocks * XLayout<Q4>::kBlockBytes;
-  p.xs_off = p.xw_off + nt * p.xw_stride;
-  p.xs_stride = round_up(blocks, 4);
-  p.yt_off = p.xs_off + nt * p.xs_stride * 4;
-  p.stg_off = round_up(p.yt_off + 2 * (int64_t)nt * kRows * 4, 128);
-  p.stg_stride = f32_in ? cols * 4 : round_up(blocks * kQABytes, 16);
-  p.total = p.stg_off + (f32_in ? 2 : nt) * p.stg_stride + 1024;
-  return p;
-}
-
-// In a 128-byte-swizzled box of 32 rows x 128 bytes, byte `col` of row r
-// sits at r * 128 + (((col / 16) ^ (r % 8)) * 16) + col % 16: the 16-byte
-// chunk index is XORed with r mod 8.
-// A bounded wait whose result is the same on every lane of the warp.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
-  const bool got = mbar_wait_bounded(bar, parity, status, kStatusTmaTimeout);
-  return __all_sync(0xffffffffu, got) != 0;
-}
-
-// Named barrier over the consumer warps only (the producer never joins);
-// used in the prologue, which every consumer thread always reaches.
-__device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-}
-
-template <typename T>
-__device__ __forceinline__ T lds(const void* p) {
-  return *reinterpret_cast<const T*>(p);
-}
-
-// -8 * (sum of the eight int8 a lane multiplies in one block).
-__device__ __forceinline__ int32_t lane_sum8(uint32_t w0, uint32_t w1) {
-  return -8 * __dp4a((int32_t)w0, 0x01010101, __dp4a((int32_t)w1, 0x01010101, 0));
-}
-
-// Quantizes one token of f32 activations (in shared memory) into the
-// lane-interleaved layout, eight lanes per block (lab_quantize_q8
-// semantics). With `xq`, also writes lab_gemm's xq / xsc outputs.
-template <bool Q4>
-__device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xw, float* xs,
-                                               int64_t blocks, int8_t* xq, float* xsc) {
-  using X = XLayout<Q4>;
-  const int tid = threadIdx.x, sub = tid & 7;
-  for (int64_t base = 0; base < blocks; base += kConsumers / 8) {
-    const int64_t b = base + (tid >> 3);
-    const bool active = b < blocks;
-    const float4 v = active ? *reinterpret_cast<const float4*>(xf + b * kBlock + sub * 4)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-    float amax = fmaxf(fmaxf(fmaxf(0.0f, fabsf(v.x)), fmaxf(fabsf(v.y), fabsf(v.z))), fabsf(v.w));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    float scale, inv;
-    q8_scale(amax, scale, inv);
-    const uint32_t word = pack4(quant_q8_elem(v.x, inv), quant_q8_elem(v.y, inv),
-                                quant_q8_elem(v.z, inv), quant_q8_elem(v.w, inv));
-    const uint32_t hi_word = __shfl_down_sync(0xffffffffu, word, 4);  // sub < 4: word sub + 4
-    if (active) {
-      uint8_t* blk = xw + b * X::kBlockBytes;
-      *reinterpret_cast<uint32_t*>(blk + X::word_off(sub)) = word;
-      if (Q4 && sub < 4) *reinterpret_cast<int32_t*>(blk + sub * 16 + 8) = lane_sum8(word, hi_word);
-      if (sub == 0) xs[b] = scale;
-      if (xq != nullptr) {
-        *reinterpret_cast<uint32_t*>(xq + b * kBlock + sub * 4) = word;
-        if (sub == 0) xsc[b] = scale;
-      }
-    }
-  }
-}
-
-// QA blocks (staged in shared memory) -> the lane-interleaved layout.
-template <bool Q4>
-__device__ __forceinline__ void unpack_qa(const uint8_t* qa, uint8_t* xw, float* xs, int64_t blocks) {
-  using X = XLayout<Q4>;
-  for (int64_t i = threadIdx.x; i < blocks * 4; i += kConsumers) {
-    const int64_t b = i >> 2;
-    const int ll = (int)(i & 3);
-    const uint8_t* src = qa + b * kQABytes;
-    const uint32_t w0 = lds<uint32_t>(src + 4 * ll), w1 = lds<uint32_t>(src + 16 + 4 * ll);
-    uint8_t* dst = xw + b * X::kBlockBytes + ll * X::kLaneBytes;
-    if (Q4) {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(w0, w1, (uint32_t)lane_sum8(w0, w1), 0u);
-    } else {
-      *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
-    }
-    if (ll == 0) xs[b] = lds<float>(src + 32);
-  }
-}
+using namespace gemv;
 
 template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN>
 __global__ void __launch_bounds__(kThreads)
@@ -247,14 +110,8 @@ __global__ void __launch_bounds__(kThreads)
         const int64_t tile = blockIdx.x + (k / nch) * gridDim.x;
         const int c = (int)(k % nch);
         const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-        const int boxes = (nb * F::kWB + kBoxBytes - 1) / kBoxBytes;
-        uint8_t* stage = smem + (int64_t)s * kStageBytes;
-        // Boxes past the matrix edge are zero-filled and count in full.
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * kBox + (TMA_SCALES ? kRows * kScaleRow : 0)));
-        const int32_t y = (int32_t)(tile * kRows);
-        for (int j = 0; j < boxes; j++)
-          tma_load_2d(stage + j * kBox, &tw, c * kChunkBytes + j * kBoxBytes, y, &full[s]);
-        if (TMA_SCALES) tma_load_2d(stage + kWBoxes * kBox, &tsc, c * F::kKC, y, &full[s]);
+        issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, &tw, &tsc, c, nb,
+                                    (int32_t)(tile * kRows), &full[s]);
       }
       __syncwarp();
     }
@@ -347,43 +204,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t] = 0.0f;
 
-    // One block: weights w0 / w1 (as int8 for Q8, nibbles for Q4), its
-    // scale, and the activations of every token.
-    auto block_step = [&](int b, int32_t w0, int32_t w1, float sw, const float* xsc_b) {
-#pragma unroll
-      for (int t = 0; t < NT; t++) {
-        const uint8_t* xb = xw_l + t * sp.xw_stride + b * X::kBlockBytes;
-        int32_t d;
-        if (Q4) {
-          const uint4 xv = lds<uint4>(xb);
-          d = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, (int32_t)xv.z));
-        } else {
-          const uint2 xv = lds<uint2>(xb);
-          d = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, 0));
-        }
-        acc[t] = __fmaf_rn(__int2float_rn(d), __fmul_rn(sw, xsc_b[t]), acc[t]);
-      }
-    };
-    auto weights_of = [&](const uint8_t* stage, int bb, int32_t& w0, int32_t& w1) {
-      if (Q4) {
-        const uint32_t wv = lds<uint32_t>(stage + (bb / 8) * kBox + rowoff +
-                                          ((((bb & 7) ^ r8) & 7) << 4) + 4 * l);
-        w0 = (int32_t)(wv & 0x0f0f0f0fu);          // weights 4l..4l+3, as 0..15
-        w1 = (int32_t)((wv >> 4) & 0x0f0f0f0fu);   // weights 16+4l..16+4l+3
-      } else {
-        const uint8_t* line = stage + (bb / 4) * kBox + rowoff;
-        w0 = (int32_t)lds<uint32_t>(line + (((((bb & 3) * 2) ^ r8) & 7) << 4) + 4 * l);
-        w1 = (int32_t)lds<uint32_t>(line + (((((bb & 3) * 2 + 1) ^ r8) & 7) << 4) + 4 * l);
-      }
-    };
-    auto scale_of = [&](const uint8_t* stage, int bb, int64_t b) -> float {
-      if (TMA_SCALES) {
-        const uint8_t* sline = stage + kWBoxes * kBox + row_local * kScaleRow;
-        return Q4 ? half_bits_to_float(lds<uint16_t>(sline + bb * 2)) : lds<float>(sline + bb * 4);
-      }
-      return Q4 ? half_bits_to_float(__ldg(reinterpret_cast<const uint16_t*>(sc) + row * blocks + b))
-                : __ldg(reinterpret_cast<const float*>(sc) + row * blocks + b);
-    };
+    const LaneCtx lc{row_local, r8, l, rowoff, xw_l, sp.xw_stride, xs_s, sp.xs_stride, sc, row, blocks};
 
     for (int c = 0; c < nch; c++, k++) {
       const int s = (int)(k % stages);
@@ -392,75 +213,7 @@ __global__ void __launch_bounds__(kThreads)
         abort_flag = 1;
         return;  // the producer drains what it issued; every other wait is bounded
       }
-      const uint8_t* stage = smem + (int64_t)s * kStageBytes;
-      const int b0 = c * F::kKC;
-      const int full_boxes = nb / kPerBox;
-      // A whole box: kPerBox consecutive blocks, their scales in one 16-byte
-      // load, the activation scales in 16-byte loads.
-      auto do_box = [&](int j) {
-        const uint8_t* line = stage + j * kBox + rowoff;
-        float sws[kPerBox];
-        if (TMA_SCALES) {
-          const uint4 sv = lds<uint4>(stage + kWBoxes * kBox + row_local * kScaleRow + 16 * j);
-          if (Q4) {
-            const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-            for (int q = 0; q < 8; q++) sws[q] = half_bits_to_float((uint16_t)(u[q >> 1] >> (16 * (q & 1))));
-          } else {
-            sws[0] = __uint_as_float(sv.x);
-            sws[1] = __uint_as_float(sv.y);
-            sws[2] = __uint_as_float(sv.z);
-            sws[3] = __uint_as_float(sv.w);
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < kPerBox; q++) sws[q] = scale_of(stage, j * kPerBox + q, b0 + j * kPerBox + q);
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < kPerBox; q4 += 4) {
-          const int bq = b0 + j * kPerBox + q4;
-          float xsc[4][NT];
-#pragma unroll
-          for (int t = 0; t < NT; t++) {
-            const float4 xv = lds<float4>(xs_s + t * sp.xs_stride + bq);
-            xsc[0][t] = xv.x;
-            xsc[1][t] = xv.y;
-            xsc[2][t] = xv.z;
-            xsc[3][t] = xv.w;
-          }
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            int32_t w0, w1;
-            if (Q4) {
-              const uint32_t wv = lds<uint32_t>(line + ((((q4 + q) ^ r8) & 7) << 4) + 4 * l);
-              w0 = (int32_t)(wv & 0x0f0f0f0fu);
-              w1 = (int32_t)((wv >> 4) & 0x0f0f0f0fu);
-            } else {
-              w0 = (int32_t)lds<uint32_t>(line + (((2 * q ^ r8) & 7) << 4) + 4 * l);
-              w1 = (int32_t)lds<uint32_t>(line + ((((2 * q + 1) ^ r8) & 7) << 4) + 4 * l);
-            }
-            block_step(bq + q, w0, w1, sws[q4 + q], xsc[q]);
-          }
-        }
-      };
-      if (full_boxes == kWBoxes) {
-        // A full stage as straight-line code: later blocks' loads and dot
-        // products can be scheduled under the serial FMA chain.
-#pragma unroll
-        for (int j = 0; j < kWBoxes; j++) do_box(j);
-      } else {
-        for (int j = 0; j < full_boxes; j++) do_box(j);
-      }
-      // Blocks after the last whole box (only when cols is not a multiple of
-      // the box: 128 weights for Q8, 256 for Q4).
-      for (int bb = full_boxes * kPerBox; bb < nb; bb++) {
-        int32_t w0, w1;
-        weights_of(stage, bb, w0, w1);
-        float xsc[NT];
-#pragma unroll
-        for (int t = 0; t < NT; t++) xsc[t] = xs_s[t * sp.xs_stride + b0 + bb];
-        block_step(b0 + bb, w0, w1, scale_of(stage, bb, b0 + bb), xsc);
-      }
+      gemv_stage<Q4, NT, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, c * F::kKC, lc, acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -468,9 +221,7 @@ __global__ void __launch_bounds__(kThreads)
     float* yt = yt_s + (e & 1) * NT * kRows;
 #pragma unroll
     for (int t = 0; t < NT; t++) {
-      const float v = acc[t];
-      const float s01 = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
-      const float y = __fadd_rn(s01, __shfl_down_sync(0xffffffffu, s01, 2));
+      const float y = lane_reduce(acc[t]);
       if (l == 0 && row_local < tile_rows && t < nt) {
         if (a.ys != nullptr) a.ys[(t0 + t) * a.ldy + row0 + row_local] = y;
         yt[t * kRows + row_local] = y;
@@ -486,17 +237,8 @@ __global__ void __launch_bounds__(kThreads)
         abort_flag = 1;
         return;
       }
-      for (int t = warp; t < nt; t += kConsumerWarps) {
-        const float v = yt[t * kRows + lane];
-        float amax = fmaxf(0.0f, fabsf(v));
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        float scale, inv;
-        q8_scale(amax, scale, inv);
-        uint8_t* dst = a.ya + (t0 + t) * a.ya_stride + tile * kQABytes;
-        dst[lane] = (uint8_t)(int8_t)quant_q8_elem(v, inv);
-        if (lane == 0) *reinterpret_cast<float*>(dst + 32) = scale;
-      }
+      for (int t = warp; t < nt; t += kConsumerWarps)
+        quantize_block_out(yt[t * kRows + lane], a.ya + (t0 + t) * a.ya_stride + tile * kQABytes, lane);
       e++;
     }
   }

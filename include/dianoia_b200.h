@@ -136,6 +136,43 @@ int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const u
                      int64_t xa_stride, float* ys, int64_t ldy, uint8_t* ya, int64_t ya_stride,
                      int64_t rows, int64_t cols, int64_t n, int64_t flags, void* stream);
 
+/* A decode chain: the quantized products of one token (or any sequence of
+ * GEMVs on QA activations) run by ONE persistent kernel, so HBM keeps
+ * streaming weights across the dependencies between them. Op i reads QA
+ * activations `xa` (n = 1, stride cols / 32 * 36). If `dep` >= 0, op i
+ * starts after op `dep` has finished, inside the kernel: a data edge when xa
+ * lies in the QA output `ya` of op dep (from any 36-byte block of it, e.g.
+ * the q rows of a fused qkv output), else an ordering edge (xa was written
+ * before the launch; a step outside the chain, such as a norm, sits between
+ * the two ops). Outputs: f32 `ys` and/or QA `ya` (ya needs rows % 32
+ * == 0). Results equal one dn_linear_qa per op, bit for bit. All ops share
+ * one format.
+ * Only dep edges order the ops: a CTA starts on the next op once its own
+ * tiles of the previous one are done, so ops of different layers overlap.
+ * Each output buffer therefore belongs to one op; it may not overlap another
+ * op's output, weights or scales, nor an input other than a dependent's
+ * (DN_ERR_ARGS). A stack of layers gets one output buffer per op. */
+typedef struct dn_chain_op {
+  const void* qs;
+  const void* scales;
+  const uint8_t* xa;
+  float* ys;
+  uint8_t* ya;
+  int64_t rows, cols, dep;
+} dn_chain_op;
+
+/* Validates the ops, encodes their TMA descriptors and copies the op table to
+ * device memory (the chain's only allocations); *chain receives a handle. */
+int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, void** chain);
+/* Runs the chain on `stream` (asynchronous; capturable in a CUDA graph).
+ * DN_FLAG_PDL lets the weights start streaming while the previous kernel
+ * finishes; inputs with dep = -1 are read only after it completes. */
+int64_t dn_chain_run(void* chain, int64_t flags, void* stream);
+/* Clears the chain's completion counters (only needed after a run that
+ * reported a bounded-wait timeout; a completed run leaves them cleared). */
+int64_t dn_chain_reset(void* chain, void* stream);
+int64_t dn_chain_destroy(void* chain);
+
 /* The calling thread's last error from a lab_* call (DN_OK if none), cleared
  * by reading. */
 int64_t dn_last_error(void);
