@@ -2,39 +2,41 @@
 // by one persistent kernel, so HBM keeps streaming across the dependencies
 // between them.
 //
-// Each op is a decode GEMV (gemv_core.cuh: exact reference order, 32-row
-// tiles, QA activations in and optionally QA activations out). The ops' tiles
-// are dealt round-robin over the grid, continuing from op to op, so a CTA's
-// tiles of consecutive ops rarely coincide. Every CTA's producer warp streams
-// the weights of all its tiles of all ops, in order, through the stage ring:
-// the weights never depend on the activations, so while the consumers wait
-// for an op's input, the next weights are already on their way. An op with a
-// dependency waits for that op's completion counter (one increment per
-// finished tile, published after the tile's QA output with a gpu-scope
-// release) - a bounded spin by one thread, then a CTA barrier - and reads its
-// input through L2 (ld.global.cg), never a stale L1 line. The dependency is
-// either a data edge (the input is the earlier op's QA output) or an ordering
-// edge (the input was written before the launch; the op still starts only
-// after the earlier one, as it would with a step outside the chain between
-// them).
+// Each op is a decode GEMV on QA activations (quaddot.cuh: the reference's
+// exact summation order, four lanes per row, 32-row tiles), with f32 and/or
+// QA outputs. A CTA is four consumer warps (one 32-row tile at a time) and a
+// producer warp; several CTAs share an SM. The ops' tiles are dealt round-robin over the CTAs,
+// continuing from op to op, so consecutive ops land on different CTAs. Each
+// producer streams the weights of all of its CTA's tiles of all ops, in
+// order, through the CTA's stage ring: weights never depend on activations,
+// so while the consumer waits for an op's input the next weights are already
+// on their way. An op with a dependency waits for that op's completion
+// counter (one increment per finished tile, a gpu-scope release after the
+// tile's outputs) - a bounded spin by one thread on relaxed loads, one
+// acquire, then a bounded CTA barrier - and then reads its input through L2
+// (ld.global.cg), never a stale L1 line. The dependency is either
+// a data edge (the input is the earlier op's QA output) or an ordering edge
+// (the input was written before the launch; the op still starts only after
+// the earlier one, as it would with a step outside the chain between them).
 //
 // The grid is launched cooperatively (all CTAs co-resident), so no CTA can
 // wait on one that has not started; every wait is bounded anyway. The last
 // CTA to finish resets the counters for the next launch.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <vector>
 
 #include "dn_tmap.h"
-#include "gemv_core.cuh"
+#include "quaddot.cuh"
 
 namespace dn {
 
 // Device-side op table entry (tensor maps first: 64-byte aligned).
 struct alignas(64) ChainOpDev {
   CUtensorMap tw;         // weights: boxes of 32 rows x 128 bytes, 128-byte swizzle
-  CUtensorMap tsc;        // scales: boxes of 32 rows x 64 bytes (when tma_scales)
+  CUtensorMap tsc;        // scales: boxes of 32 rows x 64 bytes, 64-byte swizzle (when tma_scales)
   const void* scales;     // scales in global memory (when not tma_scales)
   const uint8_t* xa;      // QA input of the op
   float* ys;              // f32 outputs or null
@@ -52,23 +54,30 @@ struct ChainHost {
   int* counters = nullptr;        // nops + 1 ints (the last: CTAs done)
   int nops = 0;
   bool q4 = false;
-  int64_t max_cols = 0;
+  int64_t max_blocks = 0;
   int device = 0;
 };
 
 namespace {
 
-using namespace gemv;
+using quad::kRows;
+using gemv::Fmt;
+using gemv::kStageBytes;
+using gemv::kMaxStages;
+using gemv::kSmemPerSM;
+using gemv::kMaxSmem;
+using gemv::kSMs;
+using gemv::kBoxBytes;
+using gemv::kChunkBytes;
 
-// A barrier of the consumer warps with a bounded wait (two mbarriers used in
-// turn), so a warp that gave up can never leave the others waiting forever.
-__device__ __forceinline__ bool consumers_sync_bounded(uint64_t* bars, uint32_t& uses,
-                                                       uint32_t* status) {
-  uint64_t* b = &bars[uses & 1];
-  const uint32_t parity = (uses >> 1) & 1u;
-  uses++;
-  mbar_arrive(b);
-  return warp_wait(b, parity, status);
+constexpr int kConsumerWarps = quad::kWarps;
+constexpr int kConsumers = 32 * kConsumerWarps;
+constexpr int kThreads = kConsumers + 32;  // + the producer warp
+
+__device__ __forceinline__ int ld_relaxed(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -77,22 +86,52 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// A barrier of the consumer warps with a bounded wait (two mbarriers used in
+// turn), so a warp that gave up can never leave the others waiting forever.
+__device__ __forceinline__ bool consumers_sync(uint64_t* bars, uint32_t& uses, uint32_t* status) {
+  uint64_t* b = &bars[uses & 1];
+  const uint32_t parity = (uses >> 1) & 1u;
+  uses++;
+  mbar_arrive(b);
+  return gemv::warp_wait_sleep(b, parity, status);
+}
+
+// Shared memory from a 1024-byte aligned base: the stages; `stages` full and
+// `stages` empty barriers, two consumer and two epilogue barriers; the
+// activations; the epilogue's 2 x 32 outputs.
+struct Plan {
+  int64_t bar_off, xw_off, xs_off, yt_off, total;
+};
+__host__ __device__ inline Plan chain_plan(int stages, int64_t max_blocks, bool q4) {
+  Plan p;
+  p.bar_off = (int64_t)stages * kStageBytes;
+  p.xw_off = gemv::round_up(p.bar_off + 8 * (2 * stages + 4), 128);
+  p.xs_off = p.xw_off + max_blocks * (q4 ? 64 : 32);
+  p.yt_off = p.xs_off + gemv::round_up(max_blocks * 4, 16);
+  p.total = p.yt_off + 2 * kRows * 4 + 1024;
+  return p;
+}
+
 template <bool Q4>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
     chain_kernel(const ChainOpDev* __restrict__ ops, const int nops, int* counters,
-                 uint32_t* status, const int stages, const int64_t max_cols) {
+                 uint32_t* status, const int stages, const int64_t max_blocks, const int l2_ahead) {
   using F = Fmt<Q4>;
+  using X = quad::XQ<Q4>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const SmemPlan sp = plan<Q4>(stages, 1, max_cols, false);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_off);
+  const Plan pl = chain_plan(stages, max_blocks, Q4);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + pl.bar_off);
   uint64_t* empty = full + stages;
-  uint64_t* csync = empty + stages;  // the consumer-group barriers
+  uint64_t* csync = empty + stages;
   uint64_t* epi = csync + 2;
-  uint8_t* xw_s = smem + sp.xw_off;
-  float* xs_s = reinterpret_cast<float*>(smem + sp.xs_off);
-  float* yt_s = reinterpret_cast<float*>(smem + sp.yt_off);
-  uint8_t* stg_s = smem + sp.stg_off;
+  uint8_t* xw = smem + pl.xw_off;
+  float* xs = reinterpret_cast<float*>(smem + pl.xs_off);
+  float* yt_s = reinterpret_cast<float*>(smem + pl.yt_off);
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -102,10 +141,10 @@ __global__ void __launch_bounds__(kThreads)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
-    mbar_init(&csync[0], kConsumers);
-    mbar_init(&csync[1], kConsumers);
-    mbar_init(&epi[0], kConsumers);
-    mbar_init(&epi[1], kConsumers);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&csync[i], kConsumers);
+      mbar_init(&epi[i], kConsumers);
+    }
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -121,6 +160,10 @@ __global__ void __launch_bounds__(kThreads)
       int s = 0;
       uint32_t ph = 0;
       int64_t k = 0;
+      // The L2 prefetch cursor: chunk (pop, pt, pc) of this CTA's sequence,
+      // kept up to l2_ahead chunks past the end of the ring.
+      int pop = 0, pt = first_tile(ops[0]), pc = 0;
+      int64_t kp = 0;
       for (int op = 0; op < nops && !abort_flag; op++) {
         const ChainOpDev& o = ops[op];
         const int64_t blocks = o.cols / kBlock;
@@ -128,17 +171,39 @@ __global__ void __launch_bounds__(kThreads)
         prefetch_tmap(&o.tw);
         for (int t = first_tile(o); t < o.ntiles && !abort_flag; t += G) {
           for (int c = 0; c < nch; c++) {
+            while (kp < k + stages + l2_ahead && pop < nops) {
+              const ChainOpDev& q = ops[pop];
+              if (pt >= q.ntiles) {
+                if (++pop < nops) pt = first_tile(ops[pop]);
+                pc = 0;
+                continue;
+              }
+              const int64_t qb = q.cols / kBlock;
+              const int qnch = (int)((qb + F::kKC - 1) / F::kKC);
+              if (kp >= k + stages) {  // chunks inside the ring are loaded anyway
+                const int nb = (int)min64(F::kKC, qb - (int64_t)pc * F::kKC);
+                const int boxes = (nb * F::kWB + kBoxBytes - 1) / kBoxBytes;
+                for (int j = 0; j < boxes; j++)
+                  tma_prefetch_l2_2d(&q.tw, pc * kChunkBytes + j * kBoxBytes, pt * kRows);
+                if (q.tma_scales) tma_prefetch_l2_2d(&q.tsc, pc * F::kKC, pt * kRows);
+              }
+              kp++;
+              if (++pc == qnch) {
+                pc = 0;
+                pt += G;
+              }
+            }
             if (k >= stages &&
-                !mbar_wait_bounded(&empty[s], ph ^ 1u, status, kStatusTmaTimeout)) {
+                !mbar_wait_bounded_sleep(&empty[s], ph ^ 1u, status, kStatusTmaTimeout)) {
               abort_flag = 1;
               break;
             }
             const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
             uint8_t* stage = smem + (int64_t)s * kStageBytes;
             if (o.tma_scales)
-              issue_stage<Q4, true>(stage, &o.tw, &o.tsc, c, nb, t * kRows, &full[s]);
+              gemv::issue_stage<Q4, true>(stage, &o.tw, &o.tsc, c, nb, t * kRows, &full[s]);
             else
-              issue_stage<Q4, false>(stage, &o.tw, &o.tsc, c, nb, t * kRows, &full[s]);
+              gemv::issue_stage<Q4, false>(stage, &o.tw, &o.tsc, c, nb, t * kRows, &full[s]);
             k++;
             if (++s == stages) {
               s = 0;
@@ -161,8 +226,8 @@ __global__ void __launch_bounds__(kThreads)
   }
 
   // -------------------------------------------------------------- consumers
-  const int r8 = lane >> 2, l = lane & 3;
-  const int row_local = warp * 8 + r8;
+  const quad::Lane lc = quad::lane_ctx(warp, lane);
+  const uint8_t* xw_l = xw + lc.l * X::kLane;
   bool waited_launch = false;
   uint32_t syncs = 0;
   int s = 0;
@@ -174,71 +239,61 @@ __global__ void __launch_bounds__(kThreads)
     if (t_first >= o.ntiles) continue;  // no tile of this op here
     const int64_t blocks = o.cols / kBlock;
     const int nch = (int)((blocks + F::kKC - 1) / F::kKC);
-    // The op's input: an earlier op's output (its counter) or, for inputs
-    // made before the launch, the previous kernel in the stream (PDL).
+    // Inputs written before the launch: the previous kernel in the stream
+    // (PDL) must be complete. Inputs from an earlier op: its counter.
     if (o.ext_input && !waited_launch) {
       pdl_wait();
       waited_launch = true;
     }
-    if (o.dep >= 0) {
-      if (tid == 0) {
-        const int target = ops[o.dep].ntiles;
-        const int* cnt = counters + o.dep;
-        if (ld_acquire(cnt) < target) {
-          const uint64_t start = globaltimer_ns();
-          for (uint32_t it = 1;; it++) {
-            if (ld_acquire(cnt) >= target) break;
-            if ((it & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
-              report(status, kStatusPeerTimeout);
-              abort_flag = 1;
-              break;
-            }
+    if (o.dep >= 0 && tid == 0) {
+      const int target = ops[o.dep].ntiles;
+      const int* cnt = counters + o.dep;
+      // Spin on relaxed loads (an acquire per poll costs this SM an L1
+      // invalidation each time, which measurably slows the warps computing
+      // beside it), then one acquire load.
+      if (ld_relaxed(cnt) < target) {
+        const uint64_t start = globaltimer_ns();
+        for (uint32_t it = 1;; it++) {
+          __nanosleep(32);
+          if (ld_relaxed(cnt) >= target) break;
+          if ((it & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
+            report(status, kStatusPeerTimeout);
+            abort_flag = 1;
+            break;
           }
         }
       }
+      (void)ld_acquire(cnt);
     }
-    if (!consumers_sync_bounded(csync, syncs, status) || abort_flag) {
+    if (!consumers_sync(csync, syncs, status) || abort_flag) {
       abort_flag = 1;
       return;
     }
-    // The QA input, through L2, into the lane-interleaved layout. (The
-    // previous op's tiles of this CTA are done with the activations: every
-    // consumer passed its last stage before reaching the barrier above.)
-    {
-      const int64_t words = blocks * kQABytes / 4;
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(o.xa);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(stg_s);
-      for (int64_t i = tid; i < words; i += kConsumers) dst[i] = __ldcg(src + i);
-      if (!consumers_sync_bounded(csync, syncs, status)) {
-        abort_flag = 1;
-        return;
-      }
-      unpack_qa<Q4>(stg_s, xw_s, xs_s, blocks);
-      if (!consumers_sync_bounded(csync, syncs, status)) {
-        abort_flag = 1;
-        return;
-      }
+    quad::load_unpack<Q4>(o.xa, blocks, xw, xs, tid, kConsumers);
+    if (!consumers_sync(csync, syncs, status)) {
+      abort_flag = 1;
+      return;
     }
-    const LaneCtx lc{row_local, r8, l, (uint32_t)row_local * kBoxBytes,
-                     xw_s + l * XLayout<Q4>::kLaneBytes, sp.xw_stride, xs_s, sp.xs_stride,
-                     static_cast<const uint8_t*>(o.scales), 0, blocks};
     for (int t = t_first; t < o.ntiles; t += G) {
-      const int64_t row0 = (int64_t)t * kRows;
-      const int tile_rows = (int)min64(kRows, o.rows - row0);
-      LaneCtx c = lc;
-      c.row = row0 + min(row_local, tile_rows - 1);
-      float acc[1] = {0.0f};
-      for (int ch = 0; ch < nch; ch++) {
-        if (!warp_wait(&full[s], ph, status)) {
+      const int64_t row = (int64_t)t * kRows + lc.r;
+      const int64_t srow = row < o.rows ? row : o.rows - 1;
+      const uint8_t* gsc = o.tma_scales ? nullptr
+                                        : static_cast<const uint8_t*>(o.scales) + srow * blocks * F::kSB;
+      const uint8_t* xwp = xw_l;
+      const float* xsp = xs;
+      float acc = 0.0f;
+      // Whole stages with scales in the stage, then the rest (a partial last
+      // stage, or every stage when the scales are read from global memory).
+      const int nfull = o.tma_scales ? (int)(blocks / F::kKC) : 0;
+      int ch = 0;
+      for (; ch < nfull; ch++) {
+        if (!gemv::warp_wait(&full[s], ph, status)) {
           abort_flag = 1;
           return;  // the producer drains what it issued; every other wait is bounded
         }
-        const int nb = (int)min64(F::kKC, blocks - (int64_t)ch * F::kKC);
-        const uint8_t* stage = smem + (int64_t)s * kStageBytes;
-        if (o.tma_scales)
-          gemv_stage<Q4, 1, true>(stage, nb, ch * F::kKC, c, acc);
-        else
-          gemv_stage<Q4, 1, false>(stage, nb, ch * F::kKC, c, acc);
+        quad::stage_full<Q4>(smem + (int64_t)s * kStageBytes, lc, xwp, xsp, acc);
+        xwp += F::kKC * X::kBlock;
+        xsp += F::kKC;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         if (++s == stages) {
@@ -246,41 +301,52 @@ __global__ void __launch_bounds__(kThreads)
           ph ^= 1u;
         }
       }
-      const float y = lane_reduce(acc[0]);
-      float* yt = yt_s + (e & 1) * kRows;
-      if (l == 0 && row_local < tile_rows) {
-        if (o.ys != nullptr) o.ys[row0 + row_local] = y;
-        yt[row_local] = y;
-      }
-      if (o.ya != nullptr && tile_rows == kRows) {
-        mbar_arrive(&epi[e & 1]);
-        if (!warp_wait(&epi[e & 1], (e >> 1) & 1u, status)) {
+      for (; ch < nch; ch++) {
+        if (!gemv::warp_wait(&full[s], ph, status)) {
           abort_flag = 1;
           return;
         }
-        if (warp == 0) {
-          quantize_block_out(yt[lane], o.ya + (int64_t)t * kQABytes, lane);
-          __syncwarp();
-          if (lane == 0) {
-            // Publish the tile: its QA block is visible before the count.
-            __threadfence();
-            atomicAdd(counters + op, 1);
-          }
-        }
-        e++;
-      } else if (o.ya == nullptr) {
-        // Outputs only in f32: count the tile once its stores are issued.
+        const int nb = (int)min64(F::kKC, blocks - (int64_t)ch * F::kKC);
+        const uint8_t* stage = smem + (int64_t)s * kStageBytes;
+        if (o.tma_scales)
+          quad::stage_part<Q4, true>(stage, nb, lc, xwp, xsp, gsc, acc);
+        else
+          quad::stage_part<Q4, false>(stage, nb, lc, xwp, xsp, gsc + (int64_t)ch * F::kKC * F::kSB, acc);
+        xwp += F::kKC * X::kBlock;
+        xsp += F::kKC;
         __syncwarp();
-        if (warp == 0 && lane == 0) {
-          __threadfence();
-          atomicAdd(counters + op, 1);
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
         }
       }
+      const float y = gemv::lane_reduce(acc);  // valid on l == 0
+      float* yt = yt_s + (e & 1) * kRows;
+      if (lc.l == 0 && row < o.rows) {
+        if (o.ys != nullptr) o.ys[row] = y;
+        yt[lc.r] = y;
+      }
+      // Every warp's outputs, then (QA outputs: warp 0 quantizes the tile's
+      // block) one release per tile.
+      mbar_arrive(&epi[e & 1]);
+      if (!gemv::warp_wait(&epi[e & 1], (e >> 1) & 1u, status)) {
+        abort_flag = 1;
+        return;
+      }
+      if (warp == 0) {
+        // QA outputs need whole tiles (rows % 32 == 0, checked at creation).
+        if (o.ya != nullptr) gemv::quantize_block_out(yt[lane], o.ya + (int64_t)t * kQABytes, lane);
+        __syncwarp();
+        if (lane == 0) red_release_add(counters + op, 1);
+      }
+      e++;
     }
   }
-  // The last CTA out resets the counters for the next launch. (When thread 0
-  // of every CTA is here, every dependency wait and counter increment of the
-  // launch is behind it.)
+  // The last CTA out resets the counters for the next launch. (Thread 0 is
+  // here only after its last tile's epilogue barrier, so every consumer of
+  // the CTA is past its dependency waits; when every CTA's thread 0 is here,
+  // every wait and counter increment of the launch is behind it.)
   if (tid == 0 && !abort_flag) {
     __threadfence();
     if (atomicAdd(counters + nops, 1) == G - 1) {
@@ -288,6 +354,17 @@ __global__ void __launch_bounds__(kThreads)
       __threadfence();
     }
   }
+}
+
+// Chunks each producer pulls into L2 beyond its stage ring. DN_CHAIN_L2_AHEAD
+// overrides (0: none).
+static int chain_l2_ahead() {
+  static int v = [] {
+    const char* e = getenv("DN_CHAIN_L2_AHEAD");
+    const int n = e != nullptr ? atoi(e) : -1;
+    return n >= 0 && n <= 1024 ? n : 0;
+  }();
+  return v;
 }
 
 // Ops of different layers run at the same time (a CTA moves on to its tiles
@@ -339,7 +416,7 @@ static bool chain_buffers_disjoint(const ChainOpSpec* specs, int64_t nops, bool 
 int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost** out) {
   if (nops <= 0 || specs == nullptr || out == nullptr) return kErrArgs;
   std::vector<ChainOpDev> table((size_t)nops);
-  int64_t tile_base = 0, max_cols = 0;
+  int64_t tile_base = 0, max_blocks = 0;
   for (int64_t i = 0; i < nops; i++) {
     const ChainOpSpec& sp = specs[i];
     ChainOpDev& d = table[(size_t)i];
@@ -370,9 +447,10 @@ int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost*
       return kErrUnsupported;
     d.tma_scales = ((uintptr_t)sp.scales & 15) == 0 && (blocks * sb) % 16 == 0;
     if (d.tma_scales &&
-        !encode_tmap_2d(&d.tsc, sp.scales, q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                        (uint64_t)blocks, (uint64_t)sp.rows, (uint64_t)(blocks * sb),
-                        (uint32_t)(kChunkBytes / wb), kRows, false))
+        !encode_tmap_2d_sw64(&d.tsc, sp.scales,
+                             q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                             (uint64_t)blocks, (uint64_t)sp.rows, (uint64_t)(blocks * sb),
+                             (uint32_t)(kChunkBytes / wb), kRows))
       return kErrUnsupported;
     d.scales = sp.scales;
     d.xa = sp.xa;
@@ -384,13 +462,13 @@ int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost*
     d.ntiles = (int32_t)((sp.rows + kRows - 1) / kRows);
     d.tile_base = (int32_t)(tile_base % (1 << 30));
     tile_base += d.ntiles;
-    max_cols = sp.cols > max_cols ? sp.cols : max_cols;
+    max_blocks = blocks > max_blocks ? blocks : max_blocks;
   }
   if (!chain_buffers_disjoint(specs, nops, q4)) return kErrArgs;
   ChainHost* h = new ChainHost();
   h->nops = (int)nops;
   h->q4 = q4;
-  h->max_cols = max_cols;
+  h->max_blocks = max_blocks;
   cudaGetDevice(&h->device);
   if (cudaMalloc(&h->ops_dev, sizeof(ChainOpDev) * (size_t)nops) != cudaSuccess ||
       cudaMalloc(&h->counters, sizeof(int) * (size_t)(nops + 1)) != cudaSuccess ||
@@ -411,18 +489,29 @@ void chain_destroy(ChainHost* h) {
   delete h;
 }
 
+// CTAs per SM: more CTAs spread an op's tiles over more SMs' worth of
+// warps, fewer give each a deeper stage ring. DN_CHAIN_PER_SM overrides.
+static int chain_per_sm() {
+  static int v = [] {
+    const char* e = getenv("DN_CHAIN_PER_SM");
+    const int n = e != nullptr ? atoi(e) : 0;
+    return n >= 1 && n <= 16 ? n : 2;
+  }();
+  return v;
+}
+
 template <bool Q4>
 static int64_t chain_launch_t(ChainHost* h, uint32_t* status, cudaStream_t stream, bool pdl) {
-  const SmemPlan base = plan<Q4>(0, 1, h->max_cols, false);
-  int per_sm = 2;
-  int stages = (int)((kSmemPerSM / per_sm - 1024 - base.total) / (kStageBytes + 16));
-  if (stages < 3) {
-    per_sm = 1;
-    stages = (int)((kMaxSmem - base.total) / (kStageBytes + 16));
+  const Plan base = chain_plan(0, h->max_blocks, Q4);
+  int per_sm = chain_per_sm(), stages = 0;
+  for (; per_sm >= 1; per_sm--) {
+    // 1 KB per CTA is reserved by the system; the static abort flag is small.
+    stages = (int)((kSmemPerSM / per_sm - 1024 - 64 - base.total) / (kStageBytes + 16));
+    if (stages >= 2) break;
   }
   stages = stages > kMaxStages ? kMaxStages : stages;
-  if (stages < 2) return kErrTooLarge;
-  const SmemPlan sp = plan<Q4>(stages, 1, h->max_cols, false);
+  if (per_sm < 1 || stages < 2) return kErrTooLarge;
+  const Plan sp = chain_plan(stages, h->max_blocks, Q4);
   auto kern = chain_kernel<Q4>;
   static bool configured[64] = {};
   int dev = 0;
@@ -453,7 +542,8 @@ static int64_t chain_launch_t(ChainHost* h, uint32_t* status, cudaStream_t strea
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   const ChainOpDev* ops = h->ops_dev;
-  return cudaLaunchKernelEx(&cfg, kern, ops, h->nops, h->counters, status, stages, h->max_cols) ==
+  return cudaLaunchKernelEx(&cfg, kern, ops, h->nops, h->counters, status, stages, h->max_blocks,
+                            chain_l2_ahead()) ==
                  cudaSuccess
              ? kOk
              : kErrCuda;

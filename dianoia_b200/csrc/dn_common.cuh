@@ -119,6 +119,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `hint_ns` pass, issuing nothing meanwhile.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_wait_bounded for waits that may be long (a full stage ring): the
+// waiting thread sleeps instead of spinning, leaving issue slots to the
+// warps that compute.
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity,
+                                                        uint32_t* status, uint32_t bits) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (globaltimer_ns() - start > kWaitLimitNs) {
+      report(status, bits);
+      return false;
+    }
+  }
+}
+
 // Waits for phase `parity` of an mbarrier to complete, for at most
 // kWaitLimitNs. Returns false (and records `bits`) if it gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* status,
@@ -155,6 +185,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Pulls a box of a tensor map into L2 only (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x),
+               "r"(y)
+               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

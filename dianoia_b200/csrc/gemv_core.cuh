@@ -80,6 +80,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
   return __all_sync(0xffffffffu, got) != 0;
 }
 
+// warp_wait whose waiting lanes sleep in hardware (mbarrier try_wait with a
+// suspend-time hint) instead of spinning, so warps that wait leave the issue
+// slots to warps that compute.
+__device__ __forceinline__ bool warp_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  const bool got = mbar_wait_bounded_sleep(bar, parity, status, kStatusTmaTimeout);
+  return __all_sync(0xffffffffu, got) != 0;
+}
+
 // Named barrier over the consumer warps only (the producer never joins);
 // used in the prologue, which every consumer thread always reaches.
 __device__ __forceinline__ void consumers_sync() {

@@ -23,9 +23,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type, uint64_t row_elems,
-                    uint64_t rows, uint64_t row_bytes, uint32_t box_elems, uint32_t box_rows,
-                    bool swizzle128) {
+static bool encode(CUtensorMap* map, const void* base, CUtensorMapDataType type, uint64_t row_elems,
+                   uint64_t rows, uint64_t row_bytes, uint32_t box_elems, uint32_t box_rows,
+                   CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {row_elems, rows};
@@ -33,9 +33,22 @@ bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type
   const cuuint32_t box[2] = {box_elems, box_rows};
   const cuuint32_t estrides[2] = {1, 1};
   return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estrides,
-            CU_TENSOR_MAP_INTERLEAVE_NONE,
-            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type, uint64_t row_elems,
+                    uint64_t rows, uint64_t row_bytes, uint32_t box_elems, uint32_t box_rows,
+                    bool swizzle128) {
+  return encode(map, base, type, row_elems, rows, row_bytes, box_elems, box_rows,
+                swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+bool encode_tmap_2d_sw64(CUtensorMap* map, const void* base, CUtensorMapDataType type,
+                         uint64_t row_elems, uint64_t rows, uint64_t row_bytes, uint32_t box_elems,
+                         uint32_t box_rows) {
+  return encode(map, base, type, row_elems, rows, row_bytes, box_elems, box_rows,
+                CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 }  // namespace dn

@@ -142,3 +142,59 @@ def test_chain_rejects_bad_tables(cuda_lib):
                             _lib.ChainOp(q.data_ptr(), s.data_ptr(), ya.data_ptr(), y2.data_ptr(), ya2.data_ptr(), 64, 64, 0))
     assert L.dn_chain_create(0, ok, 2, ctypes.byref(handle)) == 0
     assert L.dn_chain_destroy(handle) == 0
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+def test_chain_ragged_shapes(cuda_lib, oracle, fmt):
+    """Partial last stages (cols 1152: 36 blocks), scales too narrow for TMA
+    (Q4_0 rows of 72 scale bytes), a partial last tile (1000 rows, f32 only)
+    and an input read from the middle of a producer's QA output."""
+    from dianoia_b200 import _lib
+    L = cuda_lib
+    rng = np.random.default_rng(11 if fmt == "q8" else 12)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    # (rows, cols, input: None = x0 | (op, first block), keep QA output)
+    spec = [(4096, 1152, None, True),      # 0
+            (1000, 1152, None, False),     # 1: f32 only, partial tile
+            (960, 2048, (0, 32), True),    # 2: reads blocks 32..95 of op 0's output
+            (352, 960, (2, 0), False)]     # 3
+    x0 = orc.activations(rng, 1, 1152)
+    outs, ref, mats = {}, [], []
+    for i, (r, c, src, _) in enumerate(spec):
+        qs, sc = orc.q4_weights(rng, r, c) if fmt == "q4" else orc.q8_weights(rng, r, c)
+        x = x0 if src is None else outs[src[0]][src[1] * 32:src[1] * 32 + c]
+        y, _, _ = oracle.gemm(fmt, qs, sc, x, r, c, 1, 1)
+        outs[i] = y
+        ref.append(y)
+        mats.append((qs, sc))
+    st = torch.cuda.current_stream().cuda_stream
+    xa0 = torch.zeros(1152 // 32 * 36, dtype=torch.uint8, device="cuda")
+    assert L.dn_quantize_qa(dev(x0).data_ptr(), xa0.data_ptr(), 1, 1152, 1152 // 32 * 36, st) == 0
+    keep, ops, ys, yas = [], [], [], {}
+    for i, ((r, c, src, qa_out), (qs, sc)) in enumerate(zip(spec, mats)):
+        q, s = dev(qs), dev(sc)
+        y = torch.full((r,), float("nan"), device="cuda")
+        ya = torch.zeros(r // 32 * 36, dtype=torch.uint8, device="cuda") if qa_out else None
+        keep += [q, s, y, ya]
+        yas[i] = ya
+        if src is None:
+            xa, dep = xa0.data_ptr(), -1
+        else:
+            xa, dep = yas[src[0]].data_ptr() + src[1] * 36, src[0]
+        ops.append(_lib.ChainOp(q.data_ptr(), s.data_ptr(), xa, y.data_ptr(),
+                                None if ya is None else ya.data_ptr(), r, c, dep))
+        ys.append(y)
+    arr = (_lib.ChainOp * len(ops))(*ops)
+    handle = ctypes.c_void_p()
+    assert L.dn_chain_create(1 if fmt == "q4" else 0, arr, len(ops), ctypes.byref(handle)) == 0
+    try:
+        for run in range(2):
+            for y in ys:
+                y.fill_(float("nan"))
+            assert L.dn_chain_run(handle, 0, st) == 0
+            torch.cuda.synchronize()
+            assert L.dn_device_status(1) == 0
+            for i, (y, want) in enumerate(zip(ys, ref)):
+                assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32)), (run, i)
+    finally:
+        L.dn_chain_destroy(handle)
