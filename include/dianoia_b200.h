@@ -173,6 +173,25 @@ int64_t dn_chain_run(void* chain, int64_t flags, void* stream);
 int64_t dn_chain_reset(void* chain, void* stream);
 int64_t dn_chain_destroy(void* chain);
 
+/* dn_linear in mode 1 with the automatic path, for callers that must not
+ * allocate: an engine that reserves all of its device memory up front and
+ * cannot have a library grow it, or code that may not call cudaMalloc and
+ * friends (no counterpart in the reference). The tensor-core path's scratch
+ * (the quantized activations) and the kernels' status word live in a fixed
+ * __device__ array of this library (9 MiB + 256 bytes, created with the
+ * module): n * cols may be at most 8 Mi (8388608), else DN_ERR_TOO_LARGE and
+ * nothing is launched. The first call on each device looks up that array's
+ * address (make it before capturing a stream). The scratch starts undefined
+ * and need not be cleared: every call quantizes its activations into it
+ * before reading them. Calls that overlap in time on one device share the
+ * scratch and race (one stream, or calls ordered by events, is safe). A
+ * bounded wait that ran out (a broken device, never an input) is recorded in
+ * the array's status word, which dn_device_status does not read. Results
+ * equal dn_linear's with DN_PATH_AUTO and mode 1. */
+int64_t dn_linear_noalloc(int64_t format, const void* qs, const void* scales, const float* xs,
+                          float* ys, int64_t rows, int64_t cols, int64_t n, int64_t ldy,
+                          int64_t flags, void* stream);
+
 /* The calling thread's last error from a lab_* call (DN_OK if none), cleared
  * by reading. */
 int64_t dn_last_error(void);
