@@ -26,8 +26,11 @@ split (lab_native.c:550-552).
 
 Metric: tokens/s of the whole job (value), plus HBM GB/s of the weight
 stream. `e2e` is the same token loop driven through the reference-facing
-C-ABI (lab_gemm_q8) with host activations and outputs, one synchronous call
-per projection as dianoia's NativeQ8Matrix.apply does. `--impl reference`
+C-ABI with host activations and outputs: on one GPU through dianoia's
+GPU-layer ABI (lab_gpu_*: one command buffer of 113 products per token, as
+its GpuForward does); `e2e_cpu_abi` through the CPU-layer ABI (lab_gemm_q8,
+one synchronous call per projection as NativeQ8Matrix.apply does), which is
+also `e2e` on N > 1. `--impl reference`
 times the reference's own CPU kernels (lab_native.c, compiled unmodified
 into oracle/_ref) on this host's cores on the same workload.
 """
@@ -387,7 +390,7 @@ def main():
     ap.add_argument("--path", choices=["chain", "ops"], default="ops",
                     help="chain: one persistent kernel per token (1 GPU); ops: one GEMV "
                          "launch per projection (always used for N > 1)")
-    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm"], default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
@@ -532,9 +535,14 @@ def main():
         chain_matches_ops = bool(torch.equal(chain_logits.view(torch.int32),
                                              stack.bufs["lm_head"].view(torch.int32)))
 
-    # End to end through the C-ABI with host buffers (rank-local shards; on
-    # N > 1 the slices are all-gathered through device copies).
-    e2e = run_e2e(args, stack, L, torch, rank, world, gather, device)
+    # End to end with host buffers: on one GPU through dianoia's GPU-layer
+    # ABI (one command buffer per token); also, and on N > 1 only, through
+    # the CPU-layer ABI (lab_gemm_q8 per projection on rank-local shards, the
+    # slices all-gathered through device copies).
+    e2e_cpu_abi = run_e2e(args, stack, L, torch, rank, world, gather, device)
+    e2e = run_e2e_gpu_layer(args, stack, L, torch) if world == 1 else None
+    if e2e is None:
+        e2e = e2e_cpu_abi
 
     cpu_baseline = None
     if rank == 0 and world == 1 and args.cpu_tokens > 0:
@@ -554,6 +562,7 @@ def main():
                          "algorithmic_bytes_per_step_per_gpu": per_rank_bytes,
                          "traffic": None},
             "e2e": e2e,
+            "e2e_cpu_abi": e2e_cpu_abi,
             "cpu_baseline": cpu_baseline,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": ("1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
@@ -788,6 +797,81 @@ def run_e2e(args, stack, L, torch, rank, world, gather, device):
     return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "api": "lab_gemm_q8 (host x / y, device weights)",
             "steps": steps, "logits_match_device_run": same}
+
+
+def run_e2e_gpu_layer(args, stack, L, torch):
+    """Token loop through dianoia's GPU-layer C-ABI (lab_gpu_*), the way its
+    GpuForward drives a GPU: weights in GPU buffers (uploaded once), and per
+    token the host writes x0 into a host-visible buffer, records all 113
+    products into one command buffer (each projection's output feeding the
+    next inside an activation buffer), commits with wait and reads the
+    logits. The commit copies x0 in and every product's outputs back; those
+    copies and the host's encode calls are inside the timed region."""
+    steps = args.e2e_steps
+    if steps <= 0 or L.lab_gpu_init() != 1:
+        return None
+    handles = []
+    try:
+        mats = []
+        for m in stack.mats:
+            qs = m["qs"].cpu().numpy().view(np.uint8)
+            sc = m["scales"].cpu().numpy().view(np.uint8)
+            at = (qs.size + 63) // 64 * 64
+            raw = np.zeros(at + sc.size, np.uint8)
+            raw[:qs.size] = qs
+            raw[at:] = sc
+            h = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
+            if h < 0:
+                raise RuntimeError("lab_gpu_wrap failed")
+            handles.append(h)
+            mats.append((h, at))
+        # Activation buffer: x0, then one output region per projection kind.
+        offs, at = {"x0": 0}, HIDDEN
+        for name in ("qkv", "o", "gate_up", "down"):
+            offs[name] = at
+            at += OUT_ROWS[name]
+        act = L.lab_gpu_buffer(4 * at)
+        logits_h = L.lab_gpu_readback_buffer(4 * VOCAB)
+        handles += [act, logits_h]
+        act_view = np.ctypeslib.as_array((ctypes.c_float * at).from_address(L.lab_gpu_contents(act)))
+        logits_view = np.ctypeslib.as_array(
+            (ctypes.c_float * VOCAB).from_address(L.lab_gpu_contents(logits_h)))
+        x0 = stack.x0.cpu().numpy()
+        logits = np.zeros(VOCAB, np.float32)
+
+        def one_token():
+            act_view[:HIDDEN] = x0
+            L.lab_gpu_begin()
+            for m, (h, sc_at) in zip(stack.mats, mats):
+                name = m["name"]
+                src = INPUT_OF[name]
+                x_off = 4 * offs["x0" if src is None else src]
+                if name == "lm_head":
+                    y, y_off = logits_h, 0
+                else:
+                    y, y_off = act, 4 * offs[name]
+                L.lab_gpu_enc_matmul_q8(h, 0, sc_at, act, x_off, y, y_off, m["rows"], m["cols"], 1)
+            if L.lab_gpu_commit(1) != 1:
+                raise RuntimeError("lab_gpu_commit failed")
+            logits[:] = logits_view
+
+        for _ in range(3):
+            one_token()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one_token()
+        dt = time.perf_counter() - t0
+        same = bool(np.array_equal(logits.view(np.uint32),
+                                   stack.bufs["lm_head"].cpu().numpy().view(np.uint32)))
+        d2h = 4 * (at - HIDDEN) + 4 * VOCAB
+        return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": 4 * HIDDEN,
+                "d2h_bytes_per_step": d2h,
+                "api": "lab_gpu_* (dianoia's GPU-layer ABI: host-visible buffers, one command "
+                       "buffer of 113 products per token, commit(wait=1))",
+                "steps": steps, "logits_match_device_run": same}
+    finally:
+        for h in handles:
+            L.lab_gpu_release(h)
 
 
 def run_cpu_baseline(args, stack):

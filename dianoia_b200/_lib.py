@@ -27,6 +27,20 @@ SIGNATURES = {
     "lab_gemm_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
     "lab_gemm_q4": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
     "lab_gemv_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
+    "lab_gpu_init": (_i64, []),
+    "lab_gpu_buffer": (_i64, [_i64]),
+    "lab_gpu_readback_buffer": (_i64, [_i64]),
+    "lab_gpu_wrap": (_i64, [_p, _i64]),
+    "lab_gpu_wrap_copies": (_i64, []),
+    "lab_gpu_contents": (_p, [_i64]),
+    "lab_gpu_release": (None, [_i64]),
+    "lab_gpu_live_buffers": (_i64, []),
+    "lab_gpu_begin": (None, []),
+    "lab_gpu_commit": (_i64, [_i64]),
+    "lab_gpu_wait": (_i64, []),
+    "lab_gpu_last_ms": (ctypes.c_double, []),
+    "lab_gpu_enc_matmul_q8": (None, [_i64] * 10),
+    "lab_gpu_enc_matmul_q4": (None, [_i64] * 10),
     "dn_linear": (_i64, [_i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),

@@ -344,6 +344,18 @@ void quantize_entry(bool q4, const float* w, QT* qs, ST* scales, int64_t rows, i
 
 }  // namespace
 
+namespace dn {
+// The current device's bounded-wait status word (device address for the
+// kernels, host address to read it), for the other C-ABI files.
+bool status_words(uint32_t** dev, volatile uint32_t** host) {
+  DeviceState* d = device_state();
+  if (d == nullptr) return false;
+  *dev = d->status_dev;
+  *host = d->status_host;
+  return true;
+}
+}  // namespace dn
+
 // ======================================================================= lab_*
 
 extern "C" {

@@ -1,0 +1,426 @@
+// dianoia's GPU-layer C-ABI (lab_gpu_*: the Vulkan layer in
+// src/vulkan/lab_vulkan.c and the Metal one export it; Dart binds it in
+// lib/src/gpu.dart:36-312), for the quantized products that GpuLinear and
+// GpuForward encode: buffers the host reads and writes in place, one
+// process-wide command buffer opened by lab_gpu_begin, products recorded by
+// lab_gpu_enc_matmul_q8 / _q4 and submitted by lab_gpu_commit.
+//
+// On B200 a buffer is device memory plus a pinned host mirror, which is what
+// lab_gpu_contents returns. The host may have written any mirror between two
+// command buffers, so lab_gpu_commit first copies to the device the input
+// ranges of the recorded products (minus what an earlier product of the same
+// command buffer writes), runs the products (activations quantized to Q8_0
+// per block, then the decode GEMV or the tensor-core GEMM, as dn_linear in
+// mode 1) and copies every range a product wrote back to the mirror. A
+// buffer used as a weight matrix is copied to the device once, at its first
+// product: dianoia writes weights once, before their first use
+// (GpuLinear.upload, gpu.dart:1293-1323, and the wrapped model file of
+// GpuForward). A command buffer identical to the previous one (a decode loop)
+// replays the CUDA graph captured for it.
+//
+// Errors: like the reference, the void functions report nothing;
+// lab_gpu_commit returns 0 when a product's arguments or a CUDA call failed.
+// Calls are serialized by one mutex (the reference's layer is single-encoder).
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "dianoia_b200.h"
+#include "dn_launch.h"
+
+namespace dn {
+bool status_words(uint32_t** dev, volatile uint32_t** host);  // abi.cu
+}
+
+namespace {
+
+constexpr int64_t kBlock = 32;  // values per Q4_0 / Q8_0 block
+
+struct Buf {
+  uint8_t* dev = nullptr;
+  uint8_t* host = nullptr;  // pinned mirror: lab_gpu_contents
+  int64_t bytes = 0;
+  bool live = false;
+  bool weights_on_device = false;  // copied once, at its first use as a matrix
+};
+
+struct Op {
+  bool q4;
+  int64_t w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n;
+  bool operator==(const Op& o) const {
+    return q4 == o.q4 && w == o.w && qs_off == o.qs_off && sc_off == o.sc_off && x == o.x &&
+           x_off == o.x_off && y == o.y && y_off == o.y_off && rows == o.rows && cols == o.cols &&
+           n == o.n;
+  }
+};
+
+struct Range {
+  int64_t buf, lo, hi;  // bytes [lo, hi) of buffer `buf`
+};
+
+std::recursive_mutex g_mu;
+bool g_ready = false;
+int g_device = -1;
+cudaStream_t g_stream = nullptr;
+cudaEvent_t g_ev0 = nullptr, g_ev1 = nullptr;
+std::vector<Buf> g_bufs;
+std::vector<int64_t> g_free;
+int64_t g_live = 0;
+std::vector<Op> g_ops;
+bool g_bad_op = false;  // an encode call got handles or ranges that do not fit
+bool g_pending = false;
+double g_last_ms = 0.0;
+
+// Scratch of the tensor-core path: the quantized activations.
+int8_t* g_xq = nullptr;
+float* g_xsc = nullptr;
+int64_t g_xcap = 0;
+
+// The graph of the last command buffer, with what it was captured from.
+cudaGraphExec_t g_exec = nullptr;
+std::vector<Op> g_exec_ops;
+std::vector<uint8_t*> g_exec_ptrs;  // device addresses the graph uses, per op (w, x, y)
+int8_t* g_exec_xq = nullptr;
+
+void drop_graph() {
+  if (g_exec != nullptr) cudaGraphExecDestroy(g_exec);
+  g_exec = nullptr;
+  g_exec_ops.clear();
+  g_exec_ptrs.clear();
+}
+
+bool wait_pending() {
+  if (!g_pending) return true;
+  g_pending = false;
+  if (cudaStreamSynchronize(g_stream) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  float ms = 0.0f;
+  if (cudaEventElapsedTime(&ms, g_ev0, g_ev1) == cudaSuccess) g_last_ms = ms;
+  uint32_t* sd = nullptr;
+  volatile uint32_t* sh = nullptr;
+  if (dn::status_words(&sd, &sh) && *sh != 0) return false;  // a bounded wait ran out
+  return true;
+}
+
+bool valid(int64_t h) { return h >= 0 && h < (int64_t)g_bufs.size() && g_bufs[h].live; }
+
+bool fits(int64_t h, int64_t off, int64_t bytes) {
+  return valid(h) && off >= 0 && bytes >= 0 && off <= g_bufs[h].bytes - bytes;
+}
+
+int64_t new_buffer(int64_t bytes) {
+  if (!g_ready || bytes < 0) return -1;
+  cudaSetDevice(g_device);
+  const size_t n = bytes == 0 ? 16 : (size_t)bytes;
+  Buf b;
+  if (cudaMalloc(&b.dev, n) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (cudaHostAlloc(&b.host, n, cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(b.dev);
+    return -1;
+  }
+  memset(b.host, 0, n);
+  if (cudaMemset(b.dev, 0, n) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFreeHost(b.host);
+    cudaFree(b.dev);
+    return -1;
+  }
+  b.bytes = bytes;
+  b.live = true;
+  int64_t h;
+  if (!g_free.empty()) {
+    h = g_free.back();
+    g_free.pop_back();
+    g_bufs[h] = b;
+  } else {
+    h = (int64_t)g_bufs.size();
+    g_bufs.push_back(b);
+  }
+  g_live++;
+  return h;
+}
+
+void encode(bool q4, int64_t w, int64_t qs_off, int64_t sc_off, int64_t x, int64_t x_off, int64_t y,
+            int64_t y_off, int64_t rows, int64_t cols, int64_t n) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  const bool ok = rows >= 0 && cols >= 0 && n >= 0 && cols % kBlock == 0 &&
+                  fits(w, qs_off, q4 ? rows * cols / 2 : rows * cols) &&
+                  fits(w, sc_off, rows * (cols / kBlock) * (q4 ? 2 : 4)) &&
+                  fits(x, x_off, n * cols * 4) && fits(y, y_off, n * rows * 4);
+  if (!ok) {
+    g_bad_op = true;
+    return;
+  }
+  g_ops.push_back(Op{q4, w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n});
+}
+
+// Adds [lo, hi) of buffer b to a list of ranges, merging overlaps.
+void add_range(std::vector<Range>& v, int64_t b, int64_t lo, int64_t hi) {
+  if (lo >= hi) return;
+  for (Range& r : v) {
+    if (r.buf == b && lo <= r.hi && r.lo <= hi) {
+      r.lo = std::min(r.lo, lo);
+      r.hi = std::max(r.hi, hi);
+      // merging may now touch a neighbour: restart with the merged range
+      const Range m = r;
+      r = v.back();
+      v.pop_back();
+      add_range(v, m.buf, m.lo, m.hi);
+      return;
+    }
+  }
+  v.push_back(Range{b, lo, hi});
+}
+
+// The parts of [lo, hi) of buffer b not covered by `written`.
+void subtract(const std::vector<Range>& written, int64_t b, int64_t lo, int64_t hi,
+              std::vector<Range>& out) {
+  std::vector<std::pair<int64_t, int64_t>> cover;
+  for (const Range& r : written)
+    if (r.buf == b && r.lo < hi && lo < r.hi) cover.push_back({std::max(r.lo, lo), std::min(r.hi, hi)});
+  std::sort(cover.begin(), cover.end());
+  int64_t at = lo;
+  for (auto& c : cover) {
+    if (c.first > at) add_range(out, b, at, c.first);
+    at = std::max(at, c.second);
+  }
+  if (at < hi) add_range(out, b, at, hi);
+}
+
+// Records the command buffer's copies and products on g_stream.
+bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
+            uint32_t* status) {
+  for (const Range& r : uploads) {
+    const Buf& b = g_bufs[r.buf];
+    if (cudaMemcpyAsync(b.dev + r.lo, b.host + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyHostToDevice,
+                        g_stream) != cudaSuccess)
+      return false;
+  }
+  for (const Op& o : g_ops) {
+    const Buf &w = g_bufs[o.w], &x = g_bufs[o.x], &y = g_bufs[o.y];
+    const dn::LinearArgs a{o.q4, w.dev + o.qs_off, w.dev + o.sc_off,
+                           reinterpret_cast<const float*>(x.dev + o.x_off), g_xq, g_xsc,
+                           reinterpret_cast<float*>(y.dev + o.y_off), o.rows, o.cols, o.n, o.rows,
+                           1, status};
+    const int64_t rc =
+        dn::path_for(a) == 0 ? dn::launch_gemv(a, g_stream, true) : dn::launch_linear(a, g_stream);
+    if (rc != 0) return false;
+  }
+  for (const Range& r : downloads) {
+    const Buf& b = g_bufs[r.buf];
+    if (cudaMemcpyAsync(b.host + r.lo, b.dev + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyDeviceToHost,
+                        g_stream) != cudaSuccess)
+      return false;
+  }
+  return true;
+}
+
+bool same_as_graph() {
+  if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_ops.size() != g_ops.size()) return false;
+  for (size_t i = 0; i < g_ops.size(); i++) {
+    const Op &a = g_ops[i], &b = g_exec_ops[i];
+    if (!(a == b) || g_exec_ptrs[3 * i] != g_bufs[a.w].dev ||
+        g_exec_ptrs[3 * i + 1] != g_bufs[a.x].dev || g_exec_ptrs[3 * i + 2] != g_bufs[a.y].dev)
+      return false;
+  }
+  return true;
+}
+
+int64_t commit(int64_t wait) {
+  if (!g_ready) return 0;
+  if (g_bad_op) {
+    g_bad_op = false;
+    g_ops.clear();
+    return 0;
+  }
+  cudaSetDevice(g_device);
+  uint32_t* status = nullptr;
+  volatile uint32_t* status_host = nullptr;
+  if (!dn::status_words(&status, &status_host)) return 0;
+  // Weights: once per buffer, outside the graph.
+  for (const Op& o : g_ops) {
+    Buf& b = g_bufs[o.w];
+    if (!b.weights_on_device) {
+      if (cudaMemcpyAsync(b.dev, b.host, (size_t)b.bytes, cudaMemcpyHostToDevice, g_stream) !=
+          cudaSuccess)
+        return 0;
+      b.weights_on_device = true;
+    }
+  }
+  // Scratch for the tensor-core path.
+  int64_t need = 0;
+  for (const Op& o : g_ops) need = std::max(need, o.n * o.cols);
+  if (need > g_xcap) {
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
+    drop_graph();
+    cudaFree(g_xq);
+    cudaFree(g_xsc);
+    g_xq = nullptr;
+    g_xsc = nullptr;
+    g_xcap = 0;
+    if (cudaMalloc(&g_xq, (size_t)need) != cudaSuccess ||
+        cudaMalloc(&g_xsc, (size_t)(need / kBlock + 1) * 4) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    g_xcap = need;
+  }
+  if (!same_as_graph()) {
+    drop_graph();
+    // Ranges to copy in (host-written inputs) and out (products' outputs).
+    std::vector<Range> uploads, written;
+    for (const Op& o : g_ops) {
+      subtract(written, o.x, o.x_off, o.x_off + o.n * o.cols * 4, uploads);
+      add_range(written, o.y, o.y_off, o.y_off + o.n * o.rows * 4);
+    }
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
+    const bool ok = record(uploads, written, status);
+    const cudaError_t e = cudaStreamEndCapture(g_stream, &graph);
+    if (!ok || e != cudaSuccess || graph == nullptr ||
+        cudaGraphInstantiate(&g_exec, graph, 0) != cudaSuccess) {
+      if (graph != nullptr) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      g_exec = nullptr;
+      return 0;
+    }
+    cudaGraphDestroy(graph);
+    g_exec_ops = g_ops;
+    g_exec_xq = g_xq;
+    for (const Op& o : g_ops) {
+      g_exec_ptrs.push_back(g_bufs[o.w].dev);
+      g_exec_ptrs.push_back(g_bufs[o.x].dev);
+      g_exec_ptrs.push_back(g_bufs[o.y].dev);
+    }
+  }
+  if (cudaEventRecord(g_ev0, g_stream) != cudaSuccess ||
+      cudaGraphLaunch(g_exec, g_stream) != cudaSuccess ||
+      cudaEventRecord(g_ev1, g_stream) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  g_pending = true;
+  if (!wait) return 1;
+  return wait_pending() ? 1 : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t lab_gpu_init(void) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (g_ready) return 1;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, dev) != cudaSuccess || p.major != 10) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&g_ev0) != cudaSuccess || cudaEventCreate(&g_ev1) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  g_device = dev;
+  g_ready = true;
+  return 1;
+}
+
+int64_t lab_gpu_buffer(int64_t bytes) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return new_buffer(bytes);
+}
+
+int64_t lab_gpu_readback_buffer(int64_t bytes) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return new_buffer(bytes);
+}
+
+int64_t lab_gpu_wrap(void* address, int64_t bytes) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  const int64_t h = new_buffer(bytes);
+  if (h >= 0 && bytes > 0) memcpy(g_bufs[h].host, address, (size_t)bytes);
+  return h;
+}
+
+int64_t lab_gpu_wrap_copies(void) { return 1; }
+
+void* lab_gpu_contents(int64_t handle) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return valid(handle) ? g_bufs[handle].host : nullptr;
+}
+
+double lab_gpu_last_ms(void) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return g_last_ms;
+}
+
+void lab_gpu_release(int64_t handle) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (!valid(handle)) return;
+  wait_pending();
+  cudaSetDevice(g_device);
+  Buf& b = g_bufs[handle];
+  for (const Op& o : g_exec_ops) {
+    if (o.w == handle || o.x == handle || o.y == handle) {
+      drop_graph();
+      break;
+    }
+  }
+  cudaFree(b.dev);
+  cudaFreeHost(b.host);
+  b = Buf();
+  g_free.push_back(handle);
+  g_live--;
+}
+
+int64_t lab_gpu_live_buffers(void) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return g_live;
+}
+
+void lab_gpu_begin(void) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  wait_pending();
+  g_ops.clear();
+  g_bad_op = false;
+}
+
+int64_t lab_gpu_commit(int64_t wait) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return commit(wait);
+}
+
+int64_t lab_gpu_wait(void) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return wait_pending() ? 1 : 0;
+}
+
+void lab_gpu_enc_matmul_q8(int64_t w, int64_t qsOffset, int64_t scalesOffset, int64_t x,
+                           int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
+                           int64_t n) {
+  encode(false, w, qsOffset, scalesOffset, x, xOffset, y, yOffset, rows, cols, n);
+}
+
+void lab_gpu_enc_matmul_q4(int64_t w, int64_t qsOffset, int64_t scalesOffset, int64_t x,
+                           int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
+                           int64_t n) {
+  encode(true, w, qsOffset, scalesOffset, x, xOffset, y, yOffset, rows, cols, n);
+}
+
+}  // extern "C"

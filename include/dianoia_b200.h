@@ -76,6 +76,63 @@ void lab_gemm_q4(const uint8_t* qs, const uint16_t* scales, const float* xs, int
 void lab_gemv_q8(const int8_t* qs, const float* scales, const float* x, int8_t* xq, float* xs,
                  float* y, int64_t rows, int64_t cols, int64_t threads, int64_t mode);
 
+/* ------------------------------------------------- lab_gpu_* (reference GPU-layer ABI)
+ *
+ * The quantized-product part of dianoia's GPU layer (src/vulkan/lab_vulkan.c;
+ * bound in lib/src/gpu.dart:36-312 and driven by GpuLinear / GpuForward):
+ * buffers are handles to memory the host reads and writes in place through
+ * lab_gpu_contents, between command buffers; lab_gpu_begin opens the single
+ * process-wide command buffer, lab_gpu_enc_matmul_* record products into it
+ * and lab_gpu_commit runs them. Here a buffer is device memory with a pinned
+ * host mirror: a commit copies in the input ranges the host may have written,
+ * runs the products and copies the written ranges back. A buffer used as
+ * weights is copied to the device once, at its first product, so weights must
+ * be written before their first use (as dianoia does). Products quantize
+ * their inputs to Q8_0 per block, like the reference's integer-dot path, and
+ * equal lab_gemm_q8 / lab_gemm_q4 in mode 1. Calls are serialized. */
+
+/* 1 when a usable B200 is present (the first call sets up), else 0.
+ * Replaces lab_gpu_init, lab_vulkan.c:295. */
+int64_t lab_gpu_init(void);
+/* A zeroed buffer of `bytes`; its handle, or -1. Replaces lab_gpu_buffer,
+ * lab_vulkan.c:582 (and lab_gpu_readback_buffer, :590, the same here). */
+int64_t lab_gpu_buffer(int64_t bytes);
+int64_t lab_gpu_readback_buffer(int64_t bytes);
+/* A buffer holding a copy of `bytes` bytes at `address`; handle or -1.
+ * Replaces lab_gpu_wrap, lab_vulkan.c:598; lab_gpu_wrap_copies (:605) is 1:
+ * the wrapped memory may be freed afterwards. */
+int64_t lab_gpu_wrap(void* address, int64_t bytes);
+int64_t lab_gpu_wrap_copies(void);
+/* The host address of a buffer's contents (NULL for a bad handle).
+ * Replaces lab_gpu_contents, lab_vulkan.c:607. */
+void* lab_gpu_contents(int64_t handle);
+/* Frees a buffer once submitted work is done; its handle is reused.
+ * Replaces lab_gpu_release, lab_vulkan.c:637. */
+void lab_gpu_release(int64_t handle);
+/* Buffers not yet released (leak checks). Replaces lab_gpu_live_buffers, :652. */
+int64_t lab_gpu_live_buffers(void);
+/* Opens the command buffer (waiting for one committed without waiting).
+ * Replaces lab_gpu_begin, lab_vulkan.c:655. */
+void lab_gpu_begin(void);
+/* Runs the recorded products; with `wait`, blocks until done. Returns 1, or 0
+ * if a product's buffers or sizes did not fit or the GPU failed.
+ * Replaces lab_gpu_commit, lab_vulkan.c:737; lab_gpu_wait (:761) waits for a
+ * command buffer committed without waiting. */
+int64_t lab_gpu_commit(int64_t wait);
+int64_t lab_gpu_wait(void);
+/* GPU time of the last waited command buffer, ms. Replaces lab_gpu_last_ms, :610. */
+double lab_gpu_last_ms(void);
+/* Y = X W^T for n tokens: W (rows x cols, Q8_0 with f32 scales, or Q4_0
+ * with fp16 scales) at byte offsets qsOffset / scalesOffset of buffer w,
+ * X [n, cols] f32 at xOffset of buffer x, Y [n, rows] f32 at yOffset of y.
+ * Replaces lab_gpu_enc_matmul_q8 / _q4, lab_vulkan.c:879-891. */
+void lab_gpu_enc_matmul_q8(int64_t w, int64_t qsOffset, int64_t scalesOffset, int64_t x,
+                           int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
+                           int64_t n);
+void lab_gpu_enc_matmul_q4(int64_t w, int64_t qsOffset, int64_t scalesOffset, int64_t x,
+                           int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
+                           int64_t n);
+
 /* ------------------------------------------------------------ dn_* (device API) */
 
 /* Status codes of the dn_* functions and of dn_last_error(). */

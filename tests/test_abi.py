@@ -34,7 +34,12 @@ def _has_gpu():
 def test_header_declares_the_reference_symbols():
     names = _lib.header_functions()
     for sym in ("lab_alloc", "lab_free", "lab_cpu_supported", "lab_quantize_q8", "lab_quantize_q4",
-                "lab_gemm_q8", "lab_gemm_q4", "lab_gemv_q8"):
+                "lab_gemm_q8", "lab_gemm_q4", "lab_gemv_q8",
+                # the GPU layer's product ABI (gpu.dart:36-312)
+                "lab_gpu_init", "lab_gpu_buffer", "lab_gpu_readback_buffer", "lab_gpu_wrap",
+                "lab_gpu_wrap_copies", "lab_gpu_contents", "lab_gpu_release", "lab_gpu_live_buffers",
+                "lab_gpu_begin", "lab_gpu_commit", "lab_gpu_wait", "lab_gpu_last_ms",
+                "lab_gpu_enc_matmul_q8", "lab_gpu_enc_matmul_q4"):
         assert sym in names
 
 
@@ -65,6 +70,17 @@ def test_no_device_behaviour(L):
         nat.NativeKernels.load(None)
     with pytest.raises(nat.StateError):
         nat.NativeKernels.instance()
+    # The GPU layer does not start; its functions refuse work without crashing.
+    assert L.lab_gpu_init() == 0
+    assert L.lab_gpu_buffer(64) == -1
+    assert L.lab_gpu_contents(0) is None
+    assert L.lab_gpu_live_buffers() == 0
+    L.lab_gpu_begin()
+    L.lab_gpu_enc_matmul_q8(0, 0, 0, 0, 0, 0, 0, 32, 32, 1)
+    assert L.lab_gpu_commit(1) == 0
+    assert L.lab_gpu_wrap_copies() == 1
+    from dianoia_b200.gpu import GpuLinear
+    assert GpuLinear.start() is None
 
 
 def test_error_strings(L):
