@@ -61,10 +61,24 @@ Q8_BLOCK_BYTES_REF = 36   # reference layout: 32 int8 + f32 scale
 Q8_BLOCK_BYTES_ALG = 34   # algorithmic credit: 32 int8 + fp16 scale (GGUF Q8_0)
 METRIC = "quantized-linear HBM GB/s (GEMV), int8 TOPS (GEMM), tokens/s at 1/2/4/8 B200"
 CHUNKS = 8                # weights are generated per 1/8 row chunk so any N in {1,2,4,8} shards alike
+# DRAM bytes of one GEMV launch per projection, from one ncu capture of each
+# (profiles/dram_decode_stack_q8_shapes.md): a layer's four, and the lm_head.
+MEASURED_DRAM_BYTES_LAYER = 9487872 + 4769024 + 28362496 + 14211072
+MEASURED_DRAM_BYTES_HEAD = 350114304 + 4418560
+# The chain kernel's DRAM bytes over reference-layout weight bytes, from one ncu
+# capture of a 4-layer chain (profiles/chain_kernel_q8_4layers.md).
+MEASURED_CHAIN_TRAFFIC_RATIO = (576637952 + 4725760) / 576552960
 
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+def set_layers(n: int) -> None:
+    global LAYERS
+    if n < 1:
+        raise SystemExit("--layers must be >= 1")
+    LAYERS = n
 
 
 def matrices():
@@ -373,7 +387,7 @@ def workload_config(world):
     return {"workload": "config3: Qwen3-1.7B-shaped Q8_0 decode-step linear stack, batch 1 "
                         "(28 x [qkv 4096x2048, o 2048x2048, gate/up 12288x2048, down 2048x6144] "
                         "+ lm_head 151936x2048)",
-            "global_batch": 1, "parallelism": f"row-sharded x{world} + all-gather",
+            "global_batch": 1, "layers": LAYERS, "parallelism": f"row-sharded x{world} + all-gather",
             "weights_bytes_per_token_ref_layout": step_bytes(Q8_BLOCK_BYTES_REF),
             "l2": "inputs larger than L2 (1.94 GB of weights streamed per step)"}
 
@@ -399,7 +413,10 @@ def main():
     ap.add_argument("--rows", type=int, default=VOCAB)
     ap.add_argument("--cols", type=int, default=HIDDEN)
     ap.add_argument("--n", type=int, default=1, help="tokens per product")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decoder layers of the stack (28; fewer only for small profiler captures)")
     args = ap.parse_args()
+    set_layers(args.layers)
     if args.workload == "gemv":
         return run_gemv_workload(args)
     if args.workload == "gemm":
@@ -560,7 +577,13 @@ def main():
                          "frac": achieved / peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
                          "algorithmic_bytes_per_step_per_gpu": per_rank_bytes,
-                         "traffic": None},
+                         "traffic": ((LAYERS * MEASURED_DRAM_BYTES_LAYER + MEASURED_DRAM_BYTES_HEAD) / world
+                                     if dchain is None else MEASURED_CHAIN_TRAFFIC_RATIO * ref_bytes),
+                         "traffic_source": ("ncu dram__bytes_read+write of each projection's GEMV "
+                                            "launch, summed per token, / N (profiles/"
+                                            "dram_decode_stack_q8_shapes.md)" if dchain is None
+                                            else "ncu dram bytes of a 4-layer chain launch, scaled "
+                                                 "by weight bytes (profiles/chain_kernel_q8_4layers.md)")},
             "e2e": e2e,
             "e2e_cpu_abi": e2e_cpu_abi,
             "cpu_baseline": cpu_baseline,
@@ -670,7 +693,9 @@ def run_gemv_workload(args):
 def run_gemm_workload(args):
     """One quantized matrix times n tokens through dn_linear (tensor-core path
     when n is above the crossover): activation quantize + GEMM per launch,
-    timed with CUDA events; reports int8 TOPS (2 * n * rows * cols per launch)."""
+    timed with CUDA events; reports int8 TOPS (2 * n * rows * cols per launch).
+    Weights, activations and outputs rotate through enough copies to exceed
+    twice the L2, so each launch reads its operands from HBM."""
     import torch
     from dianoia_b200 import _lib
     L = _lib.lib()
@@ -678,36 +703,44 @@ def run_gemm_workload(args):
     blocks = cols // 32
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0)
-    if q4:
-        qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
-        sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen).half().view(torch.int16)
-    else:
-        qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
-        sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen).half().float()
-    xs = torch.randn(n * cols, device="cuda", generator=gen)
+    per_copy = rows * cols // (2 if q4 else 1) + rows * blocks * (2 if q4 else 4) + 4 * n * (cols + rows)
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    copies = max(1, -(-2 * l2 // per_copy))
+    sets = []
+    for _ in range(copies):
+        if q4:
+            qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
+            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen).half().view(torch.int16)
+        else:
+            qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
+            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen).half().float()
+        xs = torch.randn(n * cols, device="cuda", generator=gen)
+        ys = torch.zeros(n * rows, device="cuda")
+        sets.append((qs, sc, xs, ys))
     xq = torch.zeros(n * cols, dtype=torch.int8, device="cuda")
     xsc = torch.zeros(n * blocks + 4, device="cuda")
-    ys = torch.zeros(n * rows, device="cuda")
     stream = torch.cuda.Stream()
-    path = L.dn_linear_path(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
+    qs0, sc0, xs0, _ = sets[0]
+    path = L.dn_linear_path(1 if q4 else 0, qs0.data_ptr(), sc0.data_ptr(), xs0.data_ptr(),
                             xq.data_ptr(), rows, cols, n, 1)
 
-    def launch(handle):
+    def launch(i, handle):
+        qs, sc, xs, ys = sets[i % copies]
         rc = L.dn_linear(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(), xq.data_ptr(),
                          xsc.data_ptr(), ys.data_ptr(), rows, cols, n, rows, 1, -1, 0, handle)
         if rc != 0:
             raise RuntimeError(L.dn_error_string(rc).decode())
 
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 1)):
-            launch(stream.cuda_stream)
+        for i in range(max(args.warmup, 1)):
+            launch(i, stream.cuda_stream)
         torch.cuda.synchronize()
         graph = None
         if not args.no_graph:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
-                for _ in range(args.steps):
-                    launch(torch.cuda.current_stream().cuda_stream)
+                for i in range(args.steps):
+                    launch(i, torch.cuda.current_stream().cuda_stream)
             graph.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -715,8 +748,8 @@ def run_gemm_workload(args):
         if graph is not None:
             graph.replay()
         else:
-            for _ in range(args.steps):
-                launch(stream.cuda_stream)
+            for i in range(args.steps):
+                launch(i, stream.cuda_stream)
         e1.record(stream)
         torch.cuda.synchronize()
     if L.dn_device_status(1) != 0:
@@ -737,7 +770,8 @@ def run_gemm_workload(args):
            "us_per_launch": us, "tops": ops / us / 1e6, "int8_peak_tops": int8_peak,
            "frac_of_int8_peak": ops / us / 1e6 / int8_peak,
            "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops" if peaks else "2 x fallback 1590",
-           "launches": args.steps, "graph": graph is not None,
+           "launches": args.steps, "graph": graph is not None, "copies": copies,
+           "l2": f"{copies} rotating operand copies (> 2 x L2)",
            "includes": "activation quantize (f32 -> Q8_0) + GEMM"}
     print(json.dumps(res), flush=True)
 
