@@ -406,7 +406,7 @@ def main():
                          "launch per projection (always used for N > 1)")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--workload", choices=["stack", "gemv", "gemm"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs"], default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
     ap.add_argument("--fmt", choices=["q8", "q4"], default="q8")
@@ -421,6 +421,8 @@ def main():
         return run_gemv_workload(args)
     if args.workload == "gemm":
         return run_gemm_workload(args)
+    if args.workload == "configs":
+        return run_configs_workload(args)
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -774,6 +776,130 @@ def run_gemm_workload(args):
            "l2": f"{copies} rotating operand copies (> 2 x L2)",
            "includes": "activation quantize (f32 -> Q8_0) + GEMM"}
     print(json.dumps(res), flush=True)
+
+
+# BASELINE configs 1, 2, 4, 5 and the lm_head M sweep: (config, name, fmt, rows, cols, n).
+CONFIG_CASES = (
+    [("c1", "mlp_up", "q4", 6144, 2048, 1)]
+    + [("c2", n, "q8", r, c, 1) for n, r, c in [("q", 2048, 2048), ("k", 1024, 2048), ("v", 1024, 2048),
+                                               ("o", 2048, 2048), ("gate", 6144, 2048),
+                                               ("up", 6144, 2048), ("down", 2048, 6144)]]
+    + [("c4", n, "q4", r, c, 512) for n, r, c in [("gate_up", 6144, 2048), ("down", 2048, 6144)]]
+    # vision encoder, 1024 tokens; fc2's K 4304 padded to 4320 (a multiple of the 32-block)
+    + [("c5", n, "q8", r, c, 1024) for n, r, c in [("qkv", 3456, 1152), ("o", 1152, 1152),
+                                                   ("fc1", 4304, 1152), ("fc2", 1152, 4320)]]
+    + [("c5", f"lm_head_m{m}", "q8", VOCAB, HIDDEN, m) for m in (1, 2, 4, 8, 16, 32, 64)])
+
+
+def time_linear(torch, L, fmt, rows, cols, n, steps, warmup):
+    """us per dn_linear launch (mode 1, automatic path, f32 activations in),
+    the operands rotating through copies that exceed twice the L2."""
+    q4 = fmt == "q4"
+    blocks = cols // 32
+    per_copy = rows * cols // (2 if q4 else 1) + rows * blocks * (2 if q4 else 4) + 4 * n * (cols + rows)
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    copies = max(1, -(-2 * l2 // per_copy))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(rows * 31 + cols * 7 + n)
+    sets = []
+    for _ in range(copies):
+        if q4:
+            qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
+            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen).half().view(torch.int16)
+        else:
+            qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
+            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen).half().float()
+        sets.append((qs, sc, torch.randn(n * cols, device="cuda", generator=gen),
+                     torch.zeros(n * rows, device="cuda")))
+    xq = torch.zeros(n * cols, dtype=torch.int8, device="cuda")
+    xsc = torch.zeros(n * blocks + 4, device="cuda")
+    path = L.dn_linear_path(1 if q4 else 0, sets[0][0].data_ptr(), sets[0][1].data_ptr(),
+                            sets[0][2].data_ptr(), xq.data_ptr(), rows, cols, n, 1)
+    stream = torch.cuda.Stream()
+
+    def launch(i, h):
+        qs, sc, xs, ys = sets[i % copies]
+        rc = L.dn_linear(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(), xq.data_ptr(),
+                         xsc.data_ptr(), ys.data_ptr(), rows, cols, n, rows, 1, -1, 1, h)
+        if rc != 0:
+            raise RuntimeError(L.dn_error_string(rc).decode())
+
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            launch(i, stream.cuda_stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                launch(i, torch.cuda.current_stream().cuda_stream)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    del graph
+    if L.dn_device_status(1) != 0:
+        raise SystemExit("kernel bounded wait timed out")
+    return e0.elapsed_time(e1) * 1e3 / steps, {0: "gemv", 1: "tcgen05", 2: "generic"}.get(path, path), copies
+
+
+def cpu_linear_us(ref, fmt, rows, cols, n, threads, budget_s=2.0):
+    """us per call of the reference's lab_gemm_q4 / _q8 (mode 1) on this host."""
+    from oracle import oracle as orc
+    rng = np.random.default_rng(rows + cols + n)
+    qs, sc = orc.q4_weights(rng, rows, cols) if fmt == "q4" else orc.q8_weights(rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    out = (np.zeros(n * rows, np.float32), np.zeros(n * cols, np.int8),
+           np.zeros(n * (cols // 32) + 1, np.float32))
+    ref.gemm(fmt, qs, sc, xs, rows, cols, n, 1, threads, out)
+    times, t_end = [], time.perf_counter() + budget_s
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+        t0 = time.perf_counter()
+        ref.gemm(fmt, qs, sc, xs, rows, cols, n, 1, threads, out)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6
+
+
+def run_configs_workload(args):
+    """One JSON line per BASELINE config case: the GPU time per dn_linear
+    launch (graph-replayed, operands past L2) as HBM GB/s for the decode
+    GEMVs and int8 TOPS for the GEMMs, each against its measured peak, and the
+    reference's CPU kernels (oracle/_ref, all host threads) on the same case."""
+    import torch
+    from dianoia_b200 import _lib
+    L = _lib.lib()
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    int8 = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    ref = None
+    if args.cpu_tokens > 0:
+        from oracle import oracle as orc
+        try:
+            ref = orc.Reference()
+        except FileNotFoundError:
+            ref = None
+    threads = host_threads()
+    for cfg, name, fmt, rows, cols, n in CONFIG_CASES:
+        us, path, copies = time_linear(torch, L, fmt, rows, cols, n, args.steps, max(args.warmup, 3))
+        blocks = rows * cols // 32
+        alg_bytes = blocks * (18 if fmt == "q4" else 34) + 4 * n * (cols + rows)
+        ops = 2.0 * n * rows * cols
+        res = {"config": cfg, "case": name, "fmt": fmt, "rows": rows, "cols": cols, "n": n,
+               "path": path, "us": us, "gbs_algorithmic": alg_bytes / us / 1e3,
+               "hbm_frac": alg_bytes / us / 1e3 / hbm, "tops": ops / us / 1e6,
+               "int8_frac": ops / us / 1e6 / int8, "copies": copies}
+        if ref is not None:
+            cus = cpu_linear_us(ref, fmt, rows, cols, n, threads)
+            res["cpu_reference_us"] = cus
+            res["cpu_threads"] = threads
+            res["gpu_speedup"] = cus / us
+        print(json.dumps(res), flush=True)
 
 
 def run_e2e(args, stack, L, torch, rank, world, gather, device):
