@@ -40,14 +40,17 @@
 #include "dn_launch.h"
 #include "dn_tmap.h"
 #include "gemv_core.cuh"
+#include "quaddot.cuh"
 
 namespace dn {
 namespace {
 
 using namespace gemv;
 
+// Two CTAs per SM, stated so ptxas keeps the unrolled stage in registers
+// (without a minimum it capped the kernel at 56 registers).
 template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
     gemv_i8_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
                    const __grid_constant__ CUtensorMap tsc) {
   using F = Fmt<Q4>;
@@ -204,18 +207,56 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t] = 0.0f;
 
-    const LaneCtx lc{row_local, r8, l, rowoff, xw_l, sp.xw_stride, xs_s, sp.xs_stride, sc, row, blocks};
-
-    for (int c = 0; c < nch; c++, k++) {
-      const int s = (int)(k % stages);
-      const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-      if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
-        abort_flag = 1;
-        return;  // the producer drains what it issued; every other wait is bounded
+    if constexpr (NT == 1) {
+      // One token: the quad-lane core (quaddot.cuh), whole stages and the
+      // rest in separate loops (a per-stage branch between them made the
+      // compiler issue the shared-memory loads late).
+      const quad::Lane qc = quad::lane_ctx(warp, lane);
+      const uint8_t* xwp = xw_l;
+      const float* xsp = xs_s;
+      const uint8_t* gsc = TMA_SCALES ? nullptr : sc + row * blocks * F::kSB;
+      const int nfull = TMA_SCALES ? (int)(blocks / F::kKC) : 0;
+      int c = 0;
+      for (; c < nfull; c++, k++) {
+        const int s = (int)(k % stages);
+        if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+          abort_flag = 1;
+          return;  // the producer drains what it issued; every other wait is bounded
+        }
+        quad::stage_full<Q4>(smem + (int64_t)s * kStageBytes, qc, xwp, xsp, acc[0]);
+        xwp += F::kKC * X::kBlockBytes;
+        xsp += F::kKC;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      gemv_stage<Q4, NT, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, c * F::kKC, lc, acc);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      for (; c < nch; c++, k++) {
+        const int s = (int)(k % stages);
+        const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
+        if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+          abort_flag = 1;
+          return;
+        }
+        quad::stage_part<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, qc, xwp, xsp,
+                                         gsc == nullptr ? nullptr : gsc + (int64_t)c * F::kKC * F::kSB,
+                                         acc[0]);
+        xwp += F::kKC * X::kBlockBytes;
+        xsp += F::kKC;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+    } else {
+      const LaneCtx lc{row_local, r8, l, rowoff, xw_l, sp.xw_stride, xs_s, sp.xs_stride, sc, row, blocks};
+      for (int c = 0; c < nch; c++, k++) {
+        const int s = (int)(k % stages);
+        const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
+        if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+          abort_flag = 1;
+          return;  // the producer drains what it issued; every other wait is bounded
+        }
+        gemv_stage<Q4, NT, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, c * F::kKC, lc, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
     }
 
     float* yt = yt_s + (e & 1) * NT * kRows;
@@ -318,10 +359,13 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, (uint64_t)a.rows,
                       row_bytes, kBoxBytes, kRows, true))
     return kErrUnsupported;
+  // The one-token kernel reads its scale box with a 64-byte swizzle (quaddot.cuh).
+  const CUtensorMapDataType st = Q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   if (TMA_SCALES &&
-      !encode_tmap_2d(&tsc, a.scales, Q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                      (uint64_t)blocks, (uint64_t)a.rows, (uint64_t)blocks * F::kSB, F::kKC, kRows,
-                      false))
+      !(NT == 1 ? encode_tmap_2d_sw64(&tsc, a.scales, st, (uint64_t)blocks, (uint64_t)a.rows,
+                                      (uint64_t)blocks * F::kSB, F::kKC, kRows)
+                : encode_tmap_2d(&tsc, a.scales, st, (uint64_t)blocks, (uint64_t)a.rows,
+                                 (uint64_t)blocks * F::kSB, F::kKC, kRows, false)))
     return kErrUnsupported;
   auto kern = gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN>;
   static bool configured[64] = {};  // per device: the opt-in smem limit is set

@@ -60,9 +60,10 @@ __device__ __forceinline__ uint64_t exact_d2(int32_t a, int32_t b) {
 // One token's activations in shared memory, lane-interleaved per block b:
 //   Q8_0: 32 bytes; lane l's 8 at b * 32 + 8 l (its words 4l..4l+3 and
 //         16+4l..16+4l+3 of the block);
-//   Q4_0: 64 bytes; lane l's 16 at b * 64 + 16 l: the same two words, the
-//         dp4a seed kMagic - 8 * (sum of those eight int8) (the nibbles enter
-//         the dot products unsigned, 0..15) and a pad word;
+//   Q4_0: 64 bytes; lane l's 16 at b * 64 + 16 l: the same two words,
+//         -8 * (sum of those eight int8) (the nibbles enter the dot products
+//         unsigned, 0..15; kMagic is added where it seeds the dp4a) and a pad
+//         word (the layout gemv_core.cuh's XLayout also uses);
 // and the block scales as a float array.
 template <bool Q4>
 struct XQ {
@@ -106,7 +107,7 @@ __device__ __forceinline__ void load_unpack(const uint8_t* qa, int64_t blocks, u
         const int l = (int)(i & 3);
         if (Q4) {
           const int32_t seed =
-              kMagic - 8 * __dp4a((int32_t)lo[u], 0x01010101, __dp4a((int32_t)hi[u], 0x01010101, 0));
+              -8 * __dp4a((int32_t)lo[u], 0x01010101, __dp4a((int32_t)hi[u], 0x01010101, 0));
           *reinterpret_cast<uint4*>(xw + b * 64 + 16 * l) = make_uint4(lo[u], hi[u], (uint32_t)seed, 0u);
         } else {
           *reinterpret_cast<uint2*>(xw + b * 32 + 8 * l) = make_uint2(lo[u], hi[u]);
@@ -183,7 +184,7 @@ __device__ __forceinline__ void stage_full(const uint8_t* stage, const Lane& c, 
           const uint32_t w = lds<uint32_t>(box + c.off[bb]);
           const uint4 xv = lds<uint4>(xwb + (8 * j + bb) * X::kBlock);
           d[q] = __dp4a((int32_t)((w >> 4) & 0x0f0f0f0fu), (int32_t)xv.y,
-                        __dp4a((int32_t)(w & 0x0f0f0f0fu), (int32_t)xv.x, (int32_t)xv.z));
+                        __dp4a((int32_t)(w & 0x0f0f0f0fu), (int32_t)xv.x, (int32_t)xv.z + kMagic));
         }
         const uint64_t d01 = exact_d2(d[0], d[1]), d23 = exact_d2(d[2], d[3]);
         acc = __fmaf_rn(f2_lo(d01), f2_lo(s01), acc);
@@ -239,7 +240,7 @@ __device__ __forceinline__ void stage_part(const uint8_t* stage, int nb, const L
       const uint32_t w = lds<uint32_t>(box + c.off_rt(q));
       const uint4 xv = lds<uint4>(xwb + bb * X::kBlock);
       d = __dp4a((int32_t)((w >> 4) & 0x0f0f0f0fu), (int32_t)xv.y,
-                 __dp4a((int32_t)(w & 0x0f0f0f0fu), (int32_t)xv.x, (int32_t)xv.z));
+                 __dp4a((int32_t)(w & 0x0f0f0f0fu), (int32_t)xv.x, (int32_t)xv.z + kMagic));
     } else {
       const uint32_t w0 = lds<uint32_t>(box + c.off_rt(2 * q));
       const uint32_t w1 = lds<uint32_t>(box + c.off_rt(2 * q + 1));
