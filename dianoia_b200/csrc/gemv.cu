@@ -351,6 +351,17 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   }
   stages = stages > kMaxStages ? kMaxStages : stages;
   if (stages < 2) return kErrTooLarge;
+  // Persistent grid, balanced so every CTA gets the same number of tiles.
+  const int64_t slots = (int64_t)kSMs * per_sm;
+  const int64_t waves = (ntiles + slots - 1) / slots;
+  const int64_t grid = (ntiles + waves - 1) / waves;
+  // No more stages than the stages a CTA will ever load: the shared memory
+  // left over lets the next kernel's CTAs become resident early (programmatic
+  // dependent launch) and start streaming their weights during this kernel.
+  {
+    const int64_t chunks = waves * ((blocks + F::kKC - 1) / F::kKC);
+    if (chunks < stages) stages = (int)(chunks < 2 ? 2 : chunks);
+  }
   const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN);
   if (sp.total > kMaxSmem) return kErrTooLarge;
   CUtensorMap tw, tsc;
@@ -377,10 +388,6 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
       return kErrCuda;
     configured[dev & 63] = true;
   }
-  // Persistent grid, balanced so every CTA gets the same number of tiles.
-  const int64_t slots = (int64_t)kSMs * per_sm;
-  const int64_t waves = (ntiles + slots - 1) / slots;
-  const int64_t grid = (ntiles + waves - 1) / waves;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, (unsigned)((a.n + NT - 1) / NT), 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
