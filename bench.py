@@ -161,15 +161,24 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ model
 
+def row_split(rows: int, rank: int, world: int, tiled: bool):
+    """Rows [r0, r1) of a projection on `rank` of `world`: an even split, or,
+    for the sharded chain, one on 32-row tiles (the chain's output unit)."""
+    if not tiled:
+        return rows * rank // world, rows * (rank + 1) // world
+    tiles = -(-rows // 32)
+    return min(rows, tiles * rank // world * 32), min(rows, tiles * (rank + 1) // world * 32)
+
+
 class Stack:
     """This rank's row slices of every projection, resident in HBM."""
 
-    def __init__(self, torch, rank: int, world: int, device):
+    def __init__(self, torch, rank: int, world: int, device, tiled: bool = False):
         self.torch = torch
         self.rank, self.world, self.device = rank, world, device
         self.mats = []
         for idx, (layer, name, rows, cols) in enumerate(matrices()):
-            r0, r1 = rows * rank // world, rows * (rank + 1) // world
+            r0, r1 = row_split(rows, rank, world, tiled)
             qs, sc = self._weights(idx, rows, cols, r0, r1)
             self.mats.append(dict(layer=layer, name=name, rows=rows, cols=cols, r0=r0, r1=r1,
                                   qs=qs, scales=sc))
@@ -299,6 +308,85 @@ class DecodeChain:
             self.handle = ctypes.c_void_p()
 
 
+class ShardedChain:
+    """N > 1: a token's projections as one chain kernel per GPU, each rank
+    computing its row slices. A tile's QA output goes into every rank's copy
+    of the output over NVLink and is counted in every rank's counters
+    (dn_chain_create_sharded), so no collective runs between projections.
+    Every rank maps every other rank's region (dn_peer_alloc / dn_peer_open);
+    the logits stay rank-local (each rank its rows of the whole buffer)."""
+
+    def __init__(self, torch, stack, qa, L, device, dist):
+        from dianoia_b200 import _lib
+        self.L, self.dist = L, dist
+        rank, world = stack.rank, stack.world
+        nops = len(stack.mats)
+        offs, at = [], 0
+        for m in stack.mats:
+            if m["name"] == "lm_head":
+                offs.append(None)
+                continue
+            offs.append(at)
+            at = (at + m["rows"] // 32 * 36 + 15) // 16 * 16
+        counters_off = at
+        self.region_bytes = (at + 4 * (nops + 2) + 255) // 256 * 256
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.DN_PEER_HANDLE_BYTES)()
+        _lib.check(L.dn_peer_alloc(self.region_bytes, ctypes.byref(base), handle), "dn_peer_alloc")
+        self.base = base.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle))
+        self.opened = []
+        bases = (ctypes.c_void_p * world)()
+        for p in range(world):
+            if p == rank:
+                bases[p] = self.base
+                continue
+            ptr = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * _lib.DN_PEER_HANDLE_BYTES).from_buffer_copy(handles[p])
+            _lib.check(L.dn_peer_open(h, ctypes.byref(ptr)), "dn_peer_open")
+            bases[p] = ptr.value
+            self.opened.append(ptr.value)
+        ops, row0, total, last = [], [], [], {}
+        for i, m in enumerate(stack.mats):
+            name = m["name"]
+            src = INPUT_OF[name]
+            if src is not None:
+                xa, dep = last[src]
+            else:
+                xa, dep = qa.xa0.data_ptr(), (last["down"][1] if "down" in last else -1)
+            ys = ya = None
+            if name == "lm_head":
+                ys = stack.bufs["lm_head"].data_ptr()
+            else:
+                ya = self.base + offs[i]
+                last[name] = (ya, i)
+            ops.append(_lib.ChainOp(m["qs"].data_ptr(), m["scales"].data_ptr(), xa, ys, ya,
+                                    m["r1"] - m["r0"], m["cols"], dep))
+            row0.append(m["r0"])
+            total.append(m["rows"])
+        arr = (_lib.ChainOp * nops)(*ops)
+        self.handle = ctypes.c_void_p()
+        _lib.check(L.dn_chain_create_sharded(0, arr, (ctypes.c_int64 * nops)(*row0),
+                                             (ctypes.c_int64 * nops)(*total), nops, rank, world,
+                                             bases, self.region_bytes, self.base + counters_off,
+                                             ctypes.byref(self.handle)), "dn_chain_create_sharded")
+        dist.barrier()  # every region mapped everywhere before any rank runs
+
+    def close(self):
+        if self.handle:
+            self.L.dn_chain_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+        self.dist.barrier()  # no rank still writes into another's region
+        for p in self.opened:
+            self.L.dn_peer_close(p)
+        self.opened = []
+        self.dist.barrier()
+        if self.base:
+            self.L.dn_peer_free(self.base)
+            self.base = None
+
+
 def run_step_chain(stack, qa, dchain, L, stream_handle, flags=1):
     """One token: quantize x0, then every projection in one chain kernel."""
     rc = L.dn_quantize_qa(stack.x0.data_ptr(), qa.xa0.data_ptr(), 1, HIDDEN,
@@ -383,11 +471,15 @@ def run_reference_arm(args, rank, world):
     }
 
 
-def workload_config(world):
+def workload_config(world, path="ops"):
     return {"workload": "config3: Qwen3-1.7B-shaped Q8_0 decode-step linear stack, batch 1 "
                         "(28 x [qkv 4096x2048, o 2048x2048, gate/up 12288x2048, down 2048x6144] "
                         "+ lm_head 151936x2048)",
-            "global_batch": 1, "layers": LAYERS, "parallelism": f"row-sharded x{world} + all-gather",
+            "global_batch": 1, "layers": LAYERS,
+            "parallelism": (f"row-sharded x{world}, every tile's QA output stored into the peers over "
+                            "NVLink inside the chain kernel" if world > 1 and path == "chain" else
+                            f"row-sharded x{world} + NCCL all-gather per projection" if world > 1
+                            else "1 GPU"),
             "weights_bytes_per_token_ref_layout": step_bytes(Q8_BLOCK_BYTES_REF),
             "l2": "inputs larger than L2 (1.94 GB of weights streamed per step)"}
 
@@ -401,9 +493,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--path", choices=["chain", "ops"], default="ops",
-                    help="chain: one persistent kernel per token (1 GPU); ops: one GEMV "
-                         "launch per projection (always used for N > 1)")
+    ap.add_argument("--path", choices=["auto", "chain", "ops"], default="auto",
+                    help="chain: one persistent kernel per token (on N > 1 GPUs with the "
+                         "all-gather fused into it over NVLink); ops: one GEMV launch per "
+                         "projection (N > 1: NCCL all-gather after each); auto: ops on 1 GPU, "
+                         "chain on N > 1 (the faster of the two in each case)")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs"], default="stack",
@@ -442,6 +536,10 @@ def main():
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
+        # Keep stdout to the one JSON line: NCCL's own log lines, when they
+        # are switched on without a file, go to stderr.
+        if os.environ.get("NCCL_DEBUG") and not os.environ.get("NCCL_DEBUG_FILE"):
+            os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
     from dianoia_b200 import _lib
@@ -449,7 +547,8 @@ def main():
     if L.lab_cpu_supported() != 1:
         raise SystemExit("no sm_100 device visible to libdianoia_b200")
 
-    stack = Stack(torch, rank, world, device)
+    path = args.path if args.path != "auto" else ("ops" if world == 1 else "chain")
+    stack = Stack(torch, rank, world, device, tiled=(path == "chain" and world > 1))
     torch.cuda.synchronize()
 
     chain = QAChain(torch, device)
@@ -460,8 +559,10 @@ def main():
             dist.all_gather_into_tensor(out, out[rank * n:(rank + 1) * n])
         gather_qa = gather
 
-    path = args.path if world == 1 else "ops"
-    dchain = DecodeChain(torch, stack, chain, L, device) if path == "chain" else None
+    dchain = None
+    if path == "chain":
+        dchain = (DecodeChain(torch, stack, chain, L, device) if world == 1
+                  else ShardedChain(torch, stack, chain, L, device, dist))
 
     def one_step(handle):
         if dchain is not None:
@@ -540,11 +641,15 @@ def main():
     per_rank_bytes = alg_bytes / world
     achieved = per_rank_bytes / (ms_per_step * 1e-3) / 1e9
 
-    # Checksum of the logits: identical for every N (rows do not depend on the split).
-    logits = stack.bufs["lm_head"].double()
-    checksum = float(logits.sum().item())
+    # Checksum of the logits: identical for every N (rows do not depend on the
+    # split). The sharded chain leaves each rank its own rows of the logits
+    # (the rest zero): a sum over ranks rebuilds them exactly.
+    full_logits = stack.bufs["lm_head"].clone()
+    if world > 1 and dchain is not None:
+        dist.all_reduce(full_logits)
+    checksum = float(full_logits.double().sum().item())
     chain_matches_ops = None
-    if dchain is not None:
+    if dchain is not None and world == 1:
         # The chain's logits equal the per-projection launches', bit for bit.
         chain_logits = stack.bufs["lm_head"].clone()
         with torch.cuda.stream(stream):
@@ -558,7 +663,7 @@ def main():
     # ABI (one command buffer per token); also, and on N > 1 only, through
     # the CPU-layer ABI (lab_gemm_q8 per projection on rank-local shards, the
     # slices all-gathered through device copies).
-    e2e_cpu_abi = run_e2e(args, stack, L, torch, rank, world, gather, device)
+    e2e_cpu_abi = run_e2e(args, stack, L, torch, rank, world, gather, device, full_logits)
     e2e = run_e2e_gpu_layer(args, stack, L, torch) if world == 1 else None
     if e2e is None:
         e2e = e2e_cpu_abi
@@ -573,14 +678,14 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (random-init Q8_0 weights, N(0,1) activations, seeded)",
-            "config": workload_config(world),
+            "config": workload_config(world, path),
             "hbm_gbs_per_gpu": ref_bytes / world / (ms_per_step * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
                          "algorithmic_bytes_per_step_per_gpu": per_rank_bytes,
                          "traffic": ((LAYERS * MEASURED_DRAM_BYTES_LAYER + MEASURED_DRAM_BYTES_HEAD) / world
-                                     if dchain is None else MEASURED_CHAIN_TRAFFIC_RATIO * ref_bytes),
+                                     if dchain is None else MEASURED_CHAIN_TRAFFIC_RATIO * ref_bytes / world),
                          "traffic_source": ("ncu dram__bytes_read+write of each projection's GEMV "
                                             "launch, summed per token, / N (profiles/"
                                             "dram_decode_stack_q8_shapes.md)" if dchain is None
@@ -600,12 +705,11 @@ def main():
             "logits_checksum": checksum,
         }
         print(json.dumps(res), flush=True)
+    graph = None  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     if dchain is not None:
-        del graph
-        torch.cuda.synchronize()
         dchain.close()
     if world > 1:
-        del graph
         dist.barrier()
         dist.destroy_process_group()
 
@@ -902,7 +1006,7 @@ def run_configs_workload(args):
         print(json.dumps(res), flush=True)
 
 
-def run_e2e(args, stack, L, torch, rank, world, gather, device):
+def run_e2e(args, stack, L, torch, rank, world, gather, device, full_logits):
     """Token loop through lab_gemm_q8 with host activations / outputs."""
     steps = args.e2e_steps
     if steps <= 0:
@@ -930,10 +1034,13 @@ def run_e2e(args, stack, L, torch, rank, world, gather, device):
             h2d += xin.nbytes
             d2h += ys.nbytes + m["cols"] + m["cols"] // 32 * 4
             if world > 1:
+                # All-gather of the row slices (any split): each rank adds
+                # its rows into zeros, exactly.
                 d = dev_tmp[name]
-                n = d.numel() // world
-                d[rank * n:(rank + 1) * n].copy_(torch.from_numpy(ys))
-                gather(d)
+                d.zero_()
+                d[m["r0"]:m["r1"]].copy_(torch.from_numpy(ys))
+                import torch.distributed as dist
+                dist.all_reduce(d)
                 out[:] = d.cpu().numpy()
         if L.dn_last_error() != 0:
             raise RuntimeError("lab_gemm_q8 failed")
@@ -953,7 +1060,8 @@ def run_e2e(args, stack, L, torch, rank, world, gather, device):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dt = float(t.item())
     # Same logits as the device-resident run.
-    same = bool(np.array_equal(host["lm_head"], stack.bufs["lm_head"].cpu().numpy()))
+    same = bool(np.array_equal(host["lm_head"].view(np.uint32),
+                               full_logits.cpu().numpy().view(np.uint32)))
     return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "api": "lab_gemm_q8 (host x / y, device weights)",
             "steps": steps, "logits_match_device_run": same}

@@ -48,6 +48,11 @@ SIGNATURES = {
     "dn_quantize_qa": (_i64, [_p, _p, _i64, _i64, _i64, _p]),
     "dn_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_chain_create": (_i64, [_i64, _p, _i64, _p]),
+    "dn_chain_create_sharded": (_i64, [_i64, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "dn_peer_alloc": (_i64, [_i64, _p, _p]),
+    "dn_peer_open": (_i64, [_p, _p]),
+    "dn_peer_close": (_i64, [_p]),
+    "dn_peer_free": (_i64, [_p]),
     "dn_chain_run": (_i64, [_p, _i64, _p]),
     "dn_chain_reset": (_i64, [_p, _p]),
     "dn_chain_destroy": (_i64, [_p]),
@@ -63,6 +68,7 @@ DN_Q8, DN_Q4 = 0, 1
 DN_PATH_AUTO, DN_PATH_GEMV, DN_PATH_TC, DN_PATH_GENERIC = -1, 0, 1, 2
 DN_FLAG_PDL = 1
 QA_BYTES = 36  # QA activation block: 32 int8 + f32 scale
+DN_PEER_HANDLE_BYTES = 64
 
 
 class ChainOp(ctypes.Structure):

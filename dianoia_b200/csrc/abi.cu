@@ -514,6 +514,66 @@ int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, vo
   return rc;
 }
 
+int64_t dn_chain_create_sharded(int64_t format, const dn_chain_op* ops, const int64_t* row0,
+                                const int64_t* total_rows, int64_t nops, int64_t rank,
+                                int64_t world, void* const* bases, int64_t region_bytes,
+                                int32_t* counters, void** chain) {
+  if ((format != DN_Q8 && format != DN_Q4) || ops == nullptr || chain == nullptr || nops <= 0)
+    return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  const dn::ChainShard shard{rank, world, reinterpret_cast<const void* const*>(bases),
+                             region_bytes, reinterpret_cast<int*>(counters)};
+  dn::ChainHost* h = nullptr;
+  const int64_t rc = dn::chain_create_sharded(reinterpret_cast<const dn::ChainOpSpec*>(ops), row0,
+                                              total_rows, nops, format == DN_Q4, shard, &h);
+  *chain = rc == DN_OK ? h : nullptr;
+  return rc;
+}
+
+int64_t dn_peer_alloc(int64_t bytes, void** ptr, void* handle) {
+  if (bytes <= 0 || ptr == nullptr || handle == nullptr) return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  void* p = nullptr;
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == DN_PEER_HANDLE_BYTES, "IPC handle size");
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return DN_ERR_CUDA;
+  }
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return DN_ERR_CUDA;
+  }
+  memcpy(handle, &h, sizeof h);
+  *ptr = p;
+  return DN_OK;
+}
+
+int64_t dn_peer_open(const void* handle, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return DN_ERR_CUDA;
+  }
+  *ptr = p;
+  return DN_OK;
+}
+
+int64_t dn_peer_close(void* ptr) {
+  if (ptr == nullptr) return DN_ERR_ARGS;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? DN_OK : DN_ERR_CUDA;
+}
+
+int64_t dn_peer_free(void* ptr) {
+  if (ptr == nullptr) return DN_ERR_ARGS;
+  return cudaFree(ptr) == cudaSuccess ? DN_OK : DN_ERR_CUDA;
+}
+
 int64_t dn_chain_run(void* chain, int64_t flags, void* stream) {
   DeviceState* d = device_state();
   if (d == nullptr) return DN_ERR_NO_DEVICE;

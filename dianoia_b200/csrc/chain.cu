@@ -20,8 +20,16 @@
 // the earlier one, as it would with a step outside the chain between them).
 //
 // The grid is launched cooperatively (all CTAs co-resident), so no CTA can
-// wait on one that has not started; every wait is bounded anyway. The last
-// CTA to finish resets the counters for the next launch.
+// wait on one that has not started; every wait is bounded anyway. Counters
+// only grow: run e of a chain waits for (e + 1) x the tiles of an op, e being
+// a run index the last CTA of each run advances, so a run never has to clear
+// what a faster GPU of a sharded chain may already be adding for the next one.
+//
+// Sharded chains (world > 1 GPUs): each rank computes its row slice of every
+// op; a tile's QA block goes to the same place in every rank's region over
+// NVLink (plain stores to peer memory), then lane 0 makes them visible
+// system-wide (fence.acq_rel.sys) and adds one to every rank's counter of the
+// op. No TMA reads or writes peer memory.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -44,18 +52,30 @@ struct alignas(64) ChainOpDev {
   int32_t rows, cols;
   int32_t dep;            // op to wait for (it produces xa, or only precedes this op), or -1
   int32_t ext_input;      // xa was written before the launch (wait for the previous kernel)
-  int32_t ntiles;         // 32-row tiles of the op
-  int32_t tile_base;      // global index of the op's first tile (round-robin deal)
+  int32_t ntiles;         // this rank's 32-row tiles of the op
+  int32_t tile_base;      // index of the op's first tile in the round-robin deal
   int32_t tma_scales;
+  int32_t tile0;          // the op's first tile here, in the whole output (0 unsharded)
+  int32_t ntiles_total;   // tiles of all ranks (the count dependents wait for)
+};
+
+// Where the other ranks' copies of the region are: byte offsets from this
+// rank's region to each rank's (0 for itself).
+constexpr int kMaxWorld = 8;
+struct PeerInfo {
+  int32_t world, rank;
+  int64_t delta[kMaxWorld];
 };
 
 struct ChainHost {
   ChainOpDev* ops_dev = nullptr;  // nops entries
-  int* counters = nullptr;        // nops + 1 ints (the last: CTAs done)
+  int* counters = nullptr;        // nops + 2 ints: per op, then CTAs done, then the run index
+  bool owns_counters = true;
   int nops = 0;
   bool q4 = false;
   int64_t max_blocks = 0;
   int device = 0;
+  PeerInfo peers{1, 0, {0}};
 };
 
 namespace {
@@ -74,20 +94,39 @@ constexpr int kConsumerWarps = quad::kWarps;
 constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumers + 32;  // + the producer warp
 
-__device__ __forceinline__ int ld_relaxed(const int* p) {
-  int v;
-  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Counter accesses: gpu scope for one GPU, system scope when other GPUs add
+// to the counters over NVLink.
+__device__ __forceinline__ uint32_t ld_relaxed(const int* p, bool sys) {
+  uint32_t v;
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_acquire(const int* p, bool sys) {
+  uint32_t v;
+  if (sys)
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  (void)v;
 }
 
 __device__ __forceinline__ void red_release_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void red_relaxed_sys_add(int* p, int v) {
+  asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ T* at_rank(T* local, const PeerInfo& pi, int p) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(local) + pi.delta[p]);
 }
 
 // A barrier of the consumer warps with a bounded wait (two mbarriers used in
@@ -119,7 +158,8 @@ __host__ __device__ inline Plan chain_plan(int stages, int64_t max_blocks, bool 
 template <bool Q4>
 __global__ void __launch_bounds__(kThreads, 3)
     chain_kernel(const ChainOpDev* __restrict__ ops, const int nops, int* counters,
-                 uint32_t* status, const int stages, const int64_t max_blocks, const int l2_ahead) {
+                 uint32_t* status, const int stages, const int64_t max_blocks, const int l2_ahead,
+                 const PeerInfo pi) {
   using F = Fmt<Q4>;
   using X = quad::XQ<Q4>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -228,6 +268,15 @@ __global__ void __launch_bounds__(kThreads, 3)
   // -------------------------------------------------------------- consumers
   const quad::Lane lc = quad::lane_ctx(warp, lane);
   const uint8_t* xw_l = xw + lc.l * X::kLane;
+  const bool sys = pi.world > 1;
+  // The run index (thread 0 waits and signals for the CTA): the previous
+  // kernel in the stream, hence the previous run, is complete after
+  // griddepcontrol.wait.
+  uint32_t run = 0;
+  if (tid == 0) {
+    pdl_wait();
+    run = ld_relaxed(counters + nops + 1, false);
+  }
   bool waited_launch = false;
   uint32_t syncs = 0;
   int s = 0;
@@ -246,16 +295,18 @@ __global__ void __launch_bounds__(kThreads, 3)
       waited_launch = true;
     }
     if (o.dep >= 0 && tid == 0) {
-      const int target = ops[o.dep].ntiles;
+      // This run's tiles of op dep: the counter reaches (run + 1) x its tiles
+      // (compared with wrap-around differences).
+      const uint32_t target = (run + 1u) * (uint32_t)ops[o.dep].ntiles_total;
       const int* cnt = counters + o.dep;
       // Spin on relaxed loads (an acquire per poll costs this SM an L1
       // invalidation each time, which measurably slows the warps computing
       // beside it), then one acquire load.
-      if (ld_relaxed(cnt) < target) {
+      if ((int32_t)(ld_relaxed(cnt, sys) - target) < 0) {
         const uint64_t start = globaltimer_ns();
         for (uint32_t it = 1;; it++) {
           __nanosleep(32);
-          if (ld_relaxed(cnt) >= target) break;
+          if ((int32_t)(ld_relaxed(cnt, sys) - target) >= 0) break;
           if ((it & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
             report(status, kStatusPeerTimeout);
             abort_flag = 1;
@@ -263,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 3)
           }
         }
       }
-      (void)ld_acquire(cnt);
+      ld_acquire(cnt, sys);
     }
     if (!consumers_sync(csync, syncs, status) || abort_flag) {
       abort_flag = 1;
@@ -275,7 +326,8 @@ __global__ void __launch_bounds__(kThreads, 3)
       return;
     }
     for (int t = t_first; t < o.ntiles; t += G) {
-      const int64_t row = (int64_t)t * kRows + lc.r;
+      const int64_t row = (int64_t)t * kRows + lc.r;  // row of this rank's slice
+      const int64_t grow = (int64_t)o.tile0 * kRows + row;  // row of the whole output
       const int64_t srow = row < o.rows ? row : o.rows - 1;
       const uint8_t* gsc = o.tma_scales ? nullptr
                                         : static_cast<const uint8_t*>(o.scales) + srow * blocks * F::kSB;
@@ -324,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 3)
       const float y = gemv::lane_reduce(acc);  // valid on l == 0
       float* yt = yt_s + (e & 1) * kRows;
       if (lc.l == 0 && row < o.rows) {
-        if (o.ys != nullptr) o.ys[row] = y;
+        if (o.ys != nullptr) o.ys[grow] = y;
         yt[lc.r] = y;
       }
       // Every warp's outputs, then (QA outputs: warp 0 quantizes the tile's
@@ -336,21 +388,39 @@ __global__ void __launch_bounds__(kThreads, 3)
       }
       if (warp == 0) {
         // QA outputs need whole tiles (rows % 32 == 0, checked at creation).
-        if (o.ya != nullptr) gemv::quantize_block_out(yt[lane], o.ya + (int64_t)t * kQABytes, lane);
+        uint8_t* blk = o.ya + ((int64_t)o.tile0 + t) * kQABytes;
+        if (o.ya != nullptr) gemv::quantize_block_out(yt[lane], blk, lane);
         __syncwarp();
-        if (lane == 0) red_release_add(counters + op, 1);
+        if (!sys) {
+          if (lane == 0) red_release_add(counters + op, 1);
+        } else {
+          // The block, word by word, into every other rank's region.
+          if (o.ya != nullptr) {
+            for (int i = lane; i < 9 * pi.world; i += 32) {
+              const int p = i / 9, w = i % 9;
+              if (p != pi.rank)
+                at_rank(reinterpret_cast<uint32_t*>(blk), pi, p)[w] = reinterpret_cast<const uint32_t*>(blk)[w];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
+            fence_acq_rel_sys();  // the block is visible everywhere before any count
+            for (int p = 0; p < pi.world; p++) red_relaxed_sys_add(at_rank(counters + op, pi, p), 1);
+          }
+        }
       }
       e++;
     }
   }
-  // The last CTA out resets the counters for the next launch. (Thread 0 is
-  // here only after its last tile's epilogue barrier, so every consumer of
+  // The last CTA out advances the run index for the next launch. (Thread 0
+  // is here only after its last tile's epilogue barrier, so every consumer of
   // the CTA is past its dependency waits; when every CTA's thread 0 is here,
-  // every wait and counter increment of the launch is behind it.)
+  // every wait of the launch is behind it.)
   if (tid == 0 && !abort_flag) {
     __threadfence();
     if (atomicAdd(counters + nops, 1) == G - 1) {
-      for (int i = 0; i <= nops; i++) counters[i] = 0;
+      counters[nops] = 0;
+      counters[nops + 1] = (int)(run + 1u);
       __threadfence();
     }
   }
@@ -378,7 +448,8 @@ struct Range {
   bool overlaps(const Range& o) const { return lo < o.hi && o.lo < hi && lo < hi && o.lo < o.hi; }
 };
 
-static bool chain_buffers_disjoint(const ChainOpSpec* specs, int64_t nops, bool q4) {
+static bool chain_buffers_disjoint(const ChainOpSpec* specs, const int64_t* total_rows,
+                                   int64_t nops, bool q4) {
   auto span = [](const void* p, int64_t bytes) {
     const uintptr_t a = (uintptr_t)p;
     return Range{a, p == nullptr ? a : a + (uintptr_t)bytes};
@@ -387,8 +458,8 @@ static bool chain_buffers_disjoint(const ChainOpSpec* specs, int64_t nops, bool 
   for (int64_t i = 0; i < nops; i++) {
     const ChainOpSpec& s = specs[i];
     const int64_t blocks = s.cols / kBlock;
-    outs.push_back(span(s.ys, s.rows * 4));
-    outs.push_back(span(s.ya, s.rows / kRows * kQABytes));
+    outs.push_back(span(s.ys, total_rows[i] * 4));
+    outs.push_back(span(s.ya, total_rows[i] / kRows * kQABytes));
     ins.push_back(span(s.xa, blocks * kQABytes));
     consts.push_back(span(s.qs, s.rows * blocks * (q4 ? 16 : 32)));
     consts.push_back(span(s.scales, s.rows * blocks * (q4 ? 2 : 4)));
@@ -413,28 +484,54 @@ static bool chain_buffers_disjoint(const ChainOpSpec* specs, int64_t nops, bool 
 
 }  // namespace
 
-int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost** out) {
+static int64_t create(const ChainOpSpec* specs, const int64_t* row0, const int64_t* total_rows,
+                      int64_t nops, bool q4, const ChainShard* shard, ChainHost** out) {
   if (nops <= 0 || specs == nullptr || out == nullptr) return kErrArgs;
+  PeerInfo pi{1, 0, {0}};
+  const uint8_t *region_lo = nullptr, *region_hi = nullptr;
+  if (shard != nullptr) {
+    if (shard->world < 1 || shard->world > kMaxWorld || shard->rank < 0 ||
+        shard->rank >= shard->world || shard->bases == nullptr || shard->region_bytes <= 0 ||
+        shard->counters == nullptr || ((uintptr_t)shard->counters & 3) != 0)
+      return kErrArgs;
+    pi.world = (int32_t)shard->world;
+    pi.rank = (int32_t)shard->rank;
+    for (int p = 0; p < pi.world; p++) {
+      if (shard->bases[p] == nullptr) return kErrArgs;
+      pi.delta[p] = (const char*)shard->bases[p] - (const char*)shard->bases[pi.rank];
+    }
+    region_lo = static_cast<const uint8_t*>(shard->bases[pi.rank]);
+    region_hi = region_lo + shard->region_bytes;
+    const uint8_t* c = reinterpret_cast<const uint8_t*>(shard->counters);
+    if (c < region_lo || c + 4 * (nops + 2) > region_hi) return kErrArgs;
+  }
   std::vector<ChainOpDev> table((size_t)nops);
   int64_t tile_base = 0, max_blocks = 0;
   for (int64_t i = 0; i < nops; i++) {
     const ChainOpSpec& sp = specs[i];
+    const int64_t r0 = row0[i], total = total_rows[i];
     ChainOpDev& d = table[(size_t)i];
     memset(&d, 0, sizeof d);
     const int64_t blocks = sp.cols / kBlock;
     if (sp.rows <= 0 || sp.cols <= 0 || sp.cols % kBlock != 0 || sp.xa == nullptr ||
         ((uintptr_t)sp.qs & 15) != 0 || ((uintptr_t)sp.xa & 3) != 0 ||
         (sp.ya != nullptr && ((uintptr_t)sp.ya & 3) != 0) || sp.dep >= i || sp.dep < -1 ||
-        sp.rows > INT32_MAX / 2 || sp.cols > INT32_MAX / 2)
+        total > INT32_MAX / 2 || sp.cols > INT32_MAX / 2 || r0 < 0 || r0 % kRows != 0 ||
+        r0 + sp.rows > total)
       return kErrArgs;
-    if (sp.ya != nullptr && sp.rows % kRows != 0) return kErrArgs;     // QA outputs: whole blocks
+    // QA outputs: whole blocks (this rank's rows and the whole output).
+    if (sp.ya != nullptr && (sp.rows % kRows != 0 || total % kRows != 0)) return kErrArgs;
+    // Other ranks write QA outputs into the region, so they must be inside it.
+    if (shard != nullptr && sp.ya != nullptr &&
+        (sp.ya < region_lo || sp.ya + total / kRows * kQABytes > region_hi))
+      return kErrArgs;
     d.ext_input = 1;
     if (sp.dep >= 0 && specs[sp.dep].ya != nullptr) {
       // A data edge: the input lies inside the QA output of op dep, on a
       // block boundary. An input that does not touch that output was written
       // before the launch (an ordering edge).
       const ChainOpSpec& p = specs[sp.dep];
-      const uint8_t *lo = p.ya, *hi = p.ya + p.rows / kRows * kQABytes;
+      const uint8_t *lo = p.ya, *hi = p.ya + total_rows[sp.dep] / kRows * kQABytes;
       const uint8_t* end = sp.xa + blocks * kQABytes;
       if (sp.xa < hi && lo < end) {
         if (sp.xa < lo || (sp.xa - lo) % kQABytes != 0 || end > hi) return kErrArgs;
@@ -460,21 +557,30 @@ int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost*
     d.cols = (int32_t)sp.cols;
     d.dep = (int32_t)sp.dep;
     d.ntiles = (int32_t)((sp.rows + kRows - 1) / kRows);
+    d.tile0 = (int32_t)(r0 / kRows);
+    d.ntiles_total = (int32_t)((total + kRows - 1) / kRows);
     d.tile_base = (int32_t)(tile_base % (1 << 30));
     tile_base += d.ntiles;
     max_blocks = blocks > max_blocks ? blocks : max_blocks;
   }
-  if (!chain_buffers_disjoint(specs, nops, q4)) return kErrArgs;
+  if (!chain_buffers_disjoint(specs, total_rows, nops, q4)) return kErrArgs;
   ChainHost* h = new ChainHost();
   h->nops = (int)nops;
   h->q4 = q4;
   h->max_blocks = max_blocks;
+  h->peers = pi;
   cudaGetDevice(&h->device);
+  if (shard != nullptr) {
+    h->counters = shard->counters;
+    h->owns_counters = false;
+  } else if (cudaMalloc(&h->counters, sizeof(int) * (size_t)(nops + 2)) != cudaSuccess ||
+             cudaMemset(h->counters, 0, sizeof(int) * (size_t)(nops + 2)) != cudaSuccess) {
+    chain_destroy(h);
+    return kErrCuda;
+  }
   if (cudaMalloc(&h->ops_dev, sizeof(ChainOpDev) * (size_t)nops) != cudaSuccess ||
-      cudaMalloc(&h->counters, sizeof(int) * (size_t)(nops + 1)) != cudaSuccess ||
       cudaMemcpy(h->ops_dev, table.data(), sizeof(ChainOpDev) * (size_t)nops,
-                 cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemset(h->counters, 0, sizeof(int) * (size_t)(nops + 1)) != cudaSuccess) {
+                 cudaMemcpyHostToDevice) != cudaSuccess) {
     chain_destroy(h);
     return kErrCuda;
   }
@@ -482,10 +588,24 @@ int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost*
   return kOk;
 }
 
+int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost** out) {
+  if (nops <= 0 || specs == nullptr) return kErrArgs;
+  std::vector<int64_t> row0((size_t)nops, 0), total((size_t)nops);
+  for (int64_t i = 0; i < nops; i++) total[(size_t)i] = specs[i].rows;
+  return create(specs, row0.data(), total.data(), nops, q4, nullptr, out);
+}
+
+int64_t chain_create_sharded(const ChainOpSpec* specs, const int64_t* row0,
+                             const int64_t* total_rows, int64_t nops, bool q4,
+                             const ChainShard& shard, ChainHost** out) {
+  if (row0 == nullptr || total_rows == nullptr) return kErrArgs;
+  return create(specs, row0, total_rows, nops, q4, &shard, out);
+}
+
 void chain_destroy(ChainHost* h) {
   if (h == nullptr) return;
   if (h->ops_dev != nullptr) cudaFree(h->ops_dev);
-  if (h->counters != nullptr) cudaFree(h->counters);
+  if (h->counters != nullptr && h->owns_counters) cudaFree(h->counters);
   delete h;
 }
 
@@ -543,7 +663,7 @@ static int64_t chain_launch_t(ChainHost* h, uint32_t* status, cudaStream_t strea
   cfg.numAttrs = 2;
   const ChainOpDev* ops = h->ops_dev;
   return cudaLaunchKernelEx(&cfg, kern, ops, h->nops, h->counters, status, stages, h->max_blocks,
-                            chain_l2_ahead()) ==
+                            chain_l2_ahead(), h->peers) ==
                  cudaSuccess
              ? kOk
              : kErrCuda;
@@ -557,7 +677,7 @@ int64_t chain_launch(ChainHost* h, uint32_t* status, cudaStream_t stream, bool p
 
 int64_t chain_reset(ChainHost* h, cudaStream_t stream) {
   if (h == nullptr) return kErrArgs;
-  return cudaMemsetAsync(h->counters, 0, sizeof(int) * (size_t)(h->nops + 1), stream) == cudaSuccess
+  return cudaMemsetAsync(h->counters, 0, sizeof(int) * (size_t)(h->nops + 2), stream) == cudaSuccess
              ? kOk
              : kErrCuda;
 }

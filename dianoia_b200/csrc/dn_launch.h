@@ -69,6 +69,20 @@ struct ChainOpSpec {
 };
 struct ChainHost;
 int64_t chain_create(const ChainOpSpec* specs, int64_t nops, bool q4, ChainHost** out);
+// A chain whose ops are split by output rows over `world` GPUs: op i of this
+// rank computes rows row0[i] .. row0[i] + rows of total_rows[i], and every
+// tile's QA output goes to the same place in every rank's region
+// (bases[p]: rank p's region as mapped here; the local one is bases[rank]);
+// `counters` (nops + 2 ints) lies in the local region.
+struct ChainShard {
+  int64_t rank, world;
+  const void* const* bases;
+  int64_t region_bytes;
+  int* counters;
+};
+int64_t chain_create_sharded(const ChainOpSpec* specs, const int64_t* row0,
+                             const int64_t* total_rows, int64_t nops, bool q4,
+                             const ChainShard& shard, ChainHost** out);
 void chain_destroy(ChainHost* h);
 int64_t chain_launch(ChainHost* h, uint32_t* status, cudaStream_t stream, bool pdl);
 int64_t chain_reset(ChainHost* h, cudaStream_t stream);

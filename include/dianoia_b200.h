@@ -221,12 +221,41 @@ typedef struct dn_chain_op {
 /* Validates the ops, encodes their TMA descriptors and copies the op table to
  * device memory (the chain's only allocations); *chain receives a handle. */
 int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, void** chain);
+/* Device memory that the other GPUs of this node can map: dn_peer_alloc
+ * allocates `bytes` (zeroed) on the current device and writes a
+ * DN_PEER_HANDLE_BYTES-byte handle to pass to the other processes;
+ * dn_peer_open maps another process's memory from its handle (on any GPU of
+ * the node, reached over NVLink); dn_peer_close unmaps it, dn_peer_free frees
+ * one's own. */
+#define DN_PEER_HANDLE_BYTES 64
+int64_t dn_peer_alloc(int64_t bytes, void** ptr, void* handle);
+int64_t dn_peer_open(const void* handle, void** ptr);
+int64_t dn_peer_close(void* ptr);
+int64_t dn_peer_free(void* ptr);
+
+/* A decode chain split by output rows over `world` GPUs (1..8), one process
+ * per GPU: this rank's op i holds rows row0[i] .. row0[i] + rows of the
+ * total_rows[i] rows of the whole projection (row0 a multiple of 32; rows too
+ * when the op has QA outputs). Its outputs are the WHOLE projection's: ys
+ * (here only, indexed by the whole projection's rows) and ya, where every
+ * tile's QA block is also stored into every other rank's copy, over NVLink,
+ * and the tile counted in every rank's counters, so no collective is needed
+ * between ops. bases[p] is rank p's region (dn_peer_alloc memory, the same
+ * layout on every rank) as mapped in this process (bases[rank] its own);
+ * every ya and `counters` (nops + 2 int32, zero before the first run) must
+ * lie in the local region at the same offsets on every rank. Every rank runs
+ * the chain once per token; dn_chain_reset must be called on all ranks
+ * together. */
+int64_t dn_chain_create_sharded(int64_t format, const dn_chain_op* ops, const int64_t* row0,
+                                const int64_t* total_rows, int64_t nops, int64_t rank,
+                                int64_t world, void* const* bases, int64_t region_bytes,
+                                int32_t* counters, void** chain);
 /* Runs the chain on `stream` (asynchronous; capturable in a CUDA graph).
  * DN_FLAG_PDL lets the weights start streaming while the previous kernel
  * finishes; inputs with dep = -1 are read only after it completes. */
 int64_t dn_chain_run(void* chain, int64_t flags, void* stream);
-/* Clears the chain's completion counters (only needed after a run that
- * reported a bounded-wait timeout; a completed run leaves them cleared). */
+/* Clears the chain's completion counters and its run index (only needed
+ * after a run that reported a bounded-wait timeout). */
 int64_t dn_chain_reset(void* chain, void* stream);
 int64_t dn_chain_destroy(void* chain);
 
