@@ -536,10 +536,9 @@ def main():
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
-        # Keep stdout to the one JSON line: NCCL's own log lines, when they
-        # are switched on without a file, go to stderr.
-        if os.environ.get("NCCL_DEBUG") and not os.environ.get("NCCL_DEBUG_FILE"):
-            os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
+        # Keep stdout to the one JSON line: NCCL's own log lines (switched on
+        # by the environment or an nccl.conf) go to stderr.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
     from dianoia_b200 import _lib
