@@ -52,6 +52,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr int kSlots = (int)kTmemCols / kTileTok;  // D slots: blocks in flight between MMA and drain
 constexpr int kMaxSmemTc = 226 * 1024;
 
+// The odd-block drain warps hand their f32 sums to the even ones here:
+// 128 rows x 64 tokens.
+constexpr int kXchgBytes = kTileRows * kTileTok * 4;
 constexpr int kSxBytes = kBlocksPerStage * kTileTok * 4;   // activation scales, block-major
 constexpr int kSwBytes = kTileRows * kBlocksPerStage * 4;   // weight scales, row-major (f32)
 
@@ -156,6 +159,47 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
       : "memory");
 }
 
+// 64 columns (a whole D slot) of the warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, int32_t (&v)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, "
+      "%45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, "
+      "%62, %63}, [%64];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]),
+        "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]),
+        "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]),
+        "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]),
+        "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]),
+        "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]),
+        "=r"(v[62]), "=r"(v[63])
+      : "r"(taddr)
+      : "memory");
+}
+// Waits for the warp's TMEM loads, tied to the 64 registers they write.
+__device__ __forceinline__ void tmem_wait_ld64(int32_t (&v)[64]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
+        "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]),
+        "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]),
+        "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]),
+        "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31]));
+  asm volatile(
+      ""
+      : "+r"(v[32]), "+r"(v[33]), "+r"(v[34]), "+r"(v[35]), "+r"(v[36]), "+r"(v[37]),
+        "+r"(v[38]), "+r"(v[39]), "+r"(v[40]), "+r"(v[41]), "+r"(v[42]), "+r"(v[43]),
+        "+r"(v[44]), "+r"(v[45]), "+r"(v[46]), "+r"(v[47]), "+r"(v[48]), "+r"(v[49]),
+        "+r"(v[50]), "+r"(v[51]), "+r"(v[52]), "+r"(v[53]), "+r"(v[54]), "+r"(v[55]),
+        "+r"(v[56]), "+r"(v[57]), "+r"(v[58]), "+r"(v[59]), "+r"(v[60]), "+r"(v[61]),
+        "+r"(v[62]), "+r"(v[63]));
+}
+
 // Shared-memory matrix descriptor for a K-major, 128-byte-swizzled operand
 // tile whose rows are 128 bytes: 8-row groups 1024 bytes apart (SBO), version
 // 1, layout SWIZZLE_128B. `addr` may be advanced by 32 bytes within the
@@ -215,13 +259,15 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   using S = TcShape<Q4>;
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)stages * S::kStageBytes);
+  float* xchg = reinterpret_cast<float*>(smem + (int64_t)stages * S::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)stages * S::kStageBytes + kXchgBytes);
   uint64_t* conv = full + stages;
   uint64_t* empty = conv + stages;
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + kSlots;
   uint64_t* done = tempty + kSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* xbar = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -243,9 +289,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     }
     for (int q = 0; q < kSlots; q++) {
       mbar_init(&tfull[q], 1);
-      mbar_init(&tempty[q], kEpiWarps);
+      mbar_init(&tempty[q], kEpiWarps / 2);  // a slot is drained by one warp per lane quarter
     }
     mbar_init(done, 1);
+    mbar_init(xbar, (kEpiWarps / 2) * 32);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -377,35 +424,26 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     }
   } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ drain
+    // Two warps per TMEM lane quarter, one taking the even blocks and one the
+    // odd ones, each reading a block's whole 64-column slot: while one waits
+    // for its TMEM load (tcgen05.wait::ld waits for all of a thread's loads,
+    // so a warp cannot keep a second one in flight), the other computes. The
+    // two partial f32 sums are added at the end.
     const int quarter = warp & 3;               // TMEM lanes this warp may access
-    const int half = (warp - 2) >> 2;           // which group of kEpiCols token columns
+    const int parity = (warp - 2) >> 2;         // even or odd blocks
     const int row_local = quarter * 32 + lane;
     const int64_t row = row0 + row_local;
-    const int col0 = half * kEpiCols;
-    uint64_t acc[kEpiCols / 2];                  // f32 pairs: tokens col0 + 2i, col0 + 2i + 1
+    uint64_t acc[kTileTok / 2];                 // f32 pairs: tokens 2i, 2i + 1
 #pragma unroll
-    for (int j = 0; j < kEpiCols / 2; j++) acc[j] = 0;
-    // Blocks in order; the TMEM load of block b + 1 is in flight while block
-    // b is scaled and accumulated. Stage / slot indices and their phases
-    // are running counters (no division in the loop).
+    for (int j = 0; j < kTileTok / 2; j++) acc[j] = 0;
     const int nblk = (int)blocks;
-    int32_t dn[32];
-    int slot = 0;
+    int32_t dn[kTileTok];
+    int slot = parity;                          // slot of block b is b % kSlots
     uint32_t tph = 0;
-    auto start_load = [&](int sl, uint32_t ph) -> bool {
-      bool got = !abort_flag && mbar_wait_bounded(&tfull[sl], ph, a.status, kStatusMmaTimeout);
-      if (!__all_sync(0xffffffffu, got)) {  // tcgen05.ld is warp-wide: all lanes agree
-        abort_flag = 1;
-        return false;
-      }
-      tc_fence_after();
-      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sl * kTileTok + col0), dn);
-      return true;
-    };
-    bool alive = nblk > 0 && start_load(0, 0);
     int st = 0;
     uint32_t sph = 0;
-    for (int blk = 0; blk < nblk && alive;) {
+    bool alive = true;
+    for (int k = 0; k < nst && alive; k++) {
       // This stage's scales (the producer's cp.async copies) have landed.
       bool got = !abort_flag && mbar_wait_bounded(&full[st], sph, a.status, kStatusTmaTimeout);
       if (!__all_sync(0xffffffffu, got)) {
@@ -424,33 +462,37 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
         const float4 f = *reinterpret_cast<const float4*>(stage_sw(st) + row_local * kBlocksPerStage);
         sws[0] = f.x; sws[1] = f.y; sws[2] = f.z; sws[3] = f.w;
       }
-      const float* sx_stage = stage_sx(st) + col0;
 #pragma unroll
-      for (int q = 0; q < kBlocksPerStage; q++) {
-        if (blk >= nblk || !alive) break;
-        tmem_wait_ld_regs(dn);
-        int32_t d0[32];
-#pragma unroll
-        for (int j = 0; j < 32; j++) d0[j] = dn[j];
+      for (int q = parity; q < kBlocksPerStage; q += 2) {
+        const int blk = k * kBlocksPerStage + q;
+        if (blk >= nblk) break;
+        got = !abort_flag && mbar_wait_bounded(&tfull[slot], tph, a.status, kStatusMmaTimeout);
+        if (!__all_sync(0xffffffffu, got)) {  // tcgen05.ld is warp-wide: all lanes agree
+          abort_flag = 1;
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_ld64(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slot * kTileTok), dn);
+        tmem_wait_ld64(dn);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[slot]);
-        if (++slot == kSlots) {
-          slot = 0;
+        if (lane == 0) mbar_arrive(&tempty[slot]);  // the MMA may refill the slot
+        slot += 2;
+        if (slot >= kSlots) {
+          slot -= kSlots;
           tph ^= 1u;
         }
-        if (blk + 1 < nblk && !start_load(slot, tph)) alive = false;
         const uint64_t sw2 = f2_pack(sws[q], sws[q]);
-        const float* sxq = sx_stage + q * kTileTok;
+        const float* sxq = stage_sx(st) + q * kTileTok;
 #pragma unroll
-        for (int j = 0; j < kEpiCols; j += 4) {
+        for (int j = 0; j < kTileTok; j += 4) {
           const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
           // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
-          acc[j / 2] = f2_fma(i2_to_f2(d0[j], d0[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
-          acc[j / 2 + 1] = f2_fma(i2_to_f2(d0[j + 2], d0[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
+          acc[j / 2] = f2_fma(i2_to_f2(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
+          acc[j / 2 + 1] = f2_fma(i2_to_f2(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
                                   acc[j / 2 + 1]);
         }
-        blk++;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -459,12 +501,27 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
         sph ^= 1u;
       }
     }
-    if (row < a.rows && !abort_flag) {
+    // The odd warp hands its sums to the even warp of its lane quarter
+    // (token-major in the exchange buffer, so a warp's stores hit 32 banks).
+    float* x = xchg + (int64_t)quarter * 32 * kTileTok;
+    if (parity == 1) {
 #pragma unroll
-      for (int j = 0; j < kEpiCols / 2; j++) {
-        const int64_t t = tok0 + col0 + 2 * j;
-        if (t < a.n) a.ys[t * a.ldy + row] = __uint_as_float((uint32_t)acc[j]);
-        if (t + 1 < a.n) a.ys[(t + 1) * a.ldy + row] = __uint_as_float((uint32_t)(acc[j] >> 32));
+      for (int j = 0; j < kTileTok / 2; j++) {
+        x[(2 * j) * 32 + lane] = __uint_as_float((uint32_t)acc[j]);
+        x[(2 * j + 1) * 32 + lane] = __uint_as_float((uint32_t)(acc[j] >> 32));
+      }
+      mbar_arrive(xbar);
+    } else {
+      const bool got = !abort_flag && mbar_wait_bounded(xbar, 0, a.status, kStatusMmaTimeout);
+      if (got && row < a.rows) {
+#pragma unroll
+        for (int j = 0; j < kTileTok / 2; j++) {
+          const int64_t t = tok0 + 2 * j;
+          const float y0 = __fadd_rn(__uint_as_float((uint32_t)acc[j]), x[(2 * j) * 32 + lane]);
+          const float y1 = __fadd_rn(__uint_as_float((uint32_t)(acc[j] >> 32)), x[(2 * j + 1) * 32 + lane]);
+          if (t < a.n) a.ys[t * a.ldy + row] = y0;
+          if (t + 1 < a.n) a.ys[(t + 1) * a.ldy + row] = y1;
+        }
       }
     }
   } else {
@@ -513,11 +570,11 @@ template <bool Q4>
 int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   using S = TcShape<Q4>;
   const int64_t blocks = a.cols / kBlock;
-  const int64_t bar_bytes = 8 * (3 * 16 + 2 * kSlots + 2) + 16;  // up to 16 stages
-  int stages = (int)((kMaxSmemTc - 1024 - bar_bytes) / S::kStageBytes);
+  const int64_t bar_bytes = 8 * (3 * 16 + 2 * kSlots + 3) + 16;  // up to 16 stages
+  int stages = (int)((kMaxSmemTc - 1024 - kXchgBytes - bar_bytes) / S::kStageBytes);
   stages = stages > 12 ? 12 : stages;
   if (stages < 2) return kErrTooLarge;
-  const size_t smem = 1024 + (size_t)stages * S::kStageBytes + (size_t)bar_bytes;
+  const size_t smem = 1024 + (size_t)stages * S::kStageBytes + kXchgBytes + (size_t)bar_bytes;
   CUtensorMap tw, tx;
   if (Q4) {
     if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)blocks * 16,
