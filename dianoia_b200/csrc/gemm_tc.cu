@@ -15,12 +15,18 @@
 // blocks) ahead of the drain. Warp roles:
 //   warp 0      producer: per stage, TMA copies of the weights (Q8: a 128 x
 //               128-byte box, 128-byte swizzle = the UMMA K-major SW128
-//               layout; Q4: the raw 128 x 64-byte nibbles) and the
-//               activations (64 tokens x 128 bytes, SW128) for 4 blocks of K;
-//               the other lanes stage the block scales into shared memory
+//               layout; Q4: the raw 128 x 64-byte nibbles), the activations
+//               (64 tokens x 128 bytes, SW128) and both block-scale boxes
+//               for 4 blocks of K, all completing on one mbarrier. (Shapes
+//               whose scale rows TMA cannot address - blocks per row not a
+//               multiple of 4 (Q8) or 8 (Q4), or unaligned scale arrays -
+//               stage the scales with per-lane cp.async copies instead, a
+//               path several times slower per stage.)
 //   warp 1      MMA issuer: allocates 512 TMEM columns = eight D slots of 64
-//               columns; issues one MMA per block into the next slot and
-//               commits to the slot's "full" barrier
+//               columns; transposes the stage's activation scales to the
+//               block-major order the drain reads; issues one MMA per block
+//               into the next slot from an elected lane and commits to the
+//               slot's "full" barrier
 //   warps 2-9   drain ("epilogue"): two warps per TMEM lane quarter, each
 //               owning one weight row per lane and 32 token columns; the
 //               TMEM load of the next block is in flight while the current
@@ -65,7 +71,9 @@ struct TcShape {
   static constexpr int kRawOff = kABytes + kBBytes;
   static constexpr int kSxOff = kRawOff + (Q4 ? kRawBytes : 0);
   static constexpr int kSwOff = kSxOff + kSxBytes;
-  static constexpr int kStageBytes = kSwOff + kSwBytes;
+  static constexpr int kSxbOff = kSwOff + kSwBytes;   // block-major copy of sx (TMA scales)
+  static constexpr int kStageBytes = kSxbOff + kSxBytes;
+  static_assert(kStageBytes % 1024 == 0, "SW128 operand tiles need 1024-byte aligned stages");
 };
 
 struct TcArgs {
@@ -74,6 +82,7 @@ struct TcArgs {
   float* ys;
   int64_t rows, cols, n, ldy;
   uint32_t* status;
+  int tma_scales;  // scales arrive by TMA (tsw, tsx) rather than cp.async
 };
 
 // ----------------------------------------------------------- tcgen05 PTX
@@ -255,7 +264,8 @@ __device__ __forceinline__ bool wait_tc(uint64_t* bar, uint32_t parity, uint32_t
 template <bool Q4>
 __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     gemm_tc_kernel(const TcArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
-                   const __grid_constant__ CUtensorMap tx) {
+                   const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tsw,
+                   const __grid_constant__ CUtensorMap tsx) {
   using S = TcShape<Q4>;
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
@@ -263,7 +273,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)stages * S::kStageBytes + kXchgBytes);
   uint64_t* conv = full + stages;
   uint64_t* empty = conv + stages;
-  uint64_t* tfull = empty + stages;
+  uint64_t* sready = empty + stages;
+  uint64_t* tfull = sready + stages;
   uint64_t* tempty = tfull + kSlots;
   uint64_t* done = tempty + kSlots;
   uint64_t* xbar = done + 1;
@@ -280,12 +291,16 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   auto stage_raw = [&](int s) { return smem + (int64_t)s * S::kStageBytes + S::kRawOff; };
   auto stage_sx = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSxOff); };
   auto stage_sw = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSwOff); };
+  auto stage_sxb = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSxbOff); };
+  const bool tma_scales = a.tma_scales != 0;
 
   if (tid == 0) {
     for (int s = 0; s < stages; s++) {
-      mbar_init(&full[s], 1 + 32);           // TMA bytes + the producer lanes' scale stores
+      // TMA bytes (+ the producer lanes' cp.async scale copies on that path)
+      mbar_init(&full[s], tma_scales ? 1 : 1 + 32);
       mbar_init(&conv[s], kConvWarps * 32);
       mbar_init(&empty[s], 1 + kEpiWarps);   // MMA commit + every drain warp
+      mbar_init(&sready[s], 32);             // the MMA warp's lanes, after the sx transpose
     }
     for (int q = 0; q < kSlots; q++) {
       mbar_init(&tfull[q], 1);
@@ -307,32 +322,52 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Lane 0 issues the TMA copies; all lanes stage the stage's scales into
-    // shared memory: activation scales block-major (so the drain reads four
-    // tokens in one 16-byte load), weight scales as f32 per row.
+    // One elected lane of the converged warp issues the stage's TMA copies.
+    // Stage index and phase are running counters (no division in the loop).
     if (lane == 0) {
       prefetch_tmap(&tw);
       prefetch_tmap(&tx);
+      if (tma_scales) {
+        prefetch_tmap(&tsw);
+        prefetch_tmap(&tsx);
+      }
     }
-    int k = 0;
+    __syncwarp();
+    int k = 0, s = 0;
+    uint32_t eph = 1;  // parity of empty[s] to wait for, from the ring's second pass on
     for (; k < nst; k++) {
-      const int s = k % stages;
       if (k >= stages) {
-        bool got = !abort_flag && mbar_wait_bounded(&empty[s], (uint32_t)((k / stages) - 1) & 1u,
-                                                    a.status, kStatusMmaTimeout);
-        got = __all_sync(0xffffffffu, got) != 0;
-        if (!got) {
+        const bool got = !abort_flag && mbar_wait_bounded(&empty[s], eph, a.status, kStatusMmaTimeout);
+        if (!__all_sync(0xffffffffu, got)) {
           abort_flag = 1;
           break;
         }
       }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], (uint32_t)((Q4 ? kRawBytes : kABytes) + kBBytes));
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&full[s], (uint32_t)((Q4 ? kRawBytes : kABytes) + kBBytes +
+                                                   (tma_scales ? kSxBytes + kSwBytes : 0)));
         if (Q4)
           tma_load_2d(stage_raw(s), &tw, k * (kStageK / 2), (int32_t)row0, &full[s]);
         else
           tma_load_2d(stage_a(s), &tw, k * kStageK, (int32_t)row0, &full[s]);
         tma_load_2d(stage_b(s), &tx, k * kStageK, (int32_t)tok0, &full[s]);
+        if (tma_scales) {
+          // Weight scales: Q8 the stage's 4 f32 per row; Q4 the 8 fp16 per
+          // row of the pair of stages holding this one (a box starting on a
+          // 16-byte boundary), of which the drain reads its half.
+          tma_load_2d(stage_sw(s), &tsw, Q4 ? (k >> 1) * 2 * kBlocksPerStage : k * kBlocksPerStage,
+                      (int32_t)row0, &full[s]);
+          // Activation scales, token-major: 64 tokens x 4 blocks.
+          tma_load_2d(stage_sx(s), &tsx, k * kBlocksPerStage, (int32_t)tok0, &full[s]);
+        }
+      }
+      __syncwarp();
+      if (tma_scales) {
+        if (++s == stages) {
+          s = 0;
+          eph ^= 1u;
+        }
+        continue;
       }
       float* sx = stage_sx(s);
       float* sw = stage_sw(s);
@@ -384,6 +419,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       } else {
         cp_async_arrive(&full[s]);
       }
+      if (++s == stages) {
+        s = 0;
+        eph ^= 1u;
+      }
     }
     if (abort_flag && lane == 0) {
       // Let the copies already issued land before the CTA's memory goes.
@@ -393,35 +432,76 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      for (int k = 0; k < nst; k++) {
-        const int s = k % stages;
-        const uint32_t ph = (uint32_t)(k / stages) & 1u;
-        if (!wait_tc(Q4 ? &conv[s] : &full[s], ph, a.status, kStatusTmaTimeout, &abort_flag)) break;
-        tc_fence_after();
-        const uint32_t a_addr = smem_u32(stage_a(s)), b_addr = smem_u32(stage_b(s));
-        bool ok = true;
-        for (int q = 0; q < kBlocksPerStage; q++) {
-          const int blk = k * kBlocksPerStage + q;
-          if (blk >= blocks) break;
-          const int slot = blk % kSlots, use = blk / kSlots;
-          if (use > 0 && !wait_tc(&tempty[slot], (uint32_t)(use - 1) & 1u, a.status,
-                                  kStatusMmaTimeout, &abort_flag)) {
-            ok = false;
-            break;
+    // The whole warp runs the loop; one elected lane issues. The stage's
+    // operand descriptors are formed once and the blocks' K offsets (32
+    // bytes = 2 descriptor units) and D slots are constants: block b of the
+    // tile goes to D slot b % 8 = 4 * (k & 1) + q, on its (k / 2)-th use.
+    static_assert(kSlots == 2 * kBlocksPerStage, "two stages of D slots");
+    const uint32_t smem0 = smem_u32(smem);
+    int s = 0;
+    uint32_t ph = 0;
+    for (int k = 0; k < nst; k++) {
+      bool got = !abort_flag && mbar_wait_bounded(&full[s], ph, a.status, kStatusTmaTimeout);
+      if (Q4) got = got && mbar_wait_bounded(&conv[s], ph, a.status, kStatusTmaTimeout);
+      if (!__all_sync(0xffffffffu, got)) {
+        abort_flag = 1;
+        break;
+      }
+      if (tma_scales) {
+        // Activation scales [64 tokens][4 blocks] -> [4 blocks][64 tokens],
+        // so a drain warp reads four tokens of one block in one 16-byte load.
+        const float* src = stage_sx(s);
+        float* dst = stage_sxb(s);
+#pragma unroll
+        for (int t = lane; t < kTileTok; t += 32) {
+          const float4 v = *reinterpret_cast<const float4*>(src + t * kBlocksPerStage);
+          dst[0 * kTileTok + t] = v.x;
+          dst[1 * kTileTok + t] = v.y;
+          dst[2 * kTileTok + t] = v.z;
+          dst[3 * kTileTok + t] = v.w;
+        }
+        mbar_arrive(&sready[s]);
+      }
+      tc_fence_after();
+      const uint32_t a_addr = smem0 + (uint32_t)s * (uint32_t)S::kStageBytes;
+      const uint64_t ad = sw128_desc(a_addr), bd = sw128_desc(a_addr + kABytes);
+      const int slot0 = (k & 1) * kBlocksPerStage;
+      const uint32_t tph = (uint32_t)((k >> 1) - 1) & 1u;
+      const int nq = (int)min64(kBlocksPerStage, blocks - (int64_t)k * kBlocksPerStage);
+      bool ok = true;
+#pragma unroll
+      for (int q = 0; q < kBlocksPerStage; q++) {
+        if (q < nq) {
+          if (k >= 2) {
+            const bool free = !abort_flag && mbar_wait_bounded(&tempty[slot0 + q], tph, a.status,
+                                                               kStatusMmaTimeout);
+            if (!__all_sync(0xffffffffu, free)) {
+              abort_flag = 1;
+              ok = false;
+              break;
+            }
           }
           tc_fence_after();
-          mma_i8(tmem + (uint32_t)(slot * kTileTok), sw128_desc(a_addr + q * 32),
-                 sw128_desc(b_addr + q * 32), kIdescI8);
-          mma_commit(&tfull[slot]);
+          if (elect_one()) {
+            mma_i8(tmem + (uint32_t)((slot0 + q) * kTileTok), ad + (uint64_t)(2 * q),
+                   bd + (uint64_t)(2 * q), kIdescI8);
+            mma_commit(&tfull[slot0 + q]);
+          }
+          __syncwarp();
         }
-        mma_commit(&empty[s]);
-        if (!ok) break;
       }
-      // Every MMA issued has completed once `done` arrives.
-      mma_commit(done);
-      mbar_wait_bounded(done, 0, a.status, kStatusMmaTimeout);
+      if (elect_one()) mma_commit(&empty[s]);
+      __syncwarp();
+      if (!ok) break;
+      if (++s == stages) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
+    // Every MMA issued has completed once `done` arrives.
+    if (elect_one()) mma_commit(done);
+    __syncwarp();
+    mbar_wait_bounded(done, 0, a.status, kStatusMmaTimeout);
   } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ drain
     // Two warps per TMEM lane quarter, one taking the even blocks and one the
@@ -444,16 +524,21 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     uint32_t sph = 0;
     bool alive = true;
     for (int k = 0; k < nst && alive; k++) {
-      // This stage's scales (the producer's cp.async copies) have landed.
+      // This stage's scales have landed (and, with TMA scales, the MMA warp
+      // has written the block-major copy of the activation scales).
       bool got = !abort_flag && mbar_wait_bounded(&full[st], sph, a.status, kStatusTmaTimeout);
+      if (tma_scales) got = got && mbar_wait_bounded(&sready[st], sph, a.status, kStatusMmaTimeout);
       if (!__all_sync(0xffffffffu, got)) {
         abort_flag = 1;
         break;
       }
       float sws[kBlocksPerStage];
       if (Q4) {
-        const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(stage_sw(st)) +
-                                                        row_local * kBlocksPerStage);
+        // TMA scales: 8 fp16 per row covering stages 2j and 2j + 1.
+        const uint16_t* w16 = reinterpret_cast<const uint16_t*>(stage_sw(st)) +
+                              (tma_scales ? row_local * 2 * kBlocksPerStage + (k & 1) * kBlocksPerStage
+                                          : row_local * kBlocksPerStage);
+        const uint2 h = *reinterpret_cast<const uint2*>(w16);
         sws[0] = half_bits_to_float((uint16_t)h.x);
         sws[1] = half_bits_to_float((uint16_t)(h.x >> 16));
         sws[2] = half_bits_to_float((uint16_t)h.y);
@@ -484,7 +569,7 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           tph ^= 1u;
         }
         const uint64_t sw2 = f2_pack(sws[q], sws[q]);
-        const float* sxq = stage_sx(st) + q * kTileTok;
+        const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok;
 #pragma unroll
         for (int j = 0; j < kTileTok; j += 4) {
           const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
@@ -527,10 +612,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   } else {
     // ------------------------------------------------------------ Q4 expansion
     const int ct = tid - (2 + kEpiWarps) * 32;  // 0 .. 63
+    int s = 0;
+    uint32_t ph = 0;
     for (int k = 0; k < nst; k++) {
-      const int s = k % stages;
-      if (!wait_tc(&full[s], (uint32_t)(k / stages) & 1u, a.status, kStatusTmaTimeout, &abort_flag))
-        break;
+      if (!wait_tc(&full[s], ph, a.status, kStatusTmaTimeout, &abort_flag)) break;
       const uint8_t* raw = stage_raw(s);
       uint8_t* dst = stage_a(s);
       // One (row, block) per task: 16 nibble bytes -> two swizzled 16-byte
@@ -555,6 +640,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       }
       fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
       mbar_arrive(&conv[s]);
+      if (++s == stages) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
   }
 
@@ -570,7 +659,7 @@ template <bool Q4>
 int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   using S = TcShape<Q4>;
   const int64_t blocks = a.cols / kBlock;
-  const int64_t bar_bytes = 8 * (3 * 16 + 2 * kSlots + 3) + 16;  // up to 16 stages
+  const int64_t bar_bytes = 8 * (4 * 16 + 2 * kSlots + 3) + 16;  // up to 16 stages
   int stages = (int)((kMaxSmemTc - 1024 - kXchgBytes - bar_bytes) / S::kStageBytes);
   stages = stages > 12 ? 12 : stages;
   if (stages < 2) return kErrTooLarge;
@@ -588,6 +677,21 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   if (!encode_tmap_2d(&tx, a.xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)a.cols, (uint64_t)a.n,
                       (uint64_t)a.cols, kStageK, kTileTok, true))
     return kErrUnsupported;
+  // Scales by TMA when their rows are addressable: 16-byte aligned arrays and
+  // rows whose byte length is a multiple of 16 (the Q4 box is 8 fp16 wide).
+  const bool tma_scales = blocks % (Q4 ? 8 : 4) == 0 && ((uintptr_t)a.scales & 15) == 0 &&
+                          ((uintptr_t)a.xsc & 15) == 0;
+  CUtensorMap tsw = tw, tsx = tx;  // unused copies unless tma_scales
+  if (tma_scales) {
+    const bool ok_w =
+        Q4 ? encode_tmap_2d(&tsw, a.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)blocks,
+                            (uint64_t)a.rows, (uint64_t)blocks * 2, 2 * kBlocksPerStage, kTileRows, false)
+           : encode_tmap_2d(&tsw, a.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)blocks,
+                            (uint64_t)a.rows, (uint64_t)blocks * 4, kBlocksPerStage, kTileRows, false);
+    if (!ok_w || !encode_tmap_2d(&tsx, a.xsc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)blocks,
+                                 (uint64_t)a.n, (uint64_t)blocks * 4, kBlocksPerStage, kTileTok, false))
+      return kErrUnsupported;
+  }
   auto kern = gemm_tc_kernel<Q4>;
   static bool configured[64] = {};
   int dev = 0;
@@ -598,10 +702,10 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
       return kErrCuda;
     configured[dev & 63] = true;
   }
-  TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status};
+  TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, tma_scales ? 1 : 0};
   const dim3 grid((unsigned)((a.rows + kTileRows - 1) / kTileRows),
                   (unsigned)((a.n + kTileTok - 1) / kTileTok), 1);
-  kern<<<grid, S::kThreads, smem, stream>>>(t, stages, tw, tx);
+  kern<<<grid, S::kThreads, smem, stream>>>(t, stages, tw, tx, tsw, tsx);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
