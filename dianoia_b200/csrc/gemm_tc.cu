@@ -27,11 +27,11 @@
 //               block-major order the drain reads; issues one MMA per block
 //               into the next slot from an elected lane and commits to the
 //               slot's "full" barrier
-//   warps 2-9   drain ("epilogue"): two warps per TMEM lane quarter, each
-//               owning one weight row per lane and 32 token columns; the
-//               TMEM load of the next block is in flight while the current
-//               one is scaled and accumulated (packed f32x2 math)
-//   warps 10-11 (Q4) nibble expansion: raw nibbles -> int8 (q - 8) in the
+//   warps 2-17  drain ("epilogue"): four warps per TMEM lane quarter (even
+//               or odd blocks x low or high 32 token columns), each owning
+//               one weight row per lane; per block a TMEM load, then the
+//               scale-and-accumulate in packed f32x2 math
+//   warps 18-19 (Q4) nibble expansion: raw nibbles -> int8 (q - 8) in the
 //               SW128 K-major layout the MMA reads
 // Every mbarrier wait is bounded; on a timeout the kernel records it, lets
 // its copies and MMAs finish (bounded), frees its TMEM and returns.
@@ -51,9 +51,9 @@ constexpr int kBlocksPerStage = kStageK / kBlock;
 constexpr int kABytes = kTileRows * kStageK;   // 16 KB
 constexpr int kBBytes = kTileTok * kStageK;    // 16 KB
 constexpr int kRawBytes = kTileRows * (kStageK / 2);  // Q4 nibbles: 8 KB
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
 constexpr int kConvWarps = 2;
-constexpr int kEpiCols = kTileTok / (kEpiWarps / 4);  // columns per drain warp
+constexpr int kEpiCols = kTileTok / 2;  // token columns per drain warp
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSlots = (int)kTmemCols / kTileTok;  // D slots: blocks in flight between MMA and drain
 constexpr int kMaxSmemTc = 226 * 1024;
@@ -299,12 +299,12 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       // TMA bytes (+ the producer lanes' cp.async scale copies on that path)
       mbar_init(&full[s], tma_scales ? 1 : 1 + 32);
       mbar_init(&conv[s], kConvWarps * 32);
-      mbar_init(&empty[s], 1 + kEpiWarps);   // MMA commit + every drain warp
+      mbar_init(&empty[s], 1 + kEpiWarps * 32);  // MMA commit + every drain lane
       mbar_init(&sready[s], 32);             // the MMA warp's lanes, after the sx transpose
     }
     for (int q = 0; q < kSlots; q++) {
       mbar_init(&tfull[q], 1);
-      mbar_init(&tempty[q], kEpiWarps / 2);  // a slot is drained by one warp per lane quarter
+      mbar_init(&tempty[q], kEpiWarps / 2 * 32);  // drained by one warp per lane quarter, all lanes
     }
     mbar_init(done, 1);
     mbar_init(xbar, (kEpiWarps / 2) * 32);
@@ -469,28 +469,33 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       const uint32_t tph = (uint32_t)((k >> 1) - 1) & 1u;
       const int nq = (int)min64(kBlocksPerStage, blocks - (int64_t)k * kBlocksPerStage);
       bool ok = true;
+      if (k >= 2) {
+        // The stage's D slots held stage k - 2's blocks. Each drain parity
+        // frees its slots in block order, so the last even and the last odd
+        // slot this stage uses cover all of them: two probes per stage.
+        const int qe = (nq - 1) & ~1, qo = nq >= 2 ? ((nq - 2) & ~1) + 1 : -1;
+        ok = !abort_flag && mbar_wait_bounded(&tempty[slot0 + qe], tph, a.status, kStatusMmaTimeout);
+        if (qo >= 0)
+          ok = ok && mbar_wait_bounded(&tempty[slot0 + qo], tph, a.status, kStatusMmaTimeout);
+        ok = __all_sync(0xffffffffu, ok) != 0;
+        if (!ok) abort_flag = 1;
+      }
+      tc_fence_after();
+      // One elected section per stage: the control flow around single-lane
+      // instructions costs more than the MMAs themselves.
+      if (elect_one()) {
+        if (ok) {
 #pragma unroll
-      for (int q = 0; q < kBlocksPerStage; q++) {
-        if (q < nq) {
-          if (k >= 2) {
-            const bool free = !abort_flag && mbar_wait_bounded(&tempty[slot0 + q], tph, a.status,
-                                                               kStatusMmaTimeout);
-            if (!__all_sync(0xffffffffu, free)) {
-              abort_flag = 1;
-              ok = false;
-              break;
+          for (int q = 0; q < kBlocksPerStage; q++) {
+            if (q < nq) {
+              mma_i8(tmem + (uint32_t)((slot0 + q) * kTileTok), ad + (uint64_t)(2 * q),
+                     bd + (uint64_t)(2 * q), kIdescI8);
+              mma_commit(&tfull[slot0 + q]);
             }
           }
-          tc_fence_after();
-          if (elect_one()) {
-            mma_i8(tmem + (uint32_t)((slot0 + q) * kTileTok), ad + (uint64_t)(2 * q),
-                   bd + (uint64_t)(2 * q), kIdescI8);
-            mma_commit(&tfull[slot0 + q]);
-          }
-          __syncwarp();
         }
+        mma_commit(&empty[s]);
       }
-      if (elect_one()) mma_commit(&empty[s]);
       __syncwarp();
       if (!ok) break;
       if (++s == stages) {
@@ -504,20 +509,24 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     mbar_wait_bounded(done, 0, a.status, kStatusMmaTimeout);
   } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ drain
-    // Two warps per TMEM lane quarter, one taking the even blocks and one the
-    // odd ones, each reading a block's whole 64-column slot: while one waits
-    // for its TMEM load (tcgen05.wait::ld waits for all of a thread's loads,
-    // so a warp cannot keep a second one in flight), the other computes. The
-    // two partial f32 sums are added at the end.
+    // Four warps per TMEM lane quarter: even or odd blocks times the low or
+    // high 32 token columns. Each block's step is a short serial chain in
+    // one warp (barrier probe, TMEM load, arrival, 32 columns of math), so
+    // four such warps per scheduler hide one another's latencies
+    // (tcgen05.wait::ld waits for all of a thread's loads, so a warp cannot
+    // keep a second one in flight). The even and odd partial f32 sums are
+    // added at the end.
     const int quarter = warp & 3;               // TMEM lanes this warp may access
-    const int parity = (warp - 2) >> 2;         // even or odd blocks
+    const int sub = (warp - 2) >> 2;            // 0 .. 3
+    const int parity = sub & 1;                 // even or odd blocks
+    const int col0 = (sub >> 1) * kEpiCols;     // first token column of this warp
     const int row_local = quarter * 32 + lane;
     const int64_t row = row0 + row_local;
-    uint64_t acc[kTileTok / 2];                 // f32 pairs: tokens 2i, 2i + 1
+    uint64_t acc[kEpiCols / 2];                 // f32 pairs: tokens col0 + 2i, col0 + 2i + 1
 #pragma unroll
-    for (int j = 0; j < kTileTok / 2; j++) acc[j] = 0;
+    for (int j = 0; j < kEpiCols / 2; j++) acc[j] = 0;
     const int nblk = (int)blocks;
-    int32_t dn[kTileTok];
+    int32_t dn[kEpiCols];
     int slot = parity;                          // slot of block b is b % kSlots
     uint32_t tph = 0;
     int st = 0;
@@ -558,20 +567,19 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           break;
         }
         tc_fence_after();
-        tmem_ld64(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slot * kTileTok), dn);
-        tmem_wait_ld64(dn);
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slot * kTileTok + col0), dn);
+        tmem_wait_ld_regs(dn);
         tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[slot]);  // the MMA may refill the slot
+        mbar_arrive(&tempty[slot]);  // every lane, once its own load is done: the MMA may refill the slot
         slot += 2;
         if (slot >= kSlots) {
           slot -= kSlots;
           tph ^= 1u;
         }
         const uint64_t sw2 = f2_pack(sws[q], sws[q]);
-        const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok;
+        const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok + col0;
 #pragma unroll
-        for (int j = 0; j < kTileTok; j += 4) {
+        for (int j = 0; j < kEpiCols; j += 4) {
           const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
           // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
           acc[j / 2] = f2_fma(i2_to_f2(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
@@ -579,8 +587,7 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
                                   acc[j / 2 + 1]);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
+      mbar_arrive(&empty[st]);  // every lane: done with the stage's scales
       if (++st == stages) {
         st = 0;
         sph ^= 1u;
@@ -588,10 +595,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     }
     // The odd warp hands its sums to the even warp of its lane quarter
     // (token-major in the exchange buffer, so a warp's stores hit 32 banks).
-    float* x = xchg + (int64_t)quarter * 32 * kTileTok;
+    float* x = xchg + (int64_t)quarter * 32 * kTileTok + col0 * 32;
     if (parity == 1) {
 #pragma unroll
-      for (int j = 0; j < kTileTok / 2; j++) {
+      for (int j = 0; j < kEpiCols / 2; j++) {
         x[(2 * j) * 32 + lane] = __uint_as_float((uint32_t)acc[j]);
         x[(2 * j + 1) * 32 + lane] = __uint_as_float((uint32_t)(acc[j] >> 32));
       }
@@ -600,8 +607,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       const bool got = !abort_flag && mbar_wait_bounded(xbar, 0, a.status, kStatusMmaTimeout);
       if (got && row < a.rows) {
 #pragma unroll
-        for (int j = 0; j < kTileTok / 2; j++) {
-          const int64_t t = tok0 + 2 * j;
+        for (int j = 0; j < kEpiCols / 2; j++) {
+          const int64_t t = tok0 + col0 + 2 * j;
           const float y0 = __fadd_rn(__uint_as_float((uint32_t)acc[j]), x[(2 * j) * 32 + lane]);
           const float y1 = __fadd_rn(__uint_as_float((uint32_t)(acc[j] >> 32)), x[(2 * j + 1) * 32 + lane]);
           if (t < a.n) a.ys[t * a.ldy + row] = y0;
