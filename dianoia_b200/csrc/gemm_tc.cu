@@ -24,9 +24,13 @@
 //               path several times slower per stage.)
 //   warp 1      MMA issuer: allocates 512 TMEM columns = eight D slots of 64
 //               columns; transposes the stage's activation scales to the
-//               block-major order the drain reads; issues one MMA per block
-//               into the next slot from an elected lane and commits to the
-//               slot's "full" barrier
+//               block-major order the drain reads; from an elected lane
+//               issues the stage's MMAs (one per block, each into its own D
+//               slot) and commits the stage to its "dready" barrier. A
+//               stage's slots are reused two stages later, once the drain
+//               has released that stage: one handshake per stage each way,
+//               since every mbarrier operation costs far more than the math
+//               it guards
 //   warps 2-17  drain ("epilogue"): four warps per TMEM lane quarter (even
 //               or odd blocks x low or high 32 token columns), each owning
 //               one weight row per lane; per block a TMEM load, then the
@@ -273,10 +277,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)stages * S::kStageBytes + kXchgBytes);
   uint64_t* conv = full + stages;
   uint64_t* empty = conv + stages;
-  uint64_t* sready = empty + stages;
-  uint64_t* tfull = sready + stages;
-  uint64_t* tempty = tfull + kSlots;
-  uint64_t* done = tempty + kSlots;
+  uint64_t* dready = empty + stages;
+  uint64_t* done = dready + stages;
   uint64_t* xbar = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
   __shared__ volatile int abort_flag;
@@ -300,11 +302,9 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       mbar_init(&full[s], tma_scales ? 1 : 1 + 32);
       mbar_init(&conv[s], kConvWarps * 32);
       mbar_init(&empty[s], 1 + kEpiWarps * 32);  // MMA commit + every drain lane
-      mbar_init(&sready[s], 32);             // the MMA warp's lanes, after the sx transpose
-    }
-    for (int q = 0; q < kSlots; q++) {
-      mbar_init(&tfull[q], 1);
-      mbar_init(&tempty[q], kEpiWarps / 2 * 32);  // drained by one warp per lane quarter, all lanes
+      // The stage's MMAs have completed (commit), and with TMA scales the MMA
+      // warp's lanes have written the block-major activation scales.
+      mbar_init(&dready[s], tma_scales ? 1 + 32 : 1);
     }
     mbar_init(done, 1);
     mbar_init(xbar, (kEpiWarps / 2) * 32);
@@ -438,8 +438,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     // tile goes to D slot b % 8 = 4 * (k & 1) + q, on its (k / 2)-th use.
     static_assert(kSlots == 2 * kBlocksPerStage, "two stages of D slots");
     const uint32_t smem0 = smem_u32(smem);
-    int s = 0;
-    uint32_t ph = 0;
+    int s = 0, s2 = 0;  // ring indices of stages k and k - 2
+    uint32_t ph = 0, ph2 = 0;
     for (int k = 0; k < nst; k++) {
       bool got = !abort_flag && mbar_wait_bounded(&full[s], ph, a.status, kStatusTmaTimeout);
       if (Q4) got = got && mbar_wait_bounded(&conv[s], ph, a.status, kStatusTmaTimeout);
@@ -460,25 +460,24 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           dst[2 * kTileTok + t] = v.z;
           dst[3 * kTileTok + t] = v.w;
         }
-        mbar_arrive(&sready[s]);
+        mbar_arrive(&dready[s]);
       }
       tc_fence_after();
       const uint32_t a_addr = smem0 + (uint32_t)s * (uint32_t)S::kStageBytes;
       const uint64_t ad = sw128_desc(a_addr), bd = sw128_desc(a_addr + kABytes);
       const int slot0 = (k & 1) * kBlocksPerStage;
-      const uint32_t tph = (uint32_t)((k >> 1) - 1) & 1u;
       const int nq = (int)min64(kBlocksPerStage, blocks - (int64_t)k * kBlocksPerStage);
       bool ok = true;
       if (k >= 2) {
-        // The stage's D slots held stage k - 2's blocks. Each drain parity
-        // frees its slots in block order, so the last even and the last odd
-        // slot this stage uses cover all of them: two probes per stage.
-        const int qe = (nq - 1) & ~1, qo = nq >= 2 ? ((nq - 2) & ~1) + 1 : -1;
-        ok = !abort_flag && mbar_wait_bounded(&tempty[slot0 + qe], tph, a.status, kStatusMmaTimeout);
-        if (qo >= 0)
-          ok = ok && mbar_wait_bounded(&tempty[slot0 + qo], tph, a.status, kStatusMmaTimeout);
+        // The stage's D slots held stage k - 2's blocks: they are free once
+        // the drain has released stage k - 2 (its `empty` phase completes).
+        ok = !abort_flag && mbar_wait_bounded(&empty[s2], ph2, a.status, kStatusMmaTimeout);
         ok = __all_sync(0xffffffffu, ok) != 0;
         if (!ok) abort_flag = 1;
+        if (++s2 == stages) {
+          s2 = 0;
+          ph2 ^= 1u;
+        }
       }
       tc_fence_after();
       // One elected section per stage: the control flow around single-lane
@@ -490,11 +489,11 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
             if (q < nq) {
               mma_i8(tmem + (uint32_t)((slot0 + q) * kTileTok), ad + (uint64_t)(2 * q),
                      bd + (uint64_t)(2 * q), kIdescI8);
-              mma_commit(&tfull[slot0 + q]);
             }
           }
         }
-        mma_commit(&empty[s]);
+        mma_commit(&dready[s]);  // the drain may read the stage's D slots
+        mma_commit(&empty[s]);   // the producer may refill the stage (with the drain's arrivals)
       }
       __syncwarp();
       if (!ok) break;
@@ -527,20 +526,20 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     for (int j = 0; j < kEpiCols / 2; j++) acc[j] = 0;
     const int nblk = (int)blocks;
     int32_t dn[kEpiCols];
-    int slot = parity;                          // slot of block b is b % kSlots
-    uint32_t tph = 0;
     int st = 0;
     uint32_t sph = 0;
-    bool alive = true;
-    for (int k = 0; k < nst && alive; k++) {
-      // This stage's scales have landed (and, with TMA scales, the MMA warp
-      // has written the block-major copy of the activation scales).
+    for (int k = 0; k < nst; k++) {
+      // One wait per stage: the stage's scales have landed, its MMAs have
+      // completed and (with TMA scales) the block-major activation scales
+      // are written.
       bool got = !abort_flag && mbar_wait_bounded(&full[st], sph, a.status, kStatusTmaTimeout);
-      if (tma_scales) got = got && mbar_wait_bounded(&sready[st], sph, a.status, kStatusMmaTimeout);
+      got = got && mbar_wait_bounded(&dready[st], sph, a.status, kStatusMmaTimeout);
       if (!__all_sync(0xffffffffu, got)) {
         abort_flag = 1;
         break;
       }
+      tc_fence_after();
+      const int slot0 = (k & 1) * kBlocksPerStage;
       float sws[kBlocksPerStage];
       if (Q4) {
         // TMA scales: 8 fp16 per row covering stages 2j and 2j + 1.
@@ -560,22 +559,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       for (int q = parity; q < kBlocksPerStage; q += 2) {
         const int blk = k * kBlocksPerStage + q;
         if (blk >= nblk) break;
-        got = !abort_flag && mbar_wait_bounded(&tfull[slot], tph, a.status, kStatusMmaTimeout);
-        if (!__all_sync(0xffffffffu, got)) {  // tcgen05.ld is warp-wide: all lanes agree
-          abort_flag = 1;
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slot * kTileTok + col0), dn);
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((slot0 + q) * kTileTok + col0), dn);
         tmem_wait_ld_regs(dn);
-        tc_fence_before();
-        mbar_arrive(&tempty[slot]);  // every lane, once its own load is done: the MMA may refill the slot
-        slot += 2;
-        if (slot >= kSlots) {
-          slot -= kSlots;
-          tph ^= 1u;
-        }
         const uint64_t sw2 = f2_pack(sws[q], sws[q]);
         const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok + col0;
 #pragma unroll
@@ -587,7 +572,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
                                   acc[j / 2 + 1]);
         }
       }
-      mbar_arrive(&empty[st]);  // every lane: done with the stage's scales
+      tc_fence_before();
+      mbar_arrive(&empty[st]);  // every lane: done with the stage's scales and D slots
       if (++st == stages) {
         st = 0;
         sph ^= 1u;
