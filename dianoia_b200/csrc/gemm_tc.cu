@@ -53,7 +53,7 @@ constexpr int kTileTok = 64;                   // MMA N
 constexpr int kStageK = 128;                   // int8 of K per stage = 4 blocks
 constexpr int kBlocksPerStage = kStageK / kBlock;
 constexpr int kABytes = kTileRows * kStageK;   // 16 KB
-constexpr int kBBytes = kTileTok * kStageK;    // 16 KB
+constexpr int kBBytes = kTileTok * kStageK;    // 8 KB
 constexpr int kRawBytes = kTileRows * (kStageK / 2);  // Q4 nibbles: 8 KB
 constexpr int kEpiWarps = 16;
 constexpr int kConvWarps = 2;
@@ -110,14 +110,34 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] = A * B (accumulate = false): one K = 32 step of int8 x int8 -> s32.
+// D[tmem] = A * B (+ D when `accumulate`): one K = 32 step of int8 x int8
+// -> s32.
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc) {
+                                       uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// The Q4 kernel seeds every D slot with this int32 and accumulates onto it:
+// 0x4B400000 + d, read as a float, is 1.5 * 2^23 + d exactly for |d| < 2^22,
+// so the tensor core's own int32 sum does the first step of the exact
+// int -> float conversion and the drain skips an integer add per value. (The
+// Q8 kernel, with fewer registers to spare per thread, adds the seed itself.)
+constexpr uint32_t kSeed = 0x4B400000u;
+// 32 lanes x 32 consecutive 32-bit columns of TMEM set to `v` (four stores
+// of 8 columns: a store reads its values from consecutive registers).
+__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 8)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(
+                     taddr + (uint32_t)c),
+                 "r"(v)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 // The mbarrier arrives once every tcgen05 operation this thread issued so far
 // has completed.
@@ -126,8 +146,8 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
-// The same wait, tied to the registers an earlier tcgen05.ld writes, so the
-// compiler cannot move their reads above it.
+// Waits for this thread's TMEM loads, tied to the registers an earlier
+// tcgen05.ld writes, so the compiler cannot move their reads above it.
 __device__ __forceinline__ void tmem_wait_ld_regs(int32_t (&v)[32]) {
   asm volatile(
       "tcgen05.wait::ld.sync.aligned;"
@@ -172,47 +192,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
       : "memory");
 }
 
-// 64 columns (a whole D slot) of the warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, int32_t (&v)[64]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-      "%28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, "
-      "%45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, "
-      "%62, %63}, [%64];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
-        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
-        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]),
-        "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]),
-        "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]),
-        "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]),
-        "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]),
-        "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]),
-        "=r"(v[62]), "=r"(v[63])
-      : "r"(taddr)
-      : "memory");
-}
-// Waits for the warp's TMEM loads, tied to the 64 registers they write.
-__device__ __forceinline__ void tmem_wait_ld64(int32_t (&v)[64]) {
-  asm volatile(
-      "tcgen05.wait::ld.sync.aligned;"
-      : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
-        "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]),
-        "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]),
-        "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]),
-        "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31]));
-  asm volatile(
-      ""
-      : "+r"(v[32]), "+r"(v[33]), "+r"(v[34]), "+r"(v[35]), "+r"(v[36]), "+r"(v[37]),
-        "+r"(v[38]), "+r"(v[39]), "+r"(v[40]), "+r"(v[41]), "+r"(v[42]), "+r"(v[43]),
-        "+r"(v[44]), "+r"(v[45]), "+r"(v[46]), "+r"(v[47]), "+r"(v[48]), "+r"(v[49]),
-        "+r"(v[50]), "+r"(v[51]), "+r"(v[52]), "+r"(v[53]), "+r"(v[54]), "+r"(v[55]),
-        "+r"(v[56]), "+r"(v[57]), "+r"(v[58]), "+r"(v[59]), "+r"(v[60]), "+r"(v[61]),
-        "+r"(v[62]), "+r"(v[63]));
-}
-
 // Shared-memory matrix descriptor for a K-major, 128-byte-swizzled operand
 // tile whose rows are 128 bytes: 8-row groups 1024 bytes apart (SBO), version
 // 1, layout SWIZZLE_128B. `addr` may be advanced by 32 bytes within the
@@ -246,13 +225,16 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
-// Two int32 block dots (|d| < 2^22) as floats, exactly: the bits
-// 0x4B400000 + d are the float 1.5 * 2^23 + d, and subtracting 1.5 * 2^23 is
-// exact. One integer add per value and one packed float add per pair, instead
-// of the slower int-to-float conversion.
-__device__ __forceinline__ uint64_t i2_to_f2(int32_t d0, int32_t d1) {
-  const uint64_t bits = (uint64_t)(uint32_t)(d0 + 0x4B400000) | ((uint64_t)(uint32_t)(d1 + 0x4B400000) << 32);
-  return f2_add(bits, f2_pack(-12582912.0f, -12582912.0f));
+// Two int32 block dots (|d| < 2^22) as floats, exactly, from slot values that
+// hold 0x4B400000 + d (seeded slots) or d: the bits 0x4B400000 + d are the
+// float 1.5 * 2^23 + d, and subtracting 1.5 * 2^23 is exact. One packed float
+// add per pair (and an integer add per value for unseeded slots), instead of
+// the slower int-to-float conversion.
+template <bool kSeeded>
+__device__ __forceinline__ uint64_t slot_to_f2(int32_t v0, int32_t v1) {
+  const uint32_t b0 = kSeeded ? (uint32_t)v0 : (uint32_t)(v0 + (int32_t)kSeed);
+  const uint32_t b1 = kSeeded ? (uint32_t)v1 : (uint32_t)(v1 + (int32_t)kSeed);
+  return f2_add((uint64_t)b0 | ((uint64_t)b1 << 32), f2_pack(-12582912.0f, -12582912.0f));
 }
 
 __device__ __forceinline__ bool wait_tc(uint64_t* bar, uint32_t parity, uint32_t* status,
@@ -278,7 +260,8 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   uint64_t* conv = full + stages;
   uint64_t* empty = conv + stages;
   uint64_t* dready = empty + stages;
-  uint64_t* done = dready + stages;
+  uint64_t* tinit = dready + stages;
+  uint64_t* done = tinit + 1;
   uint64_t* xbar = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
   __shared__ volatile int abort_flag;
@@ -306,6 +289,7 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       // warp's lanes have written the block-major activation scales.
       mbar_init(&dready[s], tma_scales ? 1 + 32 : 1);
     }
+    mbar_init(tinit, kEpiWarps * 32);  // every drain lane has seeded its part of all D slots
     mbar_init(done, 1);
     mbar_init(xbar, (kEpiWarps / 2) * 32);
     abort_flag = 0;
@@ -468,9 +452,15 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       const int slot0 = (k & 1) * kBlocksPerStage;
       const int nq = (int)min64(kBlocksPerStage, blocks - (int64_t)k * kBlocksPerStage);
       bool ok = true;
+      if (Q4 && k == 0) {
+        ok = !abort_flag && mbar_wait_bounded(tinit, 0, a.status, kStatusMmaTimeout);
+        ok = __all_sync(0xffffffffu, ok) != 0;
+        if (!ok) abort_flag = 1;
+      }
       if (k >= 2) {
-        // The stage's D slots held stage k - 2's blocks: they are free once
-        // the drain has released stage k - 2 (its `empty` phase completes).
+        // The stage's D slots held stage k - 2's blocks: they are free (and
+        // seeded again) once the drain has released stage k - 2 (its
+        // `empty` phase completes).
         ok = !abort_flag && mbar_wait_bounded(&empty[s2], ph2, a.status, kStatusMmaTimeout);
         ok = __all_sync(0xffffffffu, ok) != 0;
         if (!ok) abort_flag = 1;
@@ -488,7 +478,7 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           for (int q = 0; q < kBlocksPerStage; q++) {
             if (q < nq) {
               mma_i8(tmem + (uint32_t)((slot0 + q) * kTileTok), ad + (uint64_t)(2 * q),
-                     bd + (uint64_t)(2 * q), kIdescI8);
+                     bd + (uint64_t)(2 * q), kIdescI8, Q4 ? 1u : 0u);
             }
           }
         }
@@ -526,6 +516,14 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     for (int j = 0; j < kEpiCols / 2; j++) acc[j] = 0;
     const int nblk = (int)blocks;
     int32_t dn[kEpiCols];
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
+    if (Q4) {
+#pragma unroll
+      for (int q = 0; q < kSlots; q++) tmem_fill32(tlane + (uint32_t)(q * kTileTok), kSeed);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(tinit);
+    }
     int st = 0;
     uint32_t sph = 0;
     for (int k = 0; k < nst; k++) {
@@ -559,21 +557,23 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       for (int q = parity; q < kBlocksPerStage; q += 2) {
         const int blk = k * kBlocksPerStage + q;
         if (blk >= nblk) break;
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((slot0 + q) * kTileTok + col0), dn);
+        tmem_ld32(tlane + (uint32_t)((slot0 + q) * kTileTok), dn);
         tmem_wait_ld_regs(dn);
+        if (Q4) tmem_fill32(tlane + (uint32_t)((slot0 + q) * kTileTok), kSeed);  // seed for the slot's next block
         const uint64_t sw2 = f2_pack(sws[q], sws[q]);
         const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok + col0;
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 4) {
           const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
           // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
-          acc[j / 2] = f2_fma(i2_to_f2(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
-          acc[j / 2 + 1] = f2_fma(i2_to_f2(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
+          acc[j / 2] = f2_fma(slot_to_f2<Q4>(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
+          acc[j / 2 + 1] = f2_fma(slot_to_f2<Q4>(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
                                   acc[j / 2 + 1]);
         }
       }
+      if (Q4) tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&empty[st]);  // every lane: done with the stage's scales and D slots
+      mbar_arrive(&empty[st]);  // every lane: done with the stage's scales and D slots (seeded again)
       if (++st == stages) {
         st = 0;
         sph ^= 1u;
