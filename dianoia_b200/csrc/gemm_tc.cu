@@ -57,7 +57,8 @@ constexpr int kBBytes = kTileTok * kStageK;    // 8 KB
 constexpr int kRawBytes = kTileRows * (kStageK / 2);  // Q4 nibbles: 8 KB
 constexpr int kEpiWarps = 16;
 constexpr int kConvWarps = 2;
-constexpr int kEpiCols = kTileTok / 2;  // token columns per drain warp
+constexpr int kEpiCols = kTileTok * 8 / kEpiWarps;  // token columns per drain warp (32 or 64)
+static_assert(kEpiCols % 32 == 0 && kEpiCols <= kTileTok, "whole 32-column TMEM loads");
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSlots = (int)kTmemCols / kTileTok;  // D slots: blocks in flight between MMA and drain
 constexpr int kMaxSmemTc = 226 * 1024;
@@ -508,7 +509,7 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     const int quarter = warp & 3;               // TMEM lanes this warp may access
     const int sub = (warp - 2) >> 2;            // 0 .. 3
     const int parity = sub & 1;                 // even or odd blocks
-    const int col0 = (sub >> 1) * kEpiCols;     // first token column of this warp
+    const int col0 = (sub >> 1) * kEpiCols;     // first token column of this warp (0 with 8 warps)
     const int row_local = quarter * 32 + lane;
     const int64_t row = row0 + row_local;
     uint64_t acc[kEpiCols / 2];                 // f32 pairs: tokens col0 + 2i, col0 + 2i + 1
@@ -519,7 +520,9 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
     if (Q4) {
 #pragma unroll
-      for (int q = 0; q < kSlots; q++) tmem_fill32(tlane + (uint32_t)(q * kTileTok), kSeed);
+      for (int q = 0; q < kSlots; q++)
+#pragma unroll
+        for (int c = 0; c < kEpiCols; c += 32) tmem_fill32(tlane + (uint32_t)(q * kTileTok + c), kSeed);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(tinit);
@@ -557,9 +560,15 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
       for (int q = parity; q < kBlocksPerStage; q += 2) {
         const int blk = k * kBlocksPerStage + q;
         if (blk >= nblk) break;
-        tmem_ld32(tlane + (uint32_t)((slot0 + q) * kTileTok), dn);
-        tmem_wait_ld_regs(dn);
-        if (Q4) tmem_fill32(tlane + (uint32_t)((slot0 + q) * kTileTok), kSeed);  // seed for the slot's next block
+#pragma unroll
+        for (int c = 0; c < kEpiCols; c += 32)
+          tmem_ld32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), *reinterpret_cast<int32_t(*)[32]>(dn + c));
+#pragma unroll
+        for (int c = 0; c < kEpiCols; c += 32) tmem_wait_ld_regs(*reinterpret_cast<int32_t(*)[32]>(dn + c));
+        if (Q4) {  // seed for the slot's next block
+#pragma unroll
+          for (int c = 0; c < kEpiCols; c += 32) tmem_fill32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), kSeed);
+        }
         const uint64_t sw2 = f2_pack(sws[q], sws[q]);
         const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok + col0;
 #pragma unroll
