@@ -100,23 +100,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tw);
       if (TMA_SCALES) prefetch_tmap(&tsc);
     }
-    int64_t k = 0;
+    // Ring slot, its phase, chunk and tile are running counters: a 64-bit
+    // division per stage would cost more than the stage's own work.
+    int64_t k = 0, tile = blockIdx.x;
+    int s = 0, c = 0;
+    uint32_t eph = 1;  // parity of empty[s] to wait for, from the ring's second pass on
     for (; k < total; k++) {
-      const int s = (int)(k % stages);
       if (k >= stages) {
-        const bool got = mbar_wait_bounded(&empty[s], (uint32_t)((k / stages) - 1) & 1u, a.status,
-                                           kStatusTmaTimeout);
+        const bool got = mbar_wait_bounded(&empty[s], eph, a.status, kStatusTmaTimeout);
         if (!got) abort_flag = 1;
       }
       if (abort_flag) break;
       if (lane == 0) {
-        const int64_t tile = blockIdx.x + (k / nch) * gridDim.x;
-        const int c = (int)(k % nch);
         const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
         issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, &tw, &tsc, c, nb,
                                     (int32_t)(tile * kRows), &full[s]);
       }
       __syncwarp();
+      if (++s == stages) {
+        s = 0;
+        eph ^= 1u;
+      }
+      if (++c == nch) {
+        c = 0;
+        tile += gridDim.x;
+      }
     }
     if (abort_flag && lane == 0) {
       // Let the copies still in flight land before the CTA's shared memory goes.
@@ -196,8 +204,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t rowoff = (uint32_t)row_local * kBoxBytes;
   const uint8_t* sc = static_cast<const uint8_t*>(a.scales);
   const uint8_t* xw_l = xw_s + l * X::kLaneBytes;
-  int64_t k = 0;
-  uint32_t e = 0;  // epilogue barrier uses so far
+  int s = 0;        // ring slot of the next stage
+  uint32_t ph = 0;  // and the parity of its full barrier
+  uint32_t e = 0;   // epilogue barrier uses so far
   for (int64_t i = 0; i < my_tiles; i++) {
     const int64_t tile = blockIdx.x + i * gridDim.x;
     const int64_t row0 = tile * kRows;
@@ -217,9 +226,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint8_t* gsc = TMA_SCALES ? nullptr : sc + row * blocks * F::kSB;
       const int nfull = TMA_SCALES ? (int)(blocks / F::kKC) : 0;
       int c = 0;
-      for (; c < nfull; c++, k++) {
-        const int s = (int)(k % stages);
-        if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+      for (; c < nfull; c++) {
+        if (!warp_wait(&full[s], ph, a.status)) {
           abort_flag = 1;
           return;  // the producer drains what it issued; every other wait is bounded
         }
@@ -228,11 +236,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         xsp += F::kKC;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
-      for (; c < nch; c++, k++) {
-        const int s = (int)(k % stages);
+      for (; c < nch; c++) {
         const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-        if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+        if (!warp_wait(&full[s], ph, a.status)) {
           abort_flag = 1;
           return;
         }
@@ -243,19 +254,26 @@ __global__ void __launch_bounds__(kThreads, 2)
         xsp += F::kKC;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
     } else {
       const LaneCtx lc{row_local, r8, l, rowoff, xw_l, sp.xw_stride, xs_s, sp.xs_stride, sc, row, blocks};
-      for (int c = 0; c < nch; c++, k++) {
-        const int s = (int)(k % stages);
+      for (int c = 0; c < nch; c++) {
         const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-        if (!warp_wait(&full[s], (uint32_t)(k / stages) & 1u, a.status)) {
+        if (!warp_wait(&full[s], ph, a.status)) {
           abort_flag = 1;
           return;  // the producer drains what it issued; every other wait is bounded
         }
         gemv_stage<Q4, NT, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, c * F::kKC, lc, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
     }
 
