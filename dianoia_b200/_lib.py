@@ -41,6 +41,7 @@ SIGNATURES = {
     "lab_gpu_last_ms": (ctypes.c_double, []),
     "lab_gpu_enc_matmul_q8": (None, [_i64] * 10),
     "lab_gpu_enc_matmul_q4": (None, [_i64] * 10),
+    "dn_gpu_enc_batch": (None, [_p, _i64]),
     "dn_linear": (_i64, [_i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),

@@ -18,6 +18,14 @@
 // GpuForward). A command buffer identical to the previous one (a decode loop)
 // replays the CUDA graph captured for it.
 //
+// Inside a command buffer, a decode product whose input range is exactly the
+// output range of an earlier decode product (nothing written over it in
+// between) reads that output as quantized activations (QA blocks: 32 int8 and
+// their f32 scale per 32 values) which the earlier product's epilogue writes
+// to an internal buffer beside its f32 outputs. The QA blocks are what
+// quantizing those f32 outputs gives, so the results are the same; the later
+// product skips re-quantizing its input in every CTA.
+//
 // Errors: like the reference, the void functions report nothing;
 // lab_gpu_commit returns 0 when a product's arguments or a CUDA call failed.
 // Calls are serialized by one mutex (the reference's layer is single-encoder).
@@ -78,11 +86,16 @@ int8_t* g_xq = nullptr;
 float* g_xsc = nullptr;
 int64_t g_xcap = 0;
 
+// QA blocks of the products whose outputs a later product reads.
+uint8_t* g_qa = nullptr;
+int64_t g_qa_cap = 0;
+
 // The graph of the last command buffer, with what it was captured from.
 cudaGraphExec_t g_exec = nullptr;
 std::vector<Op> g_exec_ops;
 std::vector<uint8_t*> g_exec_ptrs;  // device addresses the graph uses, per op (w, x, y)
 int8_t* g_exec_xq = nullptr;
+uint8_t* g_exec_qa = nullptr;
 
 void drop_graph() {
   if (g_exec != nullptr) cudaGraphExecDestroy(g_exec);
@@ -196,22 +209,83 @@ void subtract(const std::vector<Range>& written, int64_t b, int64_t lo, int64_t 
 }
 
 // Records the command buffer's copies and products on g_stream.
+dn::LinearArgs linear_args(const Op& o, uint32_t* status) {
+  const Buf &w = g_bufs[o.w], &x = g_bufs[o.x], &y = g_bufs[o.y];
+  return dn::LinearArgs{o.q4, w.dev + o.qs_off, w.dev + o.sc_off,
+                        reinterpret_cast<const float*>(x.dev + o.x_off), g_xq, g_xsc,
+                        reinterpret_cast<float*>(y.dev + o.y_off), o.rows, o.cols, o.n, o.rows,
+                        1, status};
+}
+
+// QA links of the recorded products: src[i] is the product whose output
+// product i reads as QA blocks (or -1), qa_at[j] the byte offset in g_qa of
+// product j's QA output (or -1). Both ends must take the decode GEMV path.
+int64_t plan_links(std::vector<int>& src, std::vector<int64_t>& qa_at, uint32_t* status) {
+  const int n = (int)g_ops.size();
+  src.assign(n, -1);
+  qa_at.assign(n, -1);
+  std::vector<bool> gemv(n);
+  for (int i = 0; i < n; i++) gemv[i] = dn::path_for(linear_args(g_ops[i], status)) == 0;
+  int64_t total = 0;
+  for (int i = 0; i < n; i++) {
+    const Op& c = g_ops[i];
+    if (!gemv[i]) continue;
+    const int64_t lo = c.x_off, hi = c.x_off + c.n * c.cols * 4;
+    for (int j = i - 1; j >= 0; j--) {
+      const Op& p = g_ops[j];
+      const bool writes_here = p.y == c.x && p.y_off < hi && lo < p.y_off + p.n * p.rows * 4;
+      if (!writes_here) continue;
+      // The last write over the input range: a link if it is exactly that range.
+      if (gemv[j] && p.y_off == lo && p.n == c.n && p.rows == c.cols && p.rows % kBlock == 0) {
+        src[i] = j;
+        if (qa_at[j] < 0) {
+          qa_at[j] = total;
+          total += (p.n * (p.rows / kBlock) * dn::kQABytes + 15) / 16 * 16;
+        }
+      }
+      break;
+    }
+  }
+  return total;
+}
+
 bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
-            uint32_t* status) {
+            const std::vector<int>& src, const std::vector<int64_t>& qa_at, uint32_t* status) {
   for (const Range& r : uploads) {
     const Buf& b = g_bufs[r.buf];
     if (cudaMemcpyAsync(b.dev + r.lo, b.host + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyHostToDevice,
                         g_stream) != cudaSuccess)
       return false;
   }
-  for (const Op& o : g_ops) {
-    const Buf &w = g_bufs[o.w], &x = g_bufs[o.x], &y = g_bufs[o.y];
-    const dn::LinearArgs a{o.q4, w.dev + o.qs_off, w.dev + o.sc_off,
-                           reinterpret_cast<const float*>(x.dev + o.x_off), g_xq, g_xsc,
-                           reinterpret_cast<float*>(y.dev + o.y_off), o.rows, o.cols, o.n, o.rows,
-                           1, status};
-    const int64_t rc =
-        dn::path_for(a) == 0 ? dn::launch_gemv(a, g_stream, true) : dn::launch_linear(a, g_stream);
+  for (size_t i = 0; i < g_ops.size(); i++) {
+    const Op& o = g_ops[i];
+    const dn::LinearArgs a = linear_args(o, status);
+    int64_t rc;
+    if (src[i] >= 0 || qa_at[i] >= 0) {
+      dn::GemvArgs g{};
+      g.q4 = o.q4;
+      g.qs = a.qs;
+      g.scales = a.scales;
+      if (src[i] >= 0) {
+        g.xa = g_qa + qa_at[src[i]];
+        g.xa_stride = (o.cols / kBlock) * dn::kQABytes;
+      } else {
+        g.xs = a.xs;
+      }
+      g.ys = a.ys;
+      g.ldy = o.rows;
+      if (qa_at[i] >= 0) {
+        g.ya = g_qa + qa_at[i];
+        g.ya_stride = (o.rows / kBlock) * dn::kQABytes;
+      }
+      g.rows = o.rows;
+      g.cols = o.cols;
+      g.n = o.n;
+      g.status = status;
+      rc = dn::launch_gemv_ex(g, g_stream, true);
+    } else {
+      rc = dn::path_for(a) == 0 ? dn::launch_gemv(a, g_stream, true) : dn::launch_linear(a, g_stream);
+    }
     if (rc != 0) return false;
   }
   for (const Range& r : downloads) {
@@ -224,7 +298,8 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
 }
 
 bool same_as_graph() {
-  if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_ops.size() != g_ops.size()) return false;
+  if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_qa != g_qa || g_exec_ops.size() != g_ops.size())
+    return false;
   for (size_t i = 0; i < g_ops.size(); i++) {
     const Op &a = g_ops[i], &b = g_exec_ops[i];
     if (!(a == b) || g_exec_ptrs[3 * i] != g_bufs[a.w].dev ||
@@ -275,6 +350,20 @@ int64_t commit(int64_t wait) {
   }
   if (!same_as_graph()) {
     drop_graph();
+    std::vector<int> src;
+    std::vector<int64_t> qa_at;
+    const int64_t qa_need = plan_links(src, qa_at, status);
+    if (qa_need > g_qa_cap) {
+      if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
+      cudaFree(g_qa);
+      g_qa = nullptr;
+      g_qa_cap = 0;
+      if (cudaMalloc(&g_qa, (size_t)qa_need) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+      }
+      g_qa_cap = qa_need;
+    }
     // Ranges to copy in (host-written inputs) and out (products' outputs).
     std::vector<Range> uploads, written;
     for (const Op& o : g_ops) {
@@ -283,7 +372,7 @@ int64_t commit(int64_t wait) {
     }
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
-    const bool ok = record(uploads, written, status);
+    const bool ok = record(uploads, written, src, qa_at, status);
     const cudaError_t e = cudaStreamEndCapture(g_stream, &graph);
     if (!ok || e != cudaSuccess || graph == nullptr ||
         cudaGraphInstantiate(&g_exec, graph, 0) != cudaSuccess) {
@@ -295,6 +384,7 @@ int64_t commit(int64_t wait) {
     cudaGraphDestroy(graph);
     g_exec_ops = g_ops;
     g_exec_xq = g_xq;
+    g_exec_qa = g_qa;
     for (const Op& o : g_ops) {
       g_exec_ptrs.push_back(g_bufs[o.w].dev);
       g_exec_ptrs.push_back(g_bufs[o.x].dev);
@@ -421,6 +511,14 @@ void lab_gpu_enc_matmul_q4(int64_t w, int64_t qsOffset, int64_t scalesOffset, in
                            int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
                            int64_t n) {
   encode(true, w, qsOffset, scalesOffset, x, xOffset, y, yOffset, rows, cols, n);
+}
+
+void dn_gpu_enc_batch(const int64_t* table, int64_t count) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  for (int64_t i = 0; i < count && table != nullptr; i++) {
+    const int64_t* r = table + 11 * i;
+    encode(r[0] != 0, r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], r[9], r[10]);
+  }
 }
 
 }  // extern "C"

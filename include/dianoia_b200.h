@@ -133,6 +133,15 @@ void lab_gpu_enc_matmul_q4(int64_t w, int64_t qsOffset, int64_t scalesOffset, in
                            int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
                            int64_t n);
 
+/* Records `count` products into the open command buffer in one call, exactly as
+ * the same sequence of lab_gpu_enc_matmul_q8 / lab_gpu_enc_matmul_q4 calls
+ * would. No counterpart in the reference: it is for callers whose per-call
+ * cost is high (a Python ctypes call costs microseconds, a Dart @Native leaf
+ * call tens of nanoseconds). Row i of `table` is 11 int64 values: format
+ * (0 = Q8_0, 1 = Q4_0), w, qsOffset, scalesOffset, x, xOffset, y, yOffset,
+ * rows, cols, n. */
+void dn_gpu_enc_batch(const int64_t* table, int64_t count);
+
 /* ------------------------------------------------------------ dn_* (device API) */
 
 /* Status codes of the dn_* functions and of dn_last_error(). */

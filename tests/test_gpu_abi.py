@@ -160,3 +160,50 @@ def test_chained_command_buffer_and_replay(cuda_lib, oracle):
         for h in (w1, w2, act):
             L.lab_gpu_release(h)
     assert L.lab_gpu_contents(act) is None
+
+
+def test_batch_encode_equals_single_calls(cuda_lib, oracle):
+    """dn_gpu_enc_batch records the same command buffer as the equivalent
+    lab_gpu_enc_matmul_* calls: a Q8 product feeding a Q4 product, bit for
+    bit against the reference's kernels; a row whose ranges do not fit makes
+    the commit fail, as a single call would."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    rng = np.random.default_rng(11)
+    r1, c1, r2 = 128, 256, 64
+    q1, s1 = orc.q8_weights(rng, r1, c1)
+    q2, s2 = orc.q4_weights(rng, r2, r1)
+
+    def weights(qs, sc):
+        raw = np.concatenate([qs.view(np.uint8), sc.view(np.uint8)])
+        h = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
+        assert h >= 0
+        return h, qs.size
+
+    w1, at1 = weights(q1, s1)
+    w2, at2 = weights(q2, s2)
+    act = L.lab_gpu_buffer(4 * (c1 + r1 + r2))
+    assert act >= 0
+    view = np.ctypeslib.as_array((ctypes.c_float * (c1 + r1 + r2)).from_address(L.lab_gpu_contents(act)))
+    table = np.array([[0, w1, 0, at1, act, 0, act, 4 * c1, r1, c1, 1],
+                      [1, w2, 0, at2, act, 4 * c1, act, 4 * (c1 + r1), r2, r1, 1]], np.int64)
+    try:
+        for _ in range(2):
+            x = orc.activations(rng, 1, c1)
+            view[:c1] = x
+            view[c1:] = np.nan
+            L.lab_gpu_begin()
+            L.dn_gpu_enc_batch(table.ctypes.data, 2)
+            assert L.lab_gpu_commit(1) == 1
+            y1, _, _ = oracle.gemm("q8", q1, s1, x, r1, c1, 1, 1)
+            y2, _, _ = oracle.gemm("q4", q2, s2, y1, r2, r1, 1, 1)
+            assert np.array_equal(view[c1:c1 + r1].view(np.uint32), y1.view(np.uint32))
+            assert np.array_equal(view[c1 + r1:].view(np.uint32), y2.view(np.uint32))
+        bad = table.copy()
+        bad[1, 7] = 4 * (c1 + r1 + 1)  # r2 outputs from here run past the buffer
+        L.lab_gpu_begin()
+        L.dn_gpu_enc_batch(bad.ctypes.data, 2)
+        assert L.lab_gpu_commit(1) == 0
+    finally:
+        for h in (w1, w2, act):
+            L.lab_gpu_release(h)
