@@ -1126,11 +1126,16 @@ def run_e2e_gpu_layer(args, stack, L, torch):
                     L.lab_gpu_enc_matmul_q8(*r[1:])
             if L.lab_gpu_commit(1) != 1:
                 raise RuntimeError("lab_gpu_commit failed")
-            logits[:] = logits_view
+            # The logits are read in place in the pinned mirror (the commit's
+            # device-to-host copy put them there), as a Dart caller reads them.
+            dev_ms.append(L.lab_gpu_last_ms())
+
+        dev_ms = []
 
         def timed(batch):
             for _ in range(3):
                 one_token(batch)
+            dev_ms.clear()
             t0 = time.perf_counter()
             for _ in range(steps):
                 one_token(batch)
@@ -1138,6 +1143,8 @@ def run_e2e_gpu_layer(args, stack, L, torch):
 
         per_call = timed(False)
         value = timed(True)
+        commit_ms = float(np.median(dev_ms))
+        logits[:] = logits_view
         same = bool(np.array_equal(logits.view(np.uint32),
                                    stack.bufs["lm_head"].cpu().numpy().view(np.uint32)))
         d2h = 4 * (at - HIDDEN) + 4 * VOCAB
@@ -1146,6 +1153,9 @@ def run_e2e_gpu_layer(args, stack, L, torch):
                 "api": "lab_gpu_* (dianoia's GPU-layer ABI: host-visible buffers; per token "
                        "lab_gpu_begin, the 113 products recorded by one dn_gpu_enc_batch call, "
                        "lab_gpu_commit(wait=1))",
+                "commit_device_ms": commit_ms,
+                "commit_device_note": "median GPU time of one commit's graph (uploads, 113 "
+                                      "products, downloads), from lab_gpu_last_ms",
                 "per_call_encode_tokens_s": per_call,
                 "per_call_encode_note": "the same loop recording each product with its own "
                                         "lab_gpu_enc_matmul_q8 call: a Python ctypes call costs "

@@ -18,13 +18,14 @@
 // GpuForward). A command buffer identical to the previous one (a decode loop)
 // replays the CUDA graph captured for it.
 //
-// Inside a command buffer, a decode product whose input range is exactly the
-// output range of an earlier decode product (nothing written over it in
-// between) reads that output as quantized activations (QA blocks: 32 int8 and
-// their f32 scale per 32 values) which the earlier product's epilogue writes
-// to an internal buffer beside its f32 outputs. The QA blocks are what
-// quantizing those f32 outputs gives, so the results are the same; the later
-// product skips re-quantizing its input in every CTA.
+// Inside a command buffer, a decode product whose input is (a 32-value
+// aligned part of) the output of the earlier decode product that last wrote
+// it reads that output as quantized activations (QA blocks: 32 int8 and
+// their f32 scale per 32 values), which the earlier product's epilogue writes
+// to an internal buffer beside its f32 outputs; host-written inputs are
+// quantized once for all products that read them. QA blocks are exactly what
+// quantizing the f32 values gives, so the results are the same; the products
+// skip re-quantizing their input in every CTA.
 //
 // Errors: like the reference, the void functions report nothing;
 // lab_gpu_commit returns 0 when a product's arguments or a CUDA call failed.
@@ -217,66 +218,104 @@ dn::LinearArgs linear_args(const Op& o, uint32_t* status) {
                         1, status};
 }
 
-// QA links of the recorded products: src[i] is the product whose output
-// product i reads as QA blocks (or -1), qa_at[j] the byte offset in g_qa of
-// product j's QA output (or -1). Both ends must take the decode GEMV path.
-int64_t plan_links(std::vector<int>& src, std::vector<int64_t>& qa_at, uint32_t* status) {
+// QA links of the recorded products (decode GEMV path only). Product i reads
+// its input as QA blocks at byte xa_at[i] of g_qa (row stride xa_stride[i])
+// when the input is either
+//  * a 32-value-aligned part of the output of the last product that wrote
+//    over it (all of the output when n > 1, where token strides must agree);
+//    that product then also writes its output as QA blocks, at ya_at[j]; or
+//  * host data no earlier product wrote: quantized once, before the products,
+//    for every product that reads the same range.
+struct HostQA {
+  int64_t buf, off, n, cols, at;
+};
+struct Links {
+  std::vector<int64_t> xa_at, xa_stride, ya_at;
+  std::vector<HostQA> host;
+  int64_t bytes = 0;
+};
+
+int64_t qa_bytes(int64_t n, int64_t values) { return (n * (values / kBlock) * dn::kQABytes + 15) / 16 * 16; }
+
+Links plan_links(uint32_t* status) {
   const int n = (int)g_ops.size();
-  src.assign(n, -1);
-  qa_at.assign(n, -1);
+  Links k;
+  k.xa_at.assign(n, -1);
+  k.xa_stride.assign(n, 0);
+  k.ya_at.assign(n, -1);
   std::vector<bool> gemv(n);
   for (int i = 0; i < n; i++) gemv[i] = dn::path_for(linear_args(g_ops[i], status)) == 0;
-  int64_t total = 0;
   for (int i = 0; i < n; i++) {
     const Op& c = g_ops[i];
-    if (!gemv[i]) continue;
+    if (!gemv[i] || c.cols % kBlock != 0) continue;
     const int64_t lo = c.x_off, hi = c.x_off + c.n * c.cols * 4;
-    for (int j = i - 1; j >= 0; j--) {
+    int j = i - 1;
+    for (; j >= 0; j--) {
       const Op& p = g_ops[j];
-      const bool writes_here = p.y == c.x && p.y_off < hi && lo < p.y_off + p.n * p.rows * 4;
-      if (!writes_here) continue;
-      // The last write over the input range: a link if it is exactly that range.
-      if (gemv[j] && p.y_off == lo && p.n == c.n && p.rows == c.cols && p.rows % kBlock == 0) {
-        src[i] = j;
-        if (qa_at[j] < 0) {
-          qa_at[j] = total;
-          total += (p.n * (p.rows / kBlock) * dn::kQABytes + 15) / 16 * 16;
-        }
+      if (p.y == c.x && p.y_off < hi && lo < p.y_off + p.n * p.rows * 4) break;
+    }
+    if (j >= 0) {
+      const Op& p = g_ops[j];
+      const int64_t delta = lo - p.y_off;
+      const bool inside = delta >= 0 && hi <= p.y_off + p.n * p.rows * 4 && delta % (kBlock * 4) == 0;
+      const bool tokens_agree = (c.n == 1 && p.n == 1) || (delta == 0 && p.n == c.n && p.rows == c.cols);
+      if (!gemv[j] || p.rows % kBlock != 0 || !inside || !tokens_agree) continue;
+      if (k.ya_at[j] < 0) {
+        k.ya_at[j] = k.bytes;
+        k.bytes += qa_bytes(p.n, p.rows);
       }
-      break;
+      k.xa_at[i] = k.ya_at[j] + delta / (kBlock * 4) * dn::kQABytes;
+      k.xa_stride[i] = p.rows / kBlock * dn::kQABytes;
+    } else {
+      size_t h = 0;
+      for (; h < k.host.size(); h++) {
+        const HostQA& q = k.host[h];
+        if (q.buf == c.x && q.off == lo && q.n == c.n && q.cols == c.cols) break;
+      }
+      if (h == k.host.size()) {
+        k.host.push_back(HostQA{c.x, lo, c.n, c.cols, k.bytes});
+        k.bytes += qa_bytes(c.n, c.cols);
+      }
+      k.xa_at[i] = k.host[h].at;
+      k.xa_stride[i] = c.cols / kBlock * dn::kQABytes;
     }
   }
-  return total;
+  return k;
 }
 
 bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
-            const std::vector<int>& src, const std::vector<int64_t>& qa_at, uint32_t* status) {
+            const Links& k, uint32_t* status) {
   for (const Range& r : uploads) {
     const Buf& b = g_bufs[r.buf];
     if (cudaMemcpyAsync(b.dev + r.lo, b.host + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyHostToDevice,
                         g_stream) != cudaSuccess)
       return false;
   }
+  for (const HostQA& q : k.host) {
+    if (dn::launch_quantize_qa(reinterpret_cast<const float*>(g_bufs[q.buf].dev + q.off), g_qa + q.at,
+                               q.n, q.cols, q.cols / kBlock * dn::kQABytes, g_stream) != cudaSuccess)
+      return false;
+  }
   for (size_t i = 0; i < g_ops.size(); i++) {
     const Op& o = g_ops[i];
     const dn::LinearArgs a = linear_args(o, status);
     int64_t rc;
-    if (src[i] >= 0 || qa_at[i] >= 0) {
+    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0) {
       dn::GemvArgs g{};
       g.q4 = o.q4;
       g.qs = a.qs;
       g.scales = a.scales;
-      if (src[i] >= 0) {
-        g.xa = g_qa + qa_at[src[i]];
-        g.xa_stride = (o.cols / kBlock) * dn::kQABytes;
+      if (k.xa_at[i] >= 0) {
+        g.xa = g_qa + k.xa_at[i];
+        g.xa_stride = k.xa_stride[i];
       } else {
         g.xs = a.xs;
       }
       g.ys = a.ys;
       g.ldy = o.rows;
-      if (qa_at[i] >= 0) {
-        g.ya = g_qa + qa_at[i];
-        g.ya_stride = (o.rows / kBlock) * dn::kQABytes;
+      if (k.ya_at[i] >= 0) {
+        g.ya = g_qa + k.ya_at[i];
+        g.ya_stride = o.rows / kBlock * dn::kQABytes;
       }
       g.rows = o.rows;
       g.cols = o.cols;
@@ -350,9 +389,8 @@ int64_t commit(int64_t wait) {
   }
   if (!same_as_graph()) {
     drop_graph();
-    std::vector<int> src;
-    std::vector<int64_t> qa_at;
-    const int64_t qa_need = plan_links(src, qa_at, status);
+    const Links links = plan_links(status);
+    const int64_t qa_need = links.bytes;
     if (qa_need > g_qa_cap) {
       if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
       cudaFree(g_qa);
@@ -372,7 +410,7 @@ int64_t commit(int64_t wait) {
     }
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
-    const bool ok = record(uploads, written, src, qa_at, status);
+    const bool ok = record(uploads, written, links, status);
     const cudaError_t e = cudaStreamEndCapture(g_stream, &graph);
     if (!ok || e != cudaSuccess || graph == nullptr ||
         cudaGraphInstantiate(&g_exec, graph, 0) != cudaSuccess) {
