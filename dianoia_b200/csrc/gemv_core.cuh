@@ -25,6 +25,33 @@ constexpr int kSmemPerSM = 228 * 1024;
 constexpr int kSMs = 148;
 constexpr int kMaxStages = 16;
 
+// dp4a sums seeded with kMagic: the bits 0x4B400000 + d are the float
+// 1.5 * 2^23 + d, exact for |d| < 2^22, so subtracting kMagicF converts d to
+// float exactly, without the slower int-to-float conversion.
+constexpr int32_t kMagic = 0x4B400000;
+constexpr float kMagicF = 12582912.0f;
+
+// Packed f32x2 arithmetic (two floats per instruction).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// Two biased dp4a results as exact floats.
+__device__ __forceinline__ uint64_t exact_d2(int32_t a, int32_t b) {
+  return f2_add(f2_pack(__int_as_float(a), __int_as_float(b)), f2_pack(-kMagicF, -kMagicF));
+}
+
 template <bool Q4>
 struct Fmt {
   static constexpr int kWB = Q4 ? 16 : 32;          // weight bytes per block
@@ -191,20 +218,33 @@ __device__ __forceinline__ void gemv_stage(const uint8_t* stage, int nb, int b0,
   } sp{c.xw_stride, c.xs_stride};
   // One block: weights w0 / w1 (as int8 for Q8, nibbles for Q4), its
   // scale, and the activations of every token.
+  // The dot products are seeded with kMagic and converted to float two at a
+  // time (exact), the scale products taken two at a time (f32x2, the same
+  // roundings); each token keeps its own fma chain in the reference's order.
   auto block_step = [&](int b, int32_t w0, int32_t w1, float sw, const float* xsc_b) {
+    int32_t d[NT];
 #pragma unroll
     for (int t = 0; t < NT; t++) {
       const uint8_t* xb = xw_l + t * sp.xw_stride + b * X::kBlockBytes;
-      int32_t d;
       if (Q4) {
         const uint4 xv = lds<uint4>(xb);
-        d = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, (int32_t)xv.z));
+        d[t] = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, (int32_t)xv.z + kMagic));
       } else {
         const uint2 xv = lds<uint2>(xb);
-        d = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, 0));
+        d[t] = __dp4a(w0, (int32_t)xv.x, __dp4a(w1, (int32_t)xv.y, kMagic));
       }
-      acc[t] = __fmaf_rn(__int2float_rn(d), __fmul_rn(sw, xsc_b[t]), acc[t]);
     }
+    const uint64_t sw2 = f2_pack(sw, sw);
+#pragma unroll
+    for (int t = 0; t + 1 < NT; t += 2) {
+      const uint64_t dd = exact_d2(d[t], d[t + 1]);
+      const uint64_t ss = f2_mul(sw2, f2_pack(xsc_b[t], xsc_b[t + 1]));
+      acc[t] = __fmaf_rn(f2_lo(dd), f2_lo(ss), acc[t]);
+      acc[t + 1] = __fmaf_rn(f2_hi(dd), f2_hi(ss), acc[t + 1]);
+    }
+    if (NT & 1)
+      acc[NT - 1] = __fmaf_rn(__fsub_rn(__int_as_float(d[NT - 1]), kMagicF), __fmul_rn(sw, xsc_b[NT - 1]),
+                              acc[NT - 1]);
   };
   auto weights_of = [&](const uint8_t* stage, int bb, int32_t& w0, int32_t& w1) {
     if (Q4) {

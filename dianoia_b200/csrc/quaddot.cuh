@@ -32,29 +32,14 @@ using gemv::lds;
 
 constexpr int kRows = 32;  // rows per tile
 constexpr int kWarps = 4;  // consumer warps per tile, 8 rows each
-constexpr int32_t kMagic = 0x4B400000;
-constexpr float kMagicF = 12582912.0f;
-
-// ------------------------------------------------------------ f32x2 helpers
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
-}
-__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-// Two biased dp4a results as exact floats.
-__device__ __forceinline__ uint64_t exact_d2(int32_t a, int32_t b) {
-  return f2_add(f2_pack(__int_as_float(a), __int_as_float(b)), f2_pack(-kMagicF, -kMagicF));
-}
+using gemv::exact_d2;
+using gemv::f2_add;
+using gemv::f2_hi;
+using gemv::f2_lo;
+using gemv::f2_mul;
+using gemv::f2_pack;
+using gemv::kMagic;
+using gemv::kMagicF;
 
 // --------------------------------------------------------- activation layout
 // One token's activations in shared memory, lane-interleaved per block b:

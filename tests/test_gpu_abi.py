@@ -207,3 +207,56 @@ def test_batch_encode_equals_single_calls(cuda_lib, oracle):
     finally:
         for h in (w1, w2, act):
             L.lab_gpu_release(h)
+
+
+def test_links_for_slices_and_shared_host_inputs(cuda_lib, oracle):
+    """One token through products that the command buffer links by QA blocks:
+    P2 reads a 32-value-aligned slice of P1's output, P3 reads the same host
+    input as P1 (quantized once for both), P4 reads a slice that is not
+    32-aligned (no link: it quantizes its f32 input itself). All bit for bit
+    against the reference's kernels on the same f32 values."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    rng = np.random.default_rng(17)
+    c1, r1, r3 = 256, 192, 96
+    q1, s1 = orc.q8_weights(rng, r1, c1)
+    q2, s2 = orc.q8_weights(rng, 64, 96)      # reads P1's outputs 32 .. 127
+    q3, s3 = orc.q4_weights(rng, r3, c1)      # reads the host input, as P1
+    q4, s4 = orc.q8_weights(rng, 32, 64)      # reads P1's outputs 40 .. 103
+
+    def weights(qs, sc):
+        raw = np.concatenate([qs.view(np.uint8), sc.view(np.uint8)])
+        h = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
+        assert h >= 0
+        return h, qs.size
+
+    hs = [weights(q, s) for q, s in [(q1, s1), (q2, s2), (q3, s3), (q4, s4)]]
+    floats = c1 + r1 + 64 + r3 + 32
+    act = L.lab_gpu_buffer(4 * floats)
+    assert act >= 0
+    view = np.ctypeslib.as_array((ctypes.c_float * floats).from_address(L.lab_gpu_contents(act)))
+    y1_at, y2_at, y3_at, y4_at = c1, c1 + r1, c1 + r1 + 64, c1 + r1 + 64 + r3
+    table = np.array([
+        [0, hs[0][0], 0, hs[0][1], act, 0, act, 4 * y1_at, r1, c1, 1],
+        [0, hs[1][0], 0, hs[1][1], act, 4 * (y1_at + 32), act, 4 * y2_at, 64, 96, 1],
+        [1, hs[2][0], 0, hs[2][1], act, 0, act, 4 * y3_at, r3, c1, 1],
+        [0, hs[3][0], 0, hs[3][1], act, 4 * (y1_at + 40), act, 4 * y4_at, 32, 64, 1]], np.int64)
+    try:
+        for _ in range(2):
+            x = orc.activations(rng, 1, c1)
+            view[:c1] = x
+            view[c1:] = np.nan
+            L.lab_gpu_begin()
+            L.dn_gpu_enc_batch(table.ctypes.data, len(table))
+            assert L.lab_gpu_commit(1) == 1
+            y1, _, _ = oracle.gemm("q8", q1, s1, x, r1, c1, 1, 1)
+            y2, _, _ = oracle.gemm("q8", q2, s2, y1[32:128], 64, 96, 1, 1)
+            y3, _, _ = oracle.gemm("q4", q3, s3, x, r3, c1, 1, 1)
+            y4, _, _ = oracle.gemm("q8", q4, s4, y1[40:104], 32, 64, 1, 1)
+            for got, want in [(view[y1_at:y1_at + r1], y1), (view[y2_at:y2_at + 64], y2),
+                              (view[y3_at:y3_at + r3], y3), (view[y4_at:y4_at + 32], y4)]:
+                assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        for h, _ in hs:
+            L.lab_gpu_release(h)
+        L.lab_gpu_release(act)
