@@ -359,10 +359,14 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   using F = Fmt<Q4>;
   const int64_t ntiles = (a.rows + kRows - 1) / kRows;
   const int64_t blocks = a.cols / kBlock;
-  // Two CTAs per SM when the ring still gets at least 3 stages that way.
+  // Two CTAs per SM when the ring still gets at least 3 stages that way, and
+  // the tiles need more than one CTA per SM; with few tiles (a tall-K matrix
+  // such as the MLP down projection) each CTA gets a whole SM's shared memory,
+  // so more of its long stream is in flight.
   const SmemPlan base = plan<Q4>(0, NT, a.cols, F32_IN);
-  int per_sm = 2;
+  int per_sm = ntiles <= kSMs ? 1 : 2;
   int stages = (int)((kSmemPerSM / per_sm - 1024 - base.total) / (kStageBytes + 16));
+  if (per_sm == 1) stages = (int)((kMaxSmem - base.total) / (kStageBytes + 16));
   if (stages < 3) {
     per_sm = 1;
     stages = (int)((kMaxSmem - base.total) / (kStageBytes + 16));
