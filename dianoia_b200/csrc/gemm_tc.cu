@@ -248,7 +248,9 @@ __device__ __forceinline__ bool wait_tc(uint64_t* bar, uint32_t parity, uint32_t
   return true;
 }
 
-template <bool Q4>
+// kPartial: all tokens in one partial tile (n < 64), and drain warps whose
+// token columns are all beyond n skip their work.
+template <bool Q4, bool kPartial>
 __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     gemm_tc_kernel(const TcArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
                    const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tsw,
@@ -518,15 +520,21 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
     const int nblk = (int)blocks;
     int32_t dn[kEpiCols];
     const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
-    if (Q4) {
+    // Token columns of this warp that hold real tokens (kPartial: fewer than
+    // 64 tokens, e.g. a short prompt or a few sequences at the lm_head): a
+    // warp without any still keeps every barrier step, but loads and scales
+    // nothing.
+    const int64_t ncols = a.n - (tok0 + col0);
+    const int valid = !kPartial || ncols >= kEpiCols ? kEpiCols : (ncols <= 0 ? 0 : (int)ncols);
+    if (Q4 && valid > 0) {
 #pragma unroll
       for (int q = 0; q < kSlots; q++)
 #pragma unroll
         for (int c = 0; c < kEpiCols; c += 32) tmem_fill32(tlane + (uint32_t)(q * kTileTok + c), kSeed);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(tinit);
     }
+    if (Q4) mbar_arrive(tinit);
     int st = 0;
     uint32_t sph = 0;
     for (int k = 0; k < nst; k++) {
@@ -556,31 +564,33 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
         const float4 f = *reinterpret_cast<const float4*>(stage_sw(st) + row_local * kBlocksPerStage);
         sws[0] = f.x; sws[1] = f.y; sws[2] = f.z; sws[3] = f.w;
       }
+      if (valid > 0) {
 #pragma unroll
-      for (int q = parity; q < kBlocksPerStage; q += 2) {
-        const int blk = k * kBlocksPerStage + q;
-        if (blk >= nblk) break;
+        for (int q = parity; q < kBlocksPerStage; q += 2) {
+          const int blk = k * kBlocksPerStage + q;
+          if (blk >= nblk) break;
 #pragma unroll
-        for (int c = 0; c < kEpiCols; c += 32)
-          tmem_ld32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), *reinterpret_cast<int32_t(*)[32]>(dn + c));
+          for (int c = 0; c < kEpiCols; c += 32)
+            tmem_ld32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), *reinterpret_cast<int32_t(*)[32]>(dn + c));
 #pragma unroll
-        for (int c = 0; c < kEpiCols; c += 32) tmem_wait_ld_regs(*reinterpret_cast<int32_t(*)[32]>(dn + c));
-        if (Q4) {  // seed for the slot's next block
+          for (int c = 0; c < kEpiCols; c += 32) tmem_wait_ld_regs(*reinterpret_cast<int32_t(*)[32]>(dn + c));
+          if (Q4) {  // seed for the slot's next block
 #pragma unroll
-          for (int c = 0; c < kEpiCols; c += 32) tmem_fill32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), kSeed);
-        }
-        const uint64_t sw2 = f2_pack(sws[q], sws[q]);
-        const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok + col0;
+            for (int c = 0; c < kEpiCols; c += 32) tmem_fill32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), kSeed);
+          }
+          const uint64_t sw2 = f2_pack(sws[q], sws[q]);
+          const float* sxq = (tma_scales ? stage_sxb(st) : stage_sx(st)) + q * kTileTok + col0;
 #pragma unroll
-        for (int j = 0; j < kEpiCols; j += 4) {
-          const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
-          // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
-          acc[j / 2] = f2_fma(slot_to_f2<Q4>(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
-          acc[j / 2 + 1] = f2_fma(slot_to_f2<Q4>(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
-                                  acc[j / 2 + 1]);
+          for (int j = 0; j < kEpiCols; j += 4) {
+            const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
+            // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
+            acc[j / 2] = f2_fma(slot_to_f2<Q4>(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
+            acc[j / 2 + 1] = f2_fma(slot_to_f2<Q4>(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
+                                    acc[j / 2 + 1]);
+          }
         }
       }
-      if (Q4) tmem_wait_st();
+      if (Q4 && valid > 0) tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&empty[st]);  // every lane: done with the stage's scales and D slots (seeded again)
       if (++st == stages) {
@@ -694,15 +704,16 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
                                  (uint64_t)a.n, (uint64_t)blocks * 4, kBlocksPerStage, kTileTok, false))
       return kErrUnsupported;
   }
-  auto kern = gemm_tc_kernel<Q4>;
-  static bool configured[64] = {};
+  auto kern = a.n < kTileTok ? gemm_tc_kernel<Q4, true> : gemm_tc_kernel<Q4, false>;
+  static bool configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!configured[dev & 63]) {
+  const int variant = a.n < kTileTok ? 1 : 0;
+  if (!configured[variant][dev & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemTc) !=
         cudaSuccess)
       return kErrCuda;
-    configured[dev & 63] = true;
+    configured[variant][dev & 63] = true;
   }
   TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, tma_scales ? 1 : 0};
   const dim3 grid((unsigned)((a.rows + kTileRows - 1) / kTileRows),
