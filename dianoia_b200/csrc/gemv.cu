@@ -373,10 +373,14 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   }
   stages = stages > kMaxStages ? kMaxStages : stages;
   if (stages < 2) return kErrTooLarge;
-  // Persistent grid, balanced so every CTA gets the same number of tiles.
+  // Persistent grid of every CTA slot when the tiles need more than one
+  // wave: CTA b takes tiles b, b + grid, ..., and CTAs b and b + kSMs share
+  // an SM, so no SM holds more than ceil(ntiles / kSMs) + 1 tiles. (Sizing the
+  // grid for equal tiles per CTA instead - 192 CTAs of 2 for 384 tiles - left
+  // 44 SMs with 4 tiles and the rest with 2.)
   const int64_t slots = (int64_t)kSMs * per_sm;
   const int64_t waves = (ntiles + slots - 1) / slots;
-  const int64_t grid = (ntiles + waves - 1) / waves;
+  const int64_t grid = ntiles > slots ? slots : ntiles;
   // No more stages than the stages a CTA will ever load: the shared memory
   // left over lets the next kernel's CTAs become resident early (programmatic
   // dependent launch) and start streaming their weights during this kernel.
