@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // -------------------------------------------------------------- consumers
   const int r8 = lane >> 2, l = lane & 3;
+  pdl_launch_dependents();
   pdl_wait();  // the activations may come from the previous kernel
   bool ok = true;
   if (F32_IN) {
@@ -197,7 +198,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     consumers_sync();
     ok = !abort_flag;
   }
-  pdl_launch_dependents();
   if (!ok) return;
 
   const int row_local = warp * 8 + r8;
