@@ -19,6 +19,10 @@ __global__ void __launch_bounds__(kQuantThreads)
     quantize_q8_kernel(const float* __restrict__ xs, int8_t* __restrict__ xq,
                        float* __restrict__ xsc, int64_t n, int64_t cols, int64_t blocks,
                        bool vec) {
+  // The product after this (a programmatic dependent launch) may start its
+  // weight stream now; it waits for this grid's completion before reading
+  // the quantized activations.
+  pdl_launch_dependents();
   const int64_t gid = (int64_t)blockIdx.x * kQuantThreads + threadIdx.x;
   const int64_t blk = gid >> 3;
   const int sub = (int)(gid & 7);
@@ -59,6 +63,10 @@ __global__ void __launch_bounds__(kQuantThreads)
 __global__ void __launch_bounds__(kQuantThreads)
     quantize_qa_kernel(const float* __restrict__ xs, uint8_t* __restrict__ xa, int64_t n,
                        int64_t cols, int64_t blocks, int64_t xa_stride, bool vec) {
+  // The product after this (a programmatic dependent launch) may start its
+  // weight stream now; it waits for this grid's completion before reading
+  // the quantized activations.
+  pdl_launch_dependents();
   const int64_t gid = (int64_t)blockIdx.x * kQuantThreads + threadIdx.x;
   const int64_t blk = gid >> 3;
   const int sub = (int)(gid & 7);
