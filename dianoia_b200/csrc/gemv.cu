@@ -136,7 +136,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // -------------------------------------------------------------- consumers
   const int r8 = lane >> 2, l = lane & 3;
-  pdl_launch_dependents();
+  // A chained product (QA input) lets the next one start its weight stream
+  // right away; a single product from f32 inputs triggers after its
+  // prologue (back to back, an early start measured slower there).
+  if (!F32_IN) pdl_launch_dependents();
   pdl_wait();  // the activations may come from the previous kernel
   bool ok = true;
   if (F32_IN) {
@@ -198,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     consumers_sync();
     ok = !abort_flag;
   }
+  if (F32_IN) pdl_launch_dependents();
   if (!ok) return;
 
   const int row_local = warp * 8 + r8;
