@@ -475,6 +475,21 @@ int64_t dn_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols, in
              : DN_ERR_CUDA;
 }
 
+int64_t dn_gguf_split(int64_t format, const void* blocks, int64_t count, void* qs, void* scales,
+                      void* stream) {
+  if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;
+  if (count < 0 || (count > 0 && (blocks == nullptr || qs == nullptr || scales == nullptr)))
+    return DN_ERR_ARGS;
+  if (((uintptr_t)blocks & 1) != 0 || ((uintptr_t)qs & 3) != 0 ||
+      ((uintptr_t)scales & (format == DN_Q4 ? 1 : 3)) != 0)
+    return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_gguf_split(format == DN_Q4, blocks, count, qs, scales,
+                               static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
 int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
                      int64_t xa_stride, float* ys, int64_t ldy, uint8_t* ya, int64_t ya_stride,
                      int64_t rows, int64_t cols, int64_t n, int64_t flags, void* stream) {

@@ -87,6 +87,11 @@ void chain_destroy(ChainHost* h);
 int64_t chain_launch(ChainHost* h, uint32_t* status, cudaStream_t stream, bool pdl);
 int64_t chain_reset(ChainHost* h, cudaStream_t stream);
 
+// GGUF Q4_0 / Q8_0 blocks (count of them, 2-byte aligned) -> values (4-byte
+// aligned) and scales, the engine's split layout (gguf.cu).
+cudaError_t launch_gguf_split(bool q4, const void* blocks, int64_t count, void* qs, void* scales,
+                              cudaStream_t stream);
+
 // Quantizes n rows of cols floats to Q8_0 (lab_quantize_q8 semantics).
 cudaError_t launch_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
                                cudaStream_t stream);

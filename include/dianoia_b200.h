@@ -180,6 +180,16 @@ int64_t dn_linear(int64_t format, const void* qs, const void* scales, const floa
 int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const float* xs,
                        const int8_t* xq, int64_t rows, int64_t cols, int64_t n, int64_t mode);
 
+/* GGUF Q4_0 / Q8_0 blocks in device memory split into the engine's layout
+ * on the device, asynchronous: what dianoia's loader does on the CPU
+ * (gguf.dart:206-215 splitQ4_0, gguf.dart:269-283 splitQ8_0), so a loader
+ * can copy the file's blocks to the GPU as they are. `count` blocks of 18
+ * (Q4_0) or 34 (Q8_0) bytes, 2-byte aligned; qs (4-byte aligned) receives
+ * 16 or 32 value bytes per block; scales receives the fp16 scale bytes
+ * (Q4_0, 2-byte aligned) or the scale widened to f32 (Q8_0, 4-byte aligned). */
+int64_t dn_gguf_split(int64_t format, const void* blocks, int64_t count, void* qs, void* scales,
+                      void* stream);
+
 /* lab_quantize_q8 / lab_quantize_q4 on device memory, asynchronous. */
 int64_t dn_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
                        void* stream);
