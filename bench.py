@@ -499,6 +499,8 @@ def main():
                          "projection (N > 1: NCCL all-gather after each); auto: ops on 1 GPU, "
                          "chain on N > 1 (the faster of the two in each case)")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--neighbour-steps", type=int, default=30,
+                    help="tokens of the decode stack with norms, SwiGLU and residual adds")
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs"], default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
@@ -666,6 +668,7 @@ def main():
     e2e = run_e2e_gpu_layer(args, stack, L, torch) if world == 1 else None
     if e2e is None:
         e2e = e2e_cpu_abi
+    neighbours = run_neighbours(args, stack, L) if world == 1 else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and args.cpu_tokens > 0:
@@ -692,6 +695,7 @@ def main():
                                                  "by weight bytes (profiles/chain_kernel_q8_4layers.md)")},
             "e2e": e2e,
             "e2e_cpu_abi": e2e_cpu_abi,
+            "neighbours": neighbours,
             "cpu_baseline": cpu_baseline,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": ("1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
@@ -1079,19 +1083,7 @@ def run_e2e_gpu_layer(args, stack, L, torch):
         return None
     handles = []
     try:
-        mats = []
-        for m in stack.mats:
-            qs = m["qs"].cpu().numpy().view(np.uint8)
-            sc = m["scales"].cpu().numpy().view(np.uint8)
-            at = (qs.size + 63) // 64 * 64
-            raw = np.zeros(at + sc.size, np.uint8)
-            raw[:qs.size] = qs
-            raw[at:] = sc
-            h = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
-            if h < 0:
-                raise RuntimeError("lab_gpu_wrap failed")
-            handles.append(h)
-            mats.append((h, at))
+        mats = wrap_stack(L, stack, handles)
         # Activation buffer: x0, then one output region per projection kind.
         offs, at = {"x0": 0}, HIDDEN
         for name in ("qkv", "o", "gate_up", "down"):
@@ -1164,6 +1156,134 @@ def run_e2e_gpu_layer(args, stack, L, torch):
     finally:
         for h in handles:
             L.lab_gpu_release(h)
+
+
+def wrap_stack(L, stack, handles):
+    """Each matrix of the stack as one GPU-layer buffer: values, then the
+    scales at the next 64-byte boundary; returns (handle, scales offset)."""
+    mats = []
+    for m in stack.mats:
+        qs = m["qs"].cpu().numpy().view(np.uint8)
+        sc = m["scales"].cpu().numpy().view(np.uint8)
+        at = (qs.size + 63) // 64 * 64
+        raw = np.zeros(at + sc.size, np.uint8)
+        raw[:qs.size] = qs
+        raw[at:] = sc
+        h = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
+        if h < 0:
+            raise RuntimeError("lab_gpu_wrap failed")
+        handles.append(h)
+        mats.append((h, at))
+    return mats
+
+
+def run_neighbours(args, stack, L):
+    """The decode stack with the neighbours of its products, through the GPU
+    layer as dianoia's GpuForward encodes a Qwen3 layer (gpu.dart:1100-1190)
+    less the attention (out of this path: o reads q's rows in its place):
+    norm, qkv, o, residual add, norm, gate, up, SwiGLU, down, residual add;
+    then the final norm and the lm_head. The same weights as the projection
+    stack (gate and up are the two row halves of gate_up), RMSNorm weights
+    1 + 0.1 N(0, 1), eps 1e-6. Timed per token like `e2e` (host writes x0,
+    one dn_gpu_enc_batch, lab_gpu_commit(wait=1)), fused (norms hand QA
+    blocks to their products, SwiGLU and the adds run in product epilogues)
+    and with every op its own kernel on f32 inputs (dn_gpu_set_fusion(0), the
+    reference layer's dispatch structure)."""
+    steps = args.neighbour_steps
+    if steps <= 0 or L.lab_gpu_init() != 1:
+        return None
+    handles = []
+    try:
+        mats = wrap_stack(L, stack, handles)
+        rng = np.random.default_rng(7)
+        norms = (1 + 0.1 * rng.standard_normal((2 * LAYERS + 1) * HIDDEN)).astype(np.float32)
+        small = L.lab_gpu_wrap(norms.ctypes.data, norms.nbytes)
+        handles.append(small)
+        sizes = {"x": HIDDEN, "a": HIDDEN, "qkv": OUT_ROWS["qkv"], "m": HIDDEN, "g": INTER,
+                 "u": INTER}
+        buf = {}
+        for name, size in sizes.items():
+            buf[name] = L.lab_gpu_buffer(4 * size)
+            handles.append(buf[name])
+        logits_h = L.lab_gpu_readback_buffer(4 * VOCAB)
+        handles.append(logits_h)
+        if min(handles) < 0:
+            raise RuntimeError("lab_gpu_buffer failed")
+        x_view = np.ctypeslib.as_array((ctypes.c_float * HIDDEN).from_address(L.lab_gpu_contents(buf["x"])))
+        logits_view = np.ctypeslib.as_array(
+            (ctypes.c_float * VOCAB).from_address(L.lab_gpu_contents(logits_h)))
+        eps_bits = int(np.array([1e-6], np.float64).view(np.int64)[0])
+        B = buf
+
+        def norm(slot):
+            return [2, B["x"], 0, small, 4 * HIDDEN * slot, B["a"], 0, 1, HIDDEN, eps_bits, 0]
+
+        def add():
+            return [4, B["m"], 0, B["x"], 0, HIDDEN, 0, 0, 0, 0, 0]
+
+        table = []
+        for layer in range(LAYERS):
+            (wqkv, aqkv), (wo, ao), (wgu, agu), (wd, ad) = mats[4 * layer:4 * layer + 4]
+            half_qs, half_sc = INTER * HIDDEN, INTER * (HIDDEN // 32) * 4
+            table += [norm(2 * layer),
+                      [0, wqkv, 0, aqkv, B["a"], 0, B["qkv"], 0, OUT_ROWS["qkv"], HIDDEN, 1],
+                      [0, wo, 0, ao, B["qkv"], 0, B["m"], 0, HIDDEN, HIDDEN, 1],
+                      add(),
+                      norm(2 * layer + 1),
+                      [0, wgu, 0, agu, B["a"], 0, B["g"], 0, INTER, HIDDEN, 1],
+                      [0, wgu, half_qs, agu + half_sc, B["a"], 0, B["u"], 0, INTER, HIDDEN, 1],
+                      [3, B["g"], B["u"], INTER, 0, 0, 0, 0, 0, 0, 0],
+                      [0, wd, 0, ad, B["g"], 0, B["m"], 0, HIDDEN, INTER, 1],
+                      add()]
+        wl, al = mats[-1]
+        table += [norm(2 * LAYERS), [0, wl, 0, al, B["a"], 0, logits_h, 0, VOCAB, HIDDEN, 1]]
+        table = np.ascontiguousarray(np.array(table, np.int64))
+        x0 = stack.x0.cpu().numpy()
+
+        def run(fused):
+            L.dn_gpu_set_fusion(1 if fused else 0)
+            dev_ms = []
+
+            def one_token():
+                x_view[:] = x0
+                L.lab_gpu_begin()
+                L.dn_gpu_enc_batch(table.ctypes.data, len(table))
+                if L.lab_gpu_commit(1) != 1:
+                    raise RuntimeError("lab_gpu_commit failed")
+                dev_ms.append(L.lab_gpu_last_ms())
+
+            for _ in range(3):
+                one_token()
+            dev_ms.clear()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                one_token()
+            tps = steps / (time.perf_counter() - t0)
+            return tps, float(np.median(dev_ms)), logits_view.copy()
+
+        fused_tps, fused_ms, fused_logits = run(True)
+        plain_tps, plain_ms, plain_logits = run(False)
+        L.dn_gpu_set_fusion(1)
+        return {
+            "workload": (f"Qwen3-1.7B-shaped decode stack with its neighbours: {LAYERS} x [RMSNorm, "
+                         "qkv, o, add, RMSNorm, gate, up, SwiGLU, down, add] + RMSNorm + lm_head "
+                         "(attention omitted), batch 1, through lab_gpu_* with one "
+                         "dn_gpu_enc_batch per token"),
+            "ops_per_token": len(table),
+            "fused": {"tokens_s": fused_tps, "commit_device_ms": fused_ms,
+                      "kernels_per_token": 7 * LAYERS + 2},
+            "unfused": {"tokens_s": plain_tps, "commit_device_ms": plain_ms,
+                        "kernels_per_token": 10 * LAYERS + 2},
+            "logits_identical": bool(np.array_equal(fused_logits.view(np.uint32),
+                                                    plain_logits.view(np.uint32))),
+            "logits_finite": bool(np.isfinite(fused_logits).all()),
+            "steps": steps,
+        }
+    finally:
+        L.dn_gpu_set_fusion(1)
+        for h in handles:
+            if h >= 0:
+                L.lab_gpu_release(h)
 
 
 def run_cpu_baseline(args, stack):

@@ -41,13 +41,19 @@ SIGNATURES = {
     "lab_gpu_last_ms": (ctypes.c_double, []),
     "lab_gpu_enc_matmul_q8": (None, [_i64] * 10),
     "lab_gpu_enc_matmul_q4": (None, [_i64] * 10),
+    "lab_gpu_enc_rms_norm": (None, [_i64] * 8 + [ctypes.c_double, _i64]),
+    "lab_gpu_enc_swiglu": (None, [_i64] * 3),
+    "lab_gpu_enc_add": (None, [_i64] * 5),
     "dn_gpu_enc_batch": (None, [_p, _i64]),
+    "dn_gpu_set_fusion": (None, [_i64]),
     "dn_linear": (_i64, [_i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_gguf_split": (_i64, [_i64, _p, _i64, _p, _p, _p]),
     "dn_quantize_q4": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_quantize_qa": (_i64, [_p, _p, _i64, _i64, _i64, _p]),
+    "dn_rms_norm": (_i64, [_p, _p, _p, _p, _i64, _i64, _i64, ctypes.c_double, _i64, _i64, _p]),
+    "dn_swiglu": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_chain_create": (_i64, [_i64, _p, _i64, _p]),
     "dn_chain_create_sharded": (_i64, [_i64, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
@@ -69,6 +75,7 @@ DN_OK, DN_ERR_ARGS, DN_ERR_CUDA, DN_ERR_NO_DEVICE, DN_ERR_UNSUPPORTED, DN_ERR_TO
 DN_Q8, DN_Q4 = 0, 1
 DN_PATH_AUTO, DN_PATH_GEMV, DN_PATH_TC, DN_PATH_GENERIC = -1, 0, 1, 2
 DN_FLAG_PDL = 1
+DN_BATCH_Q8, DN_BATCH_Q4, DN_BATCH_RMS_NORM, DN_BATCH_SWIGLU, DN_BATCH_ADD = 0, 1, 2, 3, 4
 QA_BYTES = 36  # QA activation block: 32 int8 + f32 scale
 DN_PEER_HANDLE_BYTES = 64
 

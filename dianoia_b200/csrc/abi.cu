@@ -490,6 +490,35 @@ int64_t dn_gguf_split(int64_t format, const void* blocks, int64_t count, void* q
              : DN_ERR_CUDA;
 }
 
+int64_t dn_rms_norm(const float* x, const float* w, float* out, uint8_t* qa, int64_t qa_stride,
+                    int64_t rows, int64_t cols, double eps, int64_t accumulate, int64_t flags,
+                    void* stream) {
+  if (rows < 0 || cols < 0 || rows > 0x7fffffff) return DN_ERR_ARGS;
+  if (rows > 0 && cols > 0 && (x == nullptr || w == nullptr || out == nullptr)) return DN_ERR_ARGS;
+  if (((uintptr_t)x & 3) != 0 || ((uintptr_t)w & 3) != 0 || ((uintptr_t)out & 3) != 0) return DN_ERR_ARGS;
+  if (qa != nullptr && (cols % 32 != 0 || qa_stride < (cols / 32) * dn::kQABytes ||
+                        ((uintptr_t)qa & 3) != 0 || (qa_stride & 3) != 0))
+    return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  const dn::NormArgs a{x, w, out, qa, qa_stride, rows, cols, eps, accumulate != 0};
+  return dn::launch_rms_norm(a, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0) ==
+                 cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
+int64_t dn_swiglu(float* g, const float* u, uint8_t* qa, int64_t count, int64_t flags, void* stream) {
+  if (count < 0 || (count > 0 && (g == nullptr || u == nullptr))) return DN_ERR_ARGS;
+  if (((uintptr_t)g & 3) != 0 || ((uintptr_t)u & 3) != 0) return DN_ERR_ARGS;
+  if (qa != nullptr && (count % 32 != 0 || ((uintptr_t)qa & 3) != 0)) return DN_ERR_ARGS;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  const dn::SwigluArgs a{g, u, qa, count};
+  return dn::launch_swiglu(a, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0) ==
+                 cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
 int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
                      int64_t xa_stride, float* ys, int64_t ldy, uint8_t* ya, int64_t ya_stride,
                      int64_t rows, int64_t cols, int64_t n, int64_t flags, void* stream) {

@@ -78,6 +78,17 @@ __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
   return __half2float(__ushort_as_half(h));  // exact
 }
 
+// One SwiGLU output, silu(g) * u, as dianoia's CPU feed-forward computes it
+// (lib/src/shard.dart:456-460): g / (1 + exp(-g)) in double, stored to f32,
+// then an f32 product with u. CUDA's double exp differs from the C library's
+// by at most an ulp of a double, which moves the f32 result only when the
+// quotient lies within that of an f32 rounding boundary.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const double gd = (double)g;
+  const float s = __double2float_rn(__ddiv_rn(gd, __dadd_rn(1.0, exp(-gd))));
+  return __fmul_rn(s, u);
+}
+
 // --------------------------------------------------------------- PTX wrappers
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

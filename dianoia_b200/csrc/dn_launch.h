@@ -48,7 +48,46 @@ struct GemvArgs {
   int64_t ya_stride;
   int64_t rows, cols, n;
   uint32_t* status;
+  // SwiGLU in the epilogue (optional): this product computes one of the
+  // feed-forward's g and u, glu_other holds the other (same [n, ldy]
+  // layout), and h = silu(g) * u goes to glu_out and, with ya, into the QA
+  // outputs. With glu_self_gate this product's outputs are g (ys is then not
+  // written: h replaces g); otherwise they are u, written to ys as usual.
+  const float* glu_other;
+  float* glu_out;
+  bool glu_self_gate;
+  // Residual add in the epilogue (optional): res[t * ldy + r] += y, after
+  // the product's own outputs (the layer's dst += src right after it).
+  float* res;
 };
+
+// RMSNorm of `rows` rows of `cols` values: out = w * (x * r), r =
+// 1 / sqrt(mean(x^2) + eps), added into out with `accumulate`; with qa, the
+// results also as QA blocks, row t at qa + t * qa_stride (cols % 32 == 0).
+struct NormArgs {
+  const float* x;
+  const float* w;
+  float* out;
+  uint8_t* qa;
+  int64_t qa_stride;
+  int64_t rows, cols;
+  double eps;
+  bool accumulate;
+};
+cudaError_t launch_rms_norm(const NormArgs& a, cudaStream_t stream, bool pdl);
+
+// g = silu(g) * u over `count` values; with qa, also the QA blocks of the
+// results, block b at qa + b * kQABytes (count % 32 == 0).
+struct SwigluArgs {
+  float* g;
+  const float* u;
+  uint8_t* qa;
+  int64_t count;
+};
+cudaError_t launch_swiglu(const SwigluArgs& a, cudaStream_t stream, bool pdl);
+
+// dst += src over `count` f32 values (the residual add).
+cudaError_t launch_add(const float* src, float* dst, int64_t count, cudaStream_t stream, bool pdl);
 
 // The decode GEMV on either activation form (gemv.cu).
 int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl);

@@ -31,7 +31,10 @@
 // per CTA: f32 inputs are bulk-copied and quantized in the CTA (which fuses
 // lab_gemm's input quantize; CTA 0 also writes xq / xsc out), QA inputs are
 // bulk-copied as they are. Each tile's 32 outputs per token can be quantized
-// again in the epilogue (QA output) for the next product of a chain.
+// again in the epilogue (QA output) for the next product of a chain, and the
+// feed-forward's SwiGLU can run there too, on the outputs of the gate / up
+// pair's second product and the first one's (glu_* arguments), and so can the
+// residual add that follows a layer's output projections (res).
 #include <string.h>
 
 #include <algorithm>
@@ -286,8 +289,20 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int t = 0; t < NT; t++) {
       const float y = lane_reduce(acc[t]);
       if (l == 0 && row_local < tile_rows && t < nt) {
-        if (a.ys != nullptr) a.ys[(t0 + t) * a.ldy + row0 + row_local] = y;
-        yt[t * kRows + row_local] = y;
+        const int64_t at = (t0 + t) * a.ldy + row0 + row_local;
+        float v = y;
+        if (a.glu_out != nullptr) {
+          // The feed-forward's other half was written by the previous kernel,
+          // which completed before this one's dependent-launch wait.
+          const float other = a.glu_other[at];
+          v = a.glu_self_gate ? silu_mul(y, other) : silu_mul(other, y);
+          if (!a.glu_self_gate && a.ys != nullptr) a.ys[at] = y;
+          a.glu_out[at] = v;
+        } else if (a.ys != nullptr) {
+          a.ys[at] = y;
+        }
+        if (a.res != nullptr) a.res[at] = __fadd_rn(a.res[at], y);
+        yt[t * kRows + row_local] = v;
       }
     }
     if (a.ya != nullptr && tile_rows == kRows) {
@@ -467,6 +482,11 @@ bool gemv_ex_supported(const GemvArgs& g) {
     return false;
   if (g.xa != nullptr && (((uintptr_t)g.xa & 3) != 0 || (g.xa_stride & 3) != 0)) return false;
   if (g.ya != nullptr && (((uintptr_t)g.ya & 3) != 0 || (g.ya_stride & 3) != 0)) return false;
+  if (g.glu_out != nullptr &&
+      (g.glu_other == nullptr || ((uintptr_t)g.glu_out & 3) != 0 || ((uintptr_t)g.glu_other & 3) != 0))
+    return false;
+  if (g.ys != nullptr && ((uintptr_t)g.ys & 3) != 0) return false;
+  if (g.res != nullptr && ((uintptr_t)g.res & 3) != 0) return false;
   return (g.q4 ? plan<true>(2, 1, g.cols, g.xs != nullptr).total
                : plan<false>(2, 1, g.cols, g.xs != nullptr).total) <= kMaxSmem;
 }

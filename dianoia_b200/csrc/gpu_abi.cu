@@ -55,19 +55,43 @@ struct Buf {
   bool weights_on_device = false;  // copied once, at its first use as a matrix
 };
 
+enum Kind : int { kMatmul = 0, kNorm = 1, kSwiglu = 2, kAdd = 3 };
+
+// One recorded operation. Every kind writes f32 values token-major, n rows
+// of `rows` values at byte y_off of buffer y, and reads n rows of `cols`
+// values at x_off of buffer x:
+//  * kMatmul: weights w (values at qs_off, scales at sc_off), [rows, cols];
+//  * kNorm: RMSNorm of n rows of rows == cols values with the weights at
+//    qs_off of buffer w, eps, and acc (added into the output, which it then
+//    also reads);
+//  * kSwiglu: g = y and u = x, both at offset 0, count = rows == cols, n = 1;
+//    it also reads g. No weights (w = -1).
+//  * kAdd: dst = y at y_off plus src = x at x_off, count = rows == cols,
+//    n = 1; it also reads dst. No weights.
 struct Op {
+  int kind;
   bool q4;
   int64_t w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n;
+  double eps;
+  bool acc;
   bool operator==(const Op& o) const {
-    return q4 == o.q4 && w == o.w && qs_off == o.qs_off && sc_off == o.sc_off && x == o.x &&
-           x_off == o.x_off && y == o.y && y_off == o.y_off && rows == o.rows && cols == o.cols &&
-           n == o.n;
+    return kind == o.kind && q4 == o.q4 && w == o.w && qs_off == o.qs_off && sc_off == o.sc_off &&
+           x == o.x && x_off == o.x_off && y == o.y && y_off == o.y_off && rows == o.rows &&
+           cols == o.cols && n == o.n && memcmp(&eps, &o.eps, sizeof eps) == 0 && acc == o.acc;
   }
 };
 
 struct Range {
   int64_t buf, lo, hi;  // bytes [lo, hi) of buffer `buf`
 };
+
+Range writes(const Op& o) { return Range{o.y, o.y_off, o.y_off + o.n * o.rows * 4}; }
+
+void reads(const Op& o, std::vector<Range>& r) {
+  r.clear();
+  r.push_back(Range{o.x, o.x_off, o.x_off + o.n * o.cols * 4});
+  if (o.kind == kSwiglu || o.kind == kAdd || (o.kind == kNorm && o.acc)) r.push_back(writes(o));
+}
 
 std::recursive_mutex g_mu;
 bool g_ready = false;
@@ -91,8 +115,13 @@ int64_t g_xcap = 0;
 uint8_t* g_qa = nullptr;
 int64_t g_qa_cap = 0;
 
+// Fusions and QA links on (dn_gpu_set_fusion); off, every op runs as its own
+// kernel on f32 inputs, as the reference's layer dispatches them.
+bool g_fuse = true;
+
 // The graph of the last command buffer, with what it was captured from.
 cudaGraphExec_t g_exec = nullptr;
+bool g_exec_fuse = true;
 std::vector<Op> g_exec_ops;
 std::vector<uint8_t*> g_exec_ptrs;  // device addresses the graph uses, per op (w, x, y)
 int8_t* g_exec_xq = nullptr;
@@ -162,10 +191,17 @@ int64_t new_buffer(int64_t bytes) {
   return h;
 }
 
+constexpr int64_t kMaxSide = int64_t(1) << 30;  // keeps every byte count below 2^63
+
+bool sides_ok(int64_t a, int64_t b) { return a >= 0 && b >= 0 && a < kMaxSide && b < kMaxSide; }
+
 void encode(bool q4, int64_t w, int64_t qs_off, int64_t sc_off, int64_t x, int64_t x_off, int64_t y,
             int64_t y_off, int64_t rows, int64_t cols, int64_t n) {
   std::lock_guard<std::recursive_mutex> lock(g_mu);
-  const bool ok = rows >= 0 && cols >= 0 && n >= 0 && cols % kBlock == 0 &&
+  // f32 activations and scales at their natural alignment: the kernels load
+  // them as such.
+  const bool ok = sides_ok(rows, cols) && sides_ok(n, 0) && cols % kBlock == 0 &&
+                  x_off % 4 == 0 && y_off % 4 == 0 && sc_off % (q4 ? 2 : 4) == 0 &&
                   fits(w, qs_off, q4 ? rows * cols / 2 : rows * cols) &&
                   fits(w, sc_off, rows * (cols / kBlock) * (q4 ? 2 : 4)) &&
                   fits(x, x_off, n * cols * 4) && fits(y, y_off, n * rows * 4);
@@ -173,7 +209,40 @@ void encode(bool q4, int64_t w, int64_t qs_off, int64_t sc_off, int64_t x, int64
     g_bad_op = true;
     return;
   }
-  g_ops.push_back(Op{q4, w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n});
+  g_ops.push_back(Op{kMatmul, q4, w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n, 0.0, false});
+}
+
+void encode_norm(int64_t x, int64_t x_off, int64_t w, int64_t w_off, int64_t out, int64_t out_off,
+                 int64_t rows, int64_t cols, double eps, int64_t accumulate) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  const bool ok = sides_ok(rows, cols) && x_off % 4 == 0 && w_off % 4 == 0 && out_off % 4 == 0 &&
+                  fits(x, x_off, rows * cols * 4) && fits(w, w_off, cols * 4) &&
+                  fits(out, out_off, rows * cols * 4);
+  if (!ok) {
+    g_bad_op = true;
+    return;
+  }
+  g_ops.push_back(Op{kNorm, false, w, w_off, 0, x, x_off, out, out_off, cols, cols, rows, eps,
+                     accumulate != 0});
+}
+
+void encode_add(int64_t src, int64_t src_off, int64_t dst, int64_t dst_off, int64_t count) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (!sides_ok(count, 0) || src_off % 4 != 0 || dst_off % 4 != 0 || !fits(src, src_off, count * 4) ||
+      !fits(dst, dst_off, count * 4)) {
+    g_bad_op = true;
+    return;
+  }
+  g_ops.push_back(Op{kAdd, false, -1, 0, 0, src, src_off, dst, dst_off, count, count, 1, 0.0, false});
+}
+
+void encode_swiglu(int64_t g, int64_t u, int64_t count) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (!sides_ok(count, 0) || !fits(g, 0, count * 4) || !fits(u, 0, count * 4)) {
+    g_bad_op = true;
+    return;
+  }
+  g_ops.push_back(Op{kSwiglu, false, -1, 0, 0, u, 0, g, 0, count, count, 1, 0.0, false});
 }
 
 // Adds [lo, hi) of buffer b to a list of ranges, merging overlaps.
@@ -218,54 +287,103 @@ dn::LinearArgs linear_args(const Op& o, uint32_t* status) {
                         1, status};
 }
 
-// QA links of the recorded products (decode GEMV path only). Product i reads
-// its input as QA blocks at byte xa_at[i] of g_qa (row stride xa_stride[i])
-// when the input is either
-//  * a 32-value-aligned part of the output of the last product that wrote
-//    over it (all of the output when n > 1, where token strides must agree);
-//    that product then also writes its output as QA blocks, at ya_at[j]; or
-//  * host data no earlier product wrote: quantized once, before the products,
-//    for every product that reads the same range.
+// How the recorded ops run: fusions and QA links (decode GEMV path only).
+//
+// SwiGLU fusion: a SwiGLU op right after the two products that wrote its g
+// and u (the feed-forward's gate and up, in either order, same tokens and
+// rows) runs in the second product's epilogue (glu[i]), and launches nothing
+// itself (absorbed). Residual-add fusion: an add right after the product
+// that wrote all of its src, into a dst the product does not read, runs in
+// that product's epilogue (res[i]) and is absorbed too.
+//
+// QA links: every op that writes 32-value rows can also write them as QA
+// blocks (the GEMV epilogue, the norm and SwiGLU kernels); with rows a
+// multiple of 32, its QA blocks lie in the order of its values, block v/32 of
+// value v of the written range, whatever the token split. Product i reads its
+// input as QA blocks at byte xa_at[i] of g_qa (row stride xa_stride[i]) when
+// the input is either
+//  * a 32-value-aligned part of the range of the last op that wrote over it,
+//    which then also writes its values as QA blocks, at ya_at[j] (a SwiGLU
+//    run by a product: that product's QA outputs); or
+//  * host data no earlier op wrote: quantized once, before the ops, for
+//    every product that reads the same range.
 struct HostQA {
   int64_t buf, off, n, cols, at;
 };
-struct Links {
+struct Plan {
   std::vector<int64_t> xa_at, xa_stride, ya_at;
+  std::vector<int> glu;         // product i runs SwiGLU op glu[i] in its epilogue, or -1
+  std::vector<int> res;         // product i runs add op res[i] in its epilogue, or -1
+  std::vector<bool> absorbed;   // a SwiGLU op that a product's epilogue runs
   std::vector<HostQA> host;
   int64_t bytes = 0;
 };
 
 int64_t qa_bytes(int64_t n, int64_t values) { return (n * (values / kBlock) * dn::kQABytes + 15) / 16 * 16; }
 
-Links plan_links(uint32_t* status) {
+Plan plan_ops(uint32_t* status) {
   const int n = (int)g_ops.size();
-  Links k;
+  Plan k;
   k.xa_at.assign(n, -1);
   k.xa_stride.assign(n, 0);
   k.ya_at.assign(n, -1);
-  std::vector<bool> gemv(n);
-  for (int i = 0; i < n; i++) gemv[i] = dn::path_for(linear_args(g_ops[i], status)) == 0;
+  k.glu.assign(n, -1);
+  k.res.assign(n, -1);
+  k.absorbed.assign(n, false);
+  if (!g_fuse) return k;
+  std::vector<bool> gemv(n, false);
+  for (int i = 0; i < n; i++)
+    gemv[i] = g_ops[i].kind == kMatmul && dn::path_for(linear_args(g_ops[i], status)) == 0;
+  for (int i = 2; i < n; i++) {
+    const Op &s = g_ops[i], &a = g_ops[i - 2], &b = g_ops[i - 1];
+    if (s.kind != kSwiglu || !gemv[i - 2] || !gemv[i - 1] || s.x == s.y) continue;
+    const bool pair = (a.y == s.y && b.y == s.x) || (a.y == s.x && b.y == s.y);
+    if (pair && a.n == b.n && a.rows == b.rows && a.n * a.rows == s.rows && a.y_off == 0 &&
+        b.y_off == 0 && b.x != s.x && b.x != s.y) {
+      k.glu[i - 1] = i;
+      k.absorbed[i] = true;
+    }
+  }
+  for (int i = 1; i < n; i++) {
+    const Op &d = g_ops[i], &p = g_ops[i - 1];
+    if (d.kind != kAdd || !gemv[i - 1] || k.glu[i - 1] >= 0) continue;
+    const Range src{d.x, d.x_off, d.x_off + d.rows * 4}, dst = writes(d), out = writes(p);
+    const Range in{p.x, p.x_off, p.x_off + p.n * p.cols * 4};
+    auto overlap = [](const Range& a, const Range& b) { return a.buf == b.buf && a.lo < b.hi && b.lo < a.hi; };
+    if (out.buf == src.buf && out.lo == src.lo && out.hi == src.hi && !overlap(dst, in) && !overlap(dst, out)) {
+      k.res[i - 1] = i;
+      k.absorbed[i] = true;
+    }
+  }
+  // The op whose launch writes the QA blocks of op j's values, or -1.
+  std::vector<int> qa_src(n, -1);
+  for (int j = 0; j < n; j++) {
+    const Op& o = g_ops[j];
+    if (o.rows % kBlock != 0) continue;
+    if (o.kind == kMatmul) qa_src[j] = gemv[j] && k.glu[j] < 0 ? j : -1;
+    else if (o.kind == kSwiglu && k.absorbed[j]) qa_src[j] = g_ops[j - 1].rows % kBlock == 0 ? j - 1 : -1;
+    else if (o.kind != kAdd) qa_src[j] = j;
+  }
   for (int i = 0; i < n; i++) {
     const Op& c = g_ops[i];
     if (!gemv[i] || c.cols % kBlock != 0) continue;
     const int64_t lo = c.x_off, hi = c.x_off + c.n * c.cols * 4;
     int j = i - 1;
     for (; j >= 0; j--) {
-      const Op& p = g_ops[j];
-      if (p.y == c.x && p.y_off < hi && lo < p.y_off + p.n * p.rows * 4) break;
+      const Range w = writes(g_ops[j]);
+      if (w.buf == c.x && w.lo < hi && lo < w.hi) break;
     }
     if (j >= 0) {
-      const Op& p = g_ops[j];
-      const int64_t delta = lo - p.y_off;
-      const bool inside = delta >= 0 && hi <= p.y_off + p.n * p.rows * 4 && delta % (kBlock * 4) == 0;
-      const bool tokens_agree = (c.n == 1 && p.n == 1) || (delta == 0 && p.n == c.n && p.rows == c.cols);
-      if (!gemv[j] || p.rows % kBlock != 0 || !inside || !tokens_agree) continue;
-      if (k.ya_at[j] < 0) {
-        k.ya_at[j] = k.bytes;
-        k.bytes += qa_bytes(p.n, p.rows);
+      const Range w = writes(g_ops[j]);
+      const int64_t delta = lo - w.lo;
+      const int src = qa_src[j];
+      if (src < 0 || delta < 0 || hi > w.hi || delta % (kBlock * 4) != 0) continue;
+      if (k.ya_at[src] < 0) {
+        k.ya_at[src] = k.bytes;
+        k.bytes += qa_bytes(g_ops[src].n, g_ops[src].rows);
       }
-      k.xa_at[i] = k.ya_at[j] + delta / (kBlock * 4) * dn::kQABytes;
-      k.xa_stride[i] = p.rows / kBlock * dn::kQABytes;
+      k.xa_at[i] = k.ya_at[src] + delta / (kBlock * 4) * dn::kQABytes;
+      k.xa_stride[i] = c.cols / kBlock * dn::kQABytes;
     } else {
       size_t h = 0;
       for (; h < k.host.size(); h++) {
@@ -283,8 +401,10 @@ Links plan_links(uint32_t* status) {
   return k;
 }
 
+float* f32_at(int64_t buf, int64_t off) { return reinterpret_cast<float*>(g_bufs[buf].dev + off); }
+
 bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
-            const Links& k, uint32_t* status) {
+            const Plan& k, uint32_t* status) {
   for (const Range& r : uploads) {
     const Buf& b = g_bufs[r.buf];
     if (cudaMemcpyAsync(b.dev + r.lo, b.host + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyHostToDevice,
@@ -298,9 +418,28 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
   }
   for (size_t i = 0; i < g_ops.size(); i++) {
     const Op& o = g_ops[i];
+    uint8_t* qa_out = k.ya_at[i] >= 0 ? g_qa + k.ya_at[i] : nullptr;
+    if (o.kind == kNorm) {
+      const dn::NormArgs na{f32_at(o.x, o.x_off), f32_at(o.w, o.qs_off), f32_at(o.y, o.y_off), qa_out,
+                            o.rows / kBlock * dn::kQABytes, o.n, o.rows, o.eps, o.acc};
+      if (dn::launch_rms_norm(na, g_stream, true) != cudaSuccess) return false;
+      continue;
+    }
+    if (o.kind == kAdd) {
+      if (k.absorbed[i]) continue;
+      if (dn::launch_add(f32_at(o.x, o.x_off), f32_at(o.y, o.y_off), o.rows, g_stream, true) != cudaSuccess)
+        return false;
+      continue;
+    }
+    if (o.kind == kSwiglu) {
+      if (k.absorbed[i]) continue;
+      const dn::SwigluArgs sa{f32_at(o.y, 0), f32_at(o.x, 0), qa_out, o.rows};
+      if (dn::launch_swiglu(sa, g_stream, true) != cudaSuccess) return false;
+      continue;
+    }
     const dn::LinearArgs a = linear_args(o, status);
     int64_t rc;
-    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0) {
+    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0) {
       dn::GemvArgs g{};
       g.q4 = o.q4;
       g.qs = a.qs;
@@ -317,6 +456,13 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
         g.ya = g_qa + k.ya_at[i];
         g.ya_stride = o.rows / kBlock * dn::kQABytes;
       }
+      if (k.glu[i] >= 0) {
+        const Op& s = g_ops[k.glu[i]];  // g = s.y, u = s.x
+        g.glu_self_gate = o.y == s.y;
+        g.glu_other = f32_at(g.glu_self_gate ? s.x : s.y, 0);
+        g.glu_out = f32_at(s.y, 0);
+      }
+      if (k.res[i] >= 0) g.res = f32_at(g_ops[k.res[i]].y, g_ops[k.res[i]].y_off);
       g.rows = o.rows;
       g.cols = o.cols;
       g.n = o.n;
@@ -336,13 +482,16 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
   return true;
 }
 
+uint8_t* dev_of(int64_t h) { return h >= 0 ? g_bufs[h].dev : nullptr; }
+
 bool same_as_graph() {
-  if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_qa != g_qa || g_exec_ops.size() != g_ops.size())
+  if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_qa != g_qa || g_exec_ops.size() != g_ops.size() ||
+      g_exec_fuse != g_fuse)
     return false;
   for (size_t i = 0; i < g_ops.size(); i++) {
     const Op &a = g_ops[i], &b = g_exec_ops[i];
-    if (!(a == b) || g_exec_ptrs[3 * i] != g_bufs[a.w].dev ||
-        g_exec_ptrs[3 * i + 1] != g_bufs[a.x].dev || g_exec_ptrs[3 * i + 2] != g_bufs[a.y].dev)
+    if (!(a == b) || g_exec_ptrs[3 * i] != dev_of(a.w) || g_exec_ptrs[3 * i + 1] != dev_of(a.x) ||
+        g_exec_ptrs[3 * i + 2] != dev_of(a.y))
       return false;
   }
   return true;
@@ -359,8 +508,9 @@ int64_t commit(int64_t wait) {
   uint32_t* status = nullptr;
   volatile uint32_t* status_host = nullptr;
   if (!dn::status_words(&status, &status_host)) return 0;
-  // Weights: once per buffer, outside the graph.
+  // Weights (matrices and norm weights): once per buffer, outside the graph.
   for (const Op& o : g_ops) {
+    if (o.w < 0) continue;
     Buf& b = g_bufs[o.w];
     if (!b.weights_on_device) {
       if (cudaMemcpyAsync(b.dev, b.host, (size_t)b.bytes, cudaMemcpyHostToDevice, g_stream) !=
@@ -371,7 +521,8 @@ int64_t commit(int64_t wait) {
   }
   // Scratch for the tensor-core path.
   int64_t need = 0;
-  for (const Op& o : g_ops) need = std::max(need, o.n * o.cols);
+  for (const Op& o : g_ops)
+    if (o.kind == kMatmul) need = std::max(need, o.n * o.cols);
   if (need > g_xcap) {
     if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
     drop_graph();
@@ -389,8 +540,8 @@ int64_t commit(int64_t wait) {
   }
   if (!same_as_graph()) {
     drop_graph();
-    const Links links = plan_links(status);
-    const int64_t qa_need = links.bytes;
+    const Plan plan = plan_ops(status);
+    const int64_t qa_need = plan.bytes;
     if (qa_need > g_qa_cap) {
       if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
       cudaFree(g_qa);
@@ -402,15 +553,17 @@ int64_t commit(int64_t wait) {
       }
       g_qa_cap = qa_need;
     }
-    // Ranges to copy in (host-written inputs) and out (products' outputs).
-    std::vector<Range> uploads, written;
+    // Ranges to copy in (host-written inputs) and out (the ops' outputs).
+    std::vector<Range> uploads, written, in;
     for (const Op& o : g_ops) {
-      subtract(written, o.x, o.x_off, o.x_off + o.n * o.cols * 4, uploads);
-      add_range(written, o.y, o.y_off, o.y_off + o.n * o.rows * 4);
+      reads(o, in);
+      for (const Range& r : in) subtract(written, r.buf, r.lo, r.hi, uploads);
+      const Range w = writes(o);
+      add_range(written, w.buf, w.lo, w.hi);
     }
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
-    const bool ok = record(uploads, written, links, status);
+    const bool ok = record(uploads, written, plan, status);
     const cudaError_t e = cudaStreamEndCapture(g_stream, &graph);
     if (!ok || e != cudaSuccess || graph == nullptr ||
         cudaGraphInstantiate(&g_exec, graph, 0) != cudaSuccess) {
@@ -421,12 +574,13 @@ int64_t commit(int64_t wait) {
     }
     cudaGraphDestroy(graph);
     g_exec_ops = g_ops;
+    g_exec_fuse = g_fuse;
     g_exec_xq = g_xq;
     g_exec_qa = g_qa;
     for (const Op& o : g_ops) {
-      g_exec_ptrs.push_back(g_bufs[o.w].dev);
-      g_exec_ptrs.push_back(g_bufs[o.x].dev);
-      g_exec_ptrs.push_back(g_bufs[o.y].dev);
+      g_exec_ptrs.push_back(dev_of(o.w));
+      g_exec_ptrs.push_back(dev_of(o.x));
+      g_exec_ptrs.push_back(dev_of(o.y));
     }
   }
   if (cudaEventRecord(g_ev0, g_stream) != cudaSuccess ||
@@ -551,11 +705,41 @@ void lab_gpu_enc_matmul_q4(int64_t w, int64_t qsOffset, int64_t scalesOffset, in
   encode(true, w, qsOffset, scalesOffset, x, xOffset, y, yOffset, rows, cols, n);
 }
 
+void lab_gpu_enc_rms_norm(int64_t x, int64_t xOffset, int64_t w, int64_t wOffset, int64_t out,
+                          int64_t outOffset, int64_t rows, int64_t cols, double eps, int64_t accumulate) {
+  encode_norm(x, xOffset, w, wOffset, out, outOffset, rows, cols, eps, accumulate);
+}
+
+void lab_gpu_enc_swiglu(int64_t g, int64_t u, int64_t count) { encode_swiglu(g, u, count); }
+
+void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count) {
+  encode_add(src, srcOffset, dst, dstOffset, count);
+}
+
+void dn_gpu_set_fusion(int64_t on) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  g_fuse = on != 0;
+}
+
 void dn_gpu_enc_batch(const int64_t* table, int64_t count) {
   std::lock_guard<std::recursive_mutex> lock(g_mu);
   for (int64_t i = 0; i < count && table != nullptr; i++) {
     const int64_t* r = table + 11 * i;
-    encode(r[0] != 0, r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], r[9], r[10]);
+    switch (r[0]) {
+      case DN_BATCH_Q8:
+      case DN_BATCH_Q4:
+        encode(r[0] == DN_BATCH_Q4, r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], r[9], r[10]);
+        break;
+      case DN_BATCH_RMS_NORM: {
+        double eps;
+        memcpy(&eps, &r[9], sizeof eps);
+        encode_norm(r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], eps, r[10]);
+        break;
+      }
+      case DN_BATCH_SWIGLU: encode_swiglu(r[1], r[2], r[3]); break;
+      case DN_BATCH_ADD: encode_add(r[1], r[2], r[3], r[4], r[5]); break;
+      default: g_bad_op = true;
+    }
   }
 }
 

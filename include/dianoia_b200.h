@@ -114,8 +114,8 @@ int64_t lab_gpu_live_buffers(void);
 /* Opens the command buffer (waiting for one committed without waiting).
  * Replaces lab_gpu_begin, lab_vulkan.c:655. */
 void lab_gpu_begin(void);
-/* Runs the recorded products; with `wait`, blocks until done. Returns 1, or 0
- * if a product's buffers or sizes did not fit or the GPU failed.
+/* Runs the recorded operations; with `wait`, blocks until done. Returns 1, or
+ * 0 if an operation's buffers, offsets or sizes did not fit or the GPU failed.
  * Replaces lab_gpu_commit, lab_vulkan.c:737; lab_gpu_wait (:761) waits for a
  * command buffer committed without waiting. */
 int64_t lab_gpu_commit(int64_t wait);
@@ -132,14 +132,59 @@ void lab_gpu_enc_matmul_q8(int64_t w, int64_t qsOffset, int64_t scalesOffset, in
 void lab_gpu_enc_matmul_q4(int64_t w, int64_t qsOffset, int64_t scalesOffset, int64_t x,
                            int64_t xOffset, int64_t y, int64_t yOffset, int64_t rows, int64_t cols,
                            int64_t n);
+/* RMSNorm of `rows` rows of `cols` f32 values at xOffset of buffer x with the
+ * weights at wOffset of buffer w, into `out` at outOffset (added into it with
+ * `accumulate`), as dianoia's CPU path computes it (lib/src/ops.dart:12-31:
+ * the sum of squares and the reciprocal root in double). The weights' buffer
+ * is copied to the device once, like a matrix's. When a later product of the
+ * same command buffer reads the output, the norm kernel also writes it as
+ * quantized activations for that product (the fused norm -> quantize).
+ * Replaces lab_gpu_enc_rms_norm, lab_vulkan.c:899-907 (gpu.dart:180-204). */
+void lab_gpu_enc_rms_norm(int64_t x, int64_t xOffset, int64_t w, int64_t wOffset, int64_t out,
+                          int64_t outOffset, int64_t rows, int64_t cols, double eps,
+                          int64_t accumulate);
+/* g = silu(g) * u over `count` f32 values at offset 0 of buffers g and u, as
+ * dianoia's CPU feed-forward computes it (lib/src/shard.dart:456-460). Right
+ * after the two products that wrote g and u it runs in the second one's
+ * epilogue and launches nothing; its results are then also quantized there
+ * for the product that reads them. Replaces lab_gpu_enc_swiglu,
+ * lab_vulkan.c:974-978 (gpu.dart:280-285). */
+void lab_gpu_enc_swiglu(int64_t g, int64_t u, int64_t count);
+/* dst += src over `count` f32 values at the byte offsets given: the residual
+ * add of a layer without sandwich norms (lib/src/model.dart:946-950). Right
+ * after the product that wrote all of src (and does not read dst) it runs in
+ * that product's epilogue and launches nothing. Replaces lab_gpu_enc_add,
+ * lab_vulkan.c:993-998 (gpu.dart:293-297). */
+void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count);
 
-/* Records `count` products into the open command buffer in one call, exactly as
- * the same sequence of lab_gpu_enc_matmul_q8 / lab_gpu_enc_matmul_q4 calls
- * would. No counterpart in the reference: it is for callers whose per-call
- * cost is high (a Python ctypes call costs microseconds, a Dart @Native leaf
- * call tens of nanoseconds). Row i of `table` is 11 int64 values: format
- * (0 = Q8_0, 1 = Q4_0), w, qsOffset, scalesOffset, x, xOffset, y, yOffset,
- * rows, cols, n. */
+/* With on = 0, command buffers committed from now on run every operation as
+ * its own kernel on f32 inputs, with no QA links and no fusions, as the
+ * reference's GPU layer dispatches them; with on = 1 (the default) they run
+ * fused. The results are the same bit for bit; only the time differs. No
+ * counterpart in the reference. */
+void dn_gpu_set_fusion(int64_t on);
+
+/* Kinds of the rows of dn_gpu_enc_batch. */
+#define DN_BATCH_Q8 0
+#define DN_BATCH_Q4 1
+#define DN_BATCH_RMS_NORM 2
+#define DN_BATCH_SWIGLU 3
+#define DN_BATCH_ADD 4
+
+/* Records `count` operations into the open command buffer in one call,
+ * exactly as the same sequence of lab_gpu_enc_* calls would. No counterpart
+ * in the reference: it is for callers whose per-call cost is high (a Python
+ * ctypes call costs microseconds, a Dart @Native leaf call tens of
+ * nanoseconds). Row i of `table` is 11 int64 values, the kind and then the
+ * arguments of the call it stands for, in order:
+ *   DN_BATCH_Q8 / DN_BATCH_Q4: w, qsOffset, scalesOffset, x, xOffset, y,
+ *     yOffset, rows, cols, n (lab_gpu_enc_matmul_q8 / _q4);
+ *   DN_BATCH_RMS_NORM: x, xOffset, w, wOffset, out, outOffset, rows, cols,
+ *     the bits of eps as a double, accumulate (lab_gpu_enc_rms_norm);
+ *   DN_BATCH_SWIGLU: g, u, count, then unused (lab_gpu_enc_swiglu);
+ *   DN_BATCH_ADD: src, srcOffset, dst, dstOffset, count, then unused
+ *     (lab_gpu_enc_add).
+ * An unknown kind makes the next lab_gpu_commit return 0. */
 void dn_gpu_enc_batch(const int64_t* table, int64_t count);
 
 /* ------------------------------------------------------------ dn_* (device API) */
@@ -202,6 +247,21 @@ int64_t dn_quantize_q4(const float* w, uint8_t* qs, uint16_t* scales, int64_t ro
  * activations [n, cols]. */
 int64_t dn_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols, int64_t xa_stride,
                        void* stream);
+
+/* The decode path's neighbours of the products on device memory,
+ * asynchronous, as dianoia's CPU path computes them:
+ * dn_rms_norm: out = w * (x * r) per row, r = 1 / sqrt(mean(x^2) + eps)
+ *   (lib/src/ops.dart:12-31; with accumulate, added into out), `rows` rows of
+ *   `cols` values; with qa not NULL (cols % 32 == 0) the results also as QA
+ *   blocks, row t at qa + t * qa_stride.
+ * dn_swiglu: g = silu(g) * u over `count` values (lib/src/shard.dart:456-460);
+ *   with qa not NULL (count % 32 == 0) the results also as QA blocks, block
+ *   b at qa + 36 * b.
+ * flags: DN_FLAG_PDL launches with programmatic dependent launch. */
+int64_t dn_rms_norm(const float* x, const float* w, float* out, uint8_t* qa, int64_t qa_stride,
+                    int64_t rows, int64_t cols, double eps, int64_t accumulate, int64_t flags,
+                    void* stream);
+int64_t dn_swiglu(float* g, const float* u, uint8_t* qa, int64_t count, int64_t flags, void* stream);
 
 /* The decode GEMV on QA activations: ys[t * ldy + r] = (W x_t)[r] (ys may be
  * NULL), and, when ya is not NULL, the outputs quantized again into QA blocks

@@ -294,3 +294,42 @@ void orc_reference_f64(int q4, const void* qs, const void* scales, const float* 
     }
   }
 }
+
+/* ------------------------------------------------------------------ the
+ * decode path's neighbours, as dianoia's CPU path computes them. Dart's
+ * double is an IEEE binary64 and its Float32List stores round to nearest,
+ * so these C doubles and (float) casts are the same operations. */
+
+/* lib/src/ops.dart:12-31 rmsNorm, for each of `rows` rows (model.dart:939-944
+ * _normRows): sumSquares += v * v left to right in double, r = 1 / sqrt(
+ * sumSquares / n + eps) in double, out = (float)(x * r), then
+ * out = (float)(weight * out). With accumulate, the result is added into out
+ * in f32 afterwards (model.dart:946-950 _addInto). */
+void orc_rms_norm(const float* x, const float* w, float* out, int64_t rows, int64_t cols, double eps,
+                  int64_t accumulate) {
+  for (int64_t t = 0; t < rows; t++) {
+    const float* xr = x + t * cols;
+    float* o = out + t * cols;
+    double s = 0.0;
+    for (int64_t j = 0; j < cols; j++) {
+      const double v = xr[j];
+      s += v * v;
+    }
+    const double r = 1 / sqrt(s / (double)cols + eps);
+    for (int64_t j = 0; j < cols; j++) {
+      float v = (float)((double)xr[j] * r);
+      v = (float)((double)w[j] * (double)v);
+      o[j] = accumulate ? o[j] + v : v;
+    }
+  }
+}
+
+/* lib/src/shard.dart:456-460: g[j] = (float)(g / (1 + exp(-g))) in double,
+ * then g[j] = (float)(g[j] * u[j]). */
+void orc_swiglu(float* g, const float* u, int64_t count) {
+  for (int64_t j = 0; j < count; j++) {
+    const double gd = g[j];
+    const float s = (float)(gd / (1 + exp(-gd)));
+    g[j] = (float)((double)s * (double)u[j]);
+  }
+}

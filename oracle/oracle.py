@@ -67,6 +67,10 @@ class Oracle(_Lib):
         L.orc_block_dots.restype = None
         L.orc_reference_f64.argtypes = [ctypes.c_int, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]
         L.orc_reference_f64.restype = None
+        L.orc_rms_norm.argtypes = [_p, _p, _p, _i64, _i64, ctypes.c_double, _i64]
+        L.orc_rms_norm.restype = None
+        L.orc_swiglu.argtypes = [_p, _p, _i64]
+        L.orc_swiglu.restype = None
 
     def half_to_float(self, h: int) -> float:
         return self.lib.orc_half_to_float(h)
@@ -111,6 +115,22 @@ class Oracle(_Lib):
         self.lib.orc_reference_f64(1 if fmt == "q4" else 0, _ptr(qs), _ptr(scales), _ptr(xs),
                                    rows, cols, n, mode, _ptr(ref), _ptr(mag))
         return ref, mag
+
+
+    def rms_norm(self, x, w, rows: int, cols: int, eps: float, out=None) -> np.ndarray:
+        """RMSNorm of the CPU path; with `out` given, added into a copy of it."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        o = np.zeros(rows * cols, np.float32) if out is None else np.array(out, np.float32)
+        self.lib.orc_rms_norm(_ptr(x), _ptr(w), _ptr(o), rows, cols, eps, 0 if out is None else 1)
+        return o
+
+    def swiglu(self, g, u) -> np.ndarray:
+        """silu(g) * u of the CPU feed-forward, as a new array."""
+        h = np.array(g, np.float32)
+        u = np.ascontiguousarray(u, dtype=np.float32)
+        self.lib.orc_swiglu(_ptr(h), _ptr(u), h.size)
+        return h
 
 
 class Reference(_Lib):

@@ -101,3 +101,73 @@ def test_block_dots_restate_numpy(oracle, fmt):
     x = xq.reshape(n, cols // 32, 32).astype(np.int64)
     want = np.einsum("rbk,tbk->trb", w, x)
     assert np.array_equal(dots, want)
+
+
+# ------------------------------------------------------------ neighbours
+#
+# RMSNorm and SwiGLU live in dianoia's Dart code (lib/src/ops.dart:12-31,
+# lib/src/shard.dart:456-460), which cannot run here. The C restatement is
+# pinned against a second, independent restatement in Python, whose float is
+# the same IEEE double as Dart's and whose math.exp is the same C library
+# exp, with f32 stores through numpy's round-to-nearest conversion; and
+# against a few answers worked by hand.
+
+def _f32(v):
+    return float(np.float32(v))
+
+
+def _py_rms_norm(x, w, eps):
+    s = 0.0
+    for v in x:
+        s += float(v) * float(v)
+    r = 1 / __import__("math").sqrt(s / len(x) + eps)
+    return np.array([_f32(float(wj) * _f32(float(xj) * r)) for xj, wj in zip(x, w)], np.float32)
+
+
+def _py_swiglu(g, u):
+    import math
+    out = []
+    for gj, uj in zip(g, u):
+        gd = float(gj)
+        try:
+            e = math.exp(-gd)
+        except OverflowError:  # Python raises where C and Dart give infinity
+            e = math.inf
+        out.append(_f32(_f32(gd / (1 + e)) * float(uj)))
+    return np.array(out, np.float32)
+
+
+@pytest.mark.parametrize("rows,cols,eps", [(1, 2048, 1e-6), (3, 1000, 1e-5), (2, 7, 0.0)])
+def test_rms_norm_restatements_agree(oracle, rows, cols, eps):
+    rng = np.random.default_rng(rows * 1000 + cols)
+    x = (rng.standard_normal(rows * cols) * 3).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    got = oracle.rms_norm(x, w, rows, cols, eps)
+    want = np.concatenate([_py_rms_norm(x[t * cols:(t + 1) * cols], w, eps) for t in range(rows)])
+    assert np.array_equal(bits(got), bits(want))
+    prev = rng.standard_normal(rows * cols).astype(np.float32)
+    acc = oracle.rms_norm(x, w, rows, cols, eps, out=prev)
+    assert np.array_equal(bits(acc), bits((prev + want).astype(np.float32)))
+
+
+def test_rms_norm_known_answers(oracle):
+    # [3, 4]: mean square 12.5, r = 1 / sqrt(12.5); unit weights.
+    got = oracle.rms_norm(np.array([3, 4], np.float32), np.ones(2, np.float32), 1, 2, 0.0)
+    r = 1 / np.sqrt(np.float64(12.5))
+    assert got.tolist() == [np.float32(3 * r), np.float32(4 * r)]
+    # All zeros with eps 1e-6: r = 1000 exactly in double, outputs stay 0.
+    z = oracle.rms_norm(np.zeros(32, np.float32), np.full(32, 2, np.float32), 1, 32, 1e-6)
+    assert not z.any()
+    # A constant row c normalises to sign(c) * 1 / sqrt(1 + eps / c^2) * weight.
+    c = oracle.rms_norm(np.full(64, -2, np.float32), np.full(64, 0.5, np.float32), 1, 64, 0.0)
+    assert np.all(c == np.float32(-0.5))
+
+
+def test_swiglu_restatements_agree(oracle):
+    rng = np.random.default_rng(77)
+    g = (rng.standard_normal(4096) * 4).astype(np.float32)
+    g[:6] = [0.0, -0.0, 90.0, -90.0, 1e-30, -800.0]
+    u = rng.standard_normal(4096).astype(np.float32)
+    got = oracle.swiglu(g, u)
+    assert np.array_equal(bits(got), bits(_py_swiglu(g, u)))
+    assert got[0] == 0 and got[2] == np.float32(90.0) * u[2] and got[5] == 0
