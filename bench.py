@@ -502,7 +502,8 @@ def main():
     ap.add_argument("--neighbour-steps", type=int, default=30,
                     help="tokens of the decode stack with norms, SwiGLU and residual adds")
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours"],
+                    default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
     ap.add_argument("--fmt", choices=["q8", "q4"], default="q8")
@@ -519,6 +520,8 @@ def main():
         return run_gemm_workload(args)
     if args.workload == "configs":
         return run_configs_workload(args)
+    if args.workload == "neighbours":
+        return run_neighbours_workload(args)
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1271,7 +1274,10 @@ def run_neighbours(args, stack, L):
                          "dn_gpu_enc_batch per token"),
             "ops_per_token": len(table),
             "fused": {"tokens_s": fused_tps, "commit_device_ms": fused_ms,
-                      "kernels_per_token": 7 * LAYERS + 2},
+                      "kernels_per_token": 5 * LAYERS + 1,
+                      "note": "the products only: each norm runs in the prologue of its first "
+                              "reader (which hands QA blocks to the other), SwiGLU and the adds "
+                              "in product epilogues"},
             "unfused": {"tokens_s": plain_tps, "commit_device_ms": plain_ms,
                         "kernels_per_token": 10 * LAYERS + 2},
             "logits_identical": bool(np.array_equal(fused_logits.view(np.uint32),
@@ -1284,6 +1290,21 @@ def run_neighbours(args, stack, L):
         for h in handles:
             if h >= 0:
                 L.lab_gpu_release(h)
+
+
+def run_neighbours_workload(args):
+    """Only the decode stack with its neighbours (run_neighbours), one JSON
+    line; with --layers, a shorter stack for profiler captures."""
+    import torch
+    from dianoia_b200 import _lib
+    L = _lib.lib()
+    if L.lab_cpu_supported() != 1:
+        raise SystemExit("no sm_100 device visible to libdianoia_b200")
+    stack = Stack(torch, 0, 1, torch.device("cuda", 0))
+    torch.cuda.synchronize()
+    res = run_neighbours(args, stack, L)
+    res["layers"] = LAYERS
+    print(json.dumps(res), flush=True)
 
 
 def run_cpu_baseline(args, stack):

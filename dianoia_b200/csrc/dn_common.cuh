@@ -78,6 +78,42 @@ __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
   return __half2float(__ushort_as_half(h));  // exact
 }
 
+// RMSNorm (lib/src/ops.dart:12-31) pieces shared by the norm kernel and the
+// GEMV prologue that runs a norm itself, so that both give the same bits.
+// The sum of squares runs over kNormLanes threads in one fixed order: thread
+// t adds x[j]^2 (exact in double) for j = t, t + 128, ... left to right, each
+// warp reduces with xor shuffles, and the warp sums add in warp order. The
+// reference sums left to right; the two sums differ by a few ulps of a double,
+// which moves an f32 output only where x * r lies that close to an f32
+// rounding boundary.
+constexpr int kNormLanes = 128;
+
+// r = 1 / sqrt(sum / cols + eps), in double. Called by threads 0..127 (tid),
+// which `sync` (a barrier over exactly them) holds together; `red` is 4
+// doubles of shared memory.
+template <typename Sync>
+__device__ __forceinline__ double norm_factor(const float* x, int64_t cols, double eps, int tid,
+                                              double* red, Sync sync) {
+  double s = 0.0;
+  for (int64_t j = tid; j < cols; j += kNormLanes) {
+    const double v = (double)x[j];
+    s = __dadd_rn(s, __dmul_rn(v, v));
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+  if ((tid & 31) == 0) red[tid >> 5] = s;
+  sync();
+  double sum = 0.0;
+#pragma unroll
+  for (int w = 0; w < kNormLanes / 32; w++) sum = __dadd_rn(sum, red[w]);
+  return __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)cols), eps)));
+}
+
+// One normalized value: (x * r) in double stored to f32, times the weight in f32.
+__device__ __forceinline__ float norm_value(float x, float w, double r) {
+  return __fmul_rn(w, __double2float_rn(__dmul_rn((double)x, r)));
+}
+
 // One SwiGLU output, silu(g) * u, as dianoia's CPU feed-forward computes it
 // (lib/src/shard.dart:456-460): g / (1 + exp(-g)) in double, stored to f32,
 // then an f32 product with u. CUDA's double exp differs from the C library's

@@ -59,6 +59,17 @@ struct GemvArgs {
   // Residual add in the epilogue (optional): res[t * ldy + r] += y, after
   // the product's own outputs (the layer's dst += src right after it).
   float* res;
+  // RMSNorm in the prologue (optional, with xs): the product's input is
+  // token t of xs normalized with the weights norm_w and norm_eps (the norm
+  // kernel's arithmetic); CTA 0 also writes those values to norm_out (token t
+  // at norm_out + t * cols) unless it is null.
+  const float* norm_w;
+  float* norm_out;
+  double norm_eps;
+  // With f32 inputs (optional): CTA 0 also writes the quantized input as QA
+  // blocks, token t at xa_out + t * xa_out_stride, for later products.
+  uint8_t* xa_out;
+  int64_t xa_out_stride;
 };
 
 // RMSNorm of `rows` rows of `cols` values: out = w * (x * r), r =

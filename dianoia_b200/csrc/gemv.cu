@@ -34,7 +34,8 @@
 // again in the epilogue (QA output) for the next product of a chain, and the
 // feed-forward's SwiGLU can run there too, on the outputs of the gate / up
 // pair's second product and the first one's (glu_* arguments), and so can the
-// residual add that follows a layer's output projections (res).
+// residual add that follows a layer's output projections (res). With f32
+// inputs, the CTA can also run the RMSNorm that produces them (norm_*).
 #include <string.h>
 
 #include <algorithm>
@@ -71,11 +72,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // This CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
   const int64_t my_tiles = (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x;
   const int64_t total = my_tiles * nch;
-  const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN);
+  const bool norm = F32_IN && a.norm_w != nullptr;
+  const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN, norm);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_off);
   uint64_t* empty = full + stages;
-  uint64_t* xbars = empty + stages;
-  uint64_t* epi = xbars + 2;
+  uint64_t* xbars = empty + stages;  // token buffers 0 and 1, the norm's weights
+  uint64_t* epi = xbars + 3;
   uint8_t* xw_s = smem + sp.xw_off;
   float* xs_s = reinterpret_cast<float*>(smem + sp.xs_off);
   float* yt_s = reinterpret_cast<float*>(smem + sp.yt_off);
@@ -89,6 +91,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     mbar_init(&xbars[0], 1);
     mbar_init(&xbars[1], 1);
+    mbar_init(&xbars[2], 1);
     mbar_init(&epi[0], kConsumers);
     mbar_init(&epi[1], kConsumers);
     abort_flag = 0;
@@ -143,6 +146,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   // right away; a single product from f32 inputs triggers after its
   // prologue (back to back, an early start measured slower there).
   if (!F32_IN) pdl_launch_dependents();
+  float* nw_s = reinterpret_cast<float*>(smem + sp.nw_off);
+  if (norm && tid == 0) {
+    // The norm's weights do not come from the previous kernel: fetch them
+    // while it finishes.
+    mbar_arrive_expect_tx(&xbars[2], (uint32_t)(a.cols * 4));
+    bulk_g2s(nw_s, a.norm_w, (uint32_t)(a.cols * 4), &xbars[2]);
+  }
   pdl_wait();  // the activations may come from the previous kernel
   bool ok = true;
   if (F32_IN) {
@@ -157,14 +167,35 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int tt = 0; tt < min(2, nt); tt++) issue_x(tt);
     }
     const bool writer = blockIdx.x == 0 && a.xq != nullptr;
+    const bool qa_writer = blockIdx.x == 0 && a.xa_out != nullptr;
+    float* norm_out = blockIdx.x == 0 ? a.norm_out : nullptr;
+    __shared__ double norm_red[kNormLanes / 32];
+    const bool wgot = !norm || warp_wait(&xbars[2], 0, a.status);
     int tt = 0;
     for (; tt < nt; tt++) {
-      const bool got = warp_wait(&xbars[tt & 1], (uint32_t)(tt >> 1) & 1u, a.status);
+      bool got = warp_wait(&xbars[tt & 1], (uint32_t)(tt >> 1) & 1u, a.status);
+      float* xf = reinterpret_cast<float*>(stg_s + (tt & 1) * sp.stg_stride);
+      // The norm's barriers need every consumer warp: all of them go ahead,
+      // or none (a warp whose wait ran out makes every warp skip the token).
+      if (norm) got = consumers_all(got && wgot);
+      if (got && norm) {
+        // The fused RMSNorm, in place in the staging buffer.
+        const double r = norm_factor(xf, a.cols, a.norm_eps, tid, norm_red, [] { consumers_sync(); });
+        float* out = norm_out == nullptr ? nullptr : norm_out + (t0 + tt) * a.cols;
+        for (int64_t j = tid; j < a.cols; j += kConsumers) {
+          const float v = norm_value(xf[j], nw_s[j], r);
+          xf[j] = v;
+          if (out != nullptr) out[j] = v;
+        }
+        // Generic writes to a buffer the bulk copy of token tt + 2 refills.
+        fence_proxy_async_smem();
+        consumers_sync();
+      }
       if (got)
-        quantize_token<Q4>(reinterpret_cast<const float*>(stg_s + (tt & 1) * sp.stg_stride),
-                           xw_s + tt * sp.xw_stride, xs_s + tt * sp.xs_stride, blocks,
+        quantize_token<Q4>(xf, xw_s + tt * sp.xw_stride, xs_s + tt * sp.xs_stride, blocks,
                            writer ? a.xq + (t0 + tt) * a.cols : nullptr,
-                           writer ? a.xsc + (t0 + tt) * blocks : nullptr);
+                           writer ? a.xsc + (t0 + tt) * blocks : nullptr,
+                           qa_writer ? a.xa_out + (t0 + tt) * a.xa_out_stride : nullptr);
       if (!got) abort_flag = 1;
       consumers_sync();
       if (abort_flag) {
@@ -176,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (!ok && tid == 0) {
       for (int j = tt + 1; j < min(nt, tt + 2); j++)
         mbar_wait_bounded(&xbars[j & 1], (uint32_t)(j >> 1) & 1u, a.status, kStatusTmaTimeout);
+      if (norm) mbar_wait_bounded(&xbars[2], 0, a.status, kStatusTmaTimeout);
     }
   } else {
     const int64_t row_bytes = blocks * kQABytes;
@@ -382,7 +414,8 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   // the tiles need more than one CTA per SM; with few tiles (a tall-K matrix
   // such as the MLP down projection) each CTA gets a whole SM's shared memory,
   // so more of its long stream is in flight.
-  const SmemPlan base = plan<Q4>(0, NT, a.cols, F32_IN);
+  const bool norm = F32_IN && a.norm_w != nullptr;
+  const SmemPlan base = plan<Q4>(0, NT, a.cols, F32_IN, norm);
   int per_sm = ntiles <= kSMs ? 1 : 2;
   int stages = (int)((kSmemPerSM / per_sm - 1024 - base.total) / (kStageBytes + 16));
   if (per_sm == 1) stages = (int)((kMaxSmem - base.total) / (kStageBytes + 16));
@@ -407,7 +440,7 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     const int64_t chunks = waves * ((blocks + F::kKC - 1) / F::kKC);
     if (chunks < stages) stages = (int)(chunks < 2 ? 2 : chunks);
   }
-  const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN);
+  const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN, norm);
   if (sp.total > kMaxSmem) return kErrTooLarge;
   CUtensorMap tw, tsc;
   memset(&tsc, 0, sizeof tsc);
@@ -463,7 +496,7 @@ template <bool Q4>
 int64_t launch_gemv_q(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const bool f32_in = a.xs != nullptr;
   auto fits = [&](int nt) {
-    return plan<Q4>(2, nt, a.cols, f32_in).total <= kMaxSmem;
+    return plan<Q4>(2, nt, a.cols, f32_in, a.norm_w != nullptr).total <= kMaxSmem;
   };
   if (a.n <= 1 || !fits(2)) return fits(1) ? launch_gemv_s<Q4, 1>(a, stream, pdl) : kErrTooLarge;
   if (a.n <= 2 || !fits(4)) return launch_gemv_s<Q4, 2>(a, stream, pdl);
@@ -487,8 +520,16 @@ bool gemv_ex_supported(const GemvArgs& g) {
     return false;
   if (g.ys != nullptr && ((uintptr_t)g.ys & 3) != 0) return false;
   if (g.res != nullptr && ((uintptr_t)g.res & 3) != 0) return false;
-  return (g.q4 ? plan<true>(2, 1, g.cols, g.xs != nullptr).total
-               : plan<false>(2, 1, g.cols, g.xs != nullptr).total) <= kMaxSmem;
+  if (g.xa_out != nullptr && (g.xs == nullptr || ((uintptr_t)g.xa_out & 3) != 0 ||
+                              (g.xa_out_stride & 3) != 0 || g.xa_out_stride < g.cols / kBlock * kQABytes))
+    return false;
+  // The norm's weights come in by one bulk copy.
+  if (g.norm_w != nullptr && (g.xs == nullptr || ((uintptr_t)g.norm_w & 15) != 0 ||
+                              ((uintptr_t)g.norm_out & 3) != 0))
+    return false;
+  const bool norm = g.norm_w != nullptr;
+  return (g.q4 ? plan<true>(2, 1, g.cols, g.xs != nullptr, norm).total
+               : plan<false>(2, 1, g.cols, g.xs != nullptr, norm).total) <= kMaxSmem;
 }
 
 int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl) {

@@ -62,7 +62,7 @@ struct Fmt {
 __host__ __device__ inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 struct SmemPlan {
-  int64_t bar_off, xw_off, xw_stride, xs_off, xs_stride, yt_off, stg_off, stg_stride, total;
+  int64_t bar_off, xw_off, xw_stride, xs_off, xs_stride, yt_off, stg_off, stg_stride, nw_off, total;
 };
 
 // Activations in shared memory, lane-interleaved: for block b, lane l's two
@@ -79,22 +79,24 @@ struct XLayout {
 };
 
 // Layout from a 1024-byte aligned base: the stages, the barriers (`stages`
-// full, `stages` empty, two activation, two epilogue), the activations, the
-// epilogue's outputs and the input staging. `total` includes the slack to
+// full, `stages` empty, three activation, two epilogue), the activations, the
+// epilogue's outputs, the input staging and, for a product that runs an
+// RMSNorm in its prologue, the norm's weights. `total` includes the slack to
 // align the base.
 template <bool Q4>
-__host__ __device__ inline SmemPlan plan(int stages, int nt, int64_t cols, bool f32_in) {
+__host__ __device__ inline SmemPlan plan(int stages, int nt, int64_t cols, bool f32_in, bool norm) {
   const int64_t blocks = cols / kBlock;
   SmemPlan p;
   p.bar_off = (int64_t)stages * kStageBytes;
-  p.xw_off = round_up(p.bar_off + 8 * (2 * stages + 4), 128);
+  p.xw_off = round_up(p.bar_off + 8 * (2 * stages + 5), 128);
   p.xw_stride = blocks * XLayout<Q4>::kBlockBytes;
   p.xs_off = p.xw_off + nt * p.xw_stride;
   p.xs_stride = round_up(blocks, 4);
   p.yt_off = p.xs_off + nt * p.xs_stride * 4;
   p.stg_off = round_up(p.yt_off + 2 * (int64_t)nt * kRows * 4, 128);
   p.stg_stride = f32_in ? cols * 4 : round_up(blocks * kQABytes, 16);
-  p.total = p.stg_off + (f32_in ? 2 : nt) * p.stg_stride + 1024;
+  p.nw_off = round_up(p.stg_off + (f32_in ? 2 : nt) * p.stg_stride, 16);
+  p.total = p.nw_off + (norm ? cols * 4 : 0) + 1024;
   return p;
 }
 
@@ -121,6 +123,19 @@ __device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
 
+// True in every consumer thread when `v` is true in all of them (a named
+// barrier with an AND reduction; every consumer thread must reach it).
+__device__ __forceinline__ bool consumers_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kConsumers)
+      : "memory");
+  return r != 0;
+}
+
 template <typename T>
 __device__ __forceinline__ T lds(const void* p) {
   return *reinterpret_cast<const T*>(p);
@@ -133,10 +148,12 @@ __device__ __forceinline__ int32_t lane_sum8(uint32_t w0, uint32_t w1) {
 
 // Quantizes one token of f32 activations (in shared memory) into the
 // lane-interleaved layout, eight lanes per block (lab_quantize_q8
-// semantics). With `xq`, also writes lab_gemm's xq / xsc outputs.
+// semantics). With `xq`, also writes lab_gemm's xq / xsc outputs; with `qa`,
+// the same values as QA blocks (32 int8 and the f32 scale per block).
 template <bool Q4>
 __device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xw, float* xs,
-                                               int64_t blocks, int8_t* xq, float* xsc) {
+                                               int64_t blocks, int8_t* xq, float* xsc,
+                                               uint8_t* qa = nullptr) {
   using X = XLayout<Q4>;
   const int tid = threadIdx.x, sub = tid & 7;
   for (int64_t base = 0; base < blocks; base += kConsumers / 8) {
@@ -161,6 +178,10 @@ __device__ __forceinline__ void quantize_token(const float* xf, uint8_t* xw, flo
       if (xq != nullptr) {
         *reinterpret_cast<uint32_t*>(xq + b * kBlock + sub * 4) = word;
         if (sub == 0) xsc[b] = scale;
+      }
+      if (qa != nullptr) {
+        *reinterpret_cast<uint32_t*>(qa + b * kQABytes + sub * 4) = word;
+        if (sub == 0) *reinterpret_cast<float*>(qa + b * kQABytes + 32) = scale;
       }
     }
   }

@@ -87,6 +87,8 @@ struct Range {
 
 Range writes(const Op& o) { return Range{o.y, o.y_off, o.y_off + o.n * o.rows * 4}; }
 
+bool overlap(const Range& a, const Range& b) { return a.buf == b.buf && a.lo < b.hi && b.lo < a.hi; }
+
 void reads(const Op& o, std::vector<Range>& r) {
   r.clear();
   r.push_back(Range{o.x, o.x_off, o.x_off + o.n * o.cols * 4});
@@ -294,7 +296,13 @@ dn::LinearArgs linear_args(const Op& o, uint32_t* status) {
 // rows) runs in the second product's epilogue (glu[i]), and launches nothing
 // itself (absorbed). Residual-add fusion: an add right after the product
 // that wrote all of its src, into a dst the product does not read, runs in
-// that product's epilogue (res[i]) and is absorbed too.
+// that product's epilogue (res[i]) and is absorbed too. Norm fusion: a norm
+// (without accumulate) whose output only GEMV products read, each all of it
+// (same tokens and width), before anything writes the norm's input, weights
+// or output again, runs in the prologue of the first of them (normin[i]: it
+// reads the norm's input as f32 and normalizes it in the CTA), which also
+// writes the norm's outputs and, when more products read them, their QA
+// blocks (xa_out_at[i]) for those products' QA links; the norm is absorbed.
 //
 // QA links: every op that writes 32-value rows can also write them as QA
 // blocks (the GEMV epilogue, the norm and SwiGLU kernels); with rows a
@@ -314,6 +322,8 @@ struct Plan {
   std::vector<int64_t> xa_at, xa_stride, ya_at;
   std::vector<int> glu;         // product i runs SwiGLU op glu[i] in its epilogue, or -1
   std::vector<int> res;         // product i runs add op res[i] in its epilogue, or -1
+  std::vector<int> normin;      // product i runs norm op normin[i] in its prologue, or -1
+  std::vector<int64_t> xa_out_at;  // product i writes its quantized input as QA blocks there, or -1
   std::vector<bool> absorbed;   // a SwiGLU op that a product's epilogue runs
   std::vector<HostQA> host;
   int64_t bytes = 0;
@@ -329,6 +339,8 @@ Plan plan_ops(uint32_t* status) {
   k.ya_at.assign(n, -1);
   k.glu.assign(n, -1);
   k.res.assign(n, -1);
+  k.normin.assign(n, -1);
+  k.xa_out_at.assign(n, -1);
   k.absorbed.assign(n, false);
   if (!g_fuse) return k;
   std::vector<bool> gemv(n, false);
@@ -349,10 +361,57 @@ Plan plan_ops(uint32_t* status) {
     if (d.kind != kAdd || !gemv[i - 1] || k.glu[i - 1] >= 0) continue;
     const Range src{d.x, d.x_off, d.x_off + d.rows * 4}, dst = writes(d), out = writes(p);
     const Range in{p.x, p.x_off, p.x_off + p.n * p.cols * 4};
-    auto overlap = [](const Range& a, const Range& b) { return a.buf == b.buf && a.lo < b.hi && b.lo < a.hi; };
     if (out.buf == src.buf && out.lo == src.lo && out.hi == src.hi && !overlap(dst, in) && !overlap(dst, out)) {
       k.res[i - 1] = i;
       k.absorbed[i] = true;
+    }
+  }
+  // Everything op i's launch writes: its own outputs and those of the ops it absorbed.
+  auto launch_writes = [&](int i, std::vector<Range>& w) {
+    w.assign(1, writes(g_ops[i]));
+    if (k.glu[i] >= 0) w.push_back(writes(g_ops[k.glu[i]]));
+    if (k.res[i] >= 0) w.push_back(writes(g_ops[k.res[i]]));
+  };
+  std::vector<Range> in, wr;
+  for (int j = 0; j < n; j++) {
+    const Op& m = g_ops[j];
+    // f32 inputs and the weights come into the products by bulk copies.
+    if (m.kind != kNorm || m.acc || m.x_off % 16 != 0 || m.qs_off % 16 != 0) continue;
+    const Range out = writes(m), src{m.x, m.x_off, m.x_off + m.n * m.cols * 4};
+    const Range wts{m.w, m.qs_off, m.qs_off + m.cols * 4};
+    std::vector<int> readers;
+    bool ok = true;
+    for (int i = j + 1; i < n && ok; i++) {
+      reads(g_ops[i], in);
+      bool reads_out = false;
+      for (const Range& r : in) reads_out = reads_out || overlap(r, out);
+      if (k.absorbed[i]) {  // runs inside its product, whose writes were seen there
+        ok = !reads_out;
+        continue;
+      }
+      launch_writes(i, wr);
+      bool ends = false;
+      for (const Range& w : wr) ends = ends || overlap(w, out) || overlap(w, src) || overlap(w, wts);
+      if (reads_out) {
+        // A reader must take all of the norm's rows as its input and must not
+        // write what its own prologue reads, nor the norm's outputs.
+        const Op& c = g_ops[i];
+        ok = gemv[i] && c.x == out.buf && c.x_off == out.lo && c.n == m.n && c.cols == m.rows && !ends;
+        readers.push_back(i);
+      }
+      if (ends) break;
+    }
+    if (!ok || readers.empty()) continue;
+    k.normin[readers[0]] = j;
+    k.absorbed[j] = true;
+    if (readers.size() > 1) {
+      const int64_t at = k.bytes;
+      k.bytes += qa_bytes(m.n, m.rows);
+      k.xa_out_at[readers[0]] = at;
+      for (size_t r = 1; r < readers.size(); r++) {
+        k.xa_at[readers[r]] = at;
+        k.xa_stride[readers[r]] = m.rows / kBlock * dn::kQABytes;
+      }
     }
   }
   // The op whose launch writes the QA blocks of op j's values, or -1.
@@ -362,11 +421,11 @@ Plan plan_ops(uint32_t* status) {
     if (o.rows % kBlock != 0) continue;
     if (o.kind == kMatmul) qa_src[j] = gemv[j] && k.glu[j] < 0 ? j : -1;
     else if (o.kind == kSwiglu && k.absorbed[j]) qa_src[j] = g_ops[j - 1].rows % kBlock == 0 ? j - 1 : -1;
-    else if (o.kind != kAdd) qa_src[j] = j;
+    else if (o.kind != kAdd && !k.absorbed[j]) qa_src[j] = j;
   }
   for (int i = 0; i < n; i++) {
     const Op& c = g_ops[i];
-    if (!gemv[i] || c.cols % kBlock != 0) continue;
+    if (!gemv[i] || c.cols % kBlock != 0 || k.normin[i] >= 0 || k.xa_at[i] >= 0) continue;
     const int64_t lo = c.x_off, hi = c.x_off + c.n * c.cols * 4;
     int j = i - 1;
     for (; j >= 0; j--) {
@@ -420,6 +479,7 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
     const Op& o = g_ops[i];
     uint8_t* qa_out = k.ya_at[i] >= 0 ? g_qa + k.ya_at[i] : nullptr;
     if (o.kind == kNorm) {
+      if (k.absorbed[i]) continue;
       const dn::NormArgs na{f32_at(o.x, o.x_off), f32_at(o.w, o.qs_off), f32_at(o.y, o.y_off), qa_out,
                             o.rows / kBlock * dn::kQABytes, o.n, o.rows, o.eps, o.acc};
       if (dn::launch_rms_norm(na, g_stream, true) != cudaSuccess) return false;
@@ -439,7 +499,8 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
     }
     const dn::LinearArgs a = linear_args(o, status);
     int64_t rc;
-    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0) {
+    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0 || k.normin[i] >= 0) {
+      // (xa_out_at is set only together with normin.)
       dn::GemvArgs g{};
       g.q4 = o.q4;
       g.qs = a.qs;
@@ -463,6 +524,17 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
         g.glu_out = f32_at(s.y, 0);
       }
       if (k.res[i] >= 0) g.res = f32_at(g_ops[k.res[i]].y, g_ops[k.res[i]].y_off);
+      if (k.normin[i] >= 0) {
+        const Op& m = g_ops[k.normin[i]];
+        g.xs = f32_at(m.x, m.x_off);
+        g.norm_w = f32_at(m.w, m.qs_off);
+        g.norm_eps = m.eps;
+        g.norm_out = f32_at(m.y, m.y_off);
+        if (k.xa_out_at[i] >= 0) {
+          g.xa_out = g_qa + k.xa_out_at[i];
+          g.xa_out_stride = m.rows / kBlock * dn::kQABytes;
+        }
+      }
       g.rows = o.rows;
       g.cols = o.cols;
       g.n = o.n;

@@ -7,10 +7,9 @@
 //  * RMSNorm (lib/src/ops.dart:12-31): the sum of squares and
 //    r = 1 / sqrt(sum / cols + eps) in double, x * r in double stored to f32,
 //    then an f32 product with the weight; with accumulate, an f32 add into the
-//    output (the residual add of lib/src/model.dart:946-950). The sum runs as
-//    a tree here rather than left to right; every square is exact in double,
-//    so the two sums differ by a few ulps of a double at most, and the f32
-//    outputs only where x * r lies that close to an f32 rounding boundary.
+//    output (the residual add of lib/src/model.dart:946-950). The sum runs in
+//    the order of norm_factor (dn_common.cuh), which the GEMV prologue that
+//    runs a norm itself shares.
 //  * SwiGLU (lib/src/shard.dart:456-460): silu_mul (dn_common.cuh).
 //  * the residual add (lib/src/model.dart:946-950): one f32 add per value.
 //
@@ -28,10 +27,10 @@
 namespace dn {
 namespace {
 
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = kNormLanes;  // 4 warps: the shared summation order
 constexpr int kNormWarps = kNormThreads / 32;
 
-// One CTA per row. Warp w handles 32-value blocks w, w + 8, ...: lane j holds
+// One CTA per row. Warp w handles 32-value blocks w, w + 4, ...: lane j holds
 // value j of the block, so its QA block comes out of one warp reduction.
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const NormArgs a) {
   pdl_launch_dependents();  // the next product may start streaming weights
@@ -40,36 +39,42 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const NormArgs a
   const int64_t row = blockIdx.x;
   const float* x = a.x + row * a.cols;
   float* out = a.out + row * a.cols;
+  __shared__ double red[kNormWarps];
+  const double r = norm_factor(x, a.cols, a.eps, tid, red, [] { __syncthreads(); });
 
-  double s = 0.0;
-  for (int64_t j = tid; j < a.cols; j += kNormThreads) {
-    const double v = (double)x[j];
-    s = __dadd_rn(s, __dmul_rn(v, v));
-  }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-  __shared__ double part[kNormWarps];
-  if (lane == 0) part[warp] = s;
-  __syncthreads();
-  double sum = 0.0;
-#pragma unroll
-  for (int w = 0; w < kNormWarps; w++) sum = __dadd_rn(sum, part[w]);
-  const double r = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)a.cols), a.eps)));
-
-  auto value = [&](int64_t j) {
-    const float xr = __double2float_rn(__dmul_rn((double)x[j], r));
-    float v = __fmul_rn(a.w[j], xr);
-    if (a.accumulate) v = __fadd_rn(out[j], v);
-    out[j] = v;
-    return v;
-  };
+  // Blocks in chunks: every load of a chunk is issued before its stores (a
+  // store to out could alias the next load, so the compiler would not hoist it).
+  constexpr int kChunk = 8;
   const int64_t blocks = a.cols / kBlock;
-  for (int64_t b = warp; b < blocks; b += kNormWarps) {
-    const float v = value(b * kBlock + lane);
-    if (a.qa != nullptr) gemv::quantize_block_out(v, a.qa + row * a.qa_stride + b * kQABytes, lane);
+  for (int64_t b0 = warp; b0 < blocks; b0 += kNormWarps * kChunk) {
+    float xv[kChunk], wv[kChunk], ov[kChunk];
+#pragma unroll
+    for (int u = 0; u < kChunk; u++) {
+      const int64_t b = b0 + u * kNormWarps, j = b * kBlock + lane;
+      if (b < blocks) {
+        xv[u] = x[j];
+        wv[u] = a.w[j];
+        ov[u] = a.accumulate ? out[j] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kChunk; u++) {
+      const int64_t b = b0 + u * kNormWarps, j = b * kBlock + lane;
+      if (b < blocks) {  // the same in every lane
+        float v = norm_value(xv[u], wv[u], r);
+        if (a.accumulate) v = __fadd_rn(ov[u], v);
+        out[j] = v;
+        if (a.qa != nullptr) gemv::quantize_block_out(v, a.qa + row * a.qa_stride + b * kQABytes, lane);
+      }
+    }
   }
   // A trailing part block (no QA: the planner links only whole blocks).
-  if (warp == kNormWarps - 1 && blocks * kBlock + lane < a.cols) value(blocks * kBlock + lane);
+  const int64_t j = blocks * kBlock + lane;
+  if (warp == kNormWarps - 1 && j < a.cols) {
+    float v = norm_value(x[j], a.w[j], r);
+    if (a.accumulate) v = __fadd_rn(out[j], v);
+    out[j] = v;
+  }
 }
 
 constexpr int kGluThreads = 256;

@@ -273,3 +273,57 @@ def test_bad_neighbour_arguments_fail_the_commit(cuda_lib):
     finally:
         L.lab_gpu_release(a)
         L.lab_gpu_release(w)
+
+
+def test_norm_read_in_part_keeps_its_own_kernel(cuda_lib, oracle):
+    """A norm whose output one product reads whole and another only in part
+    (a 32-aligned slice) is not folded into the products' prologues: it runs
+    as its own kernel and hands QA blocks to both. A second norm read whole by
+    one product is folded into it. All bit for bit against the CPU path, fused
+    and unfused."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    rng = np.random.default_rng(23)
+    h, r1, r2 = 256, 96, 64
+    q1, s1 = orc.q8_weights(rng, r1, h)
+    q2, s2 = orc.q4_weights(rng, r2, 128)      # reads values 64 .. 191 of the norm's output
+    q3, s3 = orc.q8_weights(rng, r1, h)
+    nw = (1 + 0.1 * rng.standard_normal(2 * h)).astype(np.float32)
+
+    def wrap(raw):
+        hd = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
+        assert hd >= 0
+        return hd
+
+    hs = [wrap(np.concatenate([q.view(np.uint8), s.view(np.uint8)])) for q, s in [(q1, s1), (q2, s2), (q3, s3)]]
+    small = wrap(nw.view(np.uint8))
+    floats = 2 * h + r1 + r2 + h + r1
+    act = L.lab_gpu_buffer(4 * floats)
+    assert act >= 0
+    view = np.ctypeslib.as_array((ctypes.c_float * floats).from_address(L.lab_gpu_contents(act)))
+    a_at, y1_at, y2_at, b_at, y3_at = h, 2 * h, 2 * h + r1, 2 * h + r1 + r2, 3 * h + r1 + r2
+    eps = 1e-5
+    try:
+        for fuse in (1, 0):
+            L.dn_gpu_set_fusion(fuse)
+            x = orc.activations(rng, 1, h)
+            view[:h] = x
+            view[h:] = np.nan
+            L.lab_gpu_begin()
+            L.lab_gpu_enc_rms_norm(act, 0, small, 0, act, 4 * a_at, 1, h, eps, 0)
+            L.lab_gpu_enc_matmul_q8(hs[0], 0, q1.size, act, 4 * a_at, act, 4 * y1_at, r1, h, 1)
+            L.lab_gpu_enc_matmul_q4(hs[1], 0, q2.size, act, 4 * (a_at + 64), act, 4 * y2_at, r2, 128, 1)
+            L.lab_gpu_enc_rms_norm(act, 0, small, 4 * h, act, 4 * b_at, 1, h, eps, 0)
+            L.lab_gpu_enc_matmul_q8(hs[2], 0, q3.size, act, 4 * b_at, act, 4 * y3_at, r1, h, 1)
+            assert L.lab_gpu_commit(1) == 1
+            a = oracle.rms_norm(x, nw[:h], 1, h, eps)
+            b = oracle.rms_norm(x, nw[h:], 1, h, eps)
+            y1, _, _ = oracle.gemm("q8", q1, s1, a, r1, h, 1, 1)
+            y2, _, _ = oracle.gemm("q4", q2, s2, a[64:192], r2, 128, 1, 1)
+            y3, _, _ = oracle.gemm("q8", q3, s3, b, r1, h, 1, 1)
+            for at, want in [(a_at, a), (y1_at, y1), (y2_at, y2), (b_at, b), (y3_at, y3)]:
+                assert np.array_equal(bits(view[at:at + want.size]), bits(want)), (fuse, at)
+    finally:
+        L.dn_gpu_set_fusion(1)
+        for hd in hs + [small, act]:
+            L.lab_gpu_release(hd)
