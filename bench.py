@@ -502,7 +502,7 @@ def main():
     ap.add_argument("--neighbour-steps", type=int, default=30,
                     help="tokens of the decode stack with norms, SwiGLU and residual adds")
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours"],
+    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours", "cache"],
                     default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
@@ -522,6 +522,8 @@ def main():
         return run_configs_workload(args)
     if args.workload == "neighbours":
         return run_neighbours_workload(args)
+    if args.workload == "cache":
+        return run_cache_workload(args)
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1305,6 +1307,115 @@ def run_neighbours_workload(args):
     res = run_neighbours(args, stack, L)
     res["layers"] = LAYERS
     print(json.dumps(res), flush=True)
+
+
+def run_cache_workload(args):
+    """The config-3 stack's weights as a Q8 cache file (lib/src/q8_cache.dart
+    layout, written by dianoia_b200.q8_cache), brought into device memory two
+    ways: (1) as dianoia's GpuForward does, mapping the file and wrapping the
+    mapping (lab_gpu_wrap copies it into the buffer's host mirror; the first
+    commit copies that to the device), timed up to a first product; (2)
+    dn_gpu_wrap_file, reading the file straight into device memory through
+    pinned staging. The file was just written, so its pages are in the page
+    cache. One JSON line; both buffers give the same product, bit for bit."""
+    import tempfile
+    import torch
+    from dianoia_b200 import _lib
+    from dianoia_b200.q8_cache import Q8Cache
+    L = _lib.lib()
+    if L.lab_cpu_supported() != 1 or L.lab_gpu_init() != 1:
+        raise SystemExit("no sm_100 device visible to libdianoia_b200")
+    stack = Stack(torch, 0, 1, torch.device("cuda", 0))
+    torch.cuda.synchronize()
+
+    class Host:
+        format = "q8"
+
+        def __init__(self, m):
+            self.rows, self.cols = m["rows"], m["cols"]
+            self.qs_bytes = m["qs"].cpu().numpy().view(np.uint8)
+            self.scale_bytes = m["scales"].cpu().numpy().view(np.uint8)
+
+    tmp = tempfile.mkdtemp(prefix="dn_cache_")
+    path = os.path.join(tmp, "stack.q8cache")
+    names = [f"{i}.{m['name']}" for i, m in enumerate(stack.mats)]
+    by_name = dict(zip(names, stack.mats))
+    t0 = time.perf_counter()
+    Q8Cache.write_each(path, "bench", [(n, "q8", by_name[n]["rows"], by_name[n]["cols"]) for n in names],
+                       lambda n: Host(by_name[n]))
+    write_s = time.perf_counter() - t0
+    size = os.path.getsize(path)
+    handles = []
+    try:
+        cache = Q8Cache.open(path, "bench")
+        m0 = stack.mats[-1]  # the lm_head: a product to touch the weights
+        o = cache.offsets(names[-1], m0["rows"], m0["cols"])
+        act = L.lab_gpu_buffer(4 * HIDDEN)
+        out = L.lab_gpu_readback_buffer(4 * VOCAB)
+        handles += [act, out]
+        x = np.ctypeslib.as_array((ctypes.c_float * HIDDEN).from_address(L.lab_gpu_contents(act)))
+        x[:] = stack.x0.cpu().numpy()
+        y = np.ctypeslib.as_array((ctypes.c_float * VOCAB).from_address(L.lab_gpu_contents(out)))
+
+        def product(w):
+            L.lab_gpu_begin()
+            L.lab_gpu_enc_matmul_q8(w, o["qs"], o["scales"], act, 0, out, 0, m0["rows"], m0["cols"], 1)
+            if L.lab_gpu_commit(1) != 1:
+                raise RuntimeError("lab_gpu_commit failed")
+            return y.copy()
+
+        t0 = time.perf_counter()
+        mapped = L.lab_gpu_wrap(cache.file.address, cache.file.length)
+        handles.append(mapped)
+        wrap_s = time.perf_counter() - t0
+        y_mapped = product(mapped)
+        mapped_s = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        on_file = L.dn_gpu_wrap_file(path.encode(), 0, size)
+        handles.append(on_file)
+        file_s = time.perf_counter() - t0
+        if min(mapped, on_file) < 0:
+            raise RuntimeError("wrapping the cache failed")
+        y_file = product(on_file)
+        cache.close()
+        res = {
+            "workload": "Q8 cache of the config-3 stack (113 Q8_0 matrices, reference layout) "
+                        "into device memory",
+            "file_bytes": size, "write_s": write_s,
+            "lab_gpu_wrap_of_mapping": {"s": mapped_s, "gbs": size / mapped_s / 1e9,
+                                        "wrap_call_s": wrap_s,
+                                        "note": "lab_gpu_wrap (copy into the pinned host mirror) "
+                                                "+ the first commit's device copy and one product"},
+            "dn_gpu_wrap_file": {"s": file_s, "gbs": size / file_s / 1e9,
+                                 "note": "pread into two 32 MiB pinned chunks, each device "
+                                         "copy overlapping the next read; page-cache-hot file"},
+            "products_identical": bool(np.array_equal(y_mapped.view(np.uint32), y_file.view(np.uint32))),
+            "product_matches_stack": bool(np.array_equal(
+                y_file.view(np.uint32), run_lm_head_reference(stack, L).view(np.uint32))),
+        }
+        print(json.dumps(res), flush=True)
+    finally:
+        for h in handles:
+            if h >= 0:
+                L.lab_gpu_release(h)
+        os.remove(path)
+        os.rmdir(tmp)
+
+
+def run_lm_head_reference(stack, L):
+    """The lm_head product of x0 on the device-resident stack (dn_linear)."""
+    import torch
+    m = stack.mats[-1]
+    y = torch.empty(m["rows"], dtype=torch.float32, device=stack.device)
+    xq = torch.empty(m["cols"], dtype=torch.int8, device=stack.device)
+    xsc = torch.empty(m["cols"] // 32, dtype=torch.float32, device=stack.device)
+    rc = L.dn_linear(0, m["qs"].data_ptr(), m["scales"].data_ptr(), stack.x0.data_ptr(),
+                     xq.data_ptr(), xsc.data_ptr(), y.data_ptr(), m["rows"], m["cols"], 1, m["rows"],
+                     1, -1, 0, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    if rc != 0:
+        raise RuntimeError(f"dn_linear failed: {rc}")
+    return y.cpu().numpy()
 
 
 def run_cpu_baseline(args, stack):

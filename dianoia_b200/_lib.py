@@ -46,6 +46,7 @@ SIGNATURES = {
     "lab_gpu_enc_add": (None, [_i64] * 5),
     "dn_gpu_enc_batch": (None, [_p, _i64]),
     "dn_gpu_set_fusion": (None, [_i64]),
+    "dn_gpu_wrap_file": (_i64, [ctypes.c_char_p, _i64, _i64]),
     "dn_linear": (_i64, [_i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),

@@ -30,7 +30,10 @@
 // Errors: like the reference, the void functions report nothing;
 // lab_gpu_commit returns 0 when a product's arguments or a CUDA call failed.
 // Calls are serialized by one mutex (the reference's layer is single-encoder).
+#include <fcntl.h>
 #include <string.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <mutex>
@@ -49,7 +52,7 @@ constexpr int64_t kBlock = 32;  // values per Q4_0 / Q8_0 block
 
 struct Buf {
   uint8_t* dev = nullptr;
-  uint8_t* host = nullptr;  // pinned mirror: lab_gpu_contents
+  uint8_t* host = nullptr;  // pinned mirror: lab_gpu_contents (null: a device-only buffer)
   int64_t bytes = 0;
   bool live = false;
   bool weights_on_device = false;  // copied once, at its first use as a matrix
@@ -157,6 +160,20 @@ bool fits(int64_t h, int64_t off, int64_t bytes) {
   return valid(h) && off >= 0 && bytes >= 0 && off <= g_bufs[h].bytes - bytes;
 }
 
+int64_t add_buffer(const Buf& b) {
+  int64_t h;
+  if (!g_free.empty()) {
+    h = g_free.back();
+    g_free.pop_back();
+    g_bufs[h] = b;
+  } else {
+    h = (int64_t)g_bufs.size();
+    g_bufs.push_back(b);
+  }
+  g_live++;
+  return h;
+}
+
 int64_t new_buffer(int64_t bytes) {
   if (!g_ready || bytes < 0) return -1;
   cudaSetDevice(g_device);
@@ -180,22 +197,66 @@ int64_t new_buffer(int64_t bytes) {
   }
   b.bytes = bytes;
   b.live = true;
-  int64_t h;
-  if (!g_free.empty()) {
-    h = g_free.back();
-    g_free.pop_back();
-    g_bufs[h] = b;
-  } else {
-    h = (int64_t)g_bufs.size();
-    g_bufs.push_back(b);
-  }
-  g_live++;
-  return h;
+  return add_buffer(b);
 }
 
 constexpr int64_t kMaxSide = int64_t(1) << 30;  // keeps every byte count below 2^63
 
 bool sides_ok(int64_t a, int64_t b) { return a >= 0 && b >= 0 && a < kMaxSide && b < kMaxSide; }
+
+// Reads [offset, offset + bytes) of the file at `path` into device memory
+// through two pinned staging chunks: the read of one chunk runs while the
+// other is copied to the device. Returns a device-only buffer, or -1.
+int64_t wrap_file(const char* path, int64_t offset, int64_t bytes) {
+  if (!g_ready || path == nullptr || offset < 0 || bytes < 0) return -1;
+  const int fd = open(path, O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return -1;
+  struct stat st;
+  if (fstat(fd, &st) != 0 || offset > (int64_t)st.st_size - bytes) {
+    close(fd);
+    return -1;
+  }
+  cudaSetDevice(g_device);
+  constexpr int64_t kChunk = int64_t(32) << 20;
+  Buf b;
+  uint8_t* stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  cudaStream_t copy = nullptr;
+  bool ok = cudaMalloc(&b.dev, (size_t)(bytes == 0 ? 16 : bytes)) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; i < 2 && ok; i++)
+    ok = cudaHostAlloc(&stage[i], (size_t)std::min(kChunk, std::max<int64_t>(bytes, 16)),
+                       cudaHostAllocDefault) == cudaSuccess &&
+         cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) == cudaSuccess;
+  for (int64_t at = 0, k = 0; ok && at < bytes; at += kChunk, k++) {
+    const int i = (int)(k & 1);
+    const int64_t n = std::min(kChunk, bytes - at);
+    if (k >= 2) ok = cudaEventSynchronize(done[i]) == cudaSuccess;  // its previous copy is done
+    for (int64_t got = 0; ok && got < n;) {
+      const ssize_t r = pread(fd, stage[i] + got, (size_t)(n - got), (off_t)(offset + at + got));
+      if (r <= 0) ok = false;
+      else got += r;
+    }
+    ok = ok && cudaMemcpyAsync(b.dev + at, stage[i], (size_t)n, cudaMemcpyHostToDevice, copy) == cudaSuccess &&
+         cudaEventRecord(done[i], copy) == cudaSuccess;
+  }
+  if (copy != nullptr) ok = cudaStreamSynchronize(copy) == cudaSuccess && ok;
+  close(fd);
+  for (int i = 0; i < 2; i++) {
+    if (done[i] != nullptr) cudaEventDestroy(done[i]);
+    if (stage[i] != nullptr) cudaFreeHost(stage[i]);
+  }
+  if (copy != nullptr) cudaStreamDestroy(copy);
+  if (!ok) {
+    cudaGetLastError();
+    cudaFree(b.dev);
+    return -1;
+  }
+  b.bytes = bytes;
+  b.live = true;
+  b.weights_on_device = true;
+  return add_buffer(b);
+}
 
 void encode(bool q4, int64_t w, int64_t qs_off, int64_t sc_off, int64_t x, int64_t x_off, int64_t y,
             int64_t y_off, int64_t rows, int64_t cols, int64_t n) {
@@ -466,6 +527,7 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
             const Plan& k, uint32_t* status) {
   for (const Range& r : uploads) {
     const Buf& b = g_bufs[r.buf];
+    if (b.host == nullptr) continue;  // device-only: nothing on the host to copy
     if (cudaMemcpyAsync(b.dev + r.lo, b.host + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyHostToDevice,
                         g_stream) != cudaSuccess)
       return false;
@@ -547,6 +609,7 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
   }
   for (const Range& r : downloads) {
     const Buf& b = g_bufs[r.buf];
+    if (b.host == nullptr) continue;
     if (cudaMemcpyAsync(b.host + r.lo, b.dev + r.lo, (size_t)(r.hi - r.lo), cudaMemcpyDeviceToHost,
                         g_stream) != cudaSuccess)
       return false;
@@ -584,7 +647,7 @@ int64_t commit(int64_t wait) {
   for (const Op& o : g_ops) {
     if (o.w < 0) continue;
     Buf& b = g_bufs[o.w];
-    if (!b.weights_on_device) {
+    if (!b.weights_on_device && b.host != nullptr) {
       if (cudaMemcpyAsync(b.dev, b.host, (size_t)b.bytes, cudaMemcpyHostToDevice, g_stream) !=
           cudaSuccess)
         return 0;
@@ -786,6 +849,11 @@ void lab_gpu_enc_swiglu(int64_t g, int64_t u, int64_t count) { encode_swiglu(g, 
 
 void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count) {
   encode_add(src, srcOffset, dst, dstOffset, count);
+}
+
+int64_t dn_gpu_wrap_file(const char* path, int64_t offset, int64_t bytes) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  return wrap_file(path, offset, bytes);
 }
 
 void dn_gpu_set_fusion(int64_t on) {

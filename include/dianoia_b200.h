@@ -157,6 +157,16 @@ void lab_gpu_enc_swiglu(int64_t g, int64_t u, int64_t count);
  * lab_vulkan.c:993-998 (gpu.dart:293-297). */
 void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count);
 
+/* A GPU-layer buffer holding bytes [offset, offset + bytes) of the file at
+ * `path`, read straight into device memory (pinned staging chunks, the read
+ * of one overlapping the device copy of the other); its handle, or -1 if the
+ * file cannot be read or is shorter. For weights such as a mapped Q8 cache
+ * (lib/src/q8_cache.dart, GpuForward._wrapWeights at gpu.dart:942-979): the
+ * buffer has no host mirror (lab_gpu_contents returns NULL) and a commit
+ * copies nothing into or out of it. No counterpart in the reference, whose
+ * lab_gpu_wrap takes the mapping's address (that works here too, copying). */
+int64_t dn_gpu_wrap_file(const char* path, int64_t offset, int64_t bytes);
+
 /* With on = 0, command buffers committed from now on run every operation as
  * its own kernel on f32 inputs, with no QA links and no fusions, as the
  * reference's GPU layer dispatches them; with on = 1 (the default) they run
