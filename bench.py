@@ -1387,8 +1387,9 @@ def run_cache_workload(args):
                                         "note": "lab_gpu_wrap (copy into the pinned host mirror) "
                                                 "+ the first commit's device copy and one product"},
             "dn_gpu_wrap_file": {"s": file_s, "gbs": size / file_s / 1e9,
-                                 "note": "pread into two 32 MiB pinned chunks, each device "
-                                         "copy overlapping the next read; page-cache-hot file"},
+                                 "note": "up to 8 host threads, each a contiguous slice through "
+                                         "two 16 MiB pinned chunks (a device copy overlapping "
+                                         "the next read); page-cache-hot file"},
             "products_identical": bool(np.array_equal(y_mapped.view(np.uint32), y_file.view(np.uint32))),
             "product_matches_stack": bool(np.array_equal(
                 y_file.view(np.uint32), run_lm_head_reference(stack, L).view(np.uint32))),

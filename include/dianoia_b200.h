@@ -158,9 +158,10 @@ void lab_gpu_enc_swiglu(int64_t g, int64_t u, int64_t count);
 void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count);
 
 /* A GPU-layer buffer holding bytes [offset, offset + bytes) of the file at
- * `path`, read straight into device memory (pinned staging chunks, the read
- * of one overlapping the device copy of the other); its handle, or -1 if the
- * file cannot be read or is shorter. For weights such as a mapped Q8 cache
+ * `path`, read straight into device memory (slices on up to 8 host threads,
+ * each through pinned staging chunks whose reads overlap their device
+ * copies); its handle, or -1 if the file cannot be read or is shorter.
+ * For weights such as a mapped Q8 cache
  * (lib/src/q8_cache.dart, GpuForward._wrapWeights at gpu.dart:942-979): the
  * buffer has no host mirror (lab_gpu_contents returns NULL) and a commit
  * copies nothing into or out of it. No counterpart in the reference, whose

@@ -327,3 +327,42 @@ def test_norm_read_in_part_keeps_its_own_kernel(cuda_lib, oracle):
         L.dn_gpu_set_fusion(1)
         for hd in hs + [small, act]:
             L.lab_gpu_release(hd)
+
+
+def test_prefill_block_with_neighbours_on_the_tensor_core_path(cuda_lib, oracle):
+    """n = 20 tokens: the products take the tensor-core GEMM, so nothing is
+    fused and the norm, SwiGLU and add run as their own kernels. The norm
+    output bit for bit; each product within the reference's 1e-5 row-scale
+    bound of a double-precision sum on the inputs the GPU gave it; the
+    residual add exact; fused and unfused plans identical."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    h, f, n = 256, 512, 20
+    rng = np.random.default_rng(41)
+    layer = Layer(L, rng, h, f, n, 96, "q8")
+    try:
+        table = layer.rows("gate_up", False, "add")
+        outs = []
+        x = orc.activations(rng, n, h)
+        for fuse in (1, 0):
+            L.dn_gpu_set_fusion(fuse)
+            layer.view("x")[:] = x
+            L.lab_gpu_begin()
+            L.dn_gpu_enc_batch(table.ctypes.data, len(table))
+            assert L.lab_gpu_commit(1) == 1
+            outs.append({k: layer.view(k).copy() for k in ("a", "g", "u", "m", "x", "y")})
+        for k in outs[0]:
+            assert np.array_equal(bits(outs[0][k]), bits(outs[1][k])), k
+        got = outs[0]
+        a = oracle.rms_norm(x, layer.norm1, n, h, 1e-6)
+        assert np.array_equal(bits(got["a"]), bits(a))
+        ref, mag = oracle.reference_f64("q8", *layer.wu, got["a"], f, h, n)
+        assert orc.max_rel_err(got["u"], ref, mag) <= 1e-5
+        ref, mag = oracle.reference_f64("q8", *layer.wd, got["g"], h, f, n)
+        assert orc.max_rel_err(got["m"], ref, mag) <= 1e-5
+        assert np.array_equal(bits(got["x"]), bits((x + got["m"]).astype(np.float32)))
+        ref, mag = oracle.reference_f64("q8", *layer.wo, got["x"], 96, h, n)
+        assert orc.max_rel_err(got["y"], ref, mag) <= 1e-5
+    finally:
+        L.dn_gpu_set_fusion(1)
+        layer.release()

@@ -81,3 +81,37 @@ def test_wrap_file_rejects_what_it_cannot_read(cuda_lib, tmp_path):
     assert h >= 0 and L.lab_gpu_live_buffers() == live + 1
     L.lab_gpu_release(h)
     assert L.lab_gpu_live_buffers() == live
+
+
+def test_a_file_read_by_several_threads(cuda_lib, oracle, tmp_path):
+    """A 168 MB matrix file, read as two slices on two host threads (slices
+    are at least 64 MiB): the product on the wrapped file equals the
+    reference's kernels bit for bit."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    rng = np.random.default_rng(43)
+    rows, cols = 20480, 8192
+    qs, sc = orc.q8_weights(rng, rows, cols)
+    path = tmp_path / "big.bin"
+    with open(path, "wb") as f:
+        f.write(bytes(4096))            # a header the offsets skip
+        f.write(qs.tobytes())
+        f.write(sc.tobytes())
+    size = path.stat().st_size
+    assert size > 2 * (64 << 20)
+    h = L.dn_gpu_wrap_file(str(path).encode(), 0, size)
+    act = L.lab_gpu_buffer(4 * (cols + rows))
+    try:
+        assert h >= 0 and act >= 0
+        view = np.ctypeslib.as_array((ctypes.c_float * (cols + rows)).from_address(L.lab_gpu_contents(act)))
+        x = orc.activations(rng, 1, cols)
+        view[:cols] = x
+        L.lab_gpu_begin()
+        L.lab_gpu_enc_matmul_q8(h, 4096, 4096 + qs.size, act, 0, act, 4 * cols, rows, cols, 1)
+        assert L.lab_gpu_commit(1) == 1
+        want, _, _ = oracle.gemm("q8", qs, sc, x, rows, cols, 1, 1)
+        assert np.array_equal(view[cols:].view(np.uint32), want.view(np.uint32))
+    finally:
+        for hd in (h, act):
+            if hd >= 0:
+                L.lab_gpu_release(hd)
