@@ -28,6 +28,18 @@ SIGNATURES = {
     "lab_gemm_q4": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
     "lab_gemv_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "lab_gpu_init": (_i64, []),
+    "lab_gpu_device_name": (None, [ctypes.c_char_p, _i64]),
+    "lab_gpu_max_buffer_length": (_i64, []),
+    "lab_gpu_max_shared_memory": (_i64, []),
+    "lab_gpu_recommended_working_set": (_i64, []),
+    "lab_gpu_thermal_state": (_i64, []),
+    "lab_gpu_physical_memory": (_i64, []),
+    "lab_gpu_set_decode_rows": (None, [_i64]),
+    "lab_gpu_set_q8_group": (_i64, [_i64]),
+    "lab_gpu_set_q8_vector": (_i64, [_i64]),
+    "lab_gpu_register_q8_head": (_i64, [_i64] * 5),
+    "lab_gpu_set_profiling": (None, [_i64]),
+    "lab_gpu_profile": (_i64, [_p, _p, _i64]),
     "lab_gpu_buffer": (_i64, [_i64]),
     "lab_gpu_readback_buffer": (_i64, [_i64]),
     "lab_gpu_wrap": (_i64, [_p, _i64]),

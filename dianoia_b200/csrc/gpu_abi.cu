@@ -31,6 +31,7 @@
 // lab_gpu_commit returns 0 when a product's arguments or a CUDA call failed.
 // Calls are serialized by one mutex (the reference's layer is single-encoder).
 #include <fcntl.h>
+#include <stdio.h>
 #include <string.h>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -125,9 +126,31 @@ int64_t g_qa_cap = 0;
 // kernel on f32 inputs, as the reference's layer dispatches them.
 bool g_fuse = true;
 
+// lab_gpu_set_decode_rows(0): decode products on the generic kernel, a
+// same-device numerical reference (as the reference's old int8 GEMM is).
+bool g_generic = false;
+
+// Dispatch profiling (lab_gpu_set_profiling / lab_gpu_profile): the kinds, in
+// the reference's order (lab_vulkan.c:174-177), and per kind the GPU time and
+// dispatches since the last lab_gpu_profile. A profiled command buffer
+// records an event after its uploads and after each launch; a launch's share
+// runs from the event before it to its own.
+enum ProfKind : int {
+  kProfGemvQ8, kProfGemmQ8, kProfGemvQ4, kProfGemmQ4, kProfRmsNorm, kProfHeadNormRope, kProfConv,
+  kProfAttention, kProfSwiglu, kProfCopy, kProfQuantize, kProfGemmQ8I8, kProfGemmQ4I8,
+  kProfGemvQ8I8, kProfGemvQ4I8, kProfGemvQ8I8Vec, kProfSteer, kProfAdd, kProfKinds
+};
+bool g_profiling = false;
+double g_kind_ms[kProfKinds] = {};
+int64_t g_kind_count[kProfKinds] = {};
+std::vector<cudaEvent_t> g_prof_events;
+std::vector<int> g_prof_kinds;  // of the graph's launches, in order
+
 // The graph of the last command buffer, with what it was captured from.
 cudaGraphExec_t g_exec = nullptr;
 bool g_exec_fuse = true;
+bool g_exec_generic = false;
+bool g_exec_prof = false;
 std::vector<Op> g_exec_ops;
 std::vector<uint8_t*> g_exec_ptrs;  // device addresses the graph uses, per op (w, x, y)
 int8_t* g_exec_xq = nullptr;
@@ -149,6 +172,13 @@ bool wait_pending() {
   }
   float ms = 0.0f;
   if (cudaEventElapsedTime(&ms, g_ev0, g_ev1) == cudaSuccess) g_last_ms = ms;
+  if (g_exec_prof) {
+    for (size_t i = 0; i < g_prof_kinds.size(); i++) {
+      if (cudaEventElapsedTime(&ms, g_prof_events[i], g_prof_events[i + 1]) != cudaSuccess) continue;
+      g_kind_ms[g_prof_kinds[i]] += ms;
+      g_kind_count[g_prof_kinds[i]]++;
+    }
+  }
   uint32_t* sd = nullptr;
   volatile uint32_t* sh = nullptr;
   if (dn::status_words(&sd, &sh) && *sh != 0) return false;  // a bounded wait ran out
@@ -434,7 +464,7 @@ Plan plan_ops(uint32_t* status) {
   if (!g_fuse) return k;
   std::vector<bool> gemv(n, false);
   for (int i = 0; i < n; i++)
-    gemv[i] = g_ops[i].kind == kMatmul && dn::path_for(linear_args(g_ops[i], status)) == 0;
+    gemv[i] = g_ops[i].kind == kMatmul && !g_generic && dn::path_for(linear_args(g_ops[i], status)) == 0;
   for (int i = 2; i < n; i++) {
     const Op &s = g_ops[i], &a = g_ops[i - 2], &b = g_ops[i - 1];
     if (s.kind != kSwiglu || !gemv[i - 2] || !gemv[i - 1] || s.x == s.y) continue;
@@ -553,6 +583,14 @@ float* f32_at(int64_t buf, int64_t off) { return reinterpret_cast<float*>(g_bufs
 
 bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
             const Plan& k, uint32_t* status) {
+  // With profiling, an event after the uploads and after every launch.
+  g_prof_kinds.clear();
+  size_t ev = 0;
+  auto mark = [&](int kind) {
+    if (!g_profiling) return true;
+    if (kind >= 0) g_prof_kinds.push_back(kind);
+    return cudaEventRecord(g_prof_events[ev++], g_stream) == cudaSuccess;
+  };
   for (const Range& r : uploads) {
     const Buf& b = g_bufs[r.buf];
     if (b.host == nullptr) continue;  // device-only: nothing on the host to copy
@@ -560,9 +598,11 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
                         g_stream) != cudaSuccess)
       return false;
   }
+  if (!mark(-1)) return false;
   for (const HostQA& q : k.host) {
     if (dn::launch_quantize_qa(reinterpret_cast<const float*>(g_bufs[q.buf].dev + q.off), g_qa + q.at,
-                               q.n, q.cols, q.cols / kBlock * dn::kQABytes, g_stream) != cudaSuccess)
+                               q.n, q.cols, q.cols / kBlock * dn::kQABytes, g_stream) != cudaSuccess ||
+        !mark(kProfQuantize))
       return false;
   }
   for (size_t i = 0; i < g_ops.size(); i++) {
@@ -572,19 +612,20 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       if (k.absorbed[i]) continue;
       const dn::NormArgs na{f32_at(o.x, o.x_off), f32_at(o.w, o.qs_off), f32_at(o.y, o.y_off), qa_out,
                             o.rows / kBlock * dn::kQABytes, o.n, o.rows, o.eps, o.acc};
-      if (dn::launch_rms_norm(na, g_stream, true) != cudaSuccess) return false;
+      if (dn::launch_rms_norm(na, g_stream, true) != cudaSuccess || !mark(kProfRmsNorm)) return false;
       continue;
     }
     if (o.kind == kAdd) {
       if (k.absorbed[i]) continue;
-      if (dn::launch_add(f32_at(o.x, o.x_off), f32_at(o.y, o.y_off), o.rows, g_stream, true) != cudaSuccess)
+      if (dn::launch_add(f32_at(o.x, o.x_off), f32_at(o.y, o.y_off), o.rows, g_stream, true) != cudaSuccess ||
+          !mark(kProfAdd))
         return false;
       continue;
     }
     if (o.kind == kSwiglu) {
       if (k.absorbed[i]) continue;
       const dn::SwigluArgs sa{f32_at(o.y, 0), f32_at(o.x, 0), qa_out, o.rows};
-      if (dn::launch_swiglu(sa, g_stream, true) != cudaSuccess) return false;
+      if (dn::launch_swiglu(sa, g_stream, true) != cudaSuccess || !mark(kProfSwiglu)) return false;
       continue;
     }
     const dn::LinearArgs a = linear_args(o, status);
@@ -630,10 +671,14 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       g.n = o.n;
       g.status = status;
       rc = dn::launch_gemv_ex(g, g_stream, true);
+    } else if (g_generic) {
+      rc = dn::launch_generic(a, g_stream);
     } else {
       rc = dn::path_for(a) == 0 ? dn::launch_gemv(a, g_stream, true) : dn::launch_linear(a, g_stream);
     }
-    if (rc != 0) return false;
+    const bool tc = !g_generic && dn::path_for(a) == 1;
+    if (rc != 0 || !mark(tc ? (o.q4 ? kProfGemmQ4I8 : kProfGemmQ8I8) : (o.q4 ? kProfGemvQ4I8 : kProfGemvQ8I8)))
+      return false;
   }
   for (const Range& r : downloads) {
     const Buf& b = g_bufs[r.buf];
@@ -649,7 +694,7 @@ uint8_t* dev_of(int64_t h) { return h >= 0 ? g_bufs[h].dev : nullptr; }
 
 bool same_as_graph() {
   if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_qa != g_qa || g_exec_ops.size() != g_ops.size() ||
-      g_exec_fuse != g_fuse)
+      g_exec_fuse != g_fuse || g_exec_generic != g_generic || g_exec_prof != g_profiling)
     return false;
   for (size_t i = 0; i < g_ops.size(); i++) {
     const Op &a = g_ops[i], &b = g_exec_ops[i];
@@ -724,6 +769,14 @@ int64_t commit(int64_t wait) {
       const Range w = writes(o);
       add_range(written, w.buf, w.lo, w.hi);
     }
+    if (g_profiling) {  // one event after the uploads, one per launch at most
+      const size_t need = 1 + plan.host.size() + g_ops.size();
+      while (g_prof_events.size() < need) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreate(&e) != cudaSuccess) return 0;
+        g_prof_events.push_back(e);
+      }
+    }
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
     const bool ok = record(uploads, written, plan, status);
@@ -738,6 +791,8 @@ int64_t commit(int64_t wait) {
     cudaGraphDestroy(graph);
     g_exec_ops = g_ops;
     g_exec_fuse = g_fuse;
+    g_exec_generic = g_generic;
+    g_exec_prof = g_profiling;
     g_exec_xq = g_xq;
     g_exec_qa = g_qa;
     for (const Op& o : g_ops) {
@@ -784,6 +839,88 @@ int64_t lab_gpu_init(void) {
   g_device = dev;
   g_ready = true;
   return 1;
+}
+
+void lab_gpu_device_name(char* out, int64_t capacity) {
+  if (out == nullptr || capacity <= 0) return;
+  cudaDeviceProp p;
+  const int dev = g_ready ? g_device : 0;
+  if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) {
+    cudaGetLastError();
+    out[0] = 0;
+    return;
+  }
+  snprintf(out, (size_t)capacity, "%s", p.name);
+}
+
+// One allocation may take all of the device's memory.
+int64_t lab_gpu_max_buffer_length(void) {
+  size_t free_b = 0, total = 0;
+  if (!g_ready || cudaMemGetInfo(&free_b, &total) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return (int64_t)total;
+}
+
+// The reference's attention kernel keeps its scores in shared memory and
+// gpu.dart bounds maxSeq by this; here, the shared memory one block may opt
+// into.
+int64_t lab_gpu_max_shared_memory(void) {
+  int v = 0;
+  if (!g_ready || cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, g_device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return v;
+}
+
+int64_t lab_gpu_recommended_working_set(void) { return lab_gpu_max_buffer_length(); }
+
+int64_t lab_gpu_thermal_state(void) { return -1; }  // no such state on CUDA (as on Vulkan)
+
+int64_t lab_gpu_physical_memory(void) {
+  return (int64_t)sysconf(_SC_PHYS_PAGES) * (int64_t)sysconf(_SC_PAGESIZE);
+}
+
+// The reference's decode-GEMV shapes (rows per subgroup 1, 2, 4) are one
+// kernel here, so those and negative values keep it; 0 selects the generic
+// kernel for decode products, a same-device numerical reference.
+void lab_gpu_set_decode_rows(int64_t rows) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  g_generic = rows == 0;
+}
+
+// Vulkan workgroup sizes and a vectorized Q8 head: not modes of this
+// library, so the calls report them unavailable (0), as the reference does
+// where they are not.
+int64_t lab_gpu_set_q8_group(int64_t invocations) {
+  (void)invocations;
+  return 0;
+}
+int64_t lab_gpu_set_q8_vector(int64_t on) {
+  (void)on;
+  return 0;
+}
+int64_t lab_gpu_register_q8_head(int64_t w, int64_t qs, int64_t rows, int64_t cols, int64_t q4Body) {
+  (void)w, (void)qs, (void)rows, (void)cols, (void)q4Body;
+  return 0;
+}
+
+void lab_gpu_set_profiling(int64_t on) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  g_profiling = on != 0;
+}
+
+int64_t lab_gpu_profile(double* ms, int64_t* counts, int64_t kinds) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  for (int64_t k = 0; k < kinds && k < kProfKinds; k++) {
+    if (ms != nullptr) ms[k] = g_kind_ms[k];
+    if (counts != nullptr) counts[k] = g_kind_count[k];
+    g_kind_ms[k] = 0.0;
+    g_kind_count[k] = 0;
+  }
+  return kProfKinds;
 }
 
 int64_t lab_gpu_buffer(int64_t bytes) {

@@ -96,6 +96,36 @@ void lab_gemv_q8(const int8_t* qs, const float* scales, const float* x, int8_t* 
 int64_t lab_gpu_init(void);
 /* A zeroed buffer of `bytes`; its handle, or -1. Replaces lab_gpu_buffer,
  * lab_vulkan.c:582 (and lab_gpu_readback_buffer, :590, the same here). */
+/* Device queries (lab_vulkan.c:507-530; gpu.dart:39-60): the device's name;
+ * the longest buffer (all of the device's memory: one allocation may take
+ * it); the shared memory one block may opt into (the reference reports its
+ * attention kernel's score array there); the recommended working set (the
+ * device's memory); the thermal state (-1: none on CUDA); host RAM bytes. */
+void lab_gpu_device_name(char* out, int64_t capacity);
+int64_t lab_gpu_max_buffer_length(void);
+int64_t lab_gpu_max_shared_memory(void);
+int64_t lab_gpu_recommended_working_set(void);
+int64_t lab_gpu_thermal_state(void);
+int64_t lab_gpu_physical_memory(void);
+/* Product tuning knobs (lab_vulkan.c:670-718). set_decode_rows: 1, 2, 4 and
+ * negative values keep the one decode GEMV of this library; 0 runs decode
+ * products on the generic kernel, a same-device numerical reference.
+ * set_q8_group, set_q8_vector and register_q8_head choose Vulkan workgroup
+ * sizes and a vectorized head: unavailable here, so they return 0. */
+void lab_gpu_set_decode_rows(int64_t rows);
+int64_t lab_gpu_set_q8_group(int64_t invocations);
+int64_t lab_gpu_set_q8_vector(int64_t on);
+int64_t lab_gpu_register_q8_head(int64_t w, int64_t qs, int64_t rows, int64_t cols, int64_t q4Body);
+/* Dispatch profiling (lab_vulkan.c:719-733): with profiling on, every launch
+ * of a committed command buffer is timed, from the end of the one before it
+ * (or of the uploads) to its own end; lab_gpu_profile copies per kind, in the
+ * reference's kind order (gemv_q8, gemm_q8, gemv_q4, gemm_q4, rms_norm,
+ * head_norm_rope, conv, attention, swiglu, copy, quantize, gemm_q8_i8,
+ * gemm_q4_i8, gemv_q8_i8, gemv_q4_i8, gemv_q8_i8_vec, steer, add) the
+ * milliseconds and launches since its last call, starts over and returns the
+ * number of kinds. Fused ops count within the product that runs them. */
+void lab_gpu_set_profiling(int64_t on);
+int64_t lab_gpu_profile(double* ms, int64_t* counts, int64_t kinds);
 int64_t lab_gpu_buffer(int64_t bytes);
 int64_t lab_gpu_readback_buffer(int64_t bytes);
 /* A buffer holding a copy of `bytes` bytes at `address`; handle or -1.

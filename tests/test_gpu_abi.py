@@ -260,3 +260,68 @@ def test_links_for_slices_and_shared_host_inputs(cuda_lib, oracle):
         for h, _ in hs:
             L.lab_gpu_release(h)
         L.lab_gpu_release(act)
+
+
+def test_device_queries_and_knobs(cuda_lib):
+    """The layer's device queries and tuning knobs (lab_vulkan.c:507-718):
+    name, sizes, no thermal state; the Vulkan-only modes report unavailable."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    name = ctypes.create_string_buffer(256)
+    L.lab_gpu_device_name(name, 256)
+    assert b"B200" in name.value
+    assert L.lab_gpu_max_buffer_length() > 100 * 2**30
+    assert L.lab_gpu_recommended_working_set() == L.lab_gpu_max_buffer_length()
+    assert L.lab_gpu_max_shared_memory() >= 227 * 1024
+    assert L.lab_gpu_thermal_state() == -1
+    assert L.lab_gpu_physical_memory() > 2**30
+    assert L.lab_gpu_set_q8_group(64) == 0 and L.lab_gpu_set_q8_vector(1) == 0
+    assert L.lab_gpu_register_q8_head(0, 0, 128, 128, 0) == 0
+
+
+def test_generic_decode_rows_and_dispatch_profile(cuda_lib, oracle):
+    """lab_gpu_set_decode_rows(0) runs the same products on the generic
+    kernel (same bits); with profiling on, lab_gpu_profile reports each kind's
+    launches and time per commit in the reference's kind order, and starts
+    over after each call."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    rng = np.random.default_rng(47)
+    r1, c1 = 256, 512
+    q1, s1 = orc.q8_weights(rng, r1, c1)
+    q2, s2 = orc.q4_weights(rng, 96, r1)
+    raw = [np.concatenate([q.view(np.uint8), s.view(np.uint8)]) for q, s in [(q1, s1), (q2, s2)]]
+    w = [L.lab_gpu_wrap(r.ctypes.data, r.size) for r in raw]
+    act = L.lab_gpu_buffer(4 * (c1 + r1 + 96))
+    view = np.ctypeslib.as_array((ctypes.c_float * (c1 + r1 + 96)).from_address(L.lab_gpu_contents(act)))
+    kinds = 18
+    ms = np.zeros(kinds, np.float64)
+    counts = np.zeros(kinds, np.int64)
+    try:
+        L.lab_gpu_set_profiling(1)
+        assert L.lab_gpu_profile(ms.ctypes.data, counts.ctypes.data, kinds) == kinds  # start over
+        results = []
+        for rows_knob in (-1, 0, -1):
+            L.lab_gpu_set_decode_rows(rows_knob)
+            x = orc.activations(np.random.default_rng(5), 1, c1)
+            view[:c1] = x
+            L.lab_gpu_begin()
+            L.lab_gpu_enc_matmul_q8(w[0], 0, q1.size, act, 0, act, 4 * c1, r1, c1, 1)
+            L.lab_gpu_enc_matmul_q4(w[1], 0, q2.size, act, 4 * c1, act, 4 * (c1 + r1), 96, r1, 1)
+            assert L.lab_gpu_commit(1) == 1
+            results.append(view[c1:].copy())
+        y1, _, _ = oracle.gemm("q8", q1, s1, x, r1, c1, 1, 1)
+        y2, _, _ = oracle.gemm("q4", q2, s2, y1, 96, r1, 1, 1)
+        for got in results:
+            assert np.array_equal(got.view(np.uint32), np.concatenate([y1, y2]).view(np.uint32))
+        assert L.lab_gpu_profile(ms.ctypes.data, counts.ctypes.data, kinds) == kinds
+        # 3 commits x one Q8 and one Q4 product; the first and last quantize x0 once
+        assert counts[13] == 3 and counts[14] == 3 and counts[10] == 2
+        assert counts.sum() == 8 and (ms[counts > 0] > 0).all() and (ms[counts == 0] == 0).all()
+        L.lab_gpu_profile(ms.ctypes.data, counts.ctypes.data, kinds)
+        assert counts.sum() == 0
+    finally:
+        L.lab_gpu_set_profiling(0)
+        L.lab_gpu_set_decode_rows(-1)
+        for h in w + [act]:
+            L.lab_gpu_release(h)
