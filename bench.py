@@ -1276,10 +1276,10 @@ def run_neighbours(args, stack, L):
                          "dn_gpu_enc_batch per token"),
             "ops_per_token": len(table),
             "fused": {"tokens_s": fused_tps, "commit_device_ms": fused_ms,
-                      "kernels_per_token": 5 * LAYERS + 1,
+                      "kernels_per_token": 4 * LAYERS + 1,
                       "note": "the products only: each norm runs in the prologue of its first "
-                              "reader (which hands QA blocks to the other), SwiGLU and the adds "
-                              "in product epilogues"},
+                              "reader, gate and up run as one dual GEMV with the SwiGLU in its "
+                              "epilogue, the adds in the o and down epilogues"},
             "unfused": {"tokens_s": plain_tps, "commit_device_ms": plain_ms,
                         "kernels_per_token": 10 * LAYERS + 2},
             "logits_identical": bool(np.array_equal(fused_logits.view(np.uint32),

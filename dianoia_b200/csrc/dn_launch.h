@@ -70,6 +70,12 @@ struct GemvArgs {
   // blocks, token t at xa_out + t * xa_out_stride, for later products.
   uint8_t* xa_out;
   int64_t xa_out_stride;
+  // A second matrix of the same shape in the same launch (optional, n = 1):
+  // the feed-forward's up projection beside the gate in qs / scales. ys then
+  // receives h = silu(gate) * up (and ya its QA blocks), ys2 the up outputs.
+  const void* qs2;
+  const void* scales2;
+  float* ys2;
 };
 
 // RMSNorm of `rows` rows of `cols` values: out = w * (x * r), r =

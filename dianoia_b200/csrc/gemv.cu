@@ -53,10 +53,18 @@ using namespace gemv;
 
 // Two CTAs per SM, stated so ptxas keeps the unrolled stage in registers
 // (without a minimum it capped the kernel at 56 registers).
-template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN>
+//
+// DUAL (one token only): two matrices of the same shape, the feed-forward's
+// gate (qs, scales; tensor maps tw, tsc) and up (qs2, scales2; tw2, tsc2), in
+// one launch. A tile streams its 32 gate rows and then the same 32 up rows,
+// so the epilogue has g and u of each row in registers and writes
+// h = silu(g) * u to ys (and its QA blocks), u to ys2.
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_i8_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
-                   const __grid_constant__ CUtensorMap tsc) {
+                   const __grid_constant__ CUtensorMap tsc, const __grid_constant__ CUtensorMap tw2,
+                   const __grid_constant__ CUtensorMap tsc2) {
+  static_assert(!DUAL || NT == 1, "the dual product is for one token");
   using F = Fmt<Q4>;
   using X = XLayout<Q4>;
   constexpr int kPerBox = kBoxBytes / F::kWB;  // blocks per weight box: 4 (Q8) or 8 (Q4)
@@ -71,7 +79,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int nch = (int)((blocks + F::kKC - 1) / F::kKC);
   // This CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
   const int64_t my_tiles = (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x;
-  const int64_t total = my_tiles * nch;
+  const int tchunks = DUAL ? 2 * nch : nch;  // stages per tile
+  const int64_t total = my_tiles * tchunks;
   const bool norm = F32_IN && a.norm_w != nullptr;
   const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN, norm);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_off);
@@ -105,6 +114,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       prefetch_tmap(&tw);
       if (TMA_SCALES) prefetch_tmap(&tsc);
+      if (DUAL) prefetch_tmap(&tw2);
+      if (DUAL && TMA_SCALES) prefetch_tmap(&tsc2);
     }
     // Ring slot, its phase, chunk and tile are running counters: a 64-bit
     // division per stage would cost more than the stage's own work.
@@ -118,16 +129,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       if (abort_flag) break;
       if (lane == 0) {
-        const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-        issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, &tw, &tsc, c, nb,
-                                    (int32_t)(tile * kRows), &full[s]);
+        const bool second = DUAL && c >= nch;  // the up matrix's half of the tile
+        const int cc = second ? c - nch : c;
+        const int nb = (int)min64(F::kKC, blocks - (int64_t)cc * F::kKC);
+        issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, second ? &tw2 : &tw,
+                                    second ? &tsc2 : &tsc, cc, nb, (int32_t)(tile * kRows), &full[s]);
       }
       __syncwarp();
       if (++s == stages) {
         s = 0;
         eph ^= 1u;
       }
-      if (++c == nch) {
+      if (++c == tchunks) {
         c = 0;
         tile += gridDim.x;
       }
@@ -254,49 +267,58 @@ __global__ void __launch_bounds__(kThreads, 2)
     float acc[NT];
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+    float acc_up = 0.0f;  // DUAL: the up matrix's accumulator
 
     if constexpr (NT == 1) {
       // One token: the quad-lane core (quaddot.cuh), whole stages and the
       // rest in separate loops (a per-stage branch between them made the
-      // compiler issue the shared-memory loads late).
+      // compiler issue the shared-memory loads late). DUAL runs them for
+      // the gate rows and then for the up rows.
       const quad::Lane qc = quad::lane_ctx(warp, lane);
-      const uint8_t* xwp = xw_l;
-      const float* xsp = xs_s;
-      const uint8_t* gsc = TMA_SCALES ? nullptr : sc + row * blocks * F::kSB;
-      const int nfull = TMA_SCALES ? (int)(blocks / F::kKC) : 0;
-      int c = 0;
-      for (; c < nfull; c++) {
-        if (!warp_wait(&full[s], ph, a.status)) {
-          abort_flag = 1;
-          return;  // the producer drains what it issued; every other wait is bounded
+#pragma unroll 1
+      for (int half = 0; half < (DUAL ? 2 : 1); half++) {
+        float acc_h = 0.0f;
+        const uint8_t* xwp = xw_l;
+        const float* xsp = xs_s;
+        const uint8_t* scb = half == 0 ? sc : static_cast<const uint8_t*>(a.scales2);
+        const uint8_t* gsc = TMA_SCALES ? nullptr : scb + row * blocks * F::kSB;
+        const int nfull = TMA_SCALES ? (int)(blocks / F::kKC) : 0;
+        int c = 0;
+        for (; c < nfull; c++) {
+          if (!warp_wait(&full[s], ph, a.status)) {
+            abort_flag = 1;
+            return;  // the producer drains what it issued; every other wait is bounded
+          }
+          quad::stage_full<Q4>(smem + (int64_t)s * kStageBytes, qc, xwp, xsp, acc_h);
+          xwp += F::kKC * X::kBlockBytes;
+          xsp += F::kKC;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-        quad::stage_full<Q4>(smem + (int64_t)s * kStageBytes, qc, xwp, xsp, acc[0]);
-        xwp += F::kKC * X::kBlockBytes;
-        xsp += F::kKC;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == stages) {
-          s = 0;
-          ph ^= 1u;
+        for (; c < nch; c++) {
+          const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
+          if (!warp_wait(&full[s], ph, a.status)) {
+            abort_flag = 1;
+            return;
+          }
+          quad::stage_part<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, qc, xwp, xsp,
+                                           gsc == nullptr ? nullptr : gsc + (int64_t)c * F::kKC * F::kSB,
+                                           acc_h);
+          xwp += F::kKC * X::kBlockBytes;
+          xsp += F::kKC;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-      }
-      for (; c < nch; c++) {
-        const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-        if (!warp_wait(&full[s], ph, a.status)) {
-          abort_flag = 1;
-          return;
-        }
-        quad::stage_part<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, qc, xwp, xsp,
-                                         gsc == nullptr ? nullptr : gsc + (int64_t)c * F::kKC * F::kSB,
-                                         acc[0]);
-        xwp += F::kKC * X::kBlockBytes;
-        xsp += F::kKC;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == stages) {
-          s = 0;
-          ph ^= 1u;
-        }
+        if (half == 0) acc[0] = acc_h;
+        else acc_up = acc_h;
       }
     } else {
       const LaneCtx lc{row_local, r8, l, rowoff, xw_l, sp.xw_stride, xs_s, sp.xs_stride, sc, row, blocks};
@@ -317,13 +339,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     float* yt = yt_s + (e & 1) * NT * kRows;
+    const float up = DUAL ? lane_reduce(acc_up) : 0.0f;
 #pragma unroll
     for (int t = 0; t < NT; t++) {
       const float y = lane_reduce(acc[t]);
       if (l == 0 && row_local < tile_rows && t < nt) {
         const int64_t at = (t0 + t) * a.ldy + row0 + row_local;
         float v = y;
-        if (a.glu_out != nullptr) {
+        if (DUAL) {
+          v = silu_mul(y, up);
+          if (a.ys2 != nullptr) a.ys2[at] = up;
+          if (a.ys != nullptr) a.ys[at] = v;
+        } else if (a.glu_out != nullptr) {
           // The feed-forward's other half was written by the previous kernel,
           // which completed before this one's dependent-launch wait.
           const float other = a.glu_other[at];
@@ -405,7 +432,7 @@ __global__ void __launch_bounds__(128) generic_kernel(const LinearArgs a) {
   if (l == 0 && row_raw < a.rows) a.ys[t * a.ldy + row_raw] = y;
 }
 
-template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN>
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL>
 int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   using F = Fmt<Q4>;
   const int64_t ntiles = (a.rows + kRows - 1) / kRows;
@@ -437,26 +464,31 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   // left over lets the next kernel's CTAs become resident early (programmatic
   // dependent launch) and start streaming their weights during this kernel.
   {
-    const int64_t chunks = waves * ((blocks + F::kKC - 1) / F::kKC);
+    const int64_t chunks = waves * ((blocks + F::kKC - 1) / F::kKC) * (DUAL ? 2 : 1);
     if (chunks < stages) stages = (int)(chunks < 2 ? 2 : chunks);
   }
   const SmemPlan sp = plan<Q4>(stages, NT, a.cols, F32_IN, norm);
   if (sp.total > kMaxSmem) return kErrTooLarge;
-  CUtensorMap tw, tsc;
+  CUtensorMap tw, tsc, tw2, tsc2;
   memset(&tsc, 0, sizeof tsc);
+  memset(&tw2, 0, sizeof tw2);
+  memset(&tsc2, 0, sizeof tsc2);
   const uint64_t row_bytes = (uint64_t)blocks * F::kWB;
-  if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, (uint64_t)a.rows,
-                      row_bytes, kBoxBytes, kRows, true))
-    return kErrUnsupported;
   // The one-token kernel reads its scale box with a 64-byte swizzle (quaddot.cuh).
   const CUtensorMapDataType st = Q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  if (TMA_SCALES &&
-      !(NT == 1 ? encode_tmap_2d_sw64(&tsc, a.scales, st, (uint64_t)blocks, (uint64_t)a.rows,
-                                      (uint64_t)blocks * F::kSB, F::kKC, kRows)
-                : encode_tmap_2d(&tsc, a.scales, st, (uint64_t)blocks, (uint64_t)a.rows,
-                                 (uint64_t)blocks * F::kSB, F::kKC, kRows, false)))
+  auto maps = [&](CUtensorMap* w, CUtensorMap* sc, const void* qs, const void* scales) {
+    if (!encode_tmap_2d(w, qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, (uint64_t)a.rows, row_bytes,
+                        kBoxBytes, kRows, true))
+      return false;
+    return !TMA_SCALES ||
+           (NT == 1 ? encode_tmap_2d_sw64(sc, scales, st, (uint64_t)blocks, (uint64_t)a.rows,
+                                          (uint64_t)blocks * F::kSB, F::kKC, kRows)
+                    : encode_tmap_2d(sc, scales, st, (uint64_t)blocks, (uint64_t)a.rows,
+                                     (uint64_t)blocks * F::kSB, F::kKC, kRows, false));
+  };
+  if (!maps(&tw, &tsc, a.qs, a.scales) || (DUAL && !maps(&tw2, &tsc2, a.qs2, a.scales2)))
     return kErrUnsupported;
-  auto kern = gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN>;
+  auto kern = gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN, DUAL>;
   static bool configured[64] = {};  // per device: the opt-in smem limit is set
   int dev = 0;
   cudaGetDevice(&dev);
@@ -476,19 +508,28 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a, stages, tw, tsc) == cudaSuccess ? kOk : kErrCuda;
+  return cudaLaunchKernelEx(&cfg, kern, a, stages, tw, tsc, tw2, tsc2) == cudaSuccess ? kOk : kErrCuda;
+}
+
+template <bool Q4, int NT, bool DUAL>
+int64_t launch_gemv_d(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  const int64_t blocks = a.cols / kBlock;
+  const bool tma_scales = ((uintptr_t)a.scales & 15) == 0 && (blocks * Fmt<Q4>::kSB) % 16 == 0 &&
+                          (!DUAL || ((uintptr_t)a.scales2 & 15) == 0);
+  const bool f32_in = a.xs != nullptr;
+  if (tma_scales)
+    return f32_in ? launch_gemv_t<Q4, NT, true, true, DUAL>(a, stream, pdl)
+                  : launch_gemv_t<Q4, NT, true, false, DUAL>(a, stream, pdl);
+  return f32_in ? launch_gemv_t<Q4, NT, false, true, DUAL>(a, stream, pdl)
+                : launch_gemv_t<Q4, NT, false, false, DUAL>(a, stream, pdl);
 }
 
 template <bool Q4, int NT>
 int64_t launch_gemv_s(const GemvArgs& a, cudaStream_t stream, bool pdl) {
-  const int64_t blocks = a.cols / kBlock;
-  const bool tma_scales = ((uintptr_t)a.scales & 15) == 0 && (blocks * Fmt<Q4>::kSB) % 16 == 0;
-  const bool f32_in = a.xs != nullptr;
-  if (tma_scales)
-    return f32_in ? launch_gemv_t<Q4, NT, true, true>(a, stream, pdl)
-                  : launch_gemv_t<Q4, NT, true, false>(a, stream, pdl);
-  return f32_in ? launch_gemv_t<Q4, NT, false, true>(a, stream, pdl)
-                : launch_gemv_t<Q4, NT, false, false>(a, stream, pdl);
+  if constexpr (NT == 1) {
+    if (a.qs2 != nullptr) return launch_gemv_d<Q4, 1, true>(a, stream, pdl);
+  }
+  return launch_gemv_d<Q4, NT, false>(a, stream, pdl);
 }
 
 // Tokens per CTA: enough for n (up to 8), fewer if shared memory runs out.
@@ -498,6 +539,7 @@ int64_t launch_gemv_q(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   auto fits = [&](int nt) {
     return plan<Q4>(2, nt, a.cols, f32_in, a.norm_w != nullptr).total <= kMaxSmem;
   };
+  if (a.qs2 != nullptr && a.n != 1) return kErrUnsupported;  // the dual product is for one token
   if (a.n <= 1 || !fits(2)) return fits(1) ? launch_gemv_s<Q4, 1>(a, stream, pdl) : kErrTooLarge;
   if (a.n <= 2 || !fits(4)) return launch_gemv_s<Q4, 2>(a, stream, pdl);
   if (a.n <= 4 || !fits(8)) return launch_gemv_s<Q4, 4>(a, stream, pdl);
@@ -520,6 +562,10 @@ bool gemv_ex_supported(const GemvArgs& g) {
     return false;
   if (g.ys != nullptr && ((uintptr_t)g.ys & 3) != 0) return false;
   if (g.res != nullptr && ((uintptr_t)g.res & 3) != 0) return false;
+  if (g.qs2 != nullptr && (g.n != 1 || ((uintptr_t)g.qs2 & 15) != 0 || g.scales2 == nullptr ||
+                           ((uintptr_t)g.scales2 & (g.q4 ? 1 : 3)) != 0 || ((uintptr_t)g.ys2 & 3) != 0 ||
+                           g.glu_out != nullptr))
+    return false;
   if (g.xa_out != nullptr && (g.xs == nullptr || ((uintptr_t)g.xa_out & 3) != 0 ||
                               (g.xa_out_stride & 3) != 0 || g.xa_out_stride < g.cols / kBlock * kQABytes))
     return false;

@@ -174,7 +174,10 @@ bool wait_pending() {
   if (cudaEventElapsedTime(&ms, g_ev0, g_ev1) == cudaSuccess) g_last_ms = ms;
   if (g_exec_prof) {
     for (size_t i = 0; i < g_prof_kinds.size(); i++) {
-      if (cudaEventElapsedTime(&ms, g_prof_events[i], g_prof_events[i + 1]) != cudaSuccess) continue;
+      if (cudaEventElapsedTime(&ms, g_prof_events[i], g_prof_events[i + 1]) != cudaSuccess) {
+        cudaGetLastError();  // not sticky: keep it from a later launch's check
+        continue;
+      }
       g_kind_ms[g_prof_kinds[i]] += ms;
       g_kind_count[g_prof_kinds[i]]++;
     }
@@ -441,6 +444,8 @@ struct Plan {
   std::vector<int64_t> xa_at, xa_stride, ya_at;
   std::vector<int> glu;         // product i runs SwiGLU op glu[i] in its epilogue, or -1
   std::vector<int> res;         // product i runs add op res[i] in its epilogue, or -1
+  std::vector<int> dual;        // product i also runs product dual[i] and their SwiGLU, or -1
+  std::vector<int> runs_in;     // an absorbed op: the op whose launch runs it
   std::vector<int> normin;      // product i runs norm op normin[i] in its prologue, or -1
   std::vector<int64_t> xa_out_at;  // product i writes its quantized input as QA blocks there, or -1
   std::vector<bool> absorbed;   // a SwiGLU op that a product's epilogue runs
@@ -458,6 +463,8 @@ Plan plan_ops(uint32_t* status) {
   k.ya_at.assign(n, -1);
   k.glu.assign(n, -1);
   k.res.assign(n, -1);
+  k.dual.assign(n, -1);
+  k.runs_in.assign(n, -1);
   k.normin.assign(n, -1);
   k.xa_out_at.assign(n, -1);
   k.absorbed.assign(n, false);
@@ -469,26 +476,36 @@ Plan plan_ops(uint32_t* status) {
     const Op &s = g_ops[i], &a = g_ops[i - 2], &b = g_ops[i - 1];
     if (s.kind != kSwiglu || !gemv[i - 2] || !gemv[i - 1] || s.x == s.y) continue;
     const bool pair = (a.y == s.y && b.y == s.x) || (a.y == s.x && b.y == s.y);
-    if (pair && a.n == b.n && a.rows == b.rows && a.n * a.rows == s.rows && a.y_off == 0 &&
-        b.y_off == 0 && b.x != s.x && b.x != s.y) {
+    if (!(pair && a.n == b.n && a.rows == b.rows && a.n * a.rows == s.rows && a.y_off == 0 &&
+          b.y_off == 0 && b.x != s.x && b.x != s.y))
+      continue;
+    if (a.n == 1 && a.cols == b.cols && a.q4 == b.q4 && a.x == b.x && a.x_off == b.x_off) {
+      // One token over one input: both products in one dual launch.
+      k.dual[i - 2] = i - 1;
+      k.absorbed[i - 1] = k.absorbed[i] = true;
+      k.runs_in[i - 1] = k.runs_in[i] = i - 2;
+    } else {
       k.glu[i - 1] = i;
       k.absorbed[i] = true;
+      k.runs_in[i] = i - 1;
     }
   }
   for (int i = 1; i < n; i++) {
     const Op &d = g_ops[i], &p = g_ops[i - 1];
-    if (d.kind != kAdd || !gemv[i - 1] || k.glu[i - 1] >= 0) continue;
+    if (d.kind != kAdd || !gemv[i - 1] || k.glu[i - 1] >= 0 || k.absorbed[i - 1]) continue;
     const Range src{d.x, d.x_off, d.x_off + d.rows * 4}, dst = writes(d), out = writes(p);
     const Range in{p.x, p.x_off, p.x_off + p.n * p.cols * 4};
     if (out.buf == src.buf && out.lo == src.lo && out.hi == src.hi && !overlap(dst, in) && !overlap(dst, out)) {
       k.res[i - 1] = i;
       k.absorbed[i] = true;
+      k.runs_in[i] = i - 1;
     }
   }
   // Everything op i's launch writes: its own outputs and those of the ops it absorbed.
   auto launch_writes = [&](int i, std::vector<Range>& w) {
     w.assign(1, writes(g_ops[i]));
     if (k.glu[i] >= 0) w.push_back(writes(g_ops[k.glu[i]]));
+    if (k.dual[i] >= 0) w.push_back(writes(g_ops[k.dual[i]]));
     if (k.res[i] >= 0) w.push_back(writes(g_ops[k.res[i]]));
   };
   std::vector<Range> in, wr;
@@ -505,7 +522,9 @@ Plan plan_ops(uint32_t* status) {
       bool reads_out = false;
       for (const Range& r : in) reads_out = reads_out || overlap(r, out);
       if (k.absorbed[i]) {  // runs inside its product, whose writes were seen there
-        ok = !reads_out;
+        // The second product of a dual launch reads what the first does.
+        const bool dual_partner = g_ops[i].kind == kMatmul && k.runs_in[i] >= 0;
+        ok = ok && (dual_partner || !reads_out);
         continue;
       }
       launch_writes(i, wr);
@@ -538,13 +557,15 @@ Plan plan_ops(uint32_t* status) {
   for (int j = 0; j < n; j++) {
     const Op& o = g_ops[j];
     if (o.rows % kBlock != 0) continue;
-    if (o.kind == kMatmul) qa_src[j] = gemv[j] && k.glu[j] < 0 ? j : -1;
-    else if (o.kind == kSwiglu && k.absorbed[j]) qa_src[j] = g_ops[j - 1].rows % kBlock == 0 ? j - 1 : -1;
+    // (a product running a SwiGLU writes the SwiGLU's QA blocks, not its own)
+    if (o.kind == kMatmul) qa_src[j] = gemv[j] && k.glu[j] < 0 && k.dual[j] < 0 && !k.absorbed[j] ? j : -1;
+    else if (o.kind == kSwiglu && k.absorbed[j])
+      qa_src[j] = g_ops[k.runs_in[j]].rows % kBlock == 0 ? k.runs_in[j] : -1;
     else if (o.kind != kAdd && !k.absorbed[j]) qa_src[j] = j;
   }
   for (int i = 0; i < n; i++) {
     const Op& c = g_ops[i];
-    if (!gemv[i] || c.cols % kBlock != 0 || k.normin[i] >= 0 || k.xa_at[i] >= 0) continue;
+    if (!gemv[i] || c.cols % kBlock != 0 || k.normin[i] >= 0 || k.xa_at[i] >= 0 || k.absorbed[i]) continue;
     const int64_t lo = c.x_off, hi = c.x_off + c.n * c.cols * 4;
     int j = i - 1;
     for (; j >= 0; j--) {
@@ -583,13 +604,16 @@ float* f32_at(int64_t buf, int64_t off) { return reinterpret_cast<float*>(g_bufs
 
 bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
             const Plan& k, uint32_t* status) {
-  // With profiling, an event after the uploads and after every launch.
+  // With profiling, an event node after the uploads and after every launch
+  // (external records: timestamps in the graph), and launches without
+  // programmatic dependent launch, so that each one's share is its own.
   g_prof_kinds.clear();
   size_t ev = 0;
+  const bool pdl = !g_profiling;
   auto mark = [&](int kind) {
     if (!g_profiling) return true;
     if (kind >= 0) g_prof_kinds.push_back(kind);
-    return cudaEventRecord(g_prof_events[ev++], g_stream) == cudaSuccess;
+    return cudaEventRecordWithFlags(g_prof_events[ev++], g_stream, cudaEventRecordExternal) == cudaSuccess;
   };
   for (const Range& r : uploads) {
     const Buf& b = g_bufs[r.buf];
@@ -612,12 +636,12 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       if (k.absorbed[i]) continue;
       const dn::NormArgs na{f32_at(o.x, o.x_off), f32_at(o.w, o.qs_off), f32_at(o.y, o.y_off), qa_out,
                             o.rows / kBlock * dn::kQABytes, o.n, o.rows, o.eps, o.acc};
-      if (dn::launch_rms_norm(na, g_stream, true) != cudaSuccess || !mark(kProfRmsNorm)) return false;
+      if (dn::launch_rms_norm(na, g_stream, pdl) != cudaSuccess || !mark(kProfRmsNorm)) return false;
       continue;
     }
     if (o.kind == kAdd) {
       if (k.absorbed[i]) continue;
-      if (dn::launch_add(f32_at(o.x, o.x_off), f32_at(o.y, o.y_off), o.rows, g_stream, true) != cudaSuccess ||
+      if (dn::launch_add(f32_at(o.x, o.x_off), f32_at(o.y, o.y_off), o.rows, g_stream, pdl) != cudaSuccess ||
           !mark(kProfAdd))
         return false;
       continue;
@@ -625,12 +649,14 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
     if (o.kind == kSwiglu) {
       if (k.absorbed[i]) continue;
       const dn::SwigluArgs sa{f32_at(o.y, 0), f32_at(o.x, 0), qa_out, o.rows};
-      if (dn::launch_swiglu(sa, g_stream, true) != cudaSuccess || !mark(kProfSwiglu)) return false;
+      if (dn::launch_swiglu(sa, g_stream, pdl) != cudaSuccess || !mark(kProfSwiglu)) return false;
       continue;
     }
+    if (k.absorbed[i]) continue;  // the second product of a dual launch
     const dn::LinearArgs a = linear_args(o, status);
     int64_t rc;
-    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0 || k.normin[i] >= 0) {
+    if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0 || k.normin[i] >= 0 ||
+        k.dual[i] >= 0) {
       // (xa_out_at is set only together with normin.)
       dn::GemvArgs g{};
       g.q4 = o.q4;
@@ -655,6 +681,19 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
         g.glu_out = f32_at(s.y, 0);
       }
       if (k.res[i] >= 0) g.res = f32_at(g_ops[k.res[i]].y, g_ops[k.res[i]].y_off);
+      if (k.dual[i] >= 0) {
+        // The gate writes the SwiGLU's g buffer (s.y): its weights go first.
+        const Op& p = g_ops[k.dual[i]];
+        const Op& sw = g_ops[k.dual[i] + 1];
+        const Op& gate = o.y == sw.y ? o : p;
+        const Op& up = o.y == sw.y ? p : o;
+        g.qs = g_bufs[gate.w].dev + gate.qs_off;
+        g.scales = g_bufs[gate.w].dev + gate.sc_off;
+        g.qs2 = g_bufs[up.w].dev + up.qs_off;
+        g.scales2 = g_bufs[up.w].dev + up.sc_off;
+        g.ys = f32_at(gate.y, gate.y_off);
+        g.ys2 = f32_at(up.y, up.y_off);
+      }
       if (k.normin[i] >= 0) {
         const Op& m = g_ops[k.normin[i]];
         g.xs = f32_at(m.x, m.x_off);
@@ -670,11 +709,11 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       g.cols = o.cols;
       g.n = o.n;
       g.status = status;
-      rc = dn::launch_gemv_ex(g, g_stream, true);
+      rc = dn::launch_gemv_ex(g, g_stream, pdl);
     } else if (g_generic) {
       rc = dn::launch_generic(a, g_stream);
     } else {
-      rc = dn::path_for(a) == 0 ? dn::launch_gemv(a, g_stream, true) : dn::launch_linear(a, g_stream);
+      rc = dn::path_for(a) == 0 ? dn::launch_gemv(a, g_stream, pdl) : dn::launch_linear(a, g_stream);
     }
     const bool tc = !g_generic && dn::path_for(a) == 1;
     if (rc != 0 || !mark(tc ? (o.q4 ? kProfGemmQ4I8 : kProfGemmQ8I8) : (o.q4 ? kProfGemvQ4I8 : kProfGemvQ8I8)))

@@ -9,8 +9,10 @@ lib/src/shard.dart:456-460, restated in oracle/lab_oracle.c).
   lab_gpu_enc_matmul_* products): one feed-forward block as dianoia's
   GpuForward encodes it (gpu.dart:1180-1188: norm, gate, up, SwiGLU, down,
   and the residual: a post-norm added into it, or a plain add), where the
-  norm hands QA blocks to the gate and up products, the SwiGLU runs in the
-  up product's epilogue and the plain add in the down product's.
+  norm runs in the prologue of the gate product, gate and up run as one dual
+  GEMV with the SwiGLU in its epilogue for one token (for more tokens, up
+  takes QA blocks from gate and runs the SwiGLU in its epilogue) and the
+  plain add runs in the down product's epilogue.
   Every intermediate the host reads back, and the final product, bit for
   bit against the CPU path on the same inputs; also with the gate and up
   products swapped, with the SwiGLU kept apart from them, and with every
