@@ -27,6 +27,10 @@ SIGNATURES = {
     "lab_gemm_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
     "lab_gemm_q4": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]),
     "lab_gemv_q8": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
+    "lab_map_file": (_p, [ctypes.c_char_p, _p]),
+    "lab_unmap_file": (None, [_p, _i64]),
+    "lab_evict_file": (None, [_p, _i64]),
+    "lab_phys_footprint": (_i64, []),
     "lab_gpu_init": (_i64, []),
     "lab_gpu_device_name": (None, [ctypes.c_char_p, _i64]),
     "lab_gpu_max_buffer_length": (_i64, []),

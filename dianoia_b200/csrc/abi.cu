@@ -8,9 +8,13 @@
 // buffers that grow on demand, so concurrent calls from different threads do
 // not share scratch. Each call runs on its thread's own stream and
 // synchronizes before it returns, like the reference's CPU kernels.
+#include <fcntl.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <map>
 #include <new>
@@ -385,6 +389,44 @@ void lab_free(void* p) {
 }
 
 int64_t lab_cpu_supported(void) { return device_count() > 0 ? 1 : 0; }
+
+// Read-only private mapping of a whole file (dianoia's MappedFile, the Q8
+// cache); NULL when it cannot be opened, is empty or cannot be mapped.
+void* lab_map_file(const char* path, int64_t* size) {
+  if (path == nullptr || size == nullptr) return nullptr;
+  const int fd = open(path, O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return nullptr;
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size <= 0) {
+    close(fd);
+    return nullptr;
+  }
+  void* p = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);  // the mapping keeps the file
+  if (p == MAP_FAILED) return nullptr;
+  *size = (int64_t)st.st_size;
+  return p;
+}
+
+void lab_unmap_file(void* p, int64_t size) {
+  if (p != nullptr && size > 0) munmap(p, (size_t)size);
+}
+
+// Gives the mapping's resident pages back to the OS (a copy lives in GPU
+// memory); a later read faults them back in from the file.
+void lab_evict_file(void* p, int64_t size) {
+  if (p != nullptr && size > 0) madvise(p, (size_t)size, MADV_DONTNEED);
+}
+
+// The process's resident set in bytes (/proc/self/statm), -1 if unknown.
+int64_t lab_phys_footprint(void) {
+  FILE* f = fopen("/proc/self/statm", "r");
+  if (f == nullptr) return -1;
+  long long total = 0, resident = 0;
+  const int got = fscanf(f, "%lld %lld", &total, &resident);
+  fclose(f);
+  return got == 2 ? (int64_t)resident * (int64_t)sysconf(_SC_PAGESIZE) : -1;
+}
 
 void lab_quantize_q8(const float* w, int8_t* qs, float* scales, int64_t rows, int64_t cols) {
   quantize_entry<int8_t, float>(false, w, qs, scales, rows, cols);

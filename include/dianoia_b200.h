@@ -45,6 +45,18 @@ void lab_free(void* p);
  * else 0. Replaces lab_cpu_supported, lab_native.c:64-84; bound at native.dart:242. */
 int64_t lab_cpu_supported(void);
 
+/* Host helpers the Dart side binds from the same library (native.dart:218-240):
+ * lab_map_file maps a whole file read-only (private) and stores its length in
+ * *size, NULL if it cannot be opened, is empty or cannot be mapped
+ * (lab_native.c:109-149); lab_unmap_file unmaps it (:156); lab_evict_file
+ * gives its resident pages back to the OS, the mapping staying valid
+ * (:169-171); lab_phys_footprint is the process's resident set in bytes, -1
+ * if unknown (:876-891, which reports -1 on Linux). */
+void* lab_map_file(const char* path, int64_t* size);
+void lab_unmap_file(void* p, int64_t size);
+void lab_evict_file(void* p, int64_t size);
+int64_t lab_phys_footprint(void);
+
 /* Q8_0 quantization of rows x cols floats: per block of 32, scale = amax/127,
  * q = round-half-away(x / scale) clamped to +-127; the trailing cols % 32
  * values of a row are ignored. Replaces lab_quantize_q8, lab_native.c:407-429;

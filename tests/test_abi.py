@@ -39,7 +39,15 @@ def test_header_declares_the_reference_symbols():
                 "lab_gpu_init", "lab_gpu_buffer", "lab_gpu_readback_buffer", "lab_gpu_wrap",
                 "lab_gpu_wrap_copies", "lab_gpu_contents", "lab_gpu_release", "lab_gpu_live_buffers",
                 "lab_gpu_begin", "lab_gpu_commit", "lab_gpu_wait", "lab_gpu_last_ms",
-                "lab_gpu_enc_matmul_q8", "lab_gpu_enc_matmul_q4"):
+                "lab_gpu_enc_matmul_q8", "lab_gpu_enc_matmul_q4",
+                # the GPU layer's neighbours, queries, knobs and profiling (gpu.dart:36-312)
+                "lab_gpu_enc_rms_norm", "lab_gpu_enc_swiglu", "lab_gpu_enc_add",
+                "lab_gpu_device_name", "lab_gpu_max_buffer_length", "lab_gpu_max_shared_memory",
+                "lab_gpu_recommended_working_set", "lab_gpu_thermal_state", "lab_gpu_physical_memory",
+                "lab_gpu_set_decode_rows", "lab_gpu_set_q8_group", "lab_gpu_set_q8_vector",
+                "lab_gpu_register_q8_head", "lab_gpu_set_profiling", "lab_gpu_profile",
+                # host helpers of the same asset (native.dart:218-240)
+                "lab_map_file", "lab_unmap_file", "lab_evict_file", "lab_phys_footprint"):
         assert sym in names
 
 
@@ -104,3 +112,25 @@ def test_half_to_double_matches_numpy():
     ok = ~np.isnan(want)
     assert np.array_equal(got[ok], want[ok])
     assert np.isnan(got[~ok]).all()
+
+
+def test_file_mapping_helpers(L, tmp_path):
+    """lab_map_file / lab_unmap_file / lab_evict_file as dianoia's MappedFile
+    uses them (native.dart:268-306): the bytes of the file, still readable
+    after an eviction; NULL for a missing or empty file."""
+    data = np.random.default_rng(1).integers(0, 256, 3 * 4096 + 17, dtype=np.uint8)
+    path = tmp_path / "f.bin"
+    path.write_bytes(data.tobytes())
+    size = ctypes.c_int64(0)
+    p = L.lab_map_file(str(path).encode(), ctypes.byref(size))
+    assert p and size.value == data.size
+    view = np.ctypeslib.as_array((ctypes.c_uint8 * data.size).from_address(p))
+    assert np.array_equal(view, data)
+    L.lab_evict_file(p, size.value)
+    assert np.array_equal(view, data)
+    del view
+    L.lab_unmap_file(p, size.value)
+    assert not L.lab_map_file(str(tmp_path / "absent").encode(), ctypes.byref(size))
+    (tmp_path / "empty").write_bytes(b"")
+    assert not L.lab_map_file(str(tmp_path / "empty").encode(), ctypes.byref(size))
+    assert L.lab_phys_footprint() > 0
