@@ -60,6 +60,11 @@ SIGNATURES = {
     "lab_gpu_enc_rms_norm": (None, [_i64] * 8 + [ctypes.c_double, _i64]),
     "lab_gpu_enc_swiglu": (None, [_i64] * 3),
     "lab_gpu_enc_add": (None, [_i64] * 5),
+    "lab_gpu_enc_copy": (None, [_i64] * 5),
+    "lab_gpu_enc_steer": (None, [_i64] * 7 + [ctypes.c_double]),
+    "lab_gpu_enc_head_norm_rope": (None, [_i64] * 11 + [ctypes.c_double]),
+    "lab_gpu_enc_conv": (None, [_i64] * 8),
+    "lab_gpu_enc_attention": (None, [_i64] * 11),
     "dn_gpu_enc_batch": (None, [_p, _i64]),
     "dn_gpu_set_fusion": (None, [_i64]),
     "dn_gpu_wrap_file": (_i64, [ctypes.c_char_p, _i64, _i64]),

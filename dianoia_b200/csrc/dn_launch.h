@@ -106,6 +106,60 @@ cudaError_t launch_swiglu(const SwigluArgs& a, cudaStream_t stream, bool pdl);
 // dst += src over `count` f32 values (the residual add).
 cudaError_t launch_add(const float* src, float* dst, int64_t count, cudaStream_t stream, bool pdl);
 
+// The rest of the decode layer (mixers.cu).
+constexpr int64_t kMaxAttnKeys = 16384;  // keys one token attends to (scores in shared memory)
+constexpr int kMaxConvTaps = 16;
+
+cudaError_t launch_copy(const float* src, float* dst, int64_t count, cudaStream_t stream, bool pdl);
+
+// Per (head, token): RMSNorm over hd values with weights w, then the
+// half-split RoPE rotation from the token's table [cos(hd/2), sin(hd/2)].
+// Head h of token t at x + t * x_stride + h * hd; the table at rope + t * rope_stride.
+struct HeadNormRopeArgs {
+  float* x;
+  const float* w;
+  const float* rope;
+  int64_t x_stride, rope_stride, heads, hd, n;
+  double eps;
+};
+cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream, bool pdl);
+
+// Causal grouped-query attention of n tokens at positions position ..
+// position + n - 1 over the KV cache (rows [pos, kv_heads * hd]); q and out
+// [n, heads * hd]; gate [n, heads] before the sigmoid, or null; window > 0
+// keeps the current key and the window - 1 before it.
+struct AttentionArgs {
+  const float* q;
+  const float* keys;
+  const float* values;
+  const float* gate;
+  float* out;
+  int64_t position, n, heads, kv_heads, hd, window;
+};
+cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+
+// The gated short convolution: bcx [n, 3 * width] (B, C, X), weight
+// [width, k], history [k - 1, width] (read and updated), y [n, width].
+struct ConvArgs {
+  const float* bcx;
+  const float* weight;
+  float* history;
+  float* y;
+  int64_t width, n;
+  int k;
+};
+cudaError_t launch_conv(const ConvArgs& a, cudaStream_t stream, bool pdl);
+
+// A control vector on `rows` rows of `cols` values: mode 0 adds v, mode 1
+// subtracts scale * (x . v) * v.
+struct SteerArgs {
+  float* x;
+  const float* v;
+  int64_t rows, cols, mode;
+  double scale;
+};
+cudaError_t launch_steer(const SteerArgs& a, cudaStream_t stream, bool pdl);
+
 // The decode GEMV on either activation form (gemv.cu).
 int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl);
 bool gemv_ex_supported(const GemvArgs& g);

@@ -60,7 +60,8 @@ struct Buf {
   bool weights_on_device = false;  // copied once, at its first use as a matrix
 };
 
-enum Kind : int { kMatmul = 0, kNorm = 1, kSwiglu = 2, kAdd = 3 };
+enum Kind : int { kMatmul = 0, kNorm = 1, kSwiglu = 2, kAdd = 3, kCopy, kSteer, kHeadNormRope, kConv,
+                  kAttention };
 
 // One recorded operation. Every kind writes f32 values token-major, n rows
 // of `rows` values at byte y_off of buffer y, and reads n rows of `cols`
@@ -73,16 +74,30 @@ enum Kind : int { kMatmul = 0, kNorm = 1, kSwiglu = 2, kAdd = 3 };
 //    it also reads g. No weights (w = -1).
 //  * kAdd: dst = y at y_off plus src = x at x_off, count = rows == cols,
 //    n = 1; it also reads dst. No weights.
+// The other kinds keep their own arguments (see their encode functions) and
+// list their ranges in reads / all_writes:
+//  * kCopy: src = x at x_off, dst = y at y_off, count = rows == cols, n = 1;
+//  * kSteer: rows of x = y at y_off (n rows of cols), v = x at x_off,
+//    e[0] mode, eps the scale;
+//  * kHeadNormRope: x = y at y_off (n tokens, stride e[0] floats, rows heads
+//    of cols = hd), weights w at qs_off, rope table x at x_off (stride e[1]);
+//  * kConv: bcx = x, y = y (both at 0), weights w at qs_off, history e[0],
+//    rows = width, cols = k, n tokens;
+//  * kAttention: q = x, out = y (both at 0), keys e[0], values e[1], gate
+//    e[2] (-1: none), rows = heads, cols = hd, n tokens, position e[3],
+//    kv heads e[4], window e[5].
 struct Op {
   int kind;
   bool q4;
   int64_t w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n;
   double eps;
   bool acc;
+  int64_t e[6];
   bool operator==(const Op& o) const {
     return kind == o.kind && q4 == o.q4 && w == o.w && qs_off == o.qs_off && sc_off == o.sc_off &&
            x == o.x && x_off == o.x_off && y == o.y && y_off == o.y_off && rows == o.rows &&
-           cols == o.cols && n == o.n && memcmp(&eps, &o.eps, sizeof eps) == 0 && acc == o.acc;
+           cols == o.cols && n == o.n && memcmp(&eps, &o.eps, sizeof eps) == 0 && acc == o.acc &&
+           memcmp(e, o.e, sizeof e) == 0;
   }
 };
 
@@ -94,10 +109,66 @@ Range writes(const Op& o) { return Range{o.y, o.y_off, o.y_off + o.n * o.rows * 
 
 bool overlap(const Range& a, const Range& b) { return a.buf == b.buf && a.lo < b.hi && b.lo < a.hi; }
 
+// The extent in bytes of n rows of `width` floats `stride` floats apart.
+int64_t strided(int64_t n, int64_t stride, int64_t width) { return n <= 0 ? 0 : ((n - 1) * stride + width) * 4; }
+
 void reads(const Op& o, std::vector<Range>& r) {
   r.clear();
+  switch (o.kind) {
+    case kSteer:
+      r.push_back(Range{o.x, o.x_off, o.x_off + o.cols * 4});
+      r.push_back(Range{o.y, o.y_off, o.y_off + o.n * o.cols * 4});
+      return;
+    case kHeadNormRope:
+      r.push_back(Range{o.y, o.y_off, o.y_off + strided(o.n, o.e[0], o.rows * o.cols)});
+      r.push_back(Range{o.x, o.x_off, o.x_off + strided(o.n, o.e[1], o.cols)});
+      return;
+    case kConv:
+      r.push_back(Range{o.x, 0, o.n * 3 * o.rows * 4});
+      r.push_back(Range{o.e[0], 0, (o.cols - 1) * o.rows * 4});
+      return;
+    case kAttention: {
+      const int64_t kv = (o.e[3] + o.n) * o.e[4] * o.cols * 4;
+      r.push_back(Range{o.x, 0, o.n * o.rows * o.cols * 4});
+      r.push_back(Range{o.e[0], 0, kv});
+      r.push_back(Range{o.e[1], 0, kv});
+      if (o.e[2] >= 0) r.push_back(Range{o.e[2], 0, o.n * o.rows * 4});
+      return;
+    }
+    default:
+      break;
+  }
   r.push_back(Range{o.x, o.x_off, o.x_off + o.n * o.cols * 4});
   if (o.kind == kSwiglu || o.kind == kAdd || (o.kind == kNorm && o.acc)) r.push_back(writes(o));
+}
+
+// Every range an op writes (writes() is the first of them).
+void all_writes(const Op& o, std::vector<Range>& w) {
+  w.clear();
+  switch (o.kind) {
+    case kSteer: w.push_back(Range{o.y, o.y_off, o.y_off + o.n * o.cols * 4}); return;
+    case kHeadNormRope: w.push_back(Range{o.y, o.y_off, o.y_off + strided(o.n, o.e[0], o.rows * o.cols)}); return;
+    case kConv:
+      w.push_back(Range{o.y, 0, o.n * o.rows * 4});
+      w.push_back(Range{o.e[0], 0, (o.cols - 1) * o.rows * 4});
+      return;
+    case kAttention: w.push_back(Range{o.y, 0, o.n * o.rows * o.cols * 4}); return;
+    default: w.push_back(writes(o));
+  }
+}
+
+// The buffers an op uses (for the graph's identity and releases).
+void op_handles(const Op& o, std::vector<int64_t>& h) {
+  h.clear();
+  h.push_back(o.w);
+  h.push_back(o.x);
+  h.push_back(o.y);
+  if (o.kind == kConv) h.push_back(o.e[0]);
+  if (o.kind == kAttention) {
+    h.push_back(o.e[0]);
+    h.push_back(o.e[1]);
+    h.push_back(o.e[2]);
+  }
 }
 
 std::recursive_mutex g_mu;
@@ -360,6 +431,88 @@ void encode_add(int64_t src, int64_t src_off, int64_t dst, int64_t dst_off, int6
   g_ops.push_back(Op{kAdd, false, -1, 0, 0, src, src_off, dst, dst_off, count, count, 1, 0.0, false});
 }
 
+void encode_copy(int64_t src, int64_t src_off, int64_t dst, int64_t dst_off, int64_t count) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (!sides_ok(count, 0) || src_off % 4 != 0 || dst_off % 4 != 0 || !fits(src, src_off, count * 4) ||
+      !fits(dst, dst_off, count * 4)) {
+    g_bad_op = true;
+    return;
+  }
+  g_ops.push_back(Op{kCopy, false, -1, 0, 0, src, src_off, dst, dst_off, count, count, 1, 0.0, false});
+}
+
+void encode_steer(int64_t x, int64_t x_off, int64_t v, int64_t v_off, int64_t rows, int64_t cols,
+                  int64_t mode, double scale) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (!sides_ok(rows, cols) || (mode != 0 && mode != 1) || x_off % 4 != 0 || v_off % 4 != 0 ||
+      !fits(x, x_off, rows * cols * 4) || !fits(v, v_off, cols * 4)) {
+    g_bad_op = true;
+    return;
+  }
+  Op o{kSteer, false, -1, 0, 0, v, v_off, x, x_off, cols, cols, rows, scale, false};
+  o.e[0] = mode;
+  g_ops.push_back(o);
+}
+
+void encode_head_norm_rope(int64_t x, int64_t x_off, int64_t x_stride, int64_t w, int64_t w_off,
+                           int64_t rope, int64_t rope_off, int64_t rope_stride, int64_t heads,
+                           int64_t hd, int64_t n, double eps) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  const bool ok = sides_ok(heads, n) && n <= 65535 && hd > 0 && hd % 2 == 0 && hd <= 256 &&
+                  x_stride >= heads * hd && rope_stride >= hd && x_off % 4 == 0 && w_off % 4 == 0 &&
+                  rope_off % 4 == 0 && x_stride < kMaxSide && rope_stride < kMaxSide &&
+                  fits(x, x_off, strided(n, x_stride, heads * hd)) && fits(w, w_off, hd * 4) &&
+                  fits(rope, rope_off, strided(n, rope_stride, hd));
+  if (!ok) {
+    g_bad_op = true;
+    return;
+  }
+  Op o{kHeadNormRope, false, w, w_off, 0, rope, rope_off, x, x_off, heads, hd, n, eps, false};
+  o.e[0] = x_stride;
+  o.e[1] = rope_stride;
+  g_ops.push_back(o);
+}
+
+void encode_conv(int64_t bcx, int64_t weight, int64_t weight_off, int64_t history, int64_t y,
+                 int64_t width, int64_t k, int64_t n) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  const bool ok = sides_ok(width, n) && k >= 1 && k <= dn::kMaxConvTaps && weight_off % 4 == 0 &&
+                  fits(bcx, 0, n * 3 * width * 4) && fits(weight, weight_off, width * k * 4) &&
+                  fits(history, 0, (k - 1) * width * 4) && fits(y, 0, n * width * 4);
+  if (!ok) {
+    g_bad_op = true;
+    return;
+  }
+  Op o{kConv, false, weight, weight_off, 0, bcx, 0, y, 0, width, k, n, 0.0, false};
+  o.e[0] = history;
+  g_ops.push_back(o);
+}
+
+void encode_attention(int64_t q, int64_t keys, int64_t values, int64_t gate, int64_t out,
+                      int64_t position, int64_t n, int64_t heads, int64_t kv_heads, int64_t hd,
+                      int64_t window) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  const int64_t longest = window > 0 ? std::min(window, position + n) : position + n;
+  const int64_t kv = (position + n) * kv_heads * hd * 4;
+  const bool ok = sides_ok(heads, n) && n <= 65535 && kv_heads > 0 && hd > 0 && hd < 65536 &&
+                  heads % kv_heads == 0 && position >= 0 && position < kMaxSide && window >= 0 &&
+                  longest <= dn::kMaxAttnKeys && fits(q, 0, n * heads * hd * 4) && fits(keys, 0, kv) &&
+                  fits(values, 0, kv) && (gate < 0 || fits(gate, 0, n * heads * 4)) &&
+                  fits(out, 0, n * heads * hd * 4);
+  if (!ok) {
+    g_bad_op = true;
+    return;
+  }
+  Op o{kAttention, false, -1, 0, 0, q, 0, out, 0, heads, hd, n, 0.0, false};
+  o.e[0] = keys;
+  o.e[1] = values;
+  o.e[2] = gate < 0 ? -1 : gate;
+  o.e[3] = position;
+  o.e[4] = kv_heads;
+  o.e[5] = window;
+  g_ops.push_back(o);
+}
+
 void encode_swiglu(int64_t g, int64_t u, int64_t count) {
   std::lock_guard<std::recursive_mutex> lock(g_mu);
   if (!sides_ok(count, 0) || !fits(g, 0, count * 4) || !fits(u, 0, count * 4)) {
@@ -503,7 +656,7 @@ Plan plan_ops(uint32_t* status) {
   }
   // Everything op i's launch writes: its own outputs and those of the ops it absorbed.
   auto launch_writes = [&](int i, std::vector<Range>& w) {
-    w.assign(1, writes(g_ops[i]));
+    all_writes(g_ops[i], w);
     if (k.glu[i] >= 0) w.push_back(writes(g_ops[k.glu[i]]));
     if (k.dual[i] >= 0) w.push_back(writes(g_ops[k.dual[i]]));
     if (k.res[i] >= 0) w.push_back(writes(g_ops[k.res[i]]));
@@ -561,19 +714,22 @@ Plan plan_ops(uint32_t* status) {
     if (o.kind == kMatmul) qa_src[j] = gemv[j] && k.glu[j] < 0 && k.dual[j] < 0 && !k.absorbed[j] ? j : -1;
     else if (o.kind == kSwiglu && k.absorbed[j])
       qa_src[j] = g_ops[k.runs_in[j]].rows % kBlock == 0 ? k.runs_in[j] : -1;
-    else if (o.kind != kAdd && !k.absorbed[j]) qa_src[j] = j;
+    else if ((o.kind == kNorm || o.kind == kSwiglu) && !k.absorbed[j]) qa_src[j] = j;
   }
   for (int i = 0; i < n; i++) {
     const Op& c = g_ops[i];
     if (!gemv[i] || c.cols % kBlock != 0 || k.normin[i] >= 0 || k.xa_at[i] >= 0 || k.absorbed[i]) continue;
     const int64_t lo = c.x_off, hi = c.x_off + c.n * c.cols * 4;
     int j = i - 1;
+    std::vector<Range> ws;
     for (; j >= 0; j--) {
-      const Range w = writes(g_ops[j]);
-      if (w.buf == c.x && w.lo < hi && lo < w.hi) break;
+      all_writes(g_ops[j], ws);
+      bool hit = false;
+      for (const Range& w : ws) hit = hit || (w.buf == c.x && w.lo < hi && lo < w.hi);
+      if (hit) break;
     }
     if (j >= 0) {
-      const Range w = writes(g_ops[j]);
+      const Range w = writes(g_ops[j]);  // QA blocks come only from single-range writers
       const int64_t delta = lo - w.lo;
       const int src = qa_src[j];
       if (src < 0 || delta < 0 || hi > w.hi || delta % (kBlock * 4) != 0) continue;
@@ -650,6 +806,37 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       if (k.absorbed[i]) continue;
       const dn::SwigluArgs sa{f32_at(o.y, 0), f32_at(o.x, 0), qa_out, o.rows};
       if (dn::launch_swiglu(sa, g_stream, pdl) != cudaSuccess || !mark(kProfSwiglu)) return false;
+      continue;
+    }
+    if (o.kind == kCopy) {
+      if (dn::launch_copy(f32_at(o.x, o.x_off), f32_at(o.y, o.y_off), o.rows, g_stream, pdl) != cudaSuccess ||
+          !mark(kProfCopy))
+        return false;
+      continue;
+    }
+    if (o.kind == kSteer) {
+      const dn::SteerArgs sa{f32_at(o.y, o.y_off), f32_at(o.x, o.x_off), o.n, o.cols, o.e[0], o.eps};
+      if (dn::launch_steer(sa, g_stream, pdl) != cudaSuccess || !mark(kProfSteer)) return false;
+      continue;
+    }
+    if (o.kind == kHeadNormRope) {
+      const dn::HeadNormRopeArgs ha{f32_at(o.y, o.y_off), f32_at(o.w, o.qs_off), f32_at(o.x, o.x_off),
+                                    o.e[0], o.e[1], o.rows, o.cols, o.n, o.eps};
+      if (dn::launch_head_norm_rope(ha, g_stream, pdl) != cudaSuccess || !mark(kProfHeadNormRope))
+        return false;
+      continue;
+    }
+    if (o.kind == kConv) {
+      const dn::ConvArgs ca{f32_at(o.x, 0), f32_at(o.w, o.qs_off), f32_at(o.e[0], 0), f32_at(o.y, 0),
+                            o.rows, o.n, (int)o.cols};
+      if (dn::launch_conv(ca, g_stream, pdl) != cudaSuccess || !mark(kProfConv)) return false;
+      continue;
+    }
+    if (o.kind == kAttention) {
+      const dn::AttentionArgs aa{f32_at(o.x, 0), f32_at(o.e[0], 0), f32_at(o.e[1], 0),
+                                 o.e[2] >= 0 ? f32_at(o.e[2], 0) : nullptr, f32_at(o.y, 0),
+                                 o.e[3], o.n, o.rows, o.e[4], o.cols, o.e[5]};
+      if (dn::launch_attention(aa, g_stream, pdl) != cudaSuccess || !mark(kProfAttention)) return false;
       continue;
     }
     if (k.absorbed[i]) continue;  // the second product of a dual launch
@@ -735,11 +922,13 @@ bool same_as_graph() {
   if (g_exec == nullptr || g_exec_xq != g_xq || g_exec_qa != g_qa || g_exec_ops.size() != g_ops.size() ||
       g_exec_fuse != g_fuse || g_exec_generic != g_generic || g_exec_prof != g_profiling)
     return false;
+  std::vector<int64_t> hs;
+  size_t at = 0;
   for (size_t i = 0; i < g_ops.size(); i++) {
-    const Op &a = g_ops[i], &b = g_exec_ops[i];
-    if (!(a == b) || g_exec_ptrs[3 * i] != dev_of(a.w) || g_exec_ptrs[3 * i + 1] != dev_of(a.x) ||
-        g_exec_ptrs[3 * i + 2] != dev_of(a.y))
-      return false;
+    if (!(g_ops[i] == g_exec_ops[i])) return false;
+    op_handles(g_ops[i], hs);
+    for (int64_t h : hs)
+      if (at >= g_exec_ptrs.size() || g_exec_ptrs[at++] != dev_of(h)) return false;
   }
   return true;
 }
@@ -802,11 +991,12 @@ int64_t commit(int64_t wait) {
     }
     // Ranges to copy in (host-written inputs) and out (the ops' outputs).
     std::vector<Range> uploads, written, in;
+    std::vector<Range> outs;
     for (const Op& o : g_ops) {
       reads(o, in);
       for (const Range& r : in) subtract(written, r.buf, r.lo, r.hi, uploads);
-      const Range w = writes(o);
-      add_range(written, w.buf, w.lo, w.hi);
+      all_writes(o, outs);
+      for (const Range& w : outs) add_range(written, w.buf, w.lo, w.hi);
     }
     if (g_profiling) {  // one event after the uploads, one per launch at most
       const size_t need = 1 + plan.host.size() + g_ops.size();
@@ -834,10 +1024,10 @@ int64_t commit(int64_t wait) {
     g_exec_prof = g_profiling;
     g_exec_xq = g_xq;
     g_exec_qa = g_qa;
+    std::vector<int64_t> hs;
     for (const Op& o : g_ops) {
-      g_exec_ptrs.push_back(dev_of(o.w));
-      g_exec_ptrs.push_back(dev_of(o.x));
-      g_exec_ptrs.push_back(dev_of(o.y));
+      op_handles(o, hs);
+      for (int64_t h : hs) g_exec_ptrs.push_back(dev_of(h));
     }
   }
   if (cudaEventRecord(g_ev0, g_stream) != cudaSuccess ||
@@ -902,17 +1092,10 @@ int64_t lab_gpu_max_buffer_length(void) {
   return (int64_t)total;
 }
 
-// The reference's attention kernel keeps its scores in shared memory and
-// gpu.dart bounds maxSeq by this; here, the shared memory one block may opt
-// into.
-int64_t lab_gpu_max_shared_memory(void) {
-  int v = 0;
-  if (!g_ready || cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, g_device) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  return v;
-}
+// What gpu.dart bounds maxSeq by: the attention kernel's score array, as the
+// reference reports it (lab_vulkan.c:513-515: keys * 4 + 128 bytes). Here the
+// scores are doubles, kMaxAttnKeys of them.
+int64_t lab_gpu_max_shared_memory(void) { return dn::kMaxAttnKeys * 4 + 128; }
 
 int64_t lab_gpu_recommended_working_set(void) { return lab_gpu_max_buffer_length(); }
 
@@ -997,8 +1180,10 @@ void lab_gpu_release(int64_t handle) {
   wait_pending();
   cudaSetDevice(g_device);
   Buf& b = g_bufs[handle];
+  std::vector<int64_t> hs;
   for (const Op& o : g_exec_ops) {
-    if (o.w == handle || o.x == handle || o.y == handle) {
+    op_handles(o, hs);
+    if (std::find(hs.begin(), hs.end(), handle) != hs.end()) {
       drop_graph();
       break;
     }
@@ -1058,6 +1243,32 @@ void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOff
 int64_t dn_gpu_wrap_file(const char* path, int64_t offset, int64_t bytes) {
   std::lock_guard<std::recursive_mutex> lock(g_mu);
   return wrap_file(path, offset, bytes);
+}
+
+void lab_gpu_enc_copy(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count) {
+  encode_copy(src, srcOffset, dst, dstOffset, count);
+}
+
+void lab_gpu_enc_steer(int64_t x, int64_t xOffset, int64_t v, int64_t vOffset, int64_t rows,
+                       int64_t cols, int64_t mode, double scale) {
+  encode_steer(x, xOffset, v, vOffset, rows, cols, mode, scale);
+}
+
+void lab_gpu_enc_head_norm_rope(int64_t x, int64_t xOffset, int64_t xStride, int64_t w, int64_t wOffset,
+                                int64_t rope, int64_t ropeOffset, int64_t ropeStride, int64_t heads,
+                                int64_t hd, int64_t n, double eps) {
+  encode_head_norm_rope(x, xOffset, xStride, w, wOffset, rope, ropeOffset, ropeStride, heads, hd, n, eps);
+}
+
+void lab_gpu_enc_conv(int64_t bcx, int64_t weight, int64_t weightOffset, int64_t history, int64_t y,
+                      int64_t width, int64_t k, int64_t n) {
+  encode_conv(bcx, weight, weightOffset, history, y, width, k, n);
+}
+
+void lab_gpu_enc_attention(int64_t q, int64_t keys, int64_t values, int64_t gate, int64_t out,
+                           int64_t position, int64_t n, int64_t heads, int64_t kvHeads, int64_t hd,
+                           int64_t window) {
+  encode_attention(q, keys, values, gate, out, position, n, heads, kvHeads, hd, window);
 }
 
 void dn_gpu_set_fusion(int64_t on) {

@@ -110,8 +110,8 @@ int64_t lab_gpu_init(void);
  * lab_vulkan.c:582 (and lab_gpu_readback_buffer, :590, the same here). */
 /* Device queries (lab_vulkan.c:507-530; gpu.dart:39-60): the device's name;
  * the longest buffer (all of the device's memory: one allocation may take
- * it); the shared memory one block may opt into (the reference reports its
- * attention kernel's score array there); the recommended working set (the
+ * it); the attention kernel's score capacity as the reference reports it
+ * (keys * 4 + 128 bytes, gpu.dart bounds maxSeq by it); the recommended working set (the
  * device's memory); the thermal state (-1: none on CUDA); host RAM bytes. */
 void lab_gpu_device_name(char* out, int64_t capacity);
 int64_t lab_gpu_max_buffer_length(void);
@@ -217,6 +217,40 @@ int64_t dn_gpu_wrap_file(const char* path, int64_t offset, int64_t bytes);
  * counterpart in the reference. */
 void dn_gpu_set_fusion(int64_t on);
 
+/* The rest of a decode layer as dianoia's GpuForward encodes it, with the
+ * arithmetic of its CPU path (double where Dart computes in double, f32
+ * where it stores into a Float32List). Offsets are bytes; strides floats.
+ * lab_gpu_enc_copy: dst = src, count floats (lab_vulkan.c:985-991).
+ * lab_gpu_enc_steer: rows of cols floats at x: mode 0 adds v, mode 1
+ *   subtracts scale * (x . v) * v (lab_vulkan.c:1010-1016;
+ *   control_vector.dart:176-203).
+ * lab_gpu_enc_head_norm_rope: per (head, token) RMSNorm over hd values with
+ *   weights w, then the half-split RoPE from the token's table
+ *   [cos(hd/2), sin(hd/2)] at rope + ropeOffset + token * ropeStride; token t
+ *   of x at xOffset + t * xStride (lab_vulkan.c:916-930; shard.dart:548-557,
+ *   ops.dart:12-71). hd even, at most 256.
+ * lab_gpu_enc_conv: the gated short convolution: bcx [n, 3 width] (B, C, X),
+ *   weights [width, k] at weightOffset, history [k - 1, width] read and
+ *   updated, y [n, width] = C * causal conv of B * X (lab_vulkan.c:932-941;
+ *   shard.dart:476-516). k at most 16.
+ * lab_gpu_enc_attention: causal grouped-query attention of n tokens at
+ *   positions position.. over the KV cache (rows [position + n, kvHeads *
+ *   hd]), q and out [n, heads * hd], gate [n, heads] before the sigmoid or a
+ *   negative handle for none, window > 0 keeping the current key and the
+ *   window - 1 before it (lab_vulkan.c:949-966; shard.dart:589-628). A token
+ *   sees at most 16384 keys (what lab_gpu_max_shared_memory reports). */
+void lab_gpu_enc_copy(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count);
+void lab_gpu_enc_steer(int64_t x, int64_t xOffset, int64_t v, int64_t vOffset, int64_t rows,
+                       int64_t cols, int64_t mode, double scale);
+void lab_gpu_enc_head_norm_rope(int64_t x, int64_t xOffset, int64_t xStride, int64_t w, int64_t wOffset,
+                                int64_t rope, int64_t ropeOffset, int64_t ropeStride, int64_t heads,
+                                int64_t hd, int64_t n, double eps);
+void lab_gpu_enc_conv(int64_t bcx, int64_t weight, int64_t weightOffset, int64_t history, int64_t y,
+                      int64_t width, int64_t k, int64_t n);
+void lab_gpu_enc_attention(int64_t q, int64_t keys, int64_t values, int64_t gate, int64_t out,
+                           int64_t position, int64_t n, int64_t heads, int64_t kvHeads, int64_t hd,
+                           int64_t window);
+
 /* Kinds of the rows of dn_gpu_enc_batch. */
 #define DN_BATCH_Q8 0
 #define DN_BATCH_Q4 1
@@ -237,7 +271,9 @@ void dn_gpu_set_fusion(int64_t on);
  *   DN_BATCH_SWIGLU: g, u, count, then unused (lab_gpu_enc_swiglu);
  *   DN_BATCH_ADD: src, srcOffset, dst, dstOffset, count, then unused
  *     (lab_gpu_enc_add).
- * An unknown kind makes the next lab_gpu_commit return 0. */
+ * An unknown kind makes the next lab_gpu_commit return 0. The other
+ * encoders (copy, steer, head norm, conv, attention) are recorded by their
+ * own calls. */
 void dn_gpu_enc_batch(const int64_t* table, int64_t count);
 
 /* ------------------------------------------------------------ dn_* (device API) */

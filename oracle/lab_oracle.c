@@ -333,3 +333,102 @@ void orc_swiglu(float* g, const float* u, int64_t count) {
     g[j] = (float)((double)s * (double)u[j]);
   }
 }
+
+/* shard.dart:548-557 + ops.dart:62-71: per (token, head) the head's hd values
+ * normalised by orc_rms_norm's arithmetic with weights w, then Rope.apply with
+ * the token's table [cos(hd/2), sin(hd/2)]: x1 * cos - x2 * sin and
+ * x2 * cos + x1 * sin in double, stored to f32. Strides in floats. */
+void orc_head_norm_rope(float* x, int64_t x_stride, const float* w, const float* rope,
+                        int64_t rope_stride, int64_t heads, int64_t hd, int64_t n, double eps) {
+  const int64_t pair = hd / 2;
+  for (int64_t t = 0; t < n; t++) {
+    const float* c = rope + t * rope_stride;
+    for (int64_t h = 0; h < heads; h++) {
+      float* v = x + t * x_stride + h * hd;
+      orc_rms_norm(v, w, v, 1, hd, eps, 0);
+      for (int64_t j = 0; j < pair; j++) {
+        const double x1 = v[j], x2 = v[j + pair];
+        v[j] = (float)(x1 * (double)c[j] - x2 * (double)c[pair + j]);
+        v[j + pair] = (float)(x2 * (double)c[j] + x1 * (double)c[pair + j]);
+      }
+    }
+  }
+}
+
+/* shard.dart:589-628: causal grouped-query attention in double. */
+void orc_attention(const float* q, const float* keys, const float* values, const float* gate,
+                   float* out, int64_t position, int64_t n, int64_t heads, int64_t kv_heads,
+                   int64_t hd, int64_t window, double* scores) {
+  const int64_t q_dim = heads * hd, kv_dim = kv_heads * hd, group = heads / kv_heads;
+  const double scale = 1 / sqrt((double)hd);
+  for (int64_t t = 0; t < n; t++) {
+    const int64_t pos = position + t;
+    const int64_t start = window > 0 && pos - window + 1 > 0 ? pos - window + 1 : 0;
+    for (int64_t h = 0; h < heads; h++) {
+      const int64_t qo = t * q_dim + h * hd, kvo = (h / group) * hd;
+      double max = -INFINITY;
+      for (int64_t s = start; s <= pos; s++) {
+        double dot = 0.0;
+        for (int64_t d = 0; d < hd; d++) dot += (double)q[qo + d] * (double)keys[s * kv_dim + kvo + d];
+        const double score = dot * scale;
+        scores[s] = score;
+        if (score > max) max = score;
+      }
+      double sum = 0.0;
+      for (int64_t s = start; s <= pos; s++) {
+        const double e = exp(scores[s] - max);
+        scores[s] = e;
+        sum += e;
+      }
+      const double g = gate ? 1 / (1 + exp(-(double)gate[t * heads + h])) : 1.0;
+      for (int64_t d = 0; d < hd; d++) {
+        double acc = 0.0;
+        for (int64_t s = start; s <= pos; s++) acc += scores[s] * (double)values[s * kv_dim + kvo + d];
+        out[qo + d] = (float)(acc / sum);
+        if (gate) out[qo + d] = (float)((double)out[qo + d] * g);
+      }
+    }
+  }
+}
+
+/* shard.dart:476-516: z = B * X (f32), y = C * sum_s kernel[k-1-s] z[t-s]
+ * (the sum in double, from 0.0, s = 0 first), history = the last k - 1 z. */
+void orc_conv(const float* bcx, const float* weight, float* history, float* y, int64_t width,
+              int64_t k, int64_t n, float* z) {
+  for (int64_t t = 0; t < n; t++)
+    for (int64_t ch = 0; ch < width; ch++)
+      z[t * width + ch] = bcx[t * 3 * width + ch] * bcx[t * 3 * width + 2 * width + ch];
+  for (int64_t t = 0; t < n; t++)
+    for (int64_t ch = 0; ch < width; ch++) {
+      double acc = 0.0;
+      for (int64_t s = 0; s < k; s++) {
+        const int64_t src = t - s;
+        const float zz = src >= 0 ? z[src * width + ch] : history[(k - 1 + src) * width + ch];
+        acc += (double)weight[ch * k + k - 1 - s] * (double)zz;
+      }
+      y[t * width + ch] = (float)((double)bcx[t * 3 * width + width + ch] * acc);
+    }
+  const int64_t keep = k - 1;
+  if (n >= keep) {
+    memcpy(history, z + (n - keep) * width, (size_t)(keep * width) * sizeof(float));
+  } else {
+    memmove(history, history + n * width, (size_t)((keep - n) * width) * sizeof(float));
+    memcpy(history + (keep - n) * width, z, (size_t)(n * width) * sizeof(float));
+  }
+}
+
+/* control_vector.dart:176-203: mode 0 adds v (f32); mode 1 subtracts
+ * scale * dot * v, the dot and the update in double, stored to f32. */
+void orc_steer(float* x, const float* v, int64_t rows, int64_t cols, int64_t mode, double scale) {
+  for (int64_t t = 0; t < rows; t++) {
+    float* r = x + t * cols;
+    if (mode == 0) {
+      for (int64_t j = 0; j < cols; j++) r[j] = r[j] + v[j];
+      continue;
+    }
+    double dot = 0.0;
+    for (int64_t j = 0; j < cols; j++) dot += (double)r[j] * (double)v[j];
+    const double c = scale * dot;
+    for (int64_t j = 0; j < cols; j++) r[j] = (float)((double)r[j] - c * (double)v[j]);
+  }
+}

@@ -71,6 +71,14 @@ class Oracle(_Lib):
         L.orc_rms_norm.restype = None
         L.orc_swiglu.argtypes = [_p, _p, _i64]
         L.orc_swiglu.restype = None
+        L.orc_head_norm_rope.argtypes = [_p, _i64, _p, _p, _i64, _i64, _i64, _i64, ctypes.c_double]
+        L.orc_head_norm_rope.restype = None
+        L.orc_attention.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p]
+        L.orc_attention.restype = None
+        L.orc_conv.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _p]
+        L.orc_conv.restype = None
+        L.orc_steer.argtypes = [_p, _p, _i64, _i64, _i64, ctypes.c_double]
+        L.orc_steer.restype = None
 
     def half_to_float(self, h: int) -> float:
         return self.lib.orc_half_to_float(h)
@@ -133,6 +141,41 @@ class Oracle(_Lib):
         return h
 
 
+    def head_norm_rope(self, x, x_stride, w, rope, rope_stride, heads, hd, n, eps) -> np.ndarray:
+        """Per-head RMSNorm + RoPE of the CPU path, on a copy of x."""
+        y = np.array(x, np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        rope = np.ascontiguousarray(rope, dtype=np.float32)
+        self.lib.orc_head_norm_rope(_ptr(y), x_stride, _ptr(w), _ptr(rope), rope_stride, heads, hd, n, eps)
+        return y
+
+    def attention(self, q, keys, values, gate, position, n, heads, kv_heads, hd, window) -> np.ndarray:
+        """The CPU path's attention in double; out [n, heads * hd]."""
+        arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, keys, values)]
+        g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+        out = np.zeros(n * heads * hd, np.float32)
+        scores = np.zeros(position + n, np.float64)
+        self.lib.orc_attention(_ptr(arrs[0]), _ptr(arrs[1]), _ptr(arrs[2]), _ptr(g), _ptr(out),
+                               position, n, heads, kv_heads, hd, window, _ptr(scores))
+        return out
+
+    def conv(self, bcx, weight, history, width, k, n):
+        """The gated short conv; returns (y, updated history)."""
+        bcx = np.ascontiguousarray(bcx, dtype=np.float32)
+        weight = np.ascontiguousarray(weight, dtype=np.float32)
+        hist = np.array(history, np.float32)
+        y = np.zeros(n * width, np.float32)
+        z = np.zeros(max(n * width, 1), np.float32)
+        self.lib.orc_conv(_ptr(bcx), _ptr(weight), _ptr(hist), _ptr(y), width, k, n, _ptr(z))
+        return y, hist
+
+    def steer(self, x, v, rows, cols, mode, scale) -> np.ndarray:
+        y = np.array(x, np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        self.lib.orc_steer(_ptr(y), _ptr(v), rows, cols, mode, scale)
+        return y
+
+
 class Reference(_Lib):
     """The reference's lab_native.c, compiled here (oracle/_ref/libref_lab.so)."""
 
@@ -148,6 +191,8 @@ class Reference(_Lib):
             getattr(L, name).restype = None
         L.lab_quantize_q8.restype = None
         L.lab_quantize_q4.restype = None
+        L.lab_attention.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64]
+        L.lab_attention.restype = None
 
     def quantize_q8(self, w, rows, cols):
         w = np.ascontiguousarray(w, dtype=np.float32)
@@ -162,6 +207,15 @@ class Reference(_Lib):
         sc = np.zeros(rows * (cols // BLOCK), np.uint16)
         self.lib.lab_quantize_q4(_ptr(w), _ptr(qs), _ptr(sc), rows, cols)
         return qs, sc
+
+    def attention(self, q, keys, values, gate, position, n, heads, kv_heads, hd, window, threads=1):
+        """The reference's own C attention (lab_native.c:703-740, f32 and expf)."""
+        arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, keys, values)]
+        g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+        out = np.zeros(n * heads * hd, np.float32)
+        self.lib.lab_attention(_ptr(arrs[0]), _ptr(arrs[1]), _ptr(arrs[2]), _ptr(g), _ptr(out), n,
+                               position, heads, kv_heads, hd, window, threads)
+        return out
 
     def gemm(self, fmt, qs, scales, xs, rows, cols, n, mode=1, threads=1,
              out=None):

@@ -171,3 +171,70 @@ def test_swiglu_restatements_agree(oracle):
     got = oracle.swiglu(g, u)
     assert np.array_equal(bits(got), bits(_py_swiglu(g, u)))
     assert got[0] == 0 and got[2] == np.float32(90.0) * u[2] and got[5] == 0
+
+
+# ------------------------------------------------------------ the layer's other ops
+
+@pytest.mark.parametrize("heads,kv,hd,pos,n,window,gated", [
+    (16, 8, 128, 50, 3, 0, True), (16, 8, 128, 40, 1, 16, False), (4, 4, 64, 0, 5, 0, True),
+    (8, 2, 128, 300, 2, 64, True)])
+def test_attention_restatement_against_the_reference_c(oracle, reference, heads, kv, hd, pos, n, window, gated):
+    """orc_attention (shard.dart's double arithmetic) against the reference's
+    own lab_attention (lab_native.c:588-740, f32 with expf), compiled here:
+    within f32 rounding of the outputs."""
+    rng = np.random.default_rng(heads + pos + n)
+    q = rng.standard_normal(n * heads * hd).astype(np.float32)
+    k = rng.standard_normal((pos + n) * kv * hd).astype(np.float32)
+    v = rng.standard_normal((pos + n) * kv * hd).astype(np.float32)
+    g = rng.standard_normal(n * heads).astype(np.float32) if gated else None
+    a = oracle.attention(q, k, v, g, pos, n, heads, kv, hd, window)
+    b = reference.attention(q, k, v, g, pos, n, heads, kv, hd, window)
+    assert np.abs(a - b).max() <= 1e-5 * max(1.0, np.abs(b).max())
+
+
+def test_conv_steer_and_head_norm_restatements(oracle):
+    """orc_conv, orc_steer and orc_head_norm_rope against restatements in
+    Python (Dart's double is Python's float; f32 stores through numpy)."""
+    import math
+    rng = np.random.default_rng(12)
+    f = lambda v: float(np.float32(v))
+    width, k, n = 5, 3, 4
+    bcx = rng.standard_normal(n * 3 * width).astype(np.float32)
+    w = rng.standard_normal(width * k).astype(np.float32)
+    hist = rng.standard_normal((k - 1) * width).astype(np.float32)
+    y, h2 = oracle.conv(bcx, w, hist, width, k, n)
+    z = [[f(float(bcx[t * 3 * width + c]) * float(bcx[t * 3 * width + 2 * width + c])) for c in range(width)]
+         for t in range(n)]
+    for t in range(n):
+        for c in range(width):
+            acc = 0.0
+            for s in range(k):
+                src = t - s
+                zz = z[src][c] if src >= 0 else float(hist[(k - 1 + src) * width + c])
+                acc += float(w[c * k + k - 1 - s]) * zz
+            assert y[t * width + c] == np.float32(float(bcx[t * 3 * width + width + c]) * acc)
+    assert np.array_equal(h2, np.array(z[-(k - 1):], np.float32).ravel())
+
+    x = rng.standard_normal(3 * 16).astype(np.float32)
+    v = rng.standard_normal(16).astype(np.float32)
+    got = oracle.steer(x, v, 3, 16, 1, 0.75)
+    for t in range(3):
+        dot = 0.0
+        for j in range(16):
+            dot += float(x[t * 16 + j]) * float(v[j])
+        c = 0.75 * dot
+        want = [f(float(x[t * 16 + j]) - c * float(v[j])) for j in range(16)]
+        assert got[t * 16:(t + 1) * 16].tolist() == want
+    assert np.array_equal(oracle.steer(x, v, 3, 16, 0, 1.0), x + np.tile(v, 3))
+
+    heads, hd = 2, 8
+    xs = rng.standard_normal(heads * hd).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    rope = rng.uniform(-1, 1, hd).astype(np.float32)
+    got = oracle.head_norm_rope(xs, heads * hd, nw, rope, hd, heads, hd, 1, 1e-6)
+    for hh in range(heads):
+        seg = _py_rms_norm(xs[hh * hd:(hh + 1) * hd], nw, 1e-6)
+        for j in range(hd // 2):
+            x1, x2, c, s = float(seg[j]), float(seg[j + hd // 2]), float(rope[j]), float(rope[hd // 2 + j])
+            assert got[hh * hd + j] == np.float32(x1 * c - x2 * s)
+            assert got[hh * hd + j + hd // 2] == np.float32(x2 * c + x1 * s)
