@@ -501,6 +501,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--neighbour-steps", type=int, default=30,
                     help="tokens of the decode stack with norms, SwiGLU and residual adds")
+    ap.add_argument("--context", type=int, default=1024,
+                    help="KV-cache position of the whole decode step (with attention)")
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours", "cache"],
                     default="stack",
@@ -674,6 +676,7 @@ def main():
     if e2e is None:
         e2e = e2e_cpu_abi
     neighbours = run_neighbours(args, stack, L) if world == 1 else None
+    decode_step = run_neighbours(args, stack, L, context=args.context) if world == 1 else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and args.cpu_tokens > 0:
@@ -701,6 +704,7 @@ def main():
             "e2e": e2e,
             "e2e_cpu_abi": e2e_cpu_abi,
             "neighbours": neighbours,
+            "decode_step": decode_step,
             "cpu_baseline": cpu_baseline,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": ("1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
@@ -1182,7 +1186,7 @@ def wrap_stack(L, stack, handles):
     return mats
 
 
-def run_neighbours(args, stack, L):
+def run_neighbours(args, stack, L, context=0):
     """The decode stack with the neighbours of its products, through the GPU
     layer as dianoia's GpuForward encodes a Qwen3 layer (gpu.dart:1100-1190)
     less the attention (out of this path: o reads q's rows in its place):
@@ -1193,7 +1197,13 @@ def run_neighbours(args, stack, L):
     one dn_gpu_enc_batch, lab_gpu_commit(wait=1)), fused (norms hand QA
     blocks to their products, SwiGLU and the adds run in product epilogues)
     and with every op its own kernel on f32 inputs (dn_gpu_set_fusion(0), the
-    reference layer's dispatch structure)."""
+    reference layer's dispatch structure).
+
+    With `context` > 0 the attention is there too, as GpuForward records it
+    (gpu.dart:1100-1180): q and k per-head RMSNorm + RoPE in place, the
+    token's k and v copied into device-resident KV caches (dn_gpu_device_buffer)
+    at row `context`, causal attention over the `context` + 1 cached rows, and
+    o reading the attention's output: a whole Qwen3-1.7B-shaped decode step."""
     steps = args.neighbour_steps
     if steps <= 0 or L.lab_gpu_init() != 1:
         return None
@@ -1205,7 +1215,25 @@ def run_neighbours(args, stack, L):
         small = L.lab_gpu_wrap(norms.ctypes.data, norms.nbytes)
         handles.append(small)
         sizes = {"x": HIDDEN, "a": HIDDEN, "qkv": OUT_ROWS["qkv"], "m": HIDDEN, "g": INTER,
-                 "u": INTER}
+                 "u": INTER, "attn": HEADS * HEAD_DIM, "rope": 2 * HEAD_DIM}
+        kv_dim = KV_HEADS * HEAD_DIM
+        caches = []
+        if context > 0:
+            qk = (1 + 0.1 * rng.standard_normal(LAYERS * 2 * HEAD_DIM)).astype(np.float32)
+            qk_norms = L.lab_gpu_wrap(qk.ctypes.data, qk.nbytes)
+            handles.append(qk_norms)
+            init = rng.standard_normal((context + 1) * kv_dim).astype(np.float32)
+            stage = L.lab_gpu_buffer(init.nbytes)
+            handles.append(stage)
+            np.ctypeslib.as_array((ctypes.c_float * init.size).from_address(L.lab_gpu_contents(stage)))[:] = init
+            L.lab_gpu_begin()
+            for _ in range(2 * LAYERS):  # random history in every layer's keys and values
+                c = L.dn_gpu_device_buffer(init.nbytes)
+                handles.append(c)
+                caches.append(c)
+                L.lab_gpu_enc_copy(stage, 0, c, 0, init.size)
+            if min(handles) < 0 or L.lab_gpu_commit(1) != 1:
+                raise RuntimeError("filling the KV caches failed")
         buf = {}
         for name, size in sizes.items():
             buf[name] = L.lab_gpu_buffer(4 * size)
@@ -1226,13 +1254,34 @@ def run_neighbours(args, stack, L):
         def add():
             return [4, B["m"], 0, B["x"], 0, HIDDEN, 0, 0, 0, 0, 0]
 
+        qkv_floats = OUT_ROWS["qkv"]
+
+        def attention_block(layer):
+            """Rows between qkv and o: q and k norm + RoPE, the KV copies, attention."""
+            keys, values = caches[2 * layer], caches[2 * layer + 1]
+            q_dim = HEADS * HEAD_DIM
+
+            def hnr(x_off, heads, w_off):
+                packed = heads | (HEAD_DIM << 16) | (1 << 32)
+                return [7, B["qkv"], x_off, qkv_floats, qk_norms, w_off, B["rope"], 0, 2 * HEAD_DIM,
+                        packed, eps_bits]
+
+            return [hnr(0, HEADS, 4 * 2 * HEAD_DIM * layer),
+                    hnr(4 * q_dim, KV_HEADS, 4 * (2 * HEAD_DIM * layer + HEAD_DIM)),
+                    [5, B["qkv"], 4 * q_dim, keys, 4 * context * kv_dim, kv_dim, 0, 0, 0, 0, 0],
+                    [5, B["qkv"], 4 * (q_dim + kv_dim), values, 4 * context * kv_dim, kv_dim, 0, 0, 0, 0, 0],
+                    [9, B["qkv"], keys, values, -1, B["attn"], context, 1, HEADS, KV_HEADS, HEAD_DIM]]
+
         table = []
         for layer in range(LAYERS):
             (wqkv, aqkv), (wo, ao), (wgu, agu), (wd, ad) = mats[4 * layer:4 * layer + 4]
             half_qs, half_sc = INTER * HIDDEN, INTER * (HIDDEN // 32) * 4
+            o_in = "attn" if context > 0 else "qkv"
             table += [norm(2 * layer),
-                      [0, wqkv, 0, aqkv, B["a"], 0, B["qkv"], 0, OUT_ROWS["qkv"], HIDDEN, 1],
-                      [0, wo, 0, ao, B["qkv"], 0, B["m"], 0, HIDDEN, HIDDEN, 1],
+                      [0, wqkv, 0, aqkv, B["a"], 0, B["qkv"], 0, OUT_ROWS["qkv"], HIDDEN, 1]]
+            if context > 0:
+                table += attention_block(layer)
+            table += [[0, wo, 0, ao, B[o_in], 0, B["m"], 0, HIDDEN, HIDDEN, 1],
                       add(),
                       norm(2 * layer + 1),
                       [0, wgu, 0, agu, B["a"], 0, B["g"], 0, INTER, HIDDEN, 1],
@@ -1244,6 +1293,11 @@ def run_neighbours(args, stack, L):
         table += [norm(2 * LAYERS), [0, wl, 0, al, B["a"], 0, logits_h, 0, VOCAB, HIDDEN, 1]]
         table = np.ascontiguousarray(np.array(table, np.int64))
         x0 = stack.x0.cpu().numpy()
+        rope_view = np.ctypeslib.as_array(
+            (ctypes.c_float * (2 * HEAD_DIM)).from_address(L.lab_gpu_contents(B["rope"])))
+        half = HEAD_DIM // 2
+        angle = context / 1e6 ** (np.arange(half) * 2 / HEAD_DIM)
+        rope_view[:] = np.concatenate([np.cos(angle), np.sin(angle), np.cos(angle), np.sin(angle)])
 
         def run(fused):
             L.dn_gpu_set_fusion(1 if fused else 0)
@@ -1269,19 +1323,26 @@ def run_neighbours(args, stack, L):
         fused_tps, fused_ms, fused_logits = run(True)
         plain_tps, plain_ms, plain_logits = run(False)
         L.dn_gpu_set_fusion(1)
+        workload = (f"Qwen3-1.7B-shaped decode stack with its neighbours: {LAYERS} x [RMSNorm, "
+                    "qkv, o, add, RMSNorm, gate, up, SwiGLU, down, add] + RMSNorm + lm_head "
+                    "(attention omitted), batch 1, through lab_gpu_* with one "
+                    "dn_gpu_enc_batch per token")
+        if context > 0:
+            workload = (f"Qwen3-1.7B-shaped decode step at position {context}: {LAYERS} x [RMSNorm, "
+                        "qkv, q/k head norm + RoPE, KV copies, attention over the cache, o, add, "
+                        "RMSNorm, gate, up, SwiGLU, down, add] + RMSNorm + lm_head, batch 1, "
+                        "through lab_gpu_* with one dn_gpu_enc_batch per token; KV caches "
+                        "device-resident (dn_gpu_device_buffer)")
         return {
-            "workload": (f"Qwen3-1.7B-shaped decode stack with its neighbours: {LAYERS} x [RMSNorm, "
-                         "qkv, o, add, RMSNorm, gate, up, SwiGLU, down, add] + RMSNorm + lm_head "
-                         "(attention omitted), batch 1, through lab_gpu_* with one "
-                         "dn_gpu_enc_batch per token"),
+            "workload": workload,
             "ops_per_token": len(table),
             "fused": {"tokens_s": fused_tps, "commit_device_ms": fused_ms,
-                      "kernels_per_token": 4 * LAYERS + 1,
+                      "kernels_per_token": (4 + (5 if context > 0 else 0)) * LAYERS + 1,
                       "note": "the products only: each norm runs in the prologue of its first "
                               "reader, gate and up run as one dual GEMV with the SwiGLU in its "
                               "epilogue, the adds in the o and down epilogues"},
             "unfused": {"tokens_s": plain_tps, "commit_device_ms": plain_ms,
-                        "kernels_per_token": 10 * LAYERS + 2},
+                        "kernels_per_token": (10 + (5 if context > 0 else 0)) * LAYERS + 2},
             "logits_identical": bool(np.array_equal(fused_logits.view(np.uint32),
                                                     plain_logits.view(np.uint32))),
             "logits_finite": bool(np.isfinite(fused_logits).all()),
@@ -1306,6 +1367,7 @@ def run_neighbours_workload(args):
     torch.cuda.synchronize()
     res = run_neighbours(args, stack, L)
     res["layers"] = LAYERS
+    res["decode_step"] = run_neighbours(args, stack, L, context=args.context)
     print(json.dumps(res), flush=True)
 
 

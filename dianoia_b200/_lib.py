@@ -68,6 +68,7 @@ SIGNATURES = {
     "dn_gpu_enc_batch": (None, [_p, _i64]),
     "dn_gpu_set_fusion": (None, [_i64]),
     "dn_gpu_wrap_file": (_i64, [ctypes.c_char_p, _i64, _i64]),
+    "dn_gpu_device_buffer": (_i64, [_i64]),
     "dn_linear": (_i64, [_i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),
@@ -97,7 +98,8 @@ DN_OK, DN_ERR_ARGS, DN_ERR_CUDA, DN_ERR_NO_DEVICE, DN_ERR_UNSUPPORTED, DN_ERR_TO
 DN_Q8, DN_Q4 = 0, 1
 DN_PATH_AUTO, DN_PATH_GEMV, DN_PATH_TC, DN_PATH_GENERIC = -1, 0, 1, 2
 DN_FLAG_PDL = 1
-DN_BATCH_Q8, DN_BATCH_Q4, DN_BATCH_RMS_NORM, DN_BATCH_SWIGLU, DN_BATCH_ADD = 0, 1, 2, 3, 4
+(DN_BATCH_Q8, DN_BATCH_Q4, DN_BATCH_RMS_NORM, DN_BATCH_SWIGLU, DN_BATCH_ADD, DN_BATCH_COPY, DN_BATCH_STEER,
+ DN_BATCH_HEAD_NORM_ROPE, DN_BATCH_CONV, DN_BATCH_ATTENTION) = range(10)
 QA_BYTES = 36  # QA activation block: 32 int8 + f32 scale
 DN_PEER_HANDLE_BYTES = 64
 

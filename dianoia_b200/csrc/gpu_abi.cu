@@ -1240,6 +1240,23 @@ void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOff
   encode_add(src, srcOffset, dst, dstOffset, count);
 }
 
+int64_t dn_gpu_device_buffer(int64_t bytes) {
+  std::lock_guard<std::recursive_mutex> lock(g_mu);
+  if (!g_ready || bytes < 0) return -1;
+  cudaSetDevice(g_device);
+  Buf b;
+  const size_t n = bytes == 0 ? 16 : (size_t)bytes;
+  if (cudaMalloc(&b.dev, n) != cudaSuccess || cudaMemset(b.dev, 0, n) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(b.dev);
+    return -1;
+  }
+  b.bytes = bytes;
+  b.live = true;
+  b.weights_on_device = true;  // nothing on the host to copy, ever
+  return add_buffer(b);
+}
+
 int64_t dn_gpu_wrap_file(const char* path, int64_t offset, int64_t bytes) {
   std::lock_guard<std::recursive_mutex> lock(g_mu);
   return wrap_file(path, offset, bytes);
@@ -1293,6 +1310,26 @@ void dn_gpu_enc_batch(const int64_t* table, int64_t count) {
       }
       case DN_BATCH_SWIGLU: encode_swiglu(r[1], r[2], r[3]); break;
       case DN_BATCH_ADD: encode_add(r[1], r[2], r[3], r[4], r[5]); break;
+      case DN_BATCH_COPY: encode_copy(r[1], r[2], r[3], r[4], r[5]); break;
+      case DN_BATCH_STEER: {
+        double scale;
+        memcpy(&scale, &r[8], sizeof scale);
+        encode_steer(r[1], r[2], r[3], r[4], r[5], r[6], r[7], scale);
+        break;
+      }
+      case DN_BATCH_HEAD_NORM_ROPE: {
+        double eps;
+        memcpy(&eps, &r[10], sizeof eps);
+        const int64_t p = r[9];
+        encode_head_norm_rope(r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], p & 0xffff,
+                              (p >> 16) & 0xffff, (p >> 32) & 0xffffffff, eps);
+        break;
+      }
+      case DN_BATCH_CONV: encode_conv(r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8]); break;
+      case DN_BATCH_ATTENTION:
+        encode_attention(r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], r[9], r[10] & 0xffffffff,
+                         (r[10] >> 32) & 0x7fffffff);
+        break;
       default: g_bad_op = true;
     }
   }

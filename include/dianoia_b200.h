@@ -199,6 +199,14 @@ void lab_gpu_enc_swiglu(int64_t g, int64_t u, int64_t count);
  * lab_vulkan.c:993-998 (gpu.dart:293-297). */
 void lab_gpu_enc_add(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count);
 
+/* A zeroed GPU-layer buffer in device memory only, for data the host never
+ * reads or writes: a KV cache, scratch between the ops of a command buffer.
+ * lab_gpu_contents returns NULL for it and commits copy nothing into or out
+ * of it (a lab_gpu_buffer is copied in where the host may have written it
+ * and out where the GPU wrote it, every commit). Its handle, or -1. No
+ * counterpart in the reference, whose buffers are host-visible memory. */
+int64_t dn_gpu_device_buffer(int64_t bytes);
+
 /* A GPU-layer buffer holding bytes [offset, offset + bytes) of the file at
  * `path`, read straight into device memory (slices on up to 8 host threads,
  * each through pinned staging chunks whose reads overlap their device
@@ -257,6 +265,11 @@ void lab_gpu_enc_attention(int64_t q, int64_t keys, int64_t values, int64_t gate
 #define DN_BATCH_RMS_NORM 2
 #define DN_BATCH_SWIGLU 3
 #define DN_BATCH_ADD 4
+#define DN_BATCH_COPY 5
+#define DN_BATCH_STEER 6
+#define DN_BATCH_HEAD_NORM_ROPE 7
+#define DN_BATCH_CONV 8
+#define DN_BATCH_ATTENTION 9
 
 /* Records `count` operations into the open command buffer in one call,
  * exactly as the same sequence of lab_gpu_enc_* calls would. No counterpart
@@ -270,10 +283,18 @@ void lab_gpu_enc_attention(int64_t q, int64_t keys, int64_t values, int64_t gate
  *     the bits of eps as a double, accumulate (lab_gpu_enc_rms_norm);
  *   DN_BATCH_SWIGLU: g, u, count, then unused (lab_gpu_enc_swiglu);
  *   DN_BATCH_ADD: src, srcOffset, dst, dstOffset, count, then unused
- *     (lab_gpu_enc_add).
- * An unknown kind makes the next lab_gpu_commit return 0. The other
- * encoders (copy, steer, head norm, conv, attention) are recorded by their
- * own calls. */
+ *     (lab_gpu_enc_add);
+ *   DN_BATCH_COPY: src, srcOffset, dst, dstOffset, count (lab_gpu_enc_copy);
+ *   DN_BATCH_STEER: x, xOffset, v, vOffset, rows, cols, mode, the bits of
+ *     scale as a double (lab_gpu_enc_steer);
+ *   DN_BATCH_HEAD_NORM_ROPE: x, xOffset, xStride, w, wOffset, rope,
+ *     ropeOffset, ropeStride, heads | hd << 16 | n << 32, the bits of eps
+ *     (lab_gpu_enc_head_norm_rope; heads and hd below 65536);
+ *   DN_BATCH_CONV: bcx, weight, weightOffset, history, y, width, k, n
+ *     (lab_gpu_enc_conv);
+ *   DN_BATCH_ATTENTION: q, keys, values, gate, out, position, n, heads,
+ *     kvHeads, hd | window << 32 (lab_gpu_enc_attention).
+ * An unknown kind makes the next lab_gpu_commit return 0. */
 void dn_gpu_enc_batch(const int64_t* table, int64_t count);
 
 /* ------------------------------------------------------------ dn_* (device API) */

@@ -167,3 +167,98 @@ def test_layer_ops_reject_what_does_not_fit(gpu):
     L.lab_gpu_begin()
     L.lab_gpu_enc_attention(a, big, big, -1, a, 20000, 1, 1, 1, 8, 512)
     assert L.lab_gpu_commit(1) == 1
+
+
+def test_attention_over_a_device_only_kv_cache(gpu, oracle):
+    """A decode step as GpuForward records it (gpu.dart:1100-1180), less the
+    products: q and k normed and rotated in place, the token's k and v copied
+    into device-only KV caches (dn_gpu_device_buffer: no host mirror, nothing
+    copied per commit), attention over the cached rows. Three tokens in three
+    command buffers; every output bit for bit against the CPU path."""
+    L, B = gpu
+    rng = np.random.default_rng(21)
+    heads, kv, hd, max_seq = 4, 2, 64, 8
+    q_dim, kv_dim = heads * hd, kv * hd
+    keys = L.dn_gpu_device_buffer(4 * max_seq * kv_dim)
+    values = L.dn_gpu_device_buffer(4 * max_seq * kv_dim)
+    try:
+        assert keys >= 0 and values >= 0 and L.lab_gpu_contents(keys) is None
+        w = (1 + 0.1 * rng.standard_normal(2 * hd)).astype(np.float32)
+        hw = B.make(w)
+        qkv = B.make(np.zeros(q_dim + 2 * kv_dim, np.float32))
+        rope = B.make(np.zeros(hd, np.float32))
+        out = B.make(np.zeros(q_dim, np.float32))
+        cache_k = np.zeros(max_seq * kv_dim, np.float32)
+        cache_v = np.zeros(max_seq * kv_dim, np.float32)
+        for pos in range(3):
+            x = rng.standard_normal(q_dim + 2 * kv_dim).astype(np.float32)
+            tab = rng.uniform(-1, 1, hd).astype(np.float32)
+            B.view(qkv, x.size)[:] = x
+            B.view(rope, hd)[:] = tab
+            L.lab_gpu_begin()
+            L.lab_gpu_enc_head_norm_rope(qkv, 0, q_dim + 2 * kv_dim, hw, 0, rope, 0, hd, heads, hd, 1, 1e-6)
+            L.lab_gpu_enc_head_norm_rope(qkv, 4 * q_dim, q_dim + 2 * kv_dim, hw, 4 * hd, rope, 0, hd, kv, hd, 1, 1e-6)
+            L.lab_gpu_enc_copy(qkv, 4 * q_dim, keys, 4 * pos * kv_dim, kv_dim)
+            L.lab_gpu_enc_copy(qkv, 4 * (q_dim + kv_dim), values, 4 * pos * kv_dim, kv_dim)
+            L.lab_gpu_enc_attention(qkv, keys, values, -1, out, pos, 1, heads, kv, hd, 0)
+            assert L.lab_gpu_commit(1) == 1
+            qn = oracle.head_norm_rope(x[:q_dim], q_dim, w[:hd], tab, hd, heads, hd, 1, 1e-6)
+            kn = oracle.head_norm_rope(x[q_dim:q_dim + kv_dim], kv_dim, w[hd:], tab, hd, kv, hd, 1, 1e-6)
+            cache_k[pos * kv_dim:(pos + 1) * kv_dim] = kn
+            cache_v[pos * kv_dim:(pos + 1) * kv_dim] = x[q_dim + kv_dim:]
+            want = oracle.attention(qn, cache_k, cache_v, None, pos, 1, heads, kv, hd, 0)
+            assert np.array_equal(bits(B.view(out, q_dim)), bits(want))
+            assert np.array_equal(bits(B.view(qkv, q_dim)), bits(qn))
+    finally:
+        L.lab_gpu_release(keys)
+        L.lab_gpu_release(values)
+
+
+def test_batch_rows_equal_single_calls(gpu):
+    """dn_gpu_enc_batch's rows for copy, steer, head norm + RoPE, conv and
+    attention (packed small integers) record what the single calls do."""
+    L, B = gpu
+    rng = np.random.default_rng(5)
+    heads, kv, hd, pos = 4, 2, 64, 6
+    q_dim, kv_dim = heads * hd, kv * hd
+    eps_bits = int(np.array([1e-6], np.float64).view(np.int64)[0])
+    scale_bits = int(np.array([0.5], np.float64).view(np.int64)[0])
+    x = rng.standard_normal(q_dim + 2 * kv_dim).astype(np.float32)
+    cache = rng.standard_normal((pos + 1) * kv_dim).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(2 * hd)).astype(np.float32)
+    tab = rng.uniform(-1, 1, hd).astype(np.float32)
+    v = rng.standard_normal(q_dim).astype(np.float32)
+    width, k = 64, 3
+    bcx = rng.standard_normal(2 * 3 * width).astype(np.float32)
+    cw = rng.standard_normal(width * k).astype(np.float32)
+    results = []
+    for batch in (False, True):
+        hx, hk, hv, hw, hr = B.make(x), B.make(cache), B.make(cache), B.make(w), B.make(tab)
+        ho, hs = B.make(np.zeros(q_dim, np.float32)), B.make(v)
+        hb, hcw = B.make(bcx), B.make(cw)
+        hh, hy = B.make(np.zeros((k - 1) * width, np.float32)), B.make(np.zeros(2 * width, np.float32))
+        L.lab_gpu_begin()
+        if batch:
+            t = np.array([
+                [7, hx, 0, q_dim + 2 * kv_dim, hw, 0, hr, 0, hd, heads | (hd << 16) | (1 << 32), eps_bits],
+                [7, hx, 4 * q_dim, q_dim + 2 * kv_dim, hw, 4 * hd, hr, 0, hd, kv | (hd << 16) | (1 << 32), eps_bits],
+                [5, hx, 4 * q_dim, hk, 4 * pos * kv_dim, kv_dim, 0, 0, 0, 0, 0],
+                [5, hx, 4 * (q_dim + kv_dim), hv, 4 * pos * kv_dim, kv_dim, 0, 0, 0, 0, 0],
+                [9, hx, hk, hv, -1, ho, pos, 1, heads, kv, hd | (3 << 32)],
+                [6, ho, 0, hs, 0, 1, q_dim, 1, scale_bits, 0, 0],
+                [8, hb, hcw, 0, hh, hy, width, k, 2, 0, 0]], np.int64)
+            L.dn_gpu_enc_batch(t.ctypes.data, len(t))
+        else:
+            L.lab_gpu_enc_head_norm_rope(hx, 0, q_dim + 2 * kv_dim, hw, 0, hr, 0, hd, heads, hd, 1, 1e-6)
+            L.lab_gpu_enc_head_norm_rope(hx, 4 * q_dim, q_dim + 2 * kv_dim, hw, 4 * hd, hr, 0, hd, kv, hd, 1, 1e-6)
+            L.lab_gpu_enc_copy(hx, 4 * q_dim, hk, 4 * pos * kv_dim, kv_dim)
+            L.lab_gpu_enc_copy(hx, 4 * (q_dim + kv_dim), hv, 4 * pos * kv_dim, kv_dim)
+            L.lab_gpu_enc_attention(hx, hk, hv, -1, ho, pos, 1, heads, kv, hd, 3)
+            L.lab_gpu_enc_steer(ho, 0, hs, 0, 1, q_dim, 1, 0.5)
+            L.lab_gpu_enc_conv(hb, hcw, 0, hh, hy, width, k, 2)
+        assert L.lab_gpu_commit(1) == 1
+        results.append([B.view(h, n).copy() for h, n in ((hx, x.size), (hk, cache.size), (ho, q_dim),
+                                                          (hy, 2 * width), (hh, (k - 1) * width))])
+    for a, b in zip(*results):
+        assert np.array_equal(bits(a), bits(b))
+    assert np.abs(results[0][2]).max() > 0
