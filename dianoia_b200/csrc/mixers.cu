@@ -21,8 +21,10 @@
 // over threads (the head norm's and the steer's dot, attention's q.k and its
 // max / sum): every term is exact or a double, so they differ from the CPU's
 // by a few double ulps and move an f32 output only within that of a rounding
-// boundary. The attention's value sums run in the CPU's order, one thread
-// per output dimension.
+// boundary. The attention's value sums run in the CPU's key order within a
+// slice of the keys, and the slices add in order.
+#include <cooperative_groups.h>
+
 #include "dn_common.cuh"
 #include "dn_launch.h"
 
@@ -77,28 +79,48 @@ __device__ __forceinline__ double warp_max_d(double v) {
   return v;
 }
 
-// One CTA per (head, token). Scores in shared memory as doubles (at most
-// kMaxAttnKeys keys). Phase 1: a warp per key, lanes across head_dim;
-// phase 2: max, exp and sum over the keys; phase 3: one thread per output
-// dimension sums the weighted values over the keys in order.
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttentionArgs a) {
+// A cluster of kAttnSplit CTAs per (head, token), each owning a contiguous
+// slice of the keys, so that decode attention runs on many SMs:
+//  1. each CTA scores its keys (a warp per key, lanes across head_dim) into
+//     shared memory and takes their max; the cluster's max comes from every
+//     CTA's through distributed shared memory;
+//  2. each CTA turns its scores into exp(score - max) and sums them, and sums
+//     score * value over its keys in order, one thread per output dimension
+//     (loads of eight keys issued together);
+//  3. CTA 0 adds the slices' sums in rank order and writes the outputs.
+// The arithmetic is the CPU's (the same exp(score - max) of every key); only
+// the sums are split, by warps and by slices.
+constexpr int kAttnSplit = 8;
+constexpr int kAttnMaxHd = 256;
+
+__global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThreads)
+    attention_kernel(const AttentionArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   pdl_launch_dependents();
   pdl_wait();
   extern __shared__ double scores[];
   __shared__ double part[kAttnWarps];
-  const int head = blockIdx.x;
+  __shared__ double slice_max, slice_sum;
+  __shared__ double slice_acc[kAttnMaxHd];
+  const int rank = (int)cluster.block_rank();
+  const int head = blockIdx.x / kAttnSplit;
   const int64_t t = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t pos = a.position + t;
   const int64_t start = a.window > 0 && pos - a.window + 1 > 0 ? pos - a.window + 1 : 0;
   const int64_t count = pos - start + 1;
+  const int64_t per = (count + kAttnSplit - 1) / kAttnSplit;
+  const int64_t k0 = min64(count, rank * per), k1 = min64(count, k0 + per);  // this CTA's keys
+  const int64_t mine = k1 - k0;
   const int64_t q_dim = (int64_t)a.heads * a.hd, kv_dim = (int64_t)a.kv_heads * a.hd;
   const int64_t kvo = (int64_t)(head / (a.heads / a.kv_heads)) * a.hd;
   const float* q = a.q + t * q_dim + (int64_t)head * a.hd;
   const double scale = __ddiv_rn(1.0, __dsqrt_rn((double)a.hd));
 
-  for (int64_t i = warp; i < count; i += kAttnWarps) {
-    const float* k = a.keys + (start + i) * kv_dim + kvo;
+  // 1. scores and the max
+  for (int64_t i = warp; i < mine; i += kAttnWarps) {
+    const float* k = a.keys + (start + k0 + i) * kv_dim + kvo;
     double d = 0.0;
     for (int j = lane; j < a.hd; j += 32) d = __dadd_rn(d, __dmul_rn((double)q[j], (double)k[j]));
     d = warp_sum_d(d);
@@ -106,16 +128,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const Attention
   }
   __syncthreads();
   double m = -INFINITY;
-  for (int64_t i = tid; i < count; i += kAttnThreads) m = fmax(m, scores[i]);
+  for (int64_t i = tid; i < mine; i += kAttnThreads) m = fmax(m, scores[i]);
   m = warp_max_d(m);
   if (lane == 0) part[warp] = m;
   __syncthreads();
-  m = part[0];
-#pragma unroll
-  for (int w = 1; w < kAttnWarps; w++) m = fmax(m, part[w]);
-  __syncthreads();  // part is reused below
+  if (tid == 0) {
+    double mm = part[0];
+    for (int w = 1; w < kAttnWarps; w++) mm = fmax(mm, part[w]);
+    slice_max = mm;
+  }
+  cluster.sync();
+  m = -INFINITY;
+  for (int r = 0; r < kAttnSplit; r++) m = fmax(m, *cluster.map_shared_rank(&slice_max, r));
+
+  // 2. exp and the slice's sum
   double sum = 0.0;
-  for (int64_t i = tid; i < count; i += kAttnThreads) {
+  for (int64_t i = tid; i < mine; i += kAttnThreads) {
     const double e = exp(__dsub_rn(scores[i], m));
     scores[i] = e;
     sum = __dadd_rn(sum, e);
@@ -123,20 +151,44 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const Attention
   sum = warp_sum_d(sum);
   if (lane == 0) part[warp] = sum;
   __syncthreads();
-  sum = 0.0;
-#pragma unroll
-  for (int w = 0; w < kAttnWarps; w++) sum = __dadd_rn(sum, part[w]);
-  const bool gated = a.gate != nullptr;
-  const double g = gated ? __ddiv_rn(1.0, __dadd_rn(1.0, exp(-(double)a.gate[t * a.heads + head]))) : 1.0;
-  float* out = a.out + t * q_dim + (int64_t)head * a.hd;
-  for (int d = tid; d < a.hd; d += kAttnThreads) {
-    const float* v = a.values + start * kv_dim + kvo + d;
-    double acc = 0.0;
-    for (int64_t i = 0; i < count; i++) acc = __dadd_rn(acc, __dmul_rn(scores[i], (double)v[i * kv_dim]));
-    float o = __double2float_rn(__ddiv_rn(acc, sum));
-    if (gated) o = __double2float_rn(__dmul_rn((double)o, g));
-    out[d] = o;
+  if (tid == 0) {
+    double ss = 0.0;
+    for (int w = 0; w < kAttnWarps; w++) ss = __dadd_rn(ss, part[w]);
+    slice_sum = ss;
   }
+  // ... and the slice's weighted values, in key order
+  for (int d = tid; d < a.hd; d += kAttnThreads) {
+    const float* v = a.values + (start + k0) * kv_dim + kvo + d;
+    double acc = 0.0;
+    int64_t i = 0;
+    for (; i + 8 <= mine; i += 8) {
+      float vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) vv[u] = v[(i + u) * kv_dim];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = __dadd_rn(acc, __dmul_rn(scores[i + u], (double)vv[u]));
+    }
+    for (; i < mine; i++) acc = __dadd_rn(acc, __dmul_rn(scores[i], (double)v[i * kv_dim]));
+    slice_acc[d] = acc;
+  }
+  cluster.sync();
+
+  // 3. CTA 0 adds the slices in rank order
+  if (rank == 0) {
+    double total = 0.0;
+    for (int r = 0; r < kAttnSplit; r++) total = __dadd_rn(total, *cluster.map_shared_rank(&slice_sum, r));
+    const bool gated = a.gate != nullptr;
+    const double g = gated ? __ddiv_rn(1.0, __dadd_rn(1.0, exp(-(double)a.gate[t * a.heads + head]))) : 1.0;
+    float* out = a.out + t * q_dim + (int64_t)head * a.hd;
+    for (int d = tid; d < a.hd; d += kAttnThreads) {
+      double acc = 0.0;
+      for (int r = 0; r < kAttnSplit; r++) acc = __dadd_rn(acc, cluster.map_shared_rank(slice_acc, r)[d]);
+      float o = __double2float_rn(__ddiv_rn(acc, total));
+      if (gated) o = __double2float_rn(__dmul_rn((double)o, g));
+      out[d] = o;
+    }
+  }
+  cluster.sync();  // the other CTAs' shared memory stays until CTA 0 has read it
 }
 
 // ------------------------------------------------------------------- conv
@@ -229,26 +281,18 @@ cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
   if (a.heads <= 0 || a.n <= 0) return cudaSuccess;
-  if (a.hd <= 0 || a.kv_heads <= 0 || a.heads % a.kv_heads != 0 || a.n > 65535 || a.position < 0)
+  if (a.hd <= 0 || a.hd > kAttnMaxHd || a.kv_heads <= 0 || a.heads % a.kv_heads != 0 || a.n > 65535 ||
+      a.position < 0 || a.heads > 65535 / kAttnSplit)
     return cudaErrorInvalidValue;
-  // Keys a token sees: all before it, or the window.
+  // Keys a token sees: all before it, or the window; a CTA scores its slice.
   const int64_t longest = a.window > 0 ? (a.window < a.position + a.n ? a.window : a.position + a.n)
                                        : a.position + a.n;
   if (longest > kMaxAttnKeys) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)longest * sizeof(double);
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!configured[dev & 63]) {
-    if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(kMaxAttnKeys * sizeof(double))) != cudaSuccess)
-      return cudaErrorInvalidValue;
-    configured[dev & 63] = true;
-  }
+  const size_t smem = (size_t)((longest + kAttnSplit - 1) / kAttnSplit) * sizeof(double);
   AttentionArgs c = a;
   void* args[] = {&c};
   return launch_cfg(reinterpret_cast<const void*>(attention_kernel), args,
-                    dim3((unsigned)a.heads, (unsigned)a.n), kAttnThreads, smem, stream, pdl);
+                    dim3((unsigned)(a.heads * kAttnSplit), (unsigned)a.n), kAttnThreads, smem, stream, pdl);
 }
 
 cudaError_t launch_conv(const ConvArgs& a, cudaStream_t stream, bool pdl) {
