@@ -86,7 +86,7 @@ __device__ __forceinline__ double warp_max_d(double v) {
 //     CTA's through distributed shared memory;
 //  2. each CTA turns its scores into exp(score - max) and sums them, and sums
 //     score * value over its keys in order, one thread per output dimension
-//     (loads of eight keys issued together);
+//     (loads of sixteen keys issued together);
 //  3. CTA 0 adds the slices' sums in rank order and writes the outputs.
 // The arithmetic is the CPU's (the same exp(score - max) of every key); only
 // the sums are split, by warps and by slices.
@@ -118,13 +118,38 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThread
   const float* q = a.q + t * q_dim + (int64_t)head * a.hd;
   const double scale = __ddiv_rn(1.0, __dsqrt_rn((double)a.hd));
 
-  // 1. scores and the max
-  for (int64_t i = warp; i < mine; i += kAttnWarps) {
-    const float* k = a.keys + (start + k0 + i) * kv_dim + kvo;
-    double d = 0.0;
-    for (int j = lane; j < a.hd; j += 32) d = __dadd_rn(d, __dmul_rn((double)q[j], (double)k[j]));
-    d = warp_sum_d(d);
-    if (lane == 0) scores[i] = __dmul_rn(d, scale);
+  // 1. scores and the max. Lane l holds q[l + 32 u]; a warp loads four keys
+  // at once, then reduces each (the same per-lane order for every key).
+  constexpr int kJ = kAttnMaxHd / 32;
+  constexpr int kKeys = 4;
+  double qd[kJ];
+#pragma unroll
+  for (int u = 0; u < kJ; u++) {
+    const int j = lane + 32 * u;
+    qd[u] = j < a.hd ? (double)q[j] : 0.0;
+  }
+  for (int64_t i0 = warp; i0 < mine; i0 += kAttnWarps * kKeys) {
+    float kk[kKeys][kJ];
+#pragma unroll
+    for (int c = 0; c < kKeys; c++) {
+      const int64_t i = i0 + c * kAttnWarps;
+      const float* k = a.keys + (start + k0 + min64(i, mine - 1)) * kv_dim + kvo;
+#pragma unroll
+      for (int u = 0; u < kJ; u++) {
+        const int j = lane + 32 * u;
+        kk[c][u] = j < a.hd ? k[j] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kKeys; c++) {
+      double d = 0.0;
+#pragma unroll
+      for (int u = 0; u < kJ; u++)
+        if (lane + 32 * u < a.hd) d = __dadd_rn(d, __dmul_rn(qd[u], (double)kk[c][u]));
+      d = warp_sum_d(d);
+      const int64_t i = i0 + c * kAttnWarps;
+      if (lane == 0 && i < mine) scores[i] = __dmul_rn(d, scale);
+    }
   }
   __syncthreads();
   double m = -INFINITY;
@@ -161,12 +186,12 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThread
     const float* v = a.values + (start + k0) * kv_dim + kvo + d;
     double acc = 0.0;
     int64_t i = 0;
-    for (; i + 8 <= mine; i += 8) {
-      float vv[8];
+    for (; i + 16 <= mine; i += 16) {
+      float vv[16];
 #pragma unroll
-      for (int u = 0; u < 8; u++) vv[u] = v[(i + u) * kv_dim];
+      for (int u = 0; u < 16; u++) vv[u] = v[(i + u) * kv_dim];
 #pragma unroll
-      for (int u = 0; u < 8; u++) acc = __dadd_rn(acc, __dmul_rn(scores[i + u], (double)vv[u]));
+      for (int u = 0; u < 16; u++) acc = __dadd_rn(acc, __dmul_rn(scores[i + u], (double)vv[u]));
     }
     for (; i < mine; i++) acc = __dadd_rn(acc, __dmul_rn(scores[i], (double)v[i * kv_dim]));
     slice_acc[d] = acc;
