@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kNormLanes) head_norm_rope_kernel(const HeadNo
 
 // -------------------------------------------------------------- attention
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -103,6 +103,7 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThread
   __shared__ double part[kAttnWarps];
   __shared__ double slice_max, slice_sum;
   __shared__ double slice_acc[kAttnMaxHd];
+  __shared__ double part_acc[2][kAttnMaxHd];
   const int rank = (int)cluster.block_rank();
   const int head = blockIdx.x / kAttnSplit;
   const int64_t t = blockIdx.y;
@@ -181,21 +182,30 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThread
     for (int w = 0; w < kAttnWarps; w++) ss = __dadd_rn(ss, part[w]);
     slice_sum = ss;
   }
-  // ... and the slice's weighted values, in key order
-  for (int d = tid; d < a.hd; d += kAttnThreads) {
+  // ... and the slice's weighted values, in key order: `groups` groups of
+  // threads, one thread per dimension in each, take consecutive parts of the
+  // slice's keys; the parts add in order.
+  const int groups = a.hd <= kAttnThreads / 2 ? 2 : 1;
+  const int g_id = tid / (kAttnThreads / groups), d0 = tid % (kAttnThreads / groups);
+  const int64_t half = (mine + groups - 1) / groups;
+  const int64_t i_lo = min64(mine, g_id * half), i_hi = min64(mine, i_lo + half);
+  for (int d = d0; d < a.hd; d += kAttnThreads / groups) {
     const float* v = a.values + (start + k0) * kv_dim + kvo + d;
     double acc = 0.0;
-    int64_t i = 0;
-    for (; i + 16 <= mine; i += 16) {
+    int64_t i = i_lo;
+    for (; i + 16 <= i_hi; i += 16) {
       float vv[16];
 #pragma unroll
       for (int u = 0; u < 16; u++) vv[u] = v[(i + u) * kv_dim];
 #pragma unroll
       for (int u = 0; u < 16; u++) acc = __dadd_rn(acc, __dmul_rn(scores[i + u], (double)vv[u]));
     }
-    for (; i < mine; i++) acc = __dadd_rn(acc, __dmul_rn(scores[i], (double)v[i * kv_dim]));
-    slice_acc[d] = acc;
+    for (; i < i_hi; i++) acc = __dadd_rn(acc, __dmul_rn(scores[i], (double)v[i * kv_dim]));
+    part_acc[g_id][d] = acc;
   }
+  __syncthreads();
+  for (int d = tid; d < a.hd; d += kAttnThreads)
+    slice_acc[d] = groups == 2 ? __dadd_rn(part_acc[0][d], part_acc[1][d]) : part_acc[0][d];
   cluster.sync();
 
   // 3. CTA 0 adds the slices in rank order
