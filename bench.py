@@ -1215,7 +1215,7 @@ def run_neighbours(args, stack, L, context=0):
         small = L.lab_gpu_wrap(norms.ctypes.data, norms.nbytes)
         handles.append(small)
         sizes = {"x": HIDDEN, "a": HIDDEN, "qkv": OUT_ROWS["qkv"], "m": HIDDEN, "g": INTER,
-                 "u": INTER, "attn": HEADS * HEAD_DIM, "rope": 2 * HEAD_DIM}
+                 "u": INTER, "attn": HEADS * HEAD_DIM, "rope": 2 * HEAD_DIM, "q": HEADS * HEAD_DIM}
         kv_dim = KV_HEADS * HEAD_DIM
         caches = []
         if context > 0:
@@ -1254,33 +1254,40 @@ def run_neighbours(args, stack, L, context=0):
         def add():
             return [4, B["m"], 0, B["x"], 0, HIDDEN, 0, 0, 0, 0, 0]
 
-        qkv_floats = OUT_ROWS["qkv"]
 
-        def attention_block(layer):
-            """Rows between qkv and o: q and k norm + RoPE, the KV copies, attention."""
+        def attention_block(layer, wqkv, aqkv):
+            """As GpuForward records it (gpu.dart:1151-1175): q, k and v products
+            (row ranges of the stacked qkv weights), k and v written straight
+            into the caches' row `context`; q and k norm + RoPE in place; attention."""
             keys, values = caches[2 * layer], caches[2 * layer + 1]
             q_dim = HEADS * HEAD_DIM
+            row = 4 * context * kv_dim
 
-            def hnr(x_off, heads, w_off):
+            def part(r0, rows, y, y_off):  # rows r0 .. r0 + rows of the stacked matrix
+                return [0, wqkv, r0 * HIDDEN, aqkv + r0 * (HIDDEN // 32) * 4, B["a"], 0, y, y_off, rows,
+                        HIDDEN, 1]
+
+            def hnr(x, x_off, stride, heads, w_off):
                 packed = heads | (HEAD_DIM << 16) | (1 << 32)
-                return [7, B["qkv"], x_off, qkv_floats, qk_norms, w_off, B["rope"], 0, 2 * HEAD_DIM,
-                        packed, eps_bits]
+                return [7, x, x_off, stride, qk_norms, w_off, B["rope"], 0, 2 * HEAD_DIM, packed, eps_bits]
 
-            return [hnr(0, HEADS, 4 * 2 * HEAD_DIM * layer),
-                    hnr(4 * q_dim, KV_HEADS, 4 * (2 * HEAD_DIM * layer + HEAD_DIM)),
-                    [5, B["qkv"], 4 * q_dim, keys, 4 * context * kv_dim, kv_dim, 0, 0, 0, 0, 0],
-                    [5, B["qkv"], 4 * (q_dim + kv_dim), values, 4 * context * kv_dim, kv_dim, 0, 0, 0, 0, 0],
-                    [9, B["qkv"], keys, values, -1, B["attn"], context, 1, HEADS, KV_HEADS, HEAD_DIM]]
+            return [part(0, q_dim, B["q"], 0),
+                    part(q_dim, kv_dim, keys, row),
+                    part(q_dim + kv_dim, kv_dim, values, row),
+                    hnr(B["q"], 0, q_dim, HEADS, 4 * 2 * HEAD_DIM * layer),
+                    hnr(keys, row, kv_dim, KV_HEADS, 4 * (2 * HEAD_DIM * layer + HEAD_DIM)),
+                    [9, B["q"], keys, values, -1, B["attn"], context, 1, HEADS, KV_HEADS, HEAD_DIM]]
 
         table = []
         for layer in range(LAYERS):
             (wqkv, aqkv), (wo, ao), (wgu, agu), (wd, ad) = mats[4 * layer:4 * layer + 4]
             half_qs, half_sc = INTER * HIDDEN, INTER * (HIDDEN // 32) * 4
             o_in = "attn" if context > 0 else "qkv"
-            table += [norm(2 * layer),
-                      [0, wqkv, 0, aqkv, B["a"], 0, B["qkv"], 0, OUT_ROWS["qkv"], HIDDEN, 1]]
+            table += [norm(2 * layer)]
             if context > 0:
-                table += attention_block(layer)
+                table += attention_block(layer, wqkv, aqkv)
+            else:
+                table += [[0, wqkv, 0, aqkv, B["a"], 0, B["qkv"], 0, OUT_ROWS["qkv"], HIDDEN, 1]]
             table += [[0, wo, 0, ao, B[o_in], 0, B["m"], 0, HIDDEN, HIDDEN, 1],
                       add(),
                       norm(2 * layer + 1),
@@ -1329,20 +1336,21 @@ def run_neighbours(args, stack, L, context=0):
                     "dn_gpu_enc_batch per token")
         if context > 0:
             workload = (f"Qwen3-1.7B-shaped decode step at position {context}: {LAYERS} x [RMSNorm, "
-                        "qkv, q/k head norm + RoPE, KV copies, attention over the cache, o, add, "
-                        "RMSNorm, gate, up, SwiGLU, down, add] + RMSNorm + lm_head, batch 1, "
-                        "through lab_gpu_* with one dn_gpu_enc_batch per token; KV caches "
-                        "device-resident (dn_gpu_device_buffer)")
+                        "q, k and v products (k and v into the KV caches' rows), q/k head norm + "
+                        "RoPE, attention over the cache, o, add, RMSNorm, gate, up, SwiGLU, down, "
+                        "add] + RMSNorm + lm_head, batch 1, as GpuForward records it, through "
+                        "lab_gpu_* with one dn_gpu_enc_batch per token; KV caches device-resident "
+                        "(dn_gpu_device_buffer)")
         return {
             "workload": workload,
             "ops_per_token": len(table),
             "fused": {"tokens_s": fused_tps, "commit_device_ms": fused_ms,
-                      "kernels_per_token": (4 + (5 if context > 0 else 0)) * LAYERS + 1,
+                      "kernels_per_token": (4 + (5 if context > 0 else 0)) * LAYERS + 1,  # +k, v, 2 norms, attention
                       "note": "the products only: each norm runs in the prologue of its first "
                               "reader, gate and up run as one dual GEMV with the SwiGLU in its "
                               "epilogue, the adds in the o and down epilogues"},
             "unfused": {"tokens_s": plain_tps, "commit_device_ms": plain_ms,
-                        "kernels_per_token": (10 + (5 if context > 0 else 0)) * LAYERS + 2},
+                        "kernels_per_token": (10 + (5 if context > 0 else 0)) * LAYERS + 2},  # the same
             "logits_identical": bool(np.array_equal(fused_logits.view(np.uint32),
                                                     plain_logits.view(np.uint32))),
             "logits_finite": bool(np.isfinite(fused_logits).all()),
