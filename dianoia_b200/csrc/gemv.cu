@@ -59,11 +59,12 @@ using namespace gemv;
 // one launch. A tile streams its 32 gate rows and then the same 32 up rows,
 // so the epilogue has g and u of each row in registers and writes
 // h = silu(g) * u to ys (and its QA blocks), u to ys2.
-template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL>
-__global__ void __launch_bounds__(kThreads, 2)
-    gemv_i8_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
-                   const __grid_constant__ CUtensorMap tsc, const __grid_constant__ CUtensorMap tw2,
-                   const __grid_constant__ CUtensorMap tsc2) {
+// The body of both kernels below (their tensor maps are __grid_constant__
+// parameters, passed here by address).
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL, bool EPI>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, const CUtensorMap* tw,
+                                          const CUtensorMap* tsc, const CUtensorMap* tw2,
+                                          const CUtensorMap* tsc2) {
   static_assert(!DUAL || NT == 1, "the dual product is for one token");
   using F = Fmt<Q4>;
   using X = XLayout<Q4>;
@@ -112,10 +113,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ------------------------------------------------------------ producer
     // The weights do not depend on the previous kernel, so no PDL wait here.
     if (lane == 0) {
-      prefetch_tmap(&tw);
-      if (TMA_SCALES) prefetch_tmap(&tsc);
-      if (DUAL) prefetch_tmap(&tw2);
-      if (DUAL && TMA_SCALES) prefetch_tmap(&tsc2);
+      prefetch_tmap(tw);
+      if (TMA_SCALES) prefetch_tmap(tsc);
+      if (DUAL) prefetch_tmap(tw2);
+      if (DUAL && TMA_SCALES) prefetch_tmap(tsc2);
     }
     // Ring slot, its phase, chunk and tile are running counters: a 64-bit
     // division per stage would cost more than the stage's own work.
@@ -132,8 +133,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const bool second = DUAL && c >= nch;  // the up matrix's half of the tile
         const int cc = second ? c - nch : c;
         const int nb = (int)min64(F::kKC, blocks - (int64_t)cc * F::kKC);
-        issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, second ? &tw2 : &tw,
-                                    second ? &tsc2 : &tsc, cc, nb, (int32_t)(tile * kRows), &full[s]);
+        issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, second ? tw2 : tw,
+                                    second ? tsc2 : tsc, cc, nb, (int32_t)(tile * kRows), &full[s]);
       }
       __syncwarp();
       if (++s == stages) {
@@ -275,20 +276,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       // compiler issue the shared-memory loads late). DUAL runs them for
       // the gate rows and then for the up rows.
       const quad::Lane qc = quad::lane_ctx(warp, lane);
-#pragma unroll 1
-      for (int half = 0; half < (DUAL ? 2 : 1); half++) {
-        float acc_h = 0.0f;
+      // One matrix's rows of the tile (scales scb) into acc_h; false when a
+      // wait ran out (the producer drains what it issued; every other wait
+      // is bounded). Called once, or for the gate and then the up rows.
+      auto run = [&](const uint8_t* scb, float& acc_h) -> bool {
         const uint8_t* xwp = xw_l;
         const float* xsp = xs_s;
-        const uint8_t* scb = half == 0 ? sc : static_cast<const uint8_t*>(a.scales2);
         const uint8_t* gsc = TMA_SCALES ? nullptr : scb + row * blocks * F::kSB;
         const int nfull = TMA_SCALES ? (int)(blocks / F::kKC) : 0;
         int c = 0;
         for (; c < nfull; c++) {
-          if (!warp_wait(&full[s], ph, a.status)) {
-            abort_flag = 1;
-            return;  // the producer drains what it issued; every other wait is bounded
-          }
+          if (!warp_wait(&full[s], ph, a.status)) return false;
           quad::stage_full<Q4>(smem + (int64_t)s * kStageBytes, qc, xwp, xsp, acc_h);
           xwp += F::kKC * X::kBlockBytes;
           xsp += F::kKC;
@@ -301,10 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         for (; c < nch; c++) {
           const int nb = (int)min64(F::kKC, blocks - (int64_t)c * F::kKC);
-          if (!warp_wait(&full[s], ph, a.status)) {
-            abort_flag = 1;
-            return;
-          }
+          if (!warp_wait(&full[s], ph, a.status)) return false;
           quad::stage_part<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, nb, qc, xwp, xsp,
                                            gsc == nullptr ? nullptr : gsc + (int64_t)c * F::kKC * F::kSB,
                                            acc_h);
@@ -317,8 +312,13 @@ __global__ void __launch_bounds__(kThreads, 2)
             ph ^= 1u;
           }
         }
-        if (half == 0) acc[0] = acc_h;
-        else acc_up = acc_h;
+        return true;
+      };
+      bool ran = run(sc, acc[0]);
+      if constexpr (DUAL) ran = ran && run(static_cast<const uint8_t*>(a.scales2), acc_up);
+      if (!ran) {
+        abort_flag = 1;
+        return;
       }
     } else {
       const LaneCtx lc{row_local, r8, l, rowoff, xw_l, sp.xw_stride, xs_s, sp.xs_stride, sc, row, blocks};
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           v = silu_mul(y, up);
           if (a.ys2 != nullptr) a.ys2[at] = up;
           if (a.ys != nullptr) a.ys[at] = v;
-        } else if (a.glu_out != nullptr) {
+        } else if (EPI && a.glu_out != nullptr) {
           // The feed-forward's other half was written by the previous kernel,
           // which completed before this one's dependent-launch wait.
           const float other = a.glu_other[at];
@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         } else if (a.ys != nullptr) {
           a.ys[at] = y;
         }
-        if (a.res != nullptr) a.res[at] = __fadd_rn(a.res[at], y);
+        if (EPI && a.res != nullptr) a.res[at] = __fadd_rn(a.res[at], y);
         yt[t * kRows + row_local] = v;
       }
     }
@@ -379,6 +379,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       e++;
     }
   }
+}
+
+// The kernels: the dual product carries the second matrix's tensor maps.
+// EPI: the SwiGLU and residual-add epilogue (glu_* and res arguments) is
+// compiled in; without it the plain products keep their own code (its
+// branches alone made the plain kernels 2 % slower).
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool EPI>
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_i8_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
+                   const __grid_constant__ CUtensorMap tsc) {
+  gemv_body<Q4, NT, TMA_SCALES, F32_IN, false, EPI>(a, stages, &tw, &tsc, &tw, &tsc);
+}
+
+template <bool Q4, bool TMA_SCALES, bool F32_IN>
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_dual_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
+                     const __grid_constant__ CUtensorMap tsc, const __grid_constant__ CUtensorMap tw2,
+                     const __grid_constant__ CUtensorMap tsc2) {
+  gemv_body<Q4, 1, TMA_SCALES, F32_IN, true, false>(a, stages, &tw, &tsc, &tw2, &tsc2);
 }
 
 // ------------------------------------------------------------------ generic
@@ -432,7 +451,7 @@ __global__ void __launch_bounds__(128) generic_kernel(const LinearArgs a) {
   if (l == 0 && row_raw < a.rows) a.ys[t * a.ldy + row_raw] = y;
 }
 
-template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL>
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL, bool EPI>
 int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   using F = Fmt<Q4>;
   const int64_t ntiles = (a.rows + kRows - 1) / kRows;
@@ -488,7 +507,8 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   };
   if (!maps(&tw, &tsc, a.qs, a.scales) || (DUAL && !maps(&tw2, &tsc2, a.qs2, a.scales2)))
     return kErrUnsupported;
-  auto kern = gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN, DUAL>;
+  const void* kern = DUAL ? reinterpret_cast<const void*>(gemv_dual_kernel<Q4, TMA_SCALES, F32_IN>)
+                          : reinterpret_cast<const void*>(gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN, EPI>);
   static bool configured[64] = {};  // per device: the opt-in smem limit is set
   int dev = 0;
   cudaGetDevice(&dev);
@@ -508,28 +528,33 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a, stages, tw, tsc, tw2, tsc2) == cudaSuccess ? kOk : kErrCuda;
+  // The plain kernel takes the first four of these, the dual one all six.
+  GemvArgs args = a;
+  int nstages = stages;
+  void* params[] = {&args, &nstages, &tw, &tsc, &tw2, &tsc2};
+  return cudaLaunchKernelExC(&cfg, kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
-template <bool Q4, int NT, bool DUAL>
+template <bool Q4, int NT, bool DUAL, bool EPI>
 int64_t launch_gemv_d(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const int64_t blocks = a.cols / kBlock;
   const bool tma_scales = ((uintptr_t)a.scales & 15) == 0 && (blocks * Fmt<Q4>::kSB) % 16 == 0 &&
                           (!DUAL || ((uintptr_t)a.scales2 & 15) == 0);
   const bool f32_in = a.xs != nullptr;
   if (tma_scales)
-    return f32_in ? launch_gemv_t<Q4, NT, true, true, DUAL>(a, stream, pdl)
-                  : launch_gemv_t<Q4, NT, true, false, DUAL>(a, stream, pdl);
-  return f32_in ? launch_gemv_t<Q4, NT, false, true, DUAL>(a, stream, pdl)
-                : launch_gemv_t<Q4, NT, false, false, DUAL>(a, stream, pdl);
+    return f32_in ? launch_gemv_t<Q4, NT, true, true, DUAL, EPI>(a, stream, pdl)
+                  : launch_gemv_t<Q4, NT, true, false, DUAL, EPI>(a, stream, pdl);
+  return f32_in ? launch_gemv_t<Q4, NT, false, true, DUAL, EPI>(a, stream, pdl)
+                : launch_gemv_t<Q4, NT, false, false, DUAL, EPI>(a, stream, pdl);
 }
 
 template <bool Q4, int NT>
 int64_t launch_gemv_s(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   if constexpr (NT == 1) {
-    if (a.qs2 != nullptr) return launch_gemv_d<Q4, 1, true>(a, stream, pdl);
+    if (a.qs2 != nullptr) return launch_gemv_d<Q4, 1, true, false>(a, stream, pdl);
   }
-  return launch_gemv_d<Q4, NT, false>(a, stream, pdl);
+  if (a.glu_out != nullptr || a.res != nullptr) return launch_gemv_d<Q4, NT, false, true>(a, stream, pdl);
+  return launch_gemv_d<Q4, NT, false, false>(a, stream, pdl);
 }
 
 // Tokens per CTA: enough for n (up to 8), fewer if shared memory runs out.
