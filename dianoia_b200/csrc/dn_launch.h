@@ -76,7 +76,19 @@ struct GemvArgs {
   const void* qs2;
   const void* scales2;
   float* ys2;
+  // Several products of the same one-token input in one launch (optional,
+  // 2 to kMaxGroups): product g has group_rows[g] rows of cols, weights at
+  // group_qs[g] / group_scales[g], outputs at group_ys[g]; its 32-row tiles
+  // start at tile group_tile0[g] (group_tile0[groups] = all tiles). No QA
+  // outputs; qs, scales, ys and rows are then unused.
+  int groups;
+  int64_t group_rows[4];
+  int64_t group_tile0[5];
+  const void* group_qs[4];
+  const void* group_scales[4];
+  float* group_ys[4];
 };
+constexpr int kMaxGroups = 4;
 
 // RMSNorm of `rows` rows of `cols` values: out = w * (x * r), r =
 // 1 / sqrt(mean(x^2) + eps), added into out with `accumulate`; with qa, the

@@ -61,10 +61,24 @@ using namespace gemv;
 // h = silu(g) * u to ys (and its QA blocks), u to ys2.
 // The body of both kernels below (their tensor maps are __grid_constant__
 // parameters, passed here by address).
-template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL, bool EPI>
+// Tensor maps of a grouped launch, one weight and one scale map per product.
+struct GroupMaps {
+  CUtensorMap w[kMaxGroups];
+  CUtensorMap sc[kMaxGroups];
+};
+
+// The product of a grouped launch that tile `tile` belongs to.
+__device__ __forceinline__ int group_of(const GemvArgs& a, int64_t tile) {
+  int g = 0;
+  while (g + 1 < a.groups && tile >= a.group_tile0[g + 1]) g++;
+  return g;
+}
+
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL, bool EPI, bool GROUP = false>
 __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, const CUtensorMap* tw,
                                           const CUtensorMap* tsc, const CUtensorMap* tw2,
-                                          const CUtensorMap* tsc2) {
+                                          const CUtensorMap* tsc2, const GroupMaps* gm = nullptr) {
+  static_assert(!GROUP || (NT == 1 && !DUAL && !EPI), "a grouped launch is of plain one-token products");
   static_assert(!DUAL || NT == 1, "the dual product is for one token");
   using F = Fmt<Q4>;
   using X = XLayout<Q4>;
@@ -74,7 +88,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t blocks = a.cols / kBlock;
-  const int64_t ntiles = (a.rows + kRows - 1) / kRows;
+  const int64_t ntiles = GROUP ? a.group_tile0[a.groups] : (a.rows + kRows - 1) / kRows;
   const int64_t t0 = (int64_t)blockIdx.y * NT;
   const int nt = (int)min64(NT, a.n - t0);
   const int nch = (int)((blocks + F::kKC - 1) / F::kKC);
@@ -133,8 +147,14 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, c
         const bool second = DUAL && c >= nch;  // the up matrix's half of the tile
         const int cc = second ? c - nch : c;
         const int nb = (int)min64(F::kKC, blocks - (int64_t)cc * F::kKC);
-        issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, second ? tw2 : tw,
-                                    second ? tsc2 : tsc, cc, nb, (int32_t)(tile * kRows), &full[s]);
+        if constexpr (GROUP) {
+          const int g = group_of(a, tile);
+          issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, &gm->w[g], &gm->sc[g], cc, nb,
+                                      (int32_t)((tile - a.group_tile0[g]) * kRows), &full[s]);
+        } else {
+          issue_stage<Q4, TMA_SCALES>(smem + (int64_t)s * kStageBytes, second ? tw2 : tw,
+                                      second ? tsc2 : tsc, cc, nb, (int32_t)(tile * kRows), &full[s]);
+        }
       }
       __syncwarp();
       if (++s == stages) {
@@ -262,8 +282,12 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, c
   uint32_t e = 0;   // epilogue barrier uses so far
   for (int64_t i = 0; i < my_tiles; i++) {
     const int64_t tile = blockIdx.x + i * gridDim.x;
-    const int64_t row0 = tile * kRows;
-    const int tile_rows = (int)min64(kRows, a.rows - row0);
+    // A grouped launch: the tile's product and its tile within that product.
+    const int gidx = GROUP ? group_of(a, tile) : 0;
+    const int64_t ltile = GROUP ? tile - a.group_tile0[gidx] : tile;
+    const int64_t rows_g = GROUP ? a.group_rows[gidx] : a.rows;
+    const int64_t row0 = ltile * kRows;
+    const int tile_rows = (int)min64(kRows, rows_g - row0);
     const int64_t row = row0 + min(row_local, tile_rows - 1);
     float acc[NT];
 #pragma unroll
@@ -314,7 +338,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, c
         }
         return true;
       };
-      bool ran = run(sc, acc[0]);
+      bool ran = run(GROUP ? static_cast<const uint8_t*>(a.group_scales[gidx]) : sc, acc[0]);
       if constexpr (DUAL) ran = ran && run(static_cast<const uint8_t*>(a.scales2), acc_up);
       if (!ran) {
         abort_flag = 1;
@@ -343,7 +367,10 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, c
 #pragma unroll
     for (int t = 0; t < NT; t++) {
       const float y = lane_reduce(acc[t]);
-      if (l == 0 && row_local < tile_rows && t < nt) {
+      if (GROUP && l == 0 && row_local < tile_rows && t < nt) {
+        float* ys = a.group_ys[gidx];
+        if (ys != nullptr) ys[(t0 + t) * rows_g + row0 + row_local] = y;
+      } else if (!GROUP && l == 0 && row_local < tile_rows && t < nt) {
         const int64_t at = (t0 + t) * a.ldy + row0 + row_local;
         float v = y;
         if (DUAL) {
@@ -364,7 +391,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const int stages, c
         yt[t * kRows + row_local] = v;
       }
     }
-    if (a.ya != nullptr && tile_rows == kRows) {
+    if (!GROUP && a.ya != nullptr && tile_rows == kRows) {
       // The tile's 32 outputs of a token are one Q8_0 block of the next
       // projection's input: quantize them here (lab_quantize_q8 semantics).
       // All consumers meet on a bounded epilogue barrier; its buffer
@@ -390,6 +417,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     gemv_i8_kernel(const GemvArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
                    const __grid_constant__ CUtensorMap tsc) {
   gemv_body<Q4, NT, TMA_SCALES, F32_IN, false, EPI>(a, stages, &tw, &tsc, &tw, &tsc);
+}
+
+// Up to kMaxGroups products of one input, one token, in one launch.
+template <bool Q4, bool TMA_SCALES, bool F32_IN>
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_group_kernel(const GemvArgs a, const int stages, const __grid_constant__ GroupMaps maps) {
+  gemv_body<Q4, 1, TMA_SCALES, F32_IN, false, false, true>(a, stages, &maps.w[0], &maps.sc[0], &maps.w[0],
+                                                          &maps.sc[0], &maps);
 }
 
 template <bool Q4, bool TMA_SCALES, bool F32_IN>
@@ -451,10 +486,10 @@ __global__ void __launch_bounds__(128) generic_kernel(const LinearArgs a) {
   if (l == 0 && row_raw < a.rows) a.ys[t * a.ldy + row_raw] = y;
 }
 
-template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL, bool EPI>
+template <bool Q4, int NT, bool TMA_SCALES, bool F32_IN, bool DUAL, bool EPI, bool GROUP = false>
 int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   using F = Fmt<Q4>;
-  const int64_t ntiles = (a.rows + kRows - 1) / kRows;
+  const int64_t ntiles = GROUP ? a.group_tile0[a.groups] : (a.rows + kRows - 1) / kRows;
   const int64_t blocks = a.cols / kBlock;
   // Two CTAs per SM when the ring still gets at least 3 stages that way, and
   // the tiles need more than one CTA per SM; with few tiles (a tall-K matrix
@@ -495,20 +530,29 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const uint64_t row_bytes = (uint64_t)blocks * F::kWB;
   // The one-token kernel reads its scale box with a 64-byte swizzle (quaddot.cuh).
   const CUtensorMapDataType st = Q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  auto maps = [&](CUtensorMap* w, CUtensorMap* sc, const void* qs, const void* scales) {
-    if (!encode_tmap_2d(w, qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, (uint64_t)a.rows, row_bytes,
+  auto maps = [&](CUtensorMap* w, CUtensorMap* sc, const void* qs, const void* scales, int64_t rows) {
+    if (!encode_tmap_2d(w, qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, (uint64_t)rows, row_bytes,
                         kBoxBytes, kRows, true))
       return false;
     return !TMA_SCALES ||
-           (NT == 1 ? encode_tmap_2d_sw64(sc, scales, st, (uint64_t)blocks, (uint64_t)a.rows,
+           (NT == 1 ? encode_tmap_2d_sw64(sc, scales, st, (uint64_t)blocks, (uint64_t)rows,
                                           (uint64_t)blocks * F::kSB, F::kKC, kRows)
-                    : encode_tmap_2d(sc, scales, st, (uint64_t)blocks, (uint64_t)a.rows,
+                    : encode_tmap_2d(sc, scales, st, (uint64_t)blocks, (uint64_t)rows,
                                      (uint64_t)blocks * F::kSB, F::kKC, kRows, false));
   };
-  if (!maps(&tw, &tsc, a.qs, a.scales) || (DUAL && !maps(&tw2, &tsc2, a.qs2, a.scales2)))
+  GroupMaps gmaps;
+  memset(&gmaps, 0, sizeof gmaps);
+  if constexpr (GROUP) {
+    for (int g = 0; g < a.groups; g++)
+      if (!maps(&gmaps.w[g], &gmaps.sc[g], a.group_qs[g], a.group_scales[g], a.group_rows[g]))
+        return kErrUnsupported;
+  } else if (!maps(&tw, &tsc, a.qs, a.scales, a.rows) ||
+             (DUAL && !maps(&tw2, &tsc2, a.qs2, a.scales2, a.rows))) {
     return kErrUnsupported;
-  const void* kern = DUAL ? reinterpret_cast<const void*>(gemv_dual_kernel<Q4, TMA_SCALES, F32_IN>)
-                          : reinterpret_cast<const void*>(gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN, EPI>);
+  }
+  const void* kern = GROUP  ? reinterpret_cast<const void*>(gemv_group_kernel<Q4, TMA_SCALES, F32_IN>)
+                     : DUAL ? reinterpret_cast<const void*>(gemv_dual_kernel<Q4, TMA_SCALES, F32_IN>)
+                            : reinterpret_cast<const void*>(gemv_i8_kernel<Q4, NT, TMA_SCALES, F32_IN, EPI>);
   static bool configured[64] = {};  // per device: the opt-in smem limit is set
   int dev = 0;
   cudaGetDevice(&dev);
@@ -528,10 +572,12 @@ int64_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // The plain kernel takes the first four of these, the dual one all six.
+  // The plain kernel takes the first four of these, the dual one all six;
+  // the grouped one the arguments, the stages and its maps.
   GemvArgs args = a;
   int nstages = stages;
   void* params[] = {&args, &nstages, &tw, &tsc, &tw2, &tsc2};
+  if (GROUP) params[2] = &gmaps;
   return cudaLaunchKernelExC(&cfg, kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -551,6 +597,17 @@ int64_t launch_gemv_d(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 template <bool Q4, int NT>
 int64_t launch_gemv_s(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   if constexpr (NT == 1) {
+    if (a.groups > 1) {
+      const int64_t blocks = a.cols / kBlock;
+      bool tma_scales = (blocks * Fmt<Q4>::kSB) % 16 == 0;
+      for (int g = 0; g < a.groups; g++) tma_scales = tma_scales && ((uintptr_t)a.group_scales[g] & 15) == 0;
+      const bool f32_in = a.xs != nullptr;
+      if (tma_scales)
+        return f32_in ? launch_gemv_t<Q4, 1, true, true, false, false, true>(a, stream, pdl)
+                      : launch_gemv_t<Q4, 1, true, false, false, false, true>(a, stream, pdl);
+      return f32_in ? launch_gemv_t<Q4, 1, false, true, false, false, true>(a, stream, pdl)
+                    : launch_gemv_t<Q4, 1, false, false, false, false, true>(a, stream, pdl);
+    }
     if (a.qs2 != nullptr) return launch_gemv_d<Q4, 1, true, false>(a, stream, pdl);
   }
   if (a.glu_out != nullptr || a.res != nullptr) return launch_gemv_d<Q4, NT, false, true>(a, stream, pdl);
@@ -564,7 +621,7 @@ int64_t launch_gemv_q(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   auto fits = [&](int nt) {
     return plan<Q4>(2, nt, a.cols, f32_in, a.norm_w != nullptr).total <= kMaxSmem;
   };
-  if (a.qs2 != nullptr && a.n != 1) return kErrUnsupported;  // the dual product is for one token
+  if ((a.qs2 != nullptr || a.groups > 1) && a.n != 1) return kErrUnsupported;  // one token only
   if (a.n <= 1 || !fits(2)) return fits(1) ? launch_gemv_s<Q4, 1>(a, stream, pdl) : kErrTooLarge;
   if (a.n <= 2 || !fits(4)) return launch_gemv_s<Q4, 2>(a, stream, pdl);
   if (a.n <= 4 || !fits(8)) return launch_gemv_s<Q4, 4>(a, stream, pdl);
@@ -587,6 +644,16 @@ bool gemv_ex_supported(const GemvArgs& g) {
     return false;
   if (g.ys != nullptr && ((uintptr_t)g.ys & 3) != 0) return false;
   if (g.res != nullptr && ((uintptr_t)g.res & 3) != 0) return false;
+  if (g.groups > 1) {
+    if (g.groups > kMaxGroups || g.n != 1 || g.ya != nullptr || g.qs2 != nullptr || g.glu_out != nullptr ||
+        g.res != nullptr || g.group_tile0[0] != 0)
+      return false;
+    for (int k = 0; k < g.groups; k++)
+      if (g.group_rows[k] <= 0 || ((uintptr_t)g.group_qs[k] & 15) != 0 || g.group_scales[k] == nullptr ||
+          ((uintptr_t)g.group_scales[k] & (g.q4 ? 1 : 3)) != 0 || ((uintptr_t)g.group_ys[k] & 3) != 0 ||
+          g.group_tile0[k + 1] - g.group_tile0[k] != (g.group_rows[k] + kRows - 1) / kRows)
+        return false;
+  }
   if (g.qs2 != nullptr && (g.n != 1 || ((uintptr_t)g.qs2 & 15) != 0 || g.scales2 == nullptr ||
                            ((uintptr_t)g.scales2 & (g.q4 ? 1 : 3)) != 0 || ((uintptr_t)g.ys2 & 3) != 0 ||
                            g.glu_out != nullptr))

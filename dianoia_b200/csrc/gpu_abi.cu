@@ -598,6 +598,7 @@ struct Plan {
   std::vector<int> glu;         // product i runs SwiGLU op glu[i] in its epilogue, or -1
   std::vector<int> res;         // product i runs add op res[i] in its epilogue, or -1
   std::vector<int> dual;        // product i also runs product dual[i] and their SwiGLU, or -1
+  std::vector<int> grp;         // product i runs itself and the grp[i] - 1 products after it (0: none)
   std::vector<int> runs_in;     // an absorbed op: the op whose launch runs it
   std::vector<int> normin;      // product i runs norm op normin[i] in its prologue, or -1
   std::vector<int64_t> xa_out_at;  // product i writes its quantized input as QA blocks there, or -1
@@ -617,6 +618,7 @@ Plan plan_ops(uint32_t* status) {
   k.glu.assign(n, -1);
   k.res.assign(n, -1);
   k.dual.assign(n, -1);
+  k.grp.assign(n, 0);
   k.runs_in.assign(n, -1);
   k.normin.assign(n, -1);
   k.xa_out_at.assign(n, -1);
@@ -654,9 +656,46 @@ Plan plan_ops(uint32_t* status) {
       k.runs_in[i] = i - 1;
     }
   }
+  // Grouped launches: consecutive one-token GEMV products of the same input
+  // (GpuForward's q, k and v), with nothing else fused into them and outputs
+  // that neither overlap each other nor the input, run as one launch over all
+  // their tiles; the first launches, the others are absorbed.
+  for (int i = 0; i < n;) {
+    auto plain = [&](int j) {
+      const Op& o = g_ops[j];
+      return gemv[j] && o.n == 1 && !k.absorbed[j] && k.glu[j] < 0 && k.dual[j] < 0 && k.res[j] < 0;
+    };
+    if (!plain(i)) {
+      i++;
+      continue;
+    }
+    const Op& f = g_ops[i];
+    const Range in{f.x, f.x_off, f.x_off + f.cols * 4};
+    std::vector<Range> outs{writes(f)};
+    int m = 1;
+    while (m < dn::kMaxGroups && i + m < n && plain(i + m)) {
+      const Op& o = g_ops[i + m];
+      if (o.x != f.x || o.x_off != f.x_off || o.cols != f.cols || o.q4 != f.q4) break;
+      const Range w = writes(o);
+      bool clash = overlap(w, in) || overlap(outs[0], in);
+      for (const Range& r : outs) clash = clash || overlap(r, w);
+      if (clash) break;
+      outs.push_back(w);
+      m++;
+    }
+    if (m >= 2) {
+      k.grp[i] = m;
+      for (int j = 1; j < m; j++) {
+        k.absorbed[i + j] = true;
+        k.runs_in[i + j] = i;
+      }
+    }
+    i += m;
+  }
   // Everything op i's launch writes: its own outputs and those of the ops it absorbed.
   auto launch_writes = [&](int i, std::vector<Range>& w) {
     all_writes(g_ops[i], w);
+    for (int j = 1; j < k.grp[i]; j++) w.push_back(writes(g_ops[i + j]));
     if (k.glu[i] >= 0) w.push_back(writes(g_ops[k.glu[i]]));
     if (k.dual[i] >= 0) w.push_back(writes(g_ops[k.dual[i]]));
     if (k.res[i] >= 0) w.push_back(writes(g_ops[k.res[i]]));
@@ -711,7 +750,8 @@ Plan plan_ops(uint32_t* status) {
     const Op& o = g_ops[j];
     if (o.rows % kBlock != 0) continue;
     // (a product running a SwiGLU writes the SwiGLU's QA blocks, not its own)
-    if (o.kind == kMatmul) qa_src[j] = gemv[j] && k.glu[j] < 0 && k.dual[j] < 0 && !k.absorbed[j] ? j : -1;
+    if (o.kind == kMatmul)
+      qa_src[j] = gemv[j] && k.glu[j] < 0 && k.dual[j] < 0 && k.grp[j] < 2 && !k.absorbed[j] ? j : -1;
     else if (o.kind == kSwiglu && k.absorbed[j])
       qa_src[j] = g_ops[k.runs_in[j]].rows % kBlock == 0 ? k.runs_in[j] : -1;
     else if ((o.kind == kNorm || o.kind == kSwiglu) && !k.absorbed[j]) qa_src[j] = j;
@@ -843,7 +883,7 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
     const dn::LinearArgs a = linear_args(o, status);
     int64_t rc;
     if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0 || k.normin[i] >= 0 ||
-        k.dual[i] >= 0) {
+        k.dual[i] >= 0 || k.grp[i] > 1) {
       // (xa_out_at is set only together with normin.)
       dn::GemvArgs g{};
       g.q4 = o.q4;
@@ -868,6 +908,18 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
         g.glu_out = f32_at(s.y, 0);
       }
       if (k.res[i] >= 0) g.res = f32_at(g_ops[k.res[i]].y, g_ops[k.res[i]].y_off);
+      if (k.grp[i] > 1) {
+        g.groups = k.grp[i];
+        g.group_tile0[0] = 0;
+        for (int j = 0; j < k.grp[i]; j++) {
+          const Op& p = g_ops[i + j];
+          g.group_rows[j] = p.rows;
+          g.group_qs[j] = g_bufs[p.w].dev + p.qs_off;
+          g.group_scales[j] = g_bufs[p.w].dev + p.sc_off;
+          g.group_ys[j] = f32_at(p.y, p.y_off);
+          g.group_tile0[j + 1] = g.group_tile0[j] + (p.rows + 31) / 32;
+        }
+      }
       if (k.dual[i] >= 0) {
         // The gate writes the SwiGLU's g buffer (s.y): its weights go first.
         const Op& p = g_ops[k.dual[i]];

@@ -368,3 +368,75 @@ def test_prefill_block_with_neighbours_on_the_tensor_core_path(cuda_lib, oracle)
     finally:
         L.dn_gpu_set_fusion(1)
         layer.release()
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+def test_grouped_products_of_one_input(cuda_lib, oracle, fmt):
+    """GpuForward's q, k and v (gpu.dart:1151-1160), and a fourth product,
+    from one RMSNorm: consecutive one-token products of the same input run as
+    one grouped launch (the norm in its prologue), each into its own buffer
+    or cache row, heights that leave a partial last tile included; then a
+    product reads one of their outputs. Bit for bit against the CPU path,
+    with the fusions on and off."""
+    L = cuda_lib
+    assert L.lab_gpu_init() == 1
+    rng = np.random.default_rng(33 + (fmt == "q4"))
+    h = 256
+    shapes = [96, 64, 64, 40]         # q, k, v, a gate with a partial tile
+    gen = orc.q4_weights if fmt == "q4" else orc.q8_weights
+    mats = [gen(rng, r, h) for r in shapes]
+    wo = gen(rng, 32, 96)             # reads q's outputs
+    nw = (1 + 0.1 * rng.standard_normal(h)).astype(np.float32)
+    hs = []
+
+    def wrap(raw):
+        hd = L.lab_gpu_wrap(raw.ctypes.data, raw.size)
+        assert hd >= 0
+        hs.append(hd)
+        return hd
+
+    def buf(floats):
+        hd = L.lab_gpu_buffer(4 * floats)
+        assert hd >= 0
+        hs.append(hd)
+        return hd
+
+    def view(hd, floats):
+        return np.ctypeslib.as_array((ctypes.c_float * floats).from_address(L.lab_gpu_contents(hd)))
+
+    try:
+        wh = [wrap(np.concatenate([q.view(np.uint8), s.view(np.uint8)])) for q, s in mats]
+        who = wrap(np.concatenate([wo[0].view(np.uint8), wo[1].view(np.uint8)]))
+        small = wrap(nw.view(np.uint8))
+        x, a, q, cache, g, o = buf(h), buf(h), buf(96), buf(4 * 64 * 2), buf(40), buf(32)
+        ops = [(wh[0], q, 0), (wh[1], cache, 4 * 64 * 2), (wh[2], cache, 4 * 64 * 5), (wh[3], g, 0)]
+        xs = orc.activations(rng, 1, h)
+        results = []
+        for fuse in (1, 0):
+            L.dn_gpu_set_fusion(fuse)
+            view(x, h)[:] = xs
+            for hd, n in ((a, h), (q, 96), (cache, 512), (g, 40), (o, 32)):
+                view(hd, n)[:] = np.nan
+            L.lab_gpu_begin()
+            L.lab_gpu_enc_rms_norm(x, 0, small, 0, a, 0, 1, h, 1e-6, 0)
+            enc = L.lab_gpu_enc_matmul_q4 if fmt == "q4" else L.lab_gpu_enc_matmul_q8
+            for (w, y, y_off), (qs, _), rows in zip(ops, mats, shapes):
+                enc(w, 0, qs.size, a, 0, y, y_off, rows, h, 1)
+            enc(who, 0, wo[0].size, q, 0, o, 0, 32, 96, 1)
+            assert L.lab_gpu_commit(1) == 1
+            results.append([view(hd, n).copy() for hd, n in ((a, h), (q, 96), (cache, 512), (g, 40), (o, 32))])
+        an = oracle.rms_norm(xs, nw, 1, h, 1e-6)
+        ys = [oracle.gemm(fmt, qs, sc, an, rows, h, 1, 1)[0] for (qs, sc), rows in zip(mats, shapes)]
+        yo, _, _ = oracle.gemm(fmt, wo[0], wo[1], ys[0], 32, 96, 1, 1)
+        for got in results:
+            assert np.array_equal(bits(got[0]), bits(an))
+            assert np.array_equal(bits(got[1]), bits(ys[0]))
+            assert np.array_equal(bits(got[2][128:192]), bits(ys[1]))
+            assert np.array_equal(bits(got[2][320:384]), bits(ys[2]))
+            assert np.isnan(got[2][:128]).all() and np.isnan(got[2][192:320]).all()
+            assert np.array_equal(bits(got[3]), bits(ys[3]))
+            assert np.array_equal(bits(got[4]), bits(yo))
+    finally:
+        L.dn_gpu_set_fusion(1)
+        for hd in hs:
+            L.lab_gpu_release(hd)
