@@ -1345,12 +1345,13 @@ def run_neighbours(args, stack, L, context=0):
             "workload": workload,
             "ops_per_token": len(table),
             "fused": {"tokens_s": fused_tps, "commit_device_ms": fused_ms,
-                      # with attention: q, k and v in one grouped launch, 2 head norms, attention
-                      "kernels_per_token": (4 + (3 if context > 0 else 0)) * LAYERS + 1,
+                      # with attention: q, k and v in one grouped launch, the q and k head
+                      # norms in one launch, attention
+                      "kernels_per_token": (4 + (2 if context > 0 else 0)) * LAYERS + 1,
                       "note": "the products only: each norm runs in the prologue of its first "
                               "reader, gate and up run as one dual GEMV with the SwiGLU in its "
                               "epilogue, the adds in the o and down epilogues; with attention, q, "
-                              "k and v run as one grouped GEMV"},
+                              "k and v run as one grouped GEMV and their head norms as one launch"},
             "unfused": {"tokens_s": plain_tps, "commit_device_ms": plain_ms,
                         "kernels_per_token": (10 + (5 if context > 0 else 0)) * LAYERS + 2},  # the same
             "logits_identical": bool(np.array_equal(fused_logits.view(np.uint32),

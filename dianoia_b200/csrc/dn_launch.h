@@ -133,6 +133,12 @@ struct HeadNormRopeArgs {
   const float* rope;
   int64_t x_stride, rope_stride, heads, hd, n;
   double eps;
+  // A second set of heads in the same launch (optional; GpuForward's k after
+  // its q): heads2 heads at x2 (stride x2_stride) with weights w2, the same
+  // table, head size, tokens and eps.
+  float* x2;
+  const float* w2;
+  int64_t x2_stride, heads2;
 };
 cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream, bool pdl);
 

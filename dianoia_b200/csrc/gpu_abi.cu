@@ -599,6 +599,7 @@ struct Plan {
   std::vector<int> res;         // product i runs add op res[i] in its epilogue, or -1
   std::vector<int> dual;        // product i also runs product dual[i] and their SwiGLU, or -1
   std::vector<int> grp;         // product i runs itself and the grp[i] - 1 products after it (0: none)
+  std::vector<int> hnr2;        // head norm i also runs head norm hnr2[i] (the next op), or -1
   std::vector<int> runs_in;     // an absorbed op: the op whose launch runs it
   std::vector<int> normin;      // product i runs norm op normin[i] in its prologue, or -1
   std::vector<int64_t> xa_out_at;  // product i writes its quantized input as QA blocks there, or -1
@@ -619,6 +620,7 @@ Plan plan_ops(uint32_t* status) {
   k.res.assign(n, -1);
   k.dual.assign(n, -1);
   k.grp.assign(n, 0);
+  k.hnr2.assign(n, -1);
   k.runs_in.assign(n, -1);
   k.normin.assign(n, -1);
   k.xa_out_at.assign(n, -1);
@@ -692,10 +694,31 @@ Plan plan_ops(uint32_t* status) {
     }
     i += m;
   }
+  // Two consecutive head norms with one table and shape (GpuForward's q, then
+  // k in its cache row) whose ranges do not overlap: one launch.
+  for (int i = 0; i + 1 < n; i++) {
+    const Op &p = g_ops[i], &q = g_ops[i + 1];
+    if (p.kind != kHeadNormRope || q.kind != kHeadNormRope || k.absorbed[i] || k.hnr2[i] >= 0) continue;
+    if (p.x != q.x || p.x_off != q.x_off || p.e[1] != q.e[1] || p.cols != q.cols || p.n != q.n ||
+        memcmp(&p.eps, &q.eps, sizeof p.eps) != 0)
+      continue;
+    std::vector<Range> wp, wq;
+    all_writes(p, wp);
+    all_writes(q, wq);
+    if (overlap(wp[0], wq[0])) continue;
+    k.hnr2[i] = i + 1;
+    k.absorbed[i + 1] = true;
+    k.runs_in[i + 1] = i;
+  }
   // Everything op i's launch writes: its own outputs and those of the ops it absorbed.
   auto launch_writes = [&](int i, std::vector<Range>& w) {
     all_writes(g_ops[i], w);
     for (int j = 1; j < k.grp[i]; j++) w.push_back(writes(g_ops[i + j]));
+    if (k.hnr2[i] >= 0) {
+      std::vector<Range> w2;
+      all_writes(g_ops[k.hnr2[i]], w2);
+      w.insert(w.end(), w2.begin(), w2.end());
+    }
     if (k.glu[i] >= 0) w.push_back(writes(g_ops[k.glu[i]]));
     if (k.dual[i] >= 0) w.push_back(writes(g_ops[k.dual[i]]));
     if (k.res[i] >= 0) w.push_back(writes(g_ops[k.res[i]]));
@@ -860,8 +883,16 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       continue;
     }
     if (o.kind == kHeadNormRope) {
-      const dn::HeadNormRopeArgs ha{f32_at(o.y, o.y_off), f32_at(o.w, o.qs_off), f32_at(o.x, o.x_off),
-                                    o.e[0], o.e[1], o.rows, o.cols, o.n, o.eps};
+      if (k.absorbed[i]) continue;  // runs in the head norm before it
+      dn::HeadNormRopeArgs ha{f32_at(o.y, o.y_off), f32_at(o.w, o.qs_off), f32_at(o.x, o.x_off),
+                              o.e[0], o.e[1], o.rows, o.cols, o.n, o.eps, nullptr, nullptr, 0, 0};
+      if (k.hnr2[i] >= 0) {
+        const Op& q = g_ops[k.hnr2[i]];
+        ha.x2 = f32_at(q.y, q.y_off);
+        ha.w2 = f32_at(q.w, q.qs_off);
+        ha.x2_stride = q.e[0];
+        ha.heads2 = q.rows;
+      }
       if (dn::launch_head_norm_rope(ha, g_stream, pdl) != cudaSuccess || !mark(kProfHeadNormRope))
         return false;
       continue;

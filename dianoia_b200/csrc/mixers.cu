@@ -44,19 +44,22 @@ __global__ void __launch_bounds__(256) copy_kernel(const float* src, float* dst,
 
 // One CTA of 128 threads per (head, token); thread j holds dimensions j and
 // j + hd / 2 of the head (hd <= 256, even).
+// With a second set of heads, CTAs heads .. heads + heads2 - 1 take those.
 __global__ void __launch_bounds__(kNormLanes) head_norm_rope_kernel(const HeadNormRopeArgs a) {
   pdl_launch_dependents();
   pdl_wait();
-  const int head = blockIdx.x;
+  const bool second = blockIdx.x >= a.heads;
+  const int head = second ? blockIdx.x - (int)a.heads : blockIdx.x;
   const int64_t t = blockIdx.y;
   const int tid = threadIdx.x, pair = (int)(a.hd / 2);
-  float* x = a.x + t * a.x_stride + (int64_t)head * a.hd;
+  float* x = second ? a.x2 + t * a.x2_stride + (int64_t)head * a.hd : a.x + t * a.x_stride + (int64_t)head * a.hd;
+  const float* w = second ? a.w2 : a.w;
   const float* tab = a.rope + t * a.rope_stride;
   __shared__ double red[kNormLanes / 32];
   const double r = norm_factor(x, a.hd, a.eps, tid, red, [] { __syncthreads(); });
   if (tid < pair) {
-    const float n1 = norm_value(x[tid], a.w[tid], r);
-    const float n2 = norm_value(x[tid + pair], a.w[tid + pair], r);
+    const float n1 = norm_value(x[tid], w[tid], r);
+    const float n2 = norm_value(x[tid + pair], w[tid + pair], r);
     const double c = (double)tab[tid], s = (double)tab[pair + tid];
     x[tid] = __double2float_rn(__dsub_rn(__dmul_rn((double)n1, c), __dmul_rn((double)n2, s)));
     x[tid + pair] = __double2float_rn(__dadd_rn(__dmul_rn((double)n2, c), __dmul_rn((double)n1, s)));
@@ -306,12 +309,14 @@ cudaError_t launch_copy(const float* src, float* dst, int64_t count, cudaStream_
 }
 
 cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.heads <= 0 || a.n <= 0) return cudaSuccess;
-  if (a.hd <= 0 || a.hd % 2 != 0 || a.hd > 2 * kNormLanes || a.n > 65535) return cudaErrorInvalidValue;
+  const int64_t heads = a.heads + (a.x2 != nullptr ? a.heads2 : 0);
+  if (heads <= 0 || a.n <= 0) return cudaSuccess;
+  if (a.hd <= 0 || a.hd % 2 != 0 || a.hd > 2 * kNormLanes || a.n > 65535 || heads > 0x7fffffff)
+    return cudaErrorInvalidValue;
   HeadNormRopeArgs c = a;
   void* args[] = {&c};
   return launch_cfg(reinterpret_cast<const void*>(head_norm_rope_kernel), args,
-                    dim3((unsigned)a.heads, (unsigned)a.n), kNormLanes, 0, stream, pdl);
+                    dim3((unsigned)heads, (unsigned)a.n), kNormLanes, 0, stream, pdl);
 }
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
