@@ -88,8 +88,8 @@ __device__ __forceinline__ double warp_max_d(double v) {
 //     shared memory and takes their max; the cluster's max comes from every
 //     CTA's through distributed shared memory;
 //  2. each CTA turns its scores into exp(score - max) and sums them, and sums
-//     score * value over its keys in order, one thread per output dimension
-//     (loads of sixteen keys issued together);
+//     score * value over its keys, each thread four dimensions of a part of
+//     the keys in order (eight keys' loads issued together);
 //  3. CTA 0 adds the slices' sums in rank order and writes the outputs.
 // The arithmetic is the CPU's (the same exp(score - max) of every key); only
 // the sums are split, by warps and by slices.
@@ -106,7 +106,7 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThread
   __shared__ double part[kAttnWarps];
   __shared__ double slice_max, slice_sum;
   __shared__ double slice_acc[kAttnMaxHd];
-  __shared__ double part_acc[2][kAttnMaxHd];
+  __shared__ double part_acc[kAttnThreads * 4];  // kgroups x hd partial sums
   const int rank = (int)cluster.block_rank();
   const int head = blockIdx.x / kAttnSplit;
   const int64_t t = blockIdx.y;
@@ -185,30 +185,50 @@ __global__ void __cluster_dims__(kAttnSplit, 1, 1) __launch_bounds__(kAttnThread
     for (int w = 0; w < kAttnWarps; w++) ss = __dadd_rn(ss, part[w]);
     slice_sum = ss;
   }
-  // ... and the slice's weighted values, in key order: `groups` groups of
-  // threads, one thread per dimension in each, take consecutive parts of the
-  // slice's keys; the parts add in order.
-  const int groups = a.hd <= kAttnThreads / 2 ? 2 : 1;
-  const int g_id = tid / (kAttnThreads / groups), d0 = tid % (kAttnThreads / groups);
-  const int64_t half = (mine + groups - 1) / groups;
-  const int64_t i_lo = min64(mine, g_id * half), i_hi = min64(mine, i_lo + half);
-  for (int d = d0; d < a.hd; d += kAttnThreads / groups) {
-    const float* v = a.values + (start + k0) * kv_dim + kvo + d;
-    double acc = 0.0;
+  // ... and the slice's weighted values: thread (kg, dg) sums dimensions
+  // 4 dg .. 4 dg + 3 (one 16-byte load per key) over part kg of the slice's
+  // keys, in order, eight keys' loads at a time; the parts add in order.
+  const int dgroups = (int)(a.hd / 4), kgroups = kAttnThreads / dgroups;
+  const int dg = tid % dgroups, kg = tid / dgroups;
+  const int64_t part_keys = (mine + kgroups - 1) / kgroups;
+  const int64_t i_lo = min64(mine, kg * part_keys), i_hi = min64(mine, i_lo + part_keys);
+  if (kg < kgroups) {
+    const float* v = a.values + (start + k0) * kv_dim + kvo + 4 * dg;
+    double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
     int64_t i = i_lo;
-    for (; i + 16 <= i_hi; i += 16) {
-      float vv[16];
+    for (; i + 8 <= i_hi; i += 8) {
+      float4 vv[8];
 #pragma unroll
-      for (int u = 0; u < 16; u++) vv[u] = v[(i + u) * kv_dim];
+      for (int u = 0; u < 8; u++) vv[u] = *reinterpret_cast<const float4*>(v + (i + u) * kv_dim);
 #pragma unroll
-      for (int u = 0; u < 16; u++) acc = __dadd_rn(acc, __dmul_rn(scores[i + u], (double)vv[u]));
+      for (int u = 0; u < 8; u++) {
+        const double e = scores[i + u];
+        acc0 = __dadd_rn(acc0, __dmul_rn(e, (double)vv[u].x));
+        acc1 = __dadd_rn(acc1, __dmul_rn(e, (double)vv[u].y));
+        acc2 = __dadd_rn(acc2, __dmul_rn(e, (double)vv[u].z));
+        acc3 = __dadd_rn(acc3, __dmul_rn(e, (double)vv[u].w));
+      }
     }
-    for (; i < i_hi; i++) acc = __dadd_rn(acc, __dmul_rn(scores[i], (double)v[i * kv_dim]));
-    part_acc[g_id][d] = acc;
+    for (; i < i_hi; i++) {
+      const float4 vv = *reinterpret_cast<const float4*>(v + i * kv_dim);
+      const double e = scores[i];
+      acc0 = __dadd_rn(acc0, __dmul_rn(e, (double)vv.x));
+      acc1 = __dadd_rn(acc1, __dmul_rn(e, (double)vv.y));
+      acc2 = __dadd_rn(acc2, __dmul_rn(e, (double)vv.z));
+      acc3 = __dadd_rn(acc3, __dmul_rn(e, (double)vv.w));
+    }
+    double* pa = part_acc + kg * a.hd + 4 * dg;
+    pa[0] = acc0;
+    pa[1] = acc1;
+    pa[2] = acc2;
+    pa[3] = acc3;
   }
   __syncthreads();
-  for (int d = tid; d < a.hd; d += kAttnThreads)
-    slice_acc[d] = groups == 2 ? __dadd_rn(part_acc[0][d], part_acc[1][d]) : part_acc[0][d];
+  for (int d = tid; d < a.hd; d += kAttnThreads) {
+    double acc = 0.0;
+    for (int p = 0; p < kgroups; p++) acc = __dadd_rn(acc, part_acc[p * a.hd + d]);
+    slice_acc[d] = acc;
+  }
   cluster.sync();
 
   // 3. CTA 0 adds the slices in rank order
@@ -321,8 +341,10 @@ cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
   if (a.heads <= 0 || a.n <= 0) return cudaSuccess;
-  if (a.hd <= 0 || a.hd > kAttnMaxHd || a.kv_heads <= 0 || a.heads % a.kv_heads != 0 || a.n > 65535 ||
-      a.position < 0 || a.heads > 65535 / kAttnSplit)
+  // The value sums load four dimensions at a time: hd a multiple of 4 (as the
+  // reference's shader reads vec4s) and 16-byte aligned values.
+  if (a.hd <= 0 || a.hd > kAttnMaxHd || a.hd % 4 != 0 || a.kv_heads <= 0 || a.heads % a.kv_heads != 0 ||
+      a.n > 65535 || a.position < 0 || a.heads > 65535 / kAttnSplit || ((uintptr_t)a.values & 15) != 0)
     return cudaErrorInvalidValue;
   // Keys a token sees: all before it, or the window; a CTA scores its slice.
   const int64_t longest = a.window > 0 ? (a.window < a.position + a.n ? a.window : a.position + a.n)
