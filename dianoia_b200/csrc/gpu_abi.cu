@@ -494,7 +494,8 @@ void encode_attention(int64_t q, int64_t keys, int64_t values, int64_t gate, int
   std::lock_guard<std::recursive_mutex> lock(g_mu);
   const int64_t longest = window > 0 ? std::min(window, position + n) : position + n;
   const int64_t kv = (position + n) * kv_heads * hd * 4;
-  const bool ok = sides_ok(heads, n) && n <= 65535 && kv_heads > 0 && hd > 0 && hd < 65536 &&
+  // hd: a multiple of 4 up to 256 (the kernel loads values four at a time).
+  const bool ok = sides_ok(heads, n) && n <= 65535 && kv_heads > 0 && hd > 0 && hd <= 256 && hd % 4 == 0 &&
                   heads % kv_heads == 0 && position >= 0 && position < kMaxSide && window >= 0 &&
                   longest <= dn::kMaxAttnKeys && fits(q, 0, n * heads * hd * 4) && fits(keys, 0, kv) &&
                   fits(values, 0, kv) && (gate < 0 || fits(gate, 0, n * heads * 4)) &&

@@ -245,7 +245,8 @@ void dn_gpu_set_fusion(int64_t on);
  *   positions position.. over the KV cache (rows [position + n, kvHeads *
  *   hd]), q and out [n, heads * hd], gate [n, heads] before the sigmoid or a
  *   negative handle for none, window > 0 keeping the current key and the
- *   window - 1 before it (lab_vulkan.c:949-966; shard.dart:589-628). A token
+ *   window - 1 before it (lab_vulkan.c:949-966; shard.dart:589-628). hd a
+ *   multiple of 4 up to 256 (the reference's shader reads vec4s); a token
  *   sees at most 16384 keys (what lab_gpu_max_shared_memory reports). */
 void lab_gpu_enc_copy(int64_t src, int64_t srcOffset, int64_t dst, int64_t dstOffset, int64_t count);
 void lab_gpu_enc_steer(int64_t x, int64_t xOffset, int64_t v, int64_t vOffset, int64_t rows,

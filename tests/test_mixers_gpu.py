@@ -152,6 +152,7 @@ def test_layer_ops_reject_what_does_not_fit(gpu):
         lambda: L.lab_gpu_enc_attention(a, a, a, -1, a, 0, 1, 3, 2, 64, 0),                   # heads % kv
         lambda: L.lab_gpu_enc_attention(a, b, b, -1, a, 10, 1, 2, 1, 8, 0),                   # keys too short
         lambda: L.lab_gpu_enc_attention(a, a, a, -1, a, 20000, 1, 1, 1, 1, 0),                # too many keys
+        lambda: L.lab_gpu_enc_attention(a, a, a, -1, a, 4, 1, 2, 1, 6, 0),                    # hd % 4 != 0
         lambda: L.lab_gpu_enc_conv(a, b, 0, b, a, 64, 17, 1),                                  # k > 16
         lambda: L.lab_gpu_enc_conv(a, b, 0, b, a, 64, 3, 1),                                   # weights short
         lambda: L.lab_gpu_enc_steer(a, 0, b, 0, 1, 128, 1, 1.0),                               # v short
