@@ -238,3 +238,21 @@ def test_conv_steer_and_head_norm_restatements(oracle):
             x1, x2, c, s = float(seg[j]), float(seg[j + hd // 2]), float(rope[j]), float(rope[hd // 2 + j])
             assert got[hh * hd + j] == np.float32(x1 * c - x2 * s)
             assert got[hh * hd + j + hd // 2] == np.float32(x2 * c + x1 * s)
+
+
+def test_conv_history_carries_across_short_chunks(oracle):
+    """orc_conv on chunks shorter than the kernel (n < k - 1, the history
+    shift of shard.dart:509-516) gives the same outputs and history as the
+    whole sequence in one chunk."""
+    rng = np.random.default_rng(14)
+    width, k, total = 6, 4, 7
+    bcx = rng.standard_normal(total * 3 * width).astype(np.float32)
+    w = rng.standard_normal(width * k).astype(np.float32)
+    hist0 = rng.standard_normal((k - 1) * width).astype(np.float32)
+    y_all, h_all = oracle.conv(bcx, w, hist0, width, k, total)
+    hist, ys = hist0, []
+    for t0, n in ((0, 1), (1, 2), (3, 1), (4, 3)):
+        y, hist = oracle.conv(bcx[t0 * 3 * width:(t0 + n) * 3 * width], w, hist, width, k, n)
+        ys.append(y)
+    assert np.array_equal(np.concatenate(ys), y_all)
+    assert np.array_equal(hist, h_all)
