@@ -92,7 +92,7 @@ struct Op {
   int64_t w, qs_off, sc_off, x, x_off, y, y_off, rows, cols, n;
   double eps;
   bool acc;
-  int64_t e[6];
+  int64_t e[6] = {};  // zero unless a kind above sets them
   bool operator==(const Op& o) const {
     return kind == o.kind && q4 == o.q4 && w == o.w && qs_off == o.qs_off && sc_off == o.sc_off &&
            x == o.x && x_off == o.x_off && y == o.y && y_off == o.y_off && rows == o.rows &&
