@@ -170,15 +170,33 @@ def row_split(rows: int, rank: int, world: int, tiled: bool):
     return min(rows, tiles * rank // world * 32), min(rows, tiles * (rank + 1) // world * 32)
 
 
+def shard_rows(name: str, rows: int, rank: int, world: int, path: str):
+    """Rows [r0, r1) of projection `name` on `rank` for a multi-GPU path:
+    "chain" splits every projection on 32-row tiles, "ops" evenly, and
+    "head" keeps the decoder layers whole on every GPU and splits only the
+    lm_head's vocabulary rows (the reference's LM-head sharding,
+    shard.dart:12-13), so a token crosses GPUs once, for its logits."""
+    if path == "head" and name != "lm_head":
+        return 0, rows
+    return row_split(rows, rank, world, path == "chain")
+
+
+def rank_bytes(mats, block_bytes: int) -> int:
+    """Weight + activation bytes one rank moves per token for its row slices
+    (the activation read in full, the slice's outputs written)."""
+    return sum((m["r1"] - m["r0"]) * (m["cols"] // 32) * block_bytes + m["cols"] * 4
+               + (m["r1"] - m["r0"]) * 4 for m in mats)
+
+
 class Stack:
     """This rank's row slices of every projection, resident in HBM."""
 
-    def __init__(self, torch, rank: int, world: int, device, tiled: bool = False):
+    def __init__(self, torch, rank: int, world: int, device, path: str = "ops"):
         self.torch = torch
         self.rank, self.world, self.device = rank, world, device
         self.mats = []
         for idx, (layer, name, rows, cols) in enumerate(matrices()):
-            r0, r1 = row_split(rows, rank, world, tiled)
+            r0, r1 = shard_rows(name, rows, rank, world, path)
             qs, sc = self._weights(idx, rows, cols, r0, r1)
             self.mats.append(dict(layer=layer, name=name, rows=rows, cols=cols, r0=r0, r1=r1,
                                   qs=qs, scales=sc))
@@ -478,6 +496,9 @@ def workload_config(world, path="ops"):
             "global_batch": 1, "layers": LAYERS,
             "parallelism": (f"row-sharded x{world}, every tile's QA output stored into the peers over "
                             "NVLink inside the chain kernel" if world > 1 and path == "chain" else
+                            f"decoder layers whole on each of {world} GPUs, lm_head vocabulary rows "
+                            f"sharded x{world} + one NCCL all-gather of the logits per token"
+                            if world > 1 and path == "head" else
                             f"row-sharded x{world} + NCCL all-gather per projection" if world > 1
                             else "1 GPU"),
             "weights_bytes_per_token_ref_layout": step_bytes(Q8_BLOCK_BYTES_REF),
@@ -493,11 +514,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--path", choices=["auto", "chain", "ops"], default="auto",
+    ap.add_argument("--path", choices=["auto", "chain", "ops", "head"], default="auto",
                     help="chain: one persistent kernel per token (on N > 1 GPUs with the "
                          "all-gather fused into it over NVLink); ops: one GEMV launch per "
-                         "projection (N > 1: NCCL all-gather after each); auto: ops on 1 GPU, "
-                         "chain on N > 1 (the faster of the two in each case)")
+                         "projection (N > 1: NCCL all-gather after each); head: the ops "
+                         "launches with the decoder layers whole on every GPU and only the "
+                         "lm_head's rows sharded (N > 1: one NCCL all-gather of the logits); "
+                         "auto: ops on 1 GPU, head on N > 1")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--neighbour-steps", type=int, default=30,
                     help="tokens of the decode stack with norms, SwiGLU and residual adds")
@@ -555,8 +578,8 @@ def main():
     if L.lab_cpu_supported() != 1:
         raise SystemExit("no sm_100 device visible to libdianoia_b200")
 
-    path = args.path if args.path != "auto" else ("ops" if world == 1 else "chain")
-    stack = Stack(torch, rank, world, device, tiled=(path == "chain" and world > 1))
+    path = args.path if args.path != "auto" else ("ops" if world == 1 else "head")
+    stack = Stack(torch, rank, world, device, path)
     torch.cuda.synchronize()
 
     chain = QAChain(torch, device)
@@ -565,7 +588,8 @@ def main():
         def gather(out):
             n = out.numel() // world
             dist.all_gather_into_tensor(out, out[rank * n:(rank + 1) * n])
-        gather_qa = gather
+        # The head path's layers are whole on every GPU: only the logits move.
+        gather_qa = gather if path != "head" else (lambda ya: None)
 
     dchain = None
     if path == "chain":
@@ -631,14 +655,13 @@ def main():
 
     ms_per_step = ms_max / args.steps
     tokens_per_s = 1e3 / ms_per_step
-    alg_bytes = step_bytes(Q8_BLOCK_BYTES_ALG)
     ref_bytes = step_bytes(Q8_BLOCK_BYTES_REF)
 
-    # Dominant kernel: the decode chain (1 GPU) or the fused quantize + GEMV
-    # launches (N GPUs). Achieved = algorithmic bytes per step / step time on
-    # the launching stream (the activation quantize and any gaps included,
-    # so this is a lower bound of the kernel's own bandwidth); on N GPUs,
-    # bytes per rank.
+    # Dominant kernel: the fused quantize + GEMV launches (or the decode
+    # chain). Achieved = algorithmic bytes per step / step time on the
+    # launching stream (the activation quantize and any gaps included, so
+    # this is a lower bound of the kernel's own bandwidth); on N GPUs, the
+    # bytes of this rank's row slices.
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -646,7 +669,7 @@ def main():
     except OSError:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    per_rank_bytes = alg_bytes / world
+    per_rank_bytes = rank_bytes(stack.mats, Q8_BLOCK_BYTES_ALG)
     achieved = per_rank_bytes / (ms_per_step * 1e-3) / 1e9
 
     # Checksum of the logits: identical for every N (rows do not depend on the
@@ -689,16 +712,19 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (random-init Q8_0 weights, N(0,1) activations, seeded)",
             "config": workload_config(world, path),
-            "hbm_gbs_per_gpu": ref_bytes / world / (ms_per_step * 1e-3) / 1e9,
+            "hbm_gbs_per_gpu": rank_bytes(stack.mats, Q8_BLOCK_BYTES_REF) / (ms_per_step * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
                          "algorithmic_bytes_per_step_per_gpu": per_rank_bytes,
-                         "traffic": ((LAYERS * MEASURED_DRAM_BYTES_LAYER + MEASURED_DRAM_BYTES_HEAD) / world
+                         "traffic": (LAYERS * MEASURED_DRAM_BYTES_LAYER + MEASURED_DRAM_BYTES_HEAD / world
+                                     if dchain is None and path == "head" else
+                                     (LAYERS * MEASURED_DRAM_BYTES_LAYER + MEASURED_DRAM_BYTES_HEAD) / world
                                      if dchain is None else MEASURED_CHAIN_TRAFFIC_RATIO * ref_bytes / world),
                          "traffic_source": ("ncu dram__bytes_read+write of each projection's GEMV "
-                                            "launch, summed per token, / N (profiles/"
-                                            "dram_decode_stack_q8_shapes.md)" if dchain is None
+                                            "launch, summed per token" +
+                                            (", the lm_head's / N" if path == "head" else ", / N") +
+                                            " (profiles/dram_decode_stack_q8_shapes.md)" if dchain is None
                                             else "ncu dram bytes of a 4-layer chain launch, scaled "
                                                  "by weight bytes (profiles/chain_kernel_q8_4layers.md)")},
             "e2e": e2e,
@@ -1045,7 +1071,7 @@ def run_e2e(args, stack, L, torch, rank, world, gather, device, full_logits):
                           xq.ctypes.data, xsc.ctypes.data, ys.ctypes.data, rl, m["cols"], 1, 1, 1)
             h2d += xin.nbytes
             d2h += ys.nbytes + m["cols"] + m["cols"] // 32 * 4
-            if world > 1:
+            if world > 1 and rl < m["rows"]:
                 # All-gather of the row slices (any split): each rank adds
                 # its rows into zeros, exactly.
                 d = dev_tmp[name]
