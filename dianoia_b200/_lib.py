@@ -88,6 +88,8 @@ SIGNATURES = {
     "dn_chain_reset": (_i64, [_p, _p]),
     "dn_chain_destroy": (_i64, [_p]),
     "dn_linear_noalloc": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
+    "dn_linear_noalloc_status": (_i64, [_i64]),
+    "dn_set_wait_limit_ns": (_i64, [_i64]),
     "dn_last_error": (_i64, []),
     "dn_device_status": (_i64, [_i64]),
     "dn_error_string": (ctypes.c_char_p, [_i64]),

@@ -19,11 +19,31 @@
 #include <map>
 #include <new>
 #include <mutex>
+#include <vector>
 
 #include "dianoia_b200.h"
 #include "dn_launch.h"
 
 using dn::LinearArgs;
+
+namespace dn {
+
+// Every translation unit with bounded waits keeps its own device copy of the
+// wait limit (dn_common.cuh) and registers a setter here while the library
+// loads; dn_set_wait_limit_ns calls them all for the current device.
+using WaitLimitSetter = bool (*)(uint64_t ns);
+
+static std::vector<WaitLimitSetter>& wait_limit_setters() {
+  static std::vector<WaitLimitSetter> v;
+  return v;
+}
+
+bool register_wait_limit_setter(WaitLimitSetter setter) {
+  wait_limit_setters().push_back(setter);
+  return true;
+}
+
+}  // namespace dn
 
 namespace {
 
@@ -682,6 +702,16 @@ int64_t dn_last_error(void) {
   const int64_t e = tl_last_error;
   tl_last_error = DN_OK;
   return e;
+}
+
+int64_t dn_set_wait_limit_ns(int64_t ns) {
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  if (ns < 0) return DN_ERR_ARGS;
+  const uint64_t v = ns == 0 ? 2000000000ull : (uint64_t)ns;
+  bool ok = true;
+  for (dn::WaitLimitSetter set : dn::wait_limit_setters()) ok = set(v) && ok;
+  return ok ? DN_OK : DN_ERR_CUDA;
 }
 
 int64_t dn_device_status(int64_t clear) {

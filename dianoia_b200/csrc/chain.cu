@@ -131,12 +131,15 @@ __device__ __forceinline__ T* at_rank(T* local, const PeerInfo& pi, int p) {
 
 // A barrier of the consumer warps with a bounded wait (two mbarriers used in
 // turn), so a warp that gave up can never leave the others waiting forever.
+// Thread 0 may reach it only after its own bounded wait for a dependency
+// (another GPU's count), so the barrier waits three times as long: that wait
+// runs out first and records its own status bit.
 __device__ __forceinline__ bool consumers_sync(uint64_t* bars, uint32_t& uses, uint32_t* status) {
   uint64_t* b = &bars[uses & 1];
   const uint32_t parity = (uses >> 1) & 1u;
   uses++;
   mbar_arrive(b);
-  return gemv::warp_wait_sleep(b, parity, status);
+  return gemv::warp_wait_sleep(b, parity, status, 3);
 }
 
 // Shared memory from a 1024-byte aligned base: the stages; `stages` full and
@@ -233,8 +236,11 @@ __global__ void __launch_bounds__(kThreads, 3)
                 pt += G;
               }
             }
+            // The consumers free a stage only after their own bounded waits
+            // (a dependency, then a barrier at three times the limit), so
+            // this one runs five times the limit.
             if (k >= stages &&
-                !mbar_wait_bounded_sleep(&empty[s], ph ^ 1u, status, kStatusTmaTimeout)) {
+                !mbar_wait_bounded_sleep(&empty[s], ph ^ 1u, status, kStatusTmaTimeout, 5)) {
               abort_flag = 1;
               break;
             }
@@ -307,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         for (uint32_t it = 1;; it++) {
           __nanosleep(32);
           if ((int32_t)(ld_relaxed(cnt, sys) - target) >= 0) break;
-          if ((it & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
+          if ((it & 63u) == 0 && globaltimer_ns() - start > wait_limit_ns()) {
             report(status, kStatusPeerTimeout);
             abort_flag = 1;
             break;

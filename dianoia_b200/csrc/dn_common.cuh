@@ -21,8 +21,32 @@ enum : uint32_t {
   kStatusMmaTimeout = 1u << 2,   // a wait for a tensor-core commit ran out
 };
 
-// How long a bounded wait spins before it records a timeout and returns.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// How long a bounded wait spins before it records a timeout and returns: 2 s
+// unless dn_set_wait_limit_ns changed it for the device.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// The limit as the kernels of this translation unit read it. Every .cu file
+// has its own copy of this module variable (no relocatable device code), so
+// each registers a setter that dn_set_wait_limit_ns calls for the current
+// device (register_wait_limit_setter, abi.cu).
+static __device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *static_cast<volatile uint64_t*>(&g_wait_limit_ns);
+}
+
+using WaitLimitSetter = bool (*)(uint64_t ns);
+bool register_wait_limit_setter(WaitLimitSetter setter);  // abi.cu
+
+namespace {
+// Copies `ns` into this translation unit's g_wait_limit_ns on the current device.
+[[maybe_unused]] bool set_wait_limit_here(uint64_t ns) {
+  if (cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof ns) == cudaSuccess) return true;
+  cudaGetLastError();
+  return false;
+}
+[[maybe_unused]] const bool g_wait_limit_registered = register_wait_limit_setter(&set_wait_limit_here);
+}  // namespace
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -192,14 +216,19 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // mbar_wait_bounded for waits that may be long (a full stage ring): the
 // waiting thread sleeps instead of spinning, leaving issue slots to the
-// warps that compute.
+// warps that compute. A wait for threads that are themselves in a bounded
+// wait (a barrier behind a wait on another GPU) runs `mult` times the limit,
+// so the inner wait gives up first and its own status bit is the one set
+// (two bits recorded at the same instant could lose one: report() is a plain
+// read-modify-write).
 __device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity,
-                                                        uint32_t* status, uint32_t bits) {
+                                                        uint32_t* status, uint32_t bits,
+                                                        uint32_t mult = 1) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-    if (globaltimer_ns() - start > kWaitLimitNs) {
+    if (globaltimer_ns() - start > mult * wait_limit_ns()) {
       report(status, bits);
       return false;
     }
@@ -214,7 +243,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   const uint64_t start = globaltimer_ns();
   for (uint32_t i = 1;; i++) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
+    if ((i & 63u) == 0 && globaltimer_ns() - start > wait_limit_ns()) {
       report(status, bits);
       return false;
     }
@@ -241,6 +270,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 3-D tiled TMA load of the box at (x, y, z), as tma_load_2d.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -181,6 +181,10 @@ cudaError_t launch_steer(const SteerArgs& a, cudaStream_t stream, bool pdl);
 // The decode GEMV on either activation form (gemv.cu).
 int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl);
 bool gemv_ex_supported(const GemvArgs& g);
+// The one-token product on QA inputs with plain outputs (gemv1.cu), which
+// launch_gemv_ex picks for the products it can take.
+bool gemv1_eligible(const GemvArgs& g);
+int64_t launch_gemv1(const GemvArgs& g, cudaStream_t stream, bool pdl);
 // f32 -> QA blocks (quantize.cu).
 cudaError_t launch_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols,
                                int64_t xa_stride, cudaStream_t stream);

@@ -24,4 +24,14 @@ bool encode_tmap_2d_sw64(CUtensorMap* map, const void* base, CUtensorMapDataType
                          uint64_t row_elems, uint64_t rows, uint64_t row_bytes, uint32_t box_elems,
                          uint32_t box_rows);
 
+// A 3-D view of a row-major byte array [rows, row_bytes] (row_bytes a
+// multiple of 128) whose box is `chunks` consecutive 128-byte chunks of
+// box_rows rows, 128-byte swizzled, landing in shared memory chunk by chunk:
+// chunk j of row r at j * box_rows * 128 + r * 128 - the layout of `chunks`
+// 2-D boxes of box_rows x 128 bytes, in one copy instead of `chunks`.
+// Coordinates (x, y, z) = (byte in the chunk, row, chunk). Returns false if
+// the driver refuses the map.
+bool encode_tmap_row_chunks(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+                            uint32_t box_rows, uint32_t chunks);
+
 }  // namespace dn

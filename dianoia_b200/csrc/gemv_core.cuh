@@ -112,8 +112,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
 // warp_wait whose waiting lanes sleep in hardware (mbarrier try_wait with a
 // suspend-time hint) instead of spinning, so warps that wait leave the issue
 // slots to warps that compute.
-__device__ __forceinline__ bool warp_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* status) {
-  const bool got = mbar_wait_bounded_sleep(bar, parity, status, kStatusTmaTimeout);
+__device__ __forceinline__ bool warp_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                                uint32_t mult = 1) {
+  const bool got = mbar_wait_bounded_sleep(bar, parity, status, kStatusTmaTimeout, mult);
   return __all_sync(0xffffffffu, got) != 0;
 }
 

@@ -66,3 +66,18 @@ extern "C" int64_t dn_linear_noalloc(int64_t format, const void* qs, const void*
   if ((flags & DN_FLAG_PDL) && dn::path_for(a) == 0) return dn::launch_gemv(a, st, true);
   return dn::launch_linear(a, st);
 }
+
+extern "C" int64_t dn_linear_noalloc_status(int64_t clear) {
+  uint8_t* base = scratch_base();
+  if (base == nullptr) return DN_ERR_NO_DEVICE;
+  uint32_t v = 0;
+  if (cudaMemcpy(&v, base, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return DN_ERR_CUDA;
+  }
+  if (clear && v != 0 && cudaMemset(base, 0, sizeof v) != cudaSuccess) {
+    cudaGetLastError();
+    return DN_ERR_CUDA;
+  }
+  return (int64_t)v;
+}

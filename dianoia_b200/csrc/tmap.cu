@@ -44,6 +44,20 @@ bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type
                 swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+bool encode_tmap_row_chunks(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+                            uint32_t box_rows, uint32_t chunks) {
+  auto fn = encode_fn();
+  if (fn == nullptr || row_bytes % 128 != 0) return false;
+  // Dimensions innermost first: a 128-byte chunk, the rows, the chunks of a row.
+  const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+  const cuuint64_t strides[2] = {row_bytes, 128};
+  const cuuint32_t box[3] = {128, box_rows, chunks};
+  const cuuint32_t estrides[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estrides,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_tmap_2d_sw64(CUtensorMap* map, const void* base, CUtensorMapDataType type,
                          uint64_t row_elems, uint64_t rows, uint64_t row_bytes, uint32_t box_elems,
                          uint32_t box_rows) {

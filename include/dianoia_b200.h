@@ -462,11 +462,17 @@ int64_t dn_chain_destroy(void* chain);
  * before reading them. Calls that overlap in time on one device share the
  * scratch and race (one stream, or calls ordered by events, is safe). A
  * bounded wait that ran out (a broken device, never an input) is recorded in
- * the array's status word, which dn_device_status does not read. Results
- * equal dn_linear's with DN_PATH_AUTO and mode 1. */
+ * the array's status word, which dn_linear_noalloc_status reads (not
+ * dn_device_status). Results equal dn_linear's with DN_PATH_AUTO and mode 1. */
 int64_t dn_linear_noalloc(int64_t format, const void* qs, const void* scales, const float* xs,
                           float* ys, int64_t rows, int64_t cols, int64_t n, int64_t ldy,
                           int64_t flags, void* stream);
+/* The status word of dn_linear_noalloc's fixed array on the current device:
+ * the same bits as dn_device_status (0 when every bounded wait completed),
+ * cleared when `clear` is non-zero. A synchronous copy of four bytes, no
+ * allocation: call it after synchronizing the streams of the calls it
+ * covers. No counterpart in the reference. */
+int64_t dn_linear_noalloc_status(int64_t clear);
 
 /* The calling thread's last error from a lab_* call (DN_OK if none), cleared
  * by reading. */
@@ -476,6 +482,15 @@ int64_t dn_last_error(void);
  * (1: bulk copy, 2: peer flag, 4: tensor-core commit); cleared by reading
  * when `clear` is non-zero. Call after synchronizing. */
 int64_t dn_device_status(int64_t clear);
+
+/* Sets how long every bounded wait of the kernels launched afterwards on the
+ * current device spins before it records a timeout in the status word and
+ * returns (ns > 0; 0 restores the default of 2 s). A synchronous copy into
+ * each kernel module: call it outside stream capture, with no kernel of the
+ * library running on the device. Returns DN_OK. (The reference's GPU layer
+ * reports a failed command buffer as commit() == 0, lab_vulkan.c:737-757;
+ * this is the knob that lets a test make such a failure happen quickly.) */
+int64_t dn_set_wait_limit_ns(int64_t ns);
 
 /* A short English description of a DN_* code. */
 const char* dn_error_string(int64_t code);

@@ -257,6 +257,30 @@ def activations(rng: np.random.Generator, n: int, cols: int) -> np.ndarray:
     return rng.standard_normal(n * cols, dtype=np.float32)
 
 
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """f32 -> the nearest bfloat16 (ties to even), returned as f32 (exact)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def pad_cols(x: np.ndarray, rows: int, cols: int, padded: int) -> np.ndarray:
+    """[rows, cols] -> [rows, padded] with zeros after each row (padded >= cols)."""
+    out = np.zeros((rows, padded), np.float32)
+    out[:, :cols] = np.asarray(x, np.float32).reshape(rows, cols)
+    return out.reshape(-1)
+
+
+def vision_weights_f32(rng: np.random.Generator, rows: int, cols: int, padded: int = 0) -> np.ndarray:
+    """Config 5's float weights before quantization: bf16 N(0, 0.02) widened to
+    f32, each row zero-padded to `padded` columns (K = 4304 is not a multiple
+    of the 32-element block; a zero block adds exactly 0 to every dot product
+    and leaves the real values' quantization unchanged). The caller quantizes
+    them with lab_quantize_q8, as the configuration specifies."""
+    w = bf16_round(rng.normal(0.0, 0.02, size=rows * cols).astype(np.float32))
+    return pad_cols(w, rows, cols, padded) if padded and padded != cols else w
+
+
 def max_rel_err(ys: np.ndarray, ref: np.ndarray, mag: np.ndarray) -> float:
     """max |y - ref| / sum|w x| (native_kernels_test.dart:160-176); 0/0 counts as 0."""
     err = np.abs(ys.astype(np.float64) - ref)

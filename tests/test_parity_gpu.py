@@ -341,3 +341,101 @@ def test_tensor_core_gemm_within_tolerance(cuda_lib, oracle, fmt, rows, cols, n)
 def test_auto_path_uses_tensor_cores_for_prefill(cuda_lib):
     assert cuda_lib.dn_linear_path(0, None, None, None, None, 6144, 2048, 512, 1) == 1
     assert cuda_lib.dn_linear_path(1, None, None, None, None, 6144, 2048, 1, 1) == 0
+
+
+# ------------------------------------------------ int32 block dots on tensor cores
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+@pytest.mark.parametrize("rows,cols,n", [(300, 32, 80), (128, 32, 16), (257, 128, 200)])
+def test_tensor_core_int32_block_dots(cuda_lib, oracle, fmt, rows, cols, n):
+    """The tcgen05 path's int32 block dots, bit for bit (lab_native.c:456-466,
+    987-1002). With unit weight scales and integer activations in which every
+    block holds a +-127, the activation quantize is exact (scale 1, inv 1), so
+    each output is the float of its row's block dots: one block dot for
+    cols = 32, and for cols = 128 a sum of four that stays below 2^24."""
+    rng = np.random.default_rng(rows * 3 + cols + n)
+    qs, _ = weights(fmt, rng, rows, cols)
+    blocks = cols // 32
+    sc = (np.full(rows * blocks, 0x3C00, np.uint16) if fmt == "q4"   # fp16 1.0
+          else np.ones(rows * blocks, np.float32))
+    xi = rng.integers(-127, 128, size=(n, cols)).astype(np.float32)
+    pos = rng.integers(0, 32, size=(n, blocks))
+    sign = rng.choice(np.array([-127.0, 127.0], np.float32), size=(n, blocks))
+    for b in range(blocks):
+        xi[np.arange(n), b * 32 + pos[:, b]] = sign[:, b]
+    xs = xi.reshape(-1)
+    ys, xq, xsc = dev_linear(cuda_lib, fmt, dev(qs), dev(sc), dev(xs), rows, cols, n, path=1)
+    assert (xsc == 1.0).all() and np.array_equal(xq, xi.astype(np.int8).reshape(-1))
+    dots = oracle.block_dots(fmt, qs, xq, rows, cols, n).reshape(n, rows, blocks)
+    want = dots.astype(np.int64).sum(axis=2)
+    assert np.abs(want).max() < 2 ** 24
+    assert same_bits(ys, want.astype(np.float32).reshape(-1))
+
+
+# ------------------------------------------------------- config 5 at full size
+
+VISION = [("qkv", 3456, 1152, 1152), ("o", 1152, 1152, 1152), ("fc1", 4304, 1152, 1152),
+          ("fc2", 1152, 4304, 4320)]
+
+
+@pytest.mark.parametrize("name,rows,cols,padded", VISION)
+def test_config5_vision_m1024(cuda_lib, oracle, name, rows, cols, padded):
+    """Config 5 as stated: 1024 image tokens; weights bf16 N(0, 0.02) quantized
+    to Q8_0 by lab_quantize_q8 (fc2's K zero-padded from 4304 to 4320 in both
+    operands); activations N(0, 1). The library's weight quantize equals the
+    oracle's bit for bit, so do the quantized activations, and the tensor-core
+    outputs are within the reference's bound."""
+    L = cuda_lib
+    n = 1024
+    rng = np.random.default_rng(5000 + rows + cols)
+    w = orc.vision_weights_f32(rng, rows, cols, padded)
+    qs, sc = oracle.quantize_q8(w, rows, padded)
+    gq = np.zeros(rows * padded, np.int8)
+    gs = np.zeros(rows * padded // 32, np.float32)
+    L.lab_quantize_q8(w.ctypes.data, gq.ctypes.data, gs.ctypes.data, rows, padded)
+    assert L.dn_last_error() == 0
+    assert np.array_equal(gq, qs) and same_bits(gs, sc)
+    xs = orc.pad_cols(orc.activations(rng, n, cols), n, cols, padded)
+    assert L.dn_linear_path(0, None, None, None, None, rows, padded, n, 1) == 1
+    ys, xq, xsc = dev_linear(L, "q8", dev(qs), dev(sc), dev(xs), rows, padded, n)
+    wq, wsc = oracle.quantize_q8(xs, n, padded)
+    assert np.array_equal(xq, wq) and same_bits(xsc, wsc)
+    ref, mag = oracle.reference_f64("q8", qs, sc, xs, rows, padded, n, 1)
+    err = orc.max_rel_err(ys, ref, mag)
+    assert err < TOL, f"{name}: max relative error {err:.3e}"
+
+
+# ------------------------------------------------------- lm_head M sweep, full size
+
+LM_ROWS, LM_COLS, LM_MAX_M = 151936, 2048, 64
+
+
+@pytest.fixture(scope="module")
+def lm_head_q8(oracle):
+    """The tied Q8_0 lm_head and 64 tokens, with the oracle's bit-exact outputs
+    for the first 8 tokens and the double-precision check for all 64 (a row's
+    result does not depend on how many tokens share the call)."""
+    rng = np.random.default_rng(151936 * 64)
+    qs, sc = orc.q8_weights(rng, LM_ROWS, LM_COLS)
+    xs = orc.activations(rng, LM_MAX_M, LM_COLS)
+    bits, _, _ = oracle.gemm("q8", qs, sc, xs[: 8 * LM_COLS], LM_ROWS, LM_COLS, 8, 1)
+    ref, mag = oracle.reference_f64("q8", qs, sc, xs, LM_ROWS, LM_COLS, LM_MAX_M, 1)
+    return dict(qs=dev(qs), sc=dev(sc), xs=xs, bits=bits, ref=ref, mag=mag)
+
+
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 16, 32, 64])
+def test_lm_head_m_sweep(cuda_lib, lm_head_q8, m):
+    """Config 5's lm_head M sweep on the whole 151936 x 2048 matrix: the GEMV
+    (small M) bit for bit, the tensor-core GEMM (from the crossover on) within
+    the bound."""
+    h = lm_head_q8
+    path = cuda_lib.dn_linear_path(0, None, None, None, None, LM_ROWS, LM_COLS, m, 1)
+    ys, _, _ = dev_linear(cuda_lib, "q8", h["qs"], h["sc"], dev(h["xs"][: m * LM_COLS]),
+                          LM_ROWS, LM_COLS, m)
+    if path == 0:
+        assert same_bits(ys, h["bits"][: m * LM_ROWS])
+    else:
+        assert path == 1
+        err = orc.max_rel_err(ys, h["ref"][: m * LM_ROWS], h["mag"][: m * LM_ROWS])
+        assert err < TOL, f"M={m}: max relative error {err:.3e}"

@@ -1,8 +1,9 @@
 """dn_linear_noalloc (scratch in the library's fixed device array, no
 allocation) against dn_linear with caller-provided scratch: the same kernels,
 so the results agree bit for bit, on two calls in a row, on the GEMV path
-(n = 1) and the tensor-core path (n = 64). Collected last, and must also pass
-alone in a fresh process."""
+(n = 1) and the tensor-core path (n = 64), with the fixed array's status word
+read back through dn_linear_noalloc_status. Collected last, and must also
+pass alone in a fresh process."""
 import numpy as np
 import pytest
 
@@ -37,6 +38,8 @@ def test_noalloc_matches_dn_linear(cuda_lib, oracle, fmt, n):
                                    rows, cols, n, rows, 0, st) == 0
         torch.cuda.synchronize()
         assert torch.equal(got.view(torch.int32), want.view(torch.int32)), call
+        # Every bounded wait of the call completed (the fixed array's status word).
+        assert L.dn_linear_noalloc_status(1) == 0
     # And against the reference's own algorithm: bit-exact on the GEMV path,
     # within the 1e-5 bound of the row's absolute-sum scale on the GEMM path.
     ref, _, _ = oracle.gemm(fmt, qs, sc, x, rows, cols, n, 1)
