@@ -40,6 +40,15 @@ import argparse
 import ctypes
 import json
 import os
+
+# The host's cores as this process may use them, taken before any OpenMP
+# runtime loads: a runtime started with a binding policy pins the main thread
+# to one core, and the affinity read afterwards would say 1.
+try:
+    HOST_THREADS = len(os.sched_getaffinity(0))
+except AttributeError:
+    HOST_THREADS = os.cpu_count() or 1
+
 import statistics
 import subprocess
 import sys
@@ -61,12 +70,12 @@ Q8_BLOCK_BYTES_REF = 36   # reference layout: 32 int8 + f32 scale
 Q8_BLOCK_BYTES_ALG = 34   # algorithmic credit: 32 int8 + fp16 scale (GGUF Q8_0)
 METRIC = "quantized-linear HBM GB/s (GEMV), int8 TOPS (GEMM), tokens/s at 1/2/4/8 B200"
 CHUNKS = 8                # weights are generated per 1/8 row chunk so any N in {1,2,4,8} shards alike
-# DRAM bytes of one GEMV launch per projection, from one ncu capture of each
-# (profiles/dram_decode_stack_q8_shapes.md): a layer's four, and the lm_head.
+# DRAM bytes (read + write) of one GEMV launch per projection, from one ncu
+# capture of each: a layer's four, and the lm_head.
 MEASURED_DRAM_BYTES_LAYER = 9487872 + 4769024 + 28362496 + 14211072
 MEASURED_DRAM_BYTES_HEAD = 350114304 + 4418560
 # The chain kernel's DRAM bytes over reference-layout weight bytes, from one ncu
-# capture of a 4-layer chain (profiles/chain_kernel_q8_4layers.md).
+# capture of a 4-layer chain.
 MEASURED_CHAIN_TRAFFIC_RATIO = (576637952 + 4725760) / 576552960
 
 
@@ -253,7 +262,99 @@ class QAChain:
                    for n, r in OUT_ROWS.items() if n != "lm_head"}
 
 
-def run_step(stack, chain, L, stream_handle, gather, gather_qa, flags=1):
+def make_gather(dist, rank, world):
+    """All-gather of a buffer whose rank p holds elements [numel * p // world,
+    numel * (p + 1) // world) - the split of row_split, by elements - in place.
+    An even split is one all_gather_into_tensor; otherwise each rank's span is
+    padded to the widest span, gathered, and copied into place."""
+    def gather(out):
+        numel = out.numel()
+        spans = [(numel * p // world, numel * (p + 1) // world) for p in range(world)]
+        lo, hi = spans[rank]
+        if numel % world == 0:
+            dist.all_gather_into_tensor(out, out[lo:hi])
+            return
+        width = max(b - a for a, b in spans)
+        send = out.new_zeros(width)
+        send[:hi - lo] = out[lo:hi]
+        recv = out.new_empty(world * width)
+        dist.all_gather_into_tensor(recv, send)
+        for p, (a, b) in enumerate(spans):
+            out[a:b] = recv[p * width:p * width + b - a]
+    return gather
+
+
+class _DevArray:
+    """A device f32 array at a raw address, for torch.as_tensor (no copy)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3}
+
+
+class FusedHead:
+    """The head path's logits all-gather fused into the lm_head product
+    (dn_linear_qa_allgather): every rank allocates one region (the whole
+    logits, then a counter and the wait's expect word) that the others map
+    (dn_peer_alloc / dn_peer_open); each rank's lm_head stores its vocabulary
+    rows into every rank's logits over NVLink and counts its tiles in every
+    rank's counter, and dn_peer_wait ends the token once all ranks' tiles are
+    in. No NCCL call and no TMA touches peer memory."""
+
+    def __init__(self, torch, stack, L, dist):
+        from dianoia_b200 import _lib
+        self.L, self.dist = L, dist
+        rank, world = stack.rank, stack.world
+        self.logits_bytes = VOCAB * 4
+        self.region_bytes = (self.logits_bytes + 256 + 4095) // 4096 * 4096
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.DN_PEER_HANDLE_BYTES)()
+        _lib.check(L.dn_peer_alloc(self.region_bytes, ctypes.byref(base), handle), "dn_peer_alloc")
+        self.base = base.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle))
+        self.opened, bases = [], []
+        for p in range(world):
+            if p == rank:
+                bases.append(self.base)
+                continue
+            ptr = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * _lib.DN_PEER_HANDLE_BYTES).from_buffer_copy(handles[p])
+            _lib.check(L.dn_peer_open(h, ctypes.byref(ptr)), "dn_peer_open")
+            bases.append(ptr.value)
+            self.opened.append(ptr.value)
+        self.ys = (ctypes.c_void_p * world)(*bases)
+        self.cnts = (ctypes.c_void_p * world)(*[b + self.logits_bytes for b in bases])
+        self.counter = self.base + self.logits_bytes
+        self.expect = self.base + self.logits_bytes + 4
+        self.tiles = sum(-(-(r1 - r0) // 32) for r0, r1 in
+                         (row_split(VOCAB, p, world, False) for p in range(world)))
+        self.world = world
+        self.logits = torch.as_tensor(_DevArray(self.base, VOCAB), device=stack.device)
+        dist.barrier()  # every region mapped everywhere before any rank stores into it
+
+    def lm_head(self, m, xa, stream_handle, flags):
+        rc = self.L.dn_linear_qa_allgather(0, m["qs"].data_ptr(), m["scales"].data_ptr(), xa.data_ptr(),
+                                           m["r1"] - m["r0"], m["cols"], m["r0"], self.ys, self.cnts,
+                                           self.world, flags, stream_handle)
+        if rc != 0:
+            raise RuntimeError(f"dn_linear_qa_allgather failed: {self.L.dn_error_string(rc).decode()}")
+        rc = self.L.dn_peer_wait(self.counter, self.expect, self.tiles, stream_handle)
+        if rc != 0:
+            raise RuntimeError(f"dn_peer_wait failed: {self.L.dn_error_string(rc).decode()}")
+
+    def close(self):
+        self.dist.barrier()  # no rank still stores into another's region
+        for p in self.opened:
+            self.L.dn_peer_close(p)
+        self.opened = []
+        self.dist.barrier()
+        if self.base:
+            self.L.dn_peer_free(self.base)
+            self.base = None
+
+
+def run_step(stack, chain, L, stream_handle, gather, gather_qa, flags=1, fused=None):
     """One token through all projections on `stream_handle`. Returns launches."""
     rc = L.dn_quantize_qa(stack.x0.data_ptr(), chain.xa0.data_ptr(), 1, HIDDEN,
                           HIDDEN // 32 * 36, stream_handle)
@@ -267,6 +368,10 @@ def run_step(stack, chain, L, stream_handle, gather, gather_qa, flags=1):
         out = stack.bufs[name]
         ya = chain.ya.get(name)
         rl = m["r1"] - m["r0"]
+        if fused is not None and name == "lm_head":
+            fused.lm_head(m, xa, stream_handle, flags)
+            launches += 2
+            continue
         rc = L.dn_linear_qa(0, m["qs"].data_ptr(), m["scales"].data_ptr(), xa.data_ptr(),
                             m["cols"] // 32 * 36, out.data_ptr() + 4 * m["r0"], rl,
                             None if ya is None else ya.data_ptr() + m["r0"] // 32 * 36,
@@ -443,11 +548,30 @@ def cpu_reference_tokens(ref, hw, x0, threads: int, tokens: int):
     return (time.perf_counter() - t0) / tokens, outs["lm_head"].copy()
 
 
-def host_threads():
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), or the platform's processor string."""
     try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def host_threads():
+    return HOST_THREADS
+
+
+def bind_cpu_threads():
+    """The reference CPU baseline runs under OpenMP with its threads pinned next
+    to one another (OMP_PROC_BIND=close). The system libgomp that its library
+    (and the oracle's) links reads this once, when it loads, so this is set
+    just before the first of them loads - and not at startup, where torch's own
+    OpenMP runtime would read it too and pin the main thread to one core."""
+    os.environ.setdefault("OMP_PROC_BIND", "close")
 
 
 def run_reference_arm(args, rank, world):
@@ -455,6 +579,7 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return None
     from oracle import oracle as orc
+    bind_cpu_threads()
     try:
         ref = orc.Reference()
     except FileNotFoundError as e:
@@ -467,7 +592,6 @@ def run_reference_arm(args, rank, world):
         hw.append((qs, sc, rows, cols))
     x0 = orc.activations(rng, 1, HIDDEN)
     threads = host_threads()
-    os.environ.setdefault("OMP_PROC_BIND", "close")
     for _ in range(args.warmup):
         cpu_reference_tokens(ref, hw, x0, threads, 1)
     times = []
@@ -481,28 +605,44 @@ def run_reference_arm(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": workload_config(world),
+        "config": workload_config(),
+        "parallelism": (f"the reference's CPU kernels on rank 0's host cores ({threads} threads); "
+                        f"ranks 1..{world - 1} idle" if world > 1 else
+                        f"the reference's CPU kernels on the host cores ({threads} threads)"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "cpu_model": cpu_model(),
+                         "omp_proc_bind": os.environ.get("OMP_PROC_BIND", "unset"),
                          "sample": f"{args.steps} full decode-step linear stacks (113 lab_gemm_q8 calls each)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "hbm_gbs": step_bytes(Q8_BLOCK_BYTES_REF) * value / 1e9,
     }
 
 
-def workload_config(world, path="ops"):
+def workload_config():
+    """The workload both arms run (the reference arm's line carries the same)."""
     return {"workload": "config3: Qwen3-1.7B-shaped Q8_0 decode-step linear stack, batch 1 "
                         "(28 x [qkv 4096x2048, o 2048x2048, gate/up 12288x2048, down 2048x6144] "
                         "+ lm_head 151936x2048)",
             "global_batch": 1, "layers": LAYERS,
-            "parallelism": (f"row-sharded x{world}, every tile's QA output stored into the peers over "
-                            "NVLink inside the chain kernel" if world > 1 and path == "chain" else
-                            f"decoder layers whole on each of {world} GPUs, lm_head vocabulary rows "
-                            f"sharded x{world} + one NCCL all-gather of the logits per token"
-                            if world > 1 and path == "head" else
-                            f"row-sharded x{world} + NCCL all-gather per projection" if world > 1
-                            else "1 GPU"),
             "weights_bytes_per_token_ref_layout": step_bytes(Q8_BLOCK_BYTES_REF),
             "l2": "inputs larger than L2 (1.94 GB of weights streamed per step)"}
+
+
+def parallelism(world, path="ops", gather="fused"):
+    """How this arm spreads the workload over the GPUs (a line's own key,
+    outside `config`, which names the workload only)."""
+    if world == 1:
+        return "1 GPU"
+    if path == "chain":
+        return (f"row-sharded x{world}, every tile's QA output stored into the peers over NVLink "
+                "inside the chain kernel")
+    if path == "head":
+        return (f"decoder layers replicated on each of {world} GPUs, lm_head vocabulary rows sharded "
+                f"x{world}; the logits all-gathered " +
+                ("inside the lm_head product (each rank's rows stored into every rank's logits over "
+                 "NVLink, then a bounded wait on its counter)" if gather == "fused"
+                 else "by one NCCL all-gather per token"))
+    return f"row-sharded x{world} + NCCL all-gather per projection"
 
 
 # ------------------------------------------------------------------ main
@@ -521,12 +661,19 @@ def main():
                          "launches with the decoder layers whole on every GPU and only the "
                          "lm_head's rows sharded (N > 1: one NCCL all-gather of the logits); "
                          "auto: ops on 1 GPU, head on N > 1")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="head path on N > 1 GPUs: the logits all-gather fused into the lm_head "
+                         "product (peer stores over NVLink), or one NCCL all-gather")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--e2e-cpu-abi", action="store_true",
+                    help="on N > 1 GPUs also time the per-projection lab_gemm_q8 loop")
     ap.add_argument("--neighbour-steps", type=int, default=30,
                     help="tokens of the decode stack with norms, SwiGLU and residual adds")
     ap.add_argument("--context", type=int, default=1024,
                     help="KV-cache position of the whole decode step (with attention)")
     ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--config-steps", type=int, default=50,
+                    help="launches per case of the configs key (0: leave it out)")
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours", "cache"],
                     default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
@@ -585,9 +732,7 @@ def main():
     chain = QAChain(torch, device)
     gather = gather_qa = None
     if world > 1:
-        def gather(out):
-            n = out.numel() // world
-            dist.all_gather_into_tensor(out, out[rank * n:(rank + 1) * n])
+        gather = make_gather(dist, rank, world)
         # The head path's layers are whole on every GPU: only the logits move.
         gather_qa = gather if path != "head" else (lambda ya: None)
 
@@ -595,15 +740,16 @@ def main():
     if path == "chain":
         dchain = (DecodeChain(torch, stack, chain, L, device) if world == 1
                   else ShardedChain(torch, stack, chain, L, device, dist))
+    fused = FusedHead(torch, stack, L, dist) if path == "head" and world > 1 and args.gather == "fused" else None
 
     def one_step(handle):
         if dchain is not None:
             return run_step_chain(stack, chain, dchain, L, handle)
-        return run_step(stack, chain, L, handle, gather, gather_qa)
+        return run_step(stack, chain, L, handle, gather, gather_qa, fused=fused)
 
     stream = torch.cuda.Stream(device=device)
     graph = None
-    launches_per_step = 2 if dchain is not None else len(stack.mats) + 1
+    launches_per_step = 2 if dchain is not None else len(stack.mats) + 1 + (1 if fused is not None else 0)
     with torch.cuda.stream(stream):
         for _ in range(2):
             one_step(stream.cuda_stream)
@@ -675,7 +821,7 @@ def main():
     # Checksum of the logits: identical for every N (rows do not depend on the
     # split). The sharded chain leaves each rank its own rows of the logits
     # (the rest zero): a sum over ranks rebuilds them exactly.
-    full_logits = stack.bufs["lm_head"].clone()
+    full_logits = (fused.logits if fused is not None else stack.bufs["lm_head"]).clone()
     if world > 1 and dchain is not None:
         dist.all_reduce(full_logits)
     checksum = float(full_logits.double().sum().item())
@@ -694,16 +840,23 @@ def main():
     # ABI (one command buffer per token); also, and on N > 1 only, through
     # the CPU-layer ABI (lab_gemm_q8 per projection on rank-local shards, the
     # slices all-gathered through device copies).
-    e2e_cpu_abi = run_e2e(args, stack, L, torch, rank, world, gather, device, full_logits)
+    e2e_cpu_abi = run_e2e(args, stack, L, torch, rank, world, gather, device, full_logits) \
+        if world == 1 or args.e2e_cpu_abi else None
+    e2e_dn = run_e2e_device_api(args, torch, stack, step, stream,
+                                fused.logits if fused is not None else stack.bufs["lm_head"], world, device,
+                                full_logits) if dchain is None else None
     e2e = run_e2e_gpu_layer(args, stack, L, torch) if world == 1 else None
     if e2e is None:
-        e2e = e2e_cpu_abi
+        e2e = e2e_dn if e2e_dn is not None else e2e_cpu_abi
     neighbours = run_neighbours(args, stack, L) if world == 1 else None
     decode_step = run_neighbours(args, stack, L, context=args.context) if world == 1 else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and args.cpu_tokens > 0:
         cpu_baseline = run_cpu_baseline(args, stack)
+    configs = None
+    if rank == 0 and world == 1 and args.config_steps > 0:
+        configs = run_configs_compact(args, torch, L)
 
     if rank == 0:
         res = {
@@ -711,7 +864,8 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (random-init Q8_0 weights, N(0,1) activations, seeded)",
-            "config": workload_config(world, path),
+            "config": workload_config(),
+            "parallelism": parallelism(world, path, args.gather),
             "hbm_gbs_per_gpu": rank_bytes(stack.mats, Q8_BLOCK_BYTES_REF) / (ms_per_step * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
@@ -721,17 +875,19 @@ def main():
                                      if dchain is None and path == "head" else
                                      (LAYERS * MEASURED_DRAM_BYTES_LAYER + MEASURED_DRAM_BYTES_HEAD) / world
                                      if dchain is None else MEASURED_CHAIN_TRAFFIC_RATIO * ref_bytes / world),
-                         "traffic_source": ("ncu dram__bytes_read+write of each projection's GEMV "
-                                            "launch, summed per token" +
-                                            (", the lm_head's / N" if path == "head" else ", / N") +
-                                            " (profiles/dram_decode_stack_q8_shapes.md)" if dchain is None
-                                            else "ncu dram bytes of a 4-layer chain launch, scaled "
-                                                 "by weight bytes (profiles/chain_kernel_q8_4layers.md)")},
+                         "traffic_source": ("ncu per-launch DRAM bytes (read + write) of each "
+                                            "projection's GEMV, summed per token" +
+                                            (", the lm_head's / N" if path == "head" else ", / N")
+                                            if dchain is None
+                                            else "ncu DRAM bytes of a 4-layer chain launch, scaled "
+                                                 "by weight bytes")},
             "e2e": e2e,
             "e2e_cpu_abi": e2e_cpu_abi,
+            "e2e_device_api": e2e_dn,
             "neighbours": neighbours,
             "decode_step": decode_step,
             "cpu_baseline": cpu_baseline,
+            "configs": configs,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": ("1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
                                   if dchain is not None else
@@ -747,6 +903,8 @@ def main():
     torch.cuda.synchronize()
     if dchain is not None:
         dchain.close()
+    if fused is not None:
+        fused.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -933,9 +1091,35 @@ CONFIG_CASES = (
     + [("c5", f"lm_head_m{m}", "q8", VOCAB, HIDDEN, m) for m in (1, 2, 4, 8, 16, 32, 64)])
 
 
-def time_linear(torch, L, fmt, rows, cols, n, steps, warmup):
+def device_weights(torch, L, fmt, rows, cols, gen, vision=False):
+    """One matrix of a configuration on the device: Q4_0 nibbles U{0..15} with
+    fp16 scales U[0.002, 0.02] (config 1 / 4), Q8_0 int8 U[-127, 127] with
+    fp16-drawn scales U[0.001, 0.01] widened to f32 (config 2 / 3 / lm_head),
+    or config 5's: bf16 N(0, 0.02) weights quantized to Q8_0 on the device
+    with lab_quantize_q8 semantics (dn_quantize_q8)."""
+    blocks = cols // 32
+    if fmt == "q4":
+        qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
+        sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen).half().view(torch.int16)
+        return qs, sc
+    if vision:
+        w = (torch.randn(rows * cols, device="cuda", generator=gen) * 0.02).bfloat16().float()
+        qs = torch.empty(rows * cols, dtype=torch.int8, device="cuda")
+        sc = torch.empty(rows * blocks, dtype=torch.float32, device="cuda")
+        rc = L.dn_quantize_q8(w.data_ptr(), qs.data_ptr(), sc.data_ptr(), rows, cols,
+                              torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(L.dn_error_string(rc).decode())
+        return qs, sc
+    qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
+    sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen).half().float()
+    return qs, sc
+
+
+def time_linear(torch, L, fmt, rows, cols, n, steps, warmup, vision=False):
     """us per dn_linear launch (mode 1, automatic path, f32 activations in),
-    the operands rotating through copies that exceed twice the L2."""
+    the operands rotating through copies that exceed twice the L2 (weights
+    generated once and copied)."""
     q4 = fmt == "q4"
     blocks = cols // 32
     per_copy = rows * cols // (2 if q4 else 1) + rows * blocks * (2 if q4 else 4) + 4 * n * (cols + rows)
@@ -943,14 +1127,10 @@ def time_linear(torch, L, fmt, rows, cols, n, steps, warmup):
     copies = max(1, -(-2 * l2 // per_copy))
     gen = torch.Generator(device="cuda")
     gen.manual_seed(rows * 31 + cols * 7 + n)
+    qs0, sc0 = device_weights(torch, L, fmt, rows, cols, gen, vision)
     sets = []
-    for _ in range(copies):
-        if q4:
-            qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
-            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen).half().view(torch.int16)
-        else:
-            qs = torch.randint(-127, 128, (rows * cols,), dtype=torch.int8, device="cuda", generator=gen)
-            sc = torch.empty(rows * blocks, device="cuda").uniform_(0.001, 0.01, generator=gen).half().float()
+    for i in range(copies):
+        qs, sc = (qs0, sc0) if i == 0 else (qs0.clone(), sc0.clone())
         sets.append((qs, sc, torch.randn(n * cols, device="cuda", generator=gen),
                      torch.zeros(n * rows, device="cuda")))
     xq = torch.zeros(n * cols, dtype=torch.int8, device="cuda")
@@ -986,6 +1166,51 @@ def time_linear(torch, L, fmt, rows, cols, n, steps, warmup):
     return e0.elapsed_time(e1) * 1e3 / steps, {0: "gemv", 1: "tcgen05", 2: "generic"}.get(path, path), copies
 
 
+CHECK_ROWS = 512  # rows of a case's output checked against the oracle
+
+
+def check_linear(torch, L, oracle, fmt, rows, cols, n, vision=False):
+    """One dn_linear launch (mode 1, automatic path) on seeded inputs, its
+    first CHECK_ROWS rows against the oracle (a row depends only on its own
+    weights): bit for bit on the GEMV, within the reference's 1e-5 bound of
+    the row's absolute-sum scale on the tensor-core GEMM. Returns (path, ok,
+    max relative error)."""
+    from oracle import oracle as orc
+    q4 = fmt == "q4"
+    blocks = cols // 32
+    r = min(rows, CHECK_ROWS)
+    rng = np.random.default_rng(rows + 3 * cols + 7 * n)
+    if vision:
+        hq, hs = oracle.quantize_q8(orc.vision_weights_f32(rng, r, cols), r, cols)
+    else:
+        hq, hs = orc.q4_weights(rng, r, cols) if q4 else orc.q8_weights(rng, r, cols)
+    xs = orc.activations(rng, n, cols)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1)
+    qs, sc = device_weights(torch, L, fmt, rows, cols, gen)
+    qs.view(torch.uint8)[:hq.nbytes] = torch.from_numpy(hq.view(np.uint8)).cuda()
+    sc.view(torch.uint8)[:hs.nbytes] = torch.from_numpy(hs.view(np.uint8)).cuda()
+    x = torch.from_numpy(xs).cuda()
+    xq = torch.zeros(n * cols, dtype=torch.int8, device="cuda")
+    xsc = torch.zeros(n * blocks + 4, device="cuda")
+    ys = torch.full((n * rows,), float("nan"), device="cuda")
+    path = L.dn_linear_path(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), x.data_ptr(), xq.data_ptr(),
+                            rows, cols, n, 1)
+    rc = L.dn_linear(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), x.data_ptr(), xq.data_ptr(),
+                     xsc.data_ptr(), ys.data_ptr(), rows, cols, n, rows, 1, -1, 0,
+                     torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    if rc != 0 or L.dn_device_status(1) != 0:
+        return path, False, None
+    got = ys.view(n, rows)[:, :r].contiguous().cpu().numpy().reshape(-1)
+    if path == 1:
+        ref, mag = oracle.reference_f64(fmt, hq, hs, xs, r, cols, n, 1)
+        err = orc.max_rel_err(got, ref, mag)
+        return path, bool(err < 1e-5), err
+    want, _, _ = oracle.gemm(fmt, hq, hs, xs, r, cols, n, 1)
+    return path, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))), 0.0
+
+
 def cpu_linear_us(ref, fmt, rows, cols, n, threads, budget_s=2.0):
     """us per call of the reference's lab_gemm_q4 / _q8 (mode 1) on this host."""
     from oracle import oracle as orc
@@ -1001,6 +1226,62 @@ def cpu_linear_us(ref, fmt, rows, cols, n, threads, budget_s=2.0):
         ref.gemm(fmt, qs, sc, xs, rows, cols, n, 1, threads, out)
         times.append(time.perf_counter() - t0)
     return statistics.median(times) * 1e6
+
+
+# The configuration cases the default bench line carries ("configs" key):
+# (config, case, fmt, rows, cols, n, vision weights).
+COMPACT_CASES = [("c1", "mlp_up_q4_gemv", "q4", 6144, 2048, 1, False),
+                 ("c2", "gate_q8_gemv", "q8", 6144, 2048, 1, False),
+                 ("c4", "gate_up_q4_m512", "q4", 6144, 2048, 512, False),
+                 ("c5", "qkv_q8_m1024", "q8", 3456, 1152, 1024, True),
+                 ("c5", "lm_head_q8_m16", "q8", VOCAB, HIDDEN, 16, False)]
+
+
+def run_configs_compact(args, torch, L):
+    """Configs 1, 2, 4, 5 and the lm_head sweep in short: per case the GPU time
+    per dn_linear launch (graph-replayed, operands past L2) as HBM GB/s and
+    int8 TOPS against the measured peaks, the reference's CPU kernels on the
+    same case (oracle/_ref, all host threads) and a check of the GPU's output
+    against the oracle outside the timed region."""
+    from oracle import oracle as orc
+    bind_cpu_threads()
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    int8 = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    try:
+        ref = orc.Reference()
+    except FileNotFoundError:
+        ref = None
+    oracle = orc.Oracle()
+    threads = host_threads()
+    out = []
+    for cfg, name, fmt, rows, cols, n, vision in COMPACT_CASES:
+        path, ok, err = check_linear(torch, L, oracle, fmt, rows, cols, n, vision)
+        us, _, copies = time_linear(torch, L, fmt, rows, cols, n, args.config_steps, 3, vision)
+        alg_bytes = rows * cols // 32 * (18 if fmt == "q4" else 34) + 4 * n * (cols + rows)
+        ops = 2.0 * n * rows * cols
+        res = {"config": cfg, "case": name, "fmt": fmt, "rows": rows, "cols": cols, "n": n,
+               "path": {0: "gemv", 1: "tcgen05", 2: "generic"}.get(path, path), "us": us,
+               "gbs_algorithmic": alg_bytes / us / 1e3, "hbm_frac": alg_bytes / us / 1e3 / hbm,
+               "tops": ops / us / 1e6, "int8_frac": ops / us / 1e6 / int8,
+               "check": ("bit-exact with the oracle" if path != 1 else
+                         "max relative error vs the oracle's double reference (bound 1e-5)"),
+               "check_rows": min(rows, CHECK_ROWS), "check_ok": ok, "max_rel_err": err,
+               "weights": "bf16 N(0,0.02) -> lab_quantize_q8" if vision else "config distribution",
+               "copies": copies}
+        if ref is not None:
+            cus = cpu_linear_us(ref, fmt, rows, cols, n, threads, budget_s=1.0)
+            res.update(cpu_reference_us=cus, cpu_threads=threads, gpu_speedup=cus / us)
+        out.append(res)
+    return {"cases": out, "peaks": {"hbm_gbs": hbm, "int8_tops": int8,
+                                    "int8_source": "2 x MEASURED_PEAKS.json bf16_tflops"},
+            "timing": f"{args.config_steps} graph-replayed launches per case, operands rotating past "
+                      "2 x L2, CUDA events; activation quantize included"}
 
 
 def run_configs_workload(args):
@@ -1022,13 +1303,15 @@ def run_configs_workload(args):
     ref = None
     if args.cpu_tokens > 0:
         from oracle import oracle as orc
+        bind_cpu_threads()
         try:
             ref = orc.Reference()
         except FileNotFoundError:
             ref = None
     threads = host_threads()
     for cfg, name, fmt, rows, cols, n in CONFIG_CASES:
-        us, path, copies = time_linear(torch, L, fmt, rows, cols, n, args.steps, max(args.warmup, 3))
+        vision = cfg == "c5" and not name.startswith("lm_head")
+        us, path, copies = time_linear(torch, L, fmt, rows, cols, n, args.steps, max(args.warmup, 3), vision)
         blocks = rows * cols // 32
         alg_bytes = blocks * (18 if fmt == "q4" else 34) + 4 * n * (cols + rows)
         ops = 2.0 * n * rows * cols
@@ -1042,6 +1325,51 @@ def run_configs_workload(args):
             res["cpu_threads"] = threads
             res["gpu_speedup"] = cus / us
         print(json.dumps(res), flush=True)
+
+
+def run_e2e_device_api(args, torch, stack, step, stream, logits_dev, world, device, full_logits):
+    """Token loop through this library's device C-ABI with host buffers: per
+    token x0 is copied in from pinned host memory, the token's launches run
+    (the captured graph of dn_quantize_qa, dn_linear_qa and, on N > 1 GPUs,
+    dn_linear_qa_allgather + dn_peer_wait), and the whole logits are copied
+    back to pinned host memory and synchronized. Host wall clock per token,
+    max over ranks."""
+    steps = args.e2e_steps
+    if steps <= 0:
+        return None
+    x0_h = stack.x0.cpu().pin_memory()
+    logits_h = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
+
+    def one_token():
+        with torch.cuda.stream(stream):
+            stack.x0.copy_(x0_h, non_blocking=True)
+            step()
+            logits_h.copy_(logits_dev, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        one_token()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_token()
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    same = bool(np.array_equal(logits_h.numpy().view(np.uint32), full_logits.cpu().numpy().view(np.uint32)))
+    return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": 4 * HIDDEN,
+            "d2h_bytes_per_step": 4 * VOCAB,
+            "api": "the library's device C-ABI with host buffers: per token x0 copied in from pinned "
+                   "memory, the token's launches (dn_quantize_qa, dn_linear_qa" +
+                   (", dn_linear_qa_allgather, dn_peer_wait" if world > 1 else "") +
+                   ", one CUDA graph), the whole logits copied back and synchronized",
+            "steps": steps, "timing": "host wall clock, max over ranks",
+            "logits_match_device_run": same}
 
 
 def run_e2e(args, stack, L, torch, rank, world, gather, device, full_logits):
@@ -1520,6 +1848,7 @@ def run_lm_head_reference(stack, L):
 
 def run_cpu_baseline(args, stack):
     from oracle import oracle as orc
+    bind_cpu_threads()
     try:
         ref = orc.Reference()
         kind = "reference"
@@ -1531,7 +1860,12 @@ def run_cpu_baseline(args, stack):
     cpu_reference_tokens(ref, hw, x0, threads, 1)  # warm-up (page-in, OpenMP pool)
     sec, logits = cpu_reference_tokens(ref, hw, x0, threads, args.cpu_tokens)
     same = bool(np.array_equal(logits, stack.bufs["lm_head"].cpu().numpy()))
+    # The same stack on one thread (one token: a bounded sample).
+    sec1, logits1 = cpu_reference_tokens(ref, hw, x0, 1, 1)
     return {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+            "cpu_model": cpu_model(), "omp_proc_bind": os.environ.get("OMP_PROC_BIND", "unset"),
+            "threads_1": {"value": 1.0 / sec1, "unit": "tokens/s", "sample": "1 token, 1 thread",
+                          "logits_bit_identical_to_gpu": bool(np.array_equal(logits1, logits))},
             "sample": f"{args.cpu_tokens} tokens of the full stack (113 lab_gemm_q8 mode-1 calls "
                       f"each, OpenMP, OMP_PROC_BIND={os.environ.get('OMP_PROC_BIND', 'unset')})",
             "logits_bit_identical_to_gpu": same}

@@ -608,6 +608,45 @@ int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const u
   return dn::launch_gemv_ex(g, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
 }
 
+int64_t dn_linear_qa_allgather(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
+                               int64_t rows, int64_t cols, int64_t row0, float* const* ys,
+                               int32_t* const* counters, int64_t world, int64_t flags, void* stream) {
+  if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;
+  if (rows < 0 || cols <= 0 || row0 < 0 || xa == nullptr || ys == nullptr || counters == nullptr ||
+      world < 1 || world > dn::kMaxGatherRanks)
+    return DN_ERR_ARGS;
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  dn::GemvArgs g{};
+  g.q4 = format == DN_Q4;
+  g.qs = qs;
+  g.scales = scales;
+  g.xa = xa;
+  g.xa_stride = (cols / 32) * dn::kQABytes;
+  g.ldy = rows;
+  g.rows = rows;
+  g.cols = cols;
+  g.n = 1;
+  g.status = d->status_dev;
+  g.gather_n = (int)world;
+  g.gather_row0 = row0;
+  for (int64_t p = 0; p < world; p++) {
+    g.gather_ys[p] = ys[p];
+    g.gather_cnt[p] = reinterpret_cast<int*>(counters[p]);
+  }
+  return dn::launch_gemv_ex(g, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
+}
+
+int64_t dn_peer_wait(const int32_t* counter, int32_t* expect, int64_t count, void* stream) {
+  if (counter == nullptr || expect == nullptr || count < 0 || count > INT32_MAX / 2) return DN_ERR_ARGS;
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_peer_wait(reinterpret_cast<const int*>(counter), reinterpret_cast<int*>(expect),
+                              (int)count, d->status_dev, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? DN_OK
+             : DN_ERR_CUDA;
+}
+
 int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, void** chain) {
   if ((format != DN_Q8 && format != DN_Q4) || ops == nullptr || chain == nullptr || nops <= 0)
     return DN_ERR_ARGS;

@@ -33,6 +33,8 @@ struct LinearArgs {
 // these from one GEMV's epilogue to the next GEMV's prologue.
 constexpr int kQABytes = 36;
 
+constexpr int kMaxGatherRanks = 8;
+
 struct GemvArgs {
   bool q4;
   const void* qs;
@@ -87,8 +89,24 @@ struct GemvArgs {
   const void* group_qs[4];
   const void* group_scales[4];
   float* group_ys[4];
+  // The all-gather of a row-sharded output fused into the epilogue
+  // (optional; one token, f32 outputs): this product computes rows
+  // gather_row0 .. gather_row0 + rows of the whole output, and stores each
+  // into every rank's copy of it, gather_ys[p] + gather_row0 + row (rank p's
+  // buffer as mapped on this GPU, plain stores over NVLink); then each CTA
+  // adds its tile count to every rank's counter gather_cnt[p], after a
+  // system-scope fence. 0 ranks: no gather.
+  int gather_n;
+  int64_t gather_row0;
+  float* gather_ys[kMaxGatherRanks];
+  int* gather_cnt[kMaxGatherRanks];
 };
 constexpr int kMaxGroups = 4;
+
+// Waits, on the stream, until *cnt has grown by `count` since the previous
+// wait with this `expect` word (device memory holding the value reached last
+// time): one thread, bounded, a timeout recorded in the status word.
+cudaError_t launch_peer_wait(const int* cnt, int* expect, int count, uint32_t* status, cudaStream_t stream);
 
 // RMSNorm of `rows` rows of `cols` values: out = w * (x * r), r =
 // 1 / sqrt(mean(x^2) + eps), added into out with `accumulate`; with qa, the

@@ -674,6 +674,10 @@ int64_t launch_gemv_ex(const GemvArgs& g, cudaStream_t stream, bool pdl) {
   if (!gemv_ex_supported(g)) return kErrUnsupported;
   if (g.rows <= 0 || g.n <= 0) return kOk;
   if (g.n > 65535 * 8) return kErrTooLarge;
+  if (g.gather_n > 0) {  // only the one-token kernel fuses the all-gather
+    if (!gemv1_eligible(g)) return kErrUnsupported;
+    return launch_gemv1(g, stream, pdl);
+  }
   if (gemv1_eligible(g)) {
     const int64_t rc = launch_gemv1(g, stream, pdl);
     if (rc != kErrTooLarge && rc != kErrUnsupported) return rc;

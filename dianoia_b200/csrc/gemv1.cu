@@ -82,7 +82,7 @@ template <bool Q4>
 __host__ __device__ inline Plan1 plan1(int stages, int64_t blocks) {
   Plan1 p;
   p.bar_off = (int64_t)stages * kStageBytes;
-  p.xw_off = gemv::round_up(p.bar_off + 8 * (2 * stages + 3), 128);
+  p.xw_off = gemv::round_up(p.bar_off + 8 * (2 * stages + 4), 128);
   p.xs_off = p.xw_off + blocks * XH<Q4>::kBlock;
   p.am_off = gemv::round_up(p.xs_off + gemv::round_up(blocks, 4) * 4, 16);
   p.stg_off = p.am_off + 16;
@@ -284,6 +284,7 @@ __global__ void __launch_bounds__(kThreads1, 4)
   uint64_t* empty = full + stages;
   uint64_t* epi = empty + stages;
   uint64_t* xbar = epi + 2;
+  uint64_t* gbar = xbar + 1;  // the fused all-gather: every consumer's stores are issued
   uint8_t* xw = smem + sp.xw_off;
   uint8_t* stg = smem + sp.stg_off;
   float* xs = reinterpret_cast<float*>(smem + sp.xs_off);
@@ -298,6 +299,7 @@ __global__ void __launch_bounds__(kThreads1, 4)
     mbar_init(&epi[0], kCThreads);
     mbar_init(&epi[1], kCThreads);
     mbar_init(xbar, 1);
+    mbar_init(gbar, kCThreads);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -418,6 +420,10 @@ __global__ void __launch_bounds__(kThreads1, 4)
     const float y = c.h == 0 ? __fadd_rn(p, o) : __fadd_rn(o, p);
     const int tile_rows = (int)min64(kRows, a.rows - tile * kRows);
     if (c.h == 0 && c.r < tile_rows && a.ys != nullptr) a.ys[tile * kRows + c.r] = y;
+    if (c.h == 0 && c.r < tile_rows) {
+      // The fused all-gather: the row into every rank's copy of the output.
+      for (int p = 0; p < a.gather_n; p++) a.gather_ys[p][a.gather_row0 + tile * kRows + c.r] = y;
+    }
     if (a.ya != nullptr && tile_rows == kRows) {
       // The tile's 32 outputs are one Q8_0 block of the next product's input
       // (lab_quantize_q8 semantics): the two warps' amax meet in shared
@@ -440,6 +446,38 @@ __global__ void __launch_bounds__(kThreads1, 4)
       e++;
     }
   }
+  if (a.gather_n > 0) {
+    // Every consumer's stores of this CTA (a bounded barrier: a warp that
+    // gave up never arrives), then one system-scope fence and the CTA's tile
+    // count into every rank's counter (the waiting side acquires).
+    mbar_arrive(gbar);
+    const bool all = tid >= 32 || gemv::warp_wait(gbar, 0, a.status);
+    if (tid == 0 && all && !abort_flag) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int p = 0; p < a.gather_n; p++)
+        asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(a.gather_cnt[p]), "r"((int)my_tiles)
+                     : "memory");
+    }
+  }
+}
+
+__global__ void peer_wait_kernel(const int* cnt, int* expect, int count, uint32_t* status) {
+  const int target = *expect + count;
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+  if (v - target < 0) {
+    const uint64_t start = globaltimer_ns();
+    for (uint32_t i = 1;; i++) {
+      __nanosleep(64);
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+      if (v - target >= 0) break;
+      if ((i & 63u) == 0 && globaltimer_ns() - start > wait_limit_ns()) {
+        report(status, kStatusPeerTimeout);
+        break;
+      }
+    }
+  }
+  *expect = target;
 }
 
 // DN_WIDE_COPIES=0 loads a stage as four 2-D boxes instead of one 3-D copy.
@@ -509,12 +547,15 @@ int64_t launch1(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   return cudaLaunchKernelExC(&cfg, kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
-// DN_GEMV1=0 routes these products to the general GEMV kernel instead (the
-// same results; for comparing the two).
+// Plain one-token products run on the general GEMV kernel (gemv.cu) unless
+// DN_GEMV1=1: chained the way a decode step chains them, that kernel measured
+// 1704 against this one's 1658 tokens/s on the config-3 stack, although this
+// one is faster launch for launch on one shape. This kernel is the one that
+// fuses the all-gather (gather_n > 0), which it always serves.
 bool gemv1_enabled() {
   static const bool on = [] {
     const char* e = getenv("DN_GEMV1");
-    return e == nullptr || atoi(e) != 0;
+    return e != nullptr && atoi(e) != 0;
   }();
   return on;
 }
@@ -524,7 +565,12 @@ bool gemv1_enabled() {
 // One token, QA input, plain outputs (f32 and/or QA), scales the TMA can
 // address (16-byte aligned arrays, rows a multiple of 16 bytes).
 bool gemv1_eligible(const GemvArgs& g) {
-  if (!gemv1_enabled()) return false;
+  if (!gemv1_enabled() && g.gather_n == 0) return false;
+  if (g.gather_n < 0 || g.gather_n > kMaxGatherRanks) return false;
+  for (int p = 0; p < g.gather_n; p++)
+    if (g.gather_ys[p] == nullptr || g.gather_cnt[p] == nullptr || ((uintptr_t)g.gather_ys[p] & 3) != 0 ||
+        ((uintptr_t)g.gather_cnt[p] & 3) != 0)
+      return false;
   if (g.n != 1 || g.xa == nullptr || g.xs != nullptr || g.groups > 1 || g.qs2 != nullptr ||
       g.glu_out != nullptr || g.res != nullptr || g.norm_w != nullptr || g.xa_out != nullptr)
     return false;
@@ -540,6 +586,11 @@ bool gemv1_eligible(const GemvArgs& g) {
 int64_t launch_gemv1(const GemvArgs& g, cudaStream_t stream, bool pdl) {
   if (g.rows <= 0) return kOk;
   return g.q4 ? launch1<true>(g, stream, pdl) : launch1<false>(g, stream, pdl);
+}
+
+cudaError_t launch_peer_wait(const int* cnt, int* expect, int count, uint32_t* status, cudaStream_t stream) {
+  peer_wait_kernel<<<1, 1, 0, stream>>>(cnt, expect, count, status);
+  return cudaGetLastError();
 }
 
 }  // namespace dn

@@ -411,6 +411,29 @@ typedef struct dn_chain_op {
 /* Validates the ops, encodes their TMA descriptors and copies the op table to
  * device memory (the chain's only allocations); *chain receives a handle. */
 int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, void** chain);
+/* The row-sharded lm_head (or any one-token product on QA input) with the
+ * all-gather of its f32 outputs fused into the product, for N GPUs of one
+ * node (north_star's row-partitioned weights with an all-gather of each
+ * GPU's output slice; the reference shards the LM head's vocabulary rows the
+ * same way, lib/src/shard.dart:12-13). This GPU computes rows row0 .. row0 +
+ * rows of the whole output from its row slice (qs, scales) and stores each
+ * into every rank's copy of the whole output, ys[p] + row0 + row (ys[p]: rank
+ * p's buffer as mapped here - dn_peer_alloc / dn_peer_open memory - the
+ * local one included; plain stores over NVLink), then adds the number of
+ * its 32-row tiles to every rank's counter (counters[p], in the same
+ * regions) after a system-scope fence. A rank's copy is complete once its
+ * counter has grown by the tiles of all ranks: dn_peer_wait. Results equal
+ * dn_linear_qa's rows bit for bit. */
+int64_t dn_linear_qa_allgather(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
+                               int64_t rows, int64_t cols, int64_t row0, float* const* ys,
+                               int32_t* const* counters, int64_t world, int64_t flags, void* stream);
+/* Waits on `stream` (one thread of the GPU, bounded: a timeout sets the
+ * peer-timeout bit of dn_device_status) until *counter has grown by `count`
+ * since the previous wait with the same `expect` word, a device int32 that
+ * holds the count reached last time (zero both before the first wait).
+ * Counters only grow, so nothing is reset between steps. */
+int64_t dn_peer_wait(const int32_t* counter, int32_t* expect, int64_t count, void* stream);
+
 /* Device memory that the other GPUs of this node can map: dn_peer_alloc
  * allocates `bytes` (zeroed) on the current device and writes a
  * DN_PEER_HANDLE_BYTES-byte handle to pass to the other processes;

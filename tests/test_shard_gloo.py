@@ -5,7 +5,8 @@ result equals the unsharded product bit for bit - a row does not depend on the
 split (lab_native.c:550-552). The sharded chain's tiled split must also start
 every slice on a 32-row tile and cover every row exactly once. The head path
 (decoder layers whole on every rank, only the lm_head's rows split) must give
-the unsharded stack's logits bit for bit."""
+the unsharded stack's logits bit for bit, gathered by bench.py's own helper
+(three ranks split the 1000 vocabulary rows unevenly)."""
 import os
 import socket
 
@@ -69,21 +70,26 @@ def _rank_main(rank, world, port, out):
         return r0, r1, x
 
     r0, r1, part = run(True)
+    # The logits gathered by bench.py's own helper (in place, any split).
+    logits = torch.full((vocab,), float("nan"))
+    logits[r0:r1] = torch.from_numpy(part)
+    bench.make_gather(dist, rank, world)(logits)
     parts = [None] * world
     dist.all_gather_object(parts, (r0, r1, part))
     if rank == 0:
         want = run(False)[2]
         got = np.concatenate([p[2] for p in sorted(parts, key=lambda p: p[0])])
         spans = sorted((p[0], p[1]) for p in parts)
-        results.append(("head", "stack", vocab, hidden, spans,
-                        bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))))
+        same = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)) and
+                    np.array_equal(logits.numpy().view(np.uint32), want.view(np.uint32)))
+        results.append(("head", "stack", vocab, hidden, spans, same))
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
         out.put(results)
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 3])
 def test_row_shards_reassemble_bit_exactly(world):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
