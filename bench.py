@@ -674,7 +674,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--config-steps", type=int, default=50,
                     help="launches per case of the configs key (0: leave it out)")
-    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours", "cache"],
+    ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours", "cache", "drain"],
                     default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
@@ -692,6 +692,8 @@ def main():
         return run_gemm_workload(args)
     if args.workload == "configs":
         return run_configs_workload(args)
+    if args.workload == "drain":
+        return run_drain_workload(args)
     if args.workload == "neighbours":
         return run_neighbours_workload(args)
     if args.workload == "cache":
@@ -1282,6 +1284,51 @@ def run_configs_compact(args, torch, L):
                                     "int8_source": "2 x MEASURED_PEAKS.json bf16_tflops"},
             "timing": f"{args.config_steps} graph-replayed launches per case, operands rotating past "
                       "2 x L2, CUDA events; activation quantize included"}
+
+
+def run_drain_workload(args):
+    """The tensor-core GEMM's own ceiling: dn_drain_probe runs only its
+    per-block drain (TMEM load, exact conversion, rank-1 scale product,
+    f32x2 accumulate) on one CTA per SM. Reports output element-blocks drained
+    per clock per SM (SM clock sampled during the run) and the int8 TOPS that
+    rate allows a GEMM (64 ops per element-block), beside the int8 peak."""
+    import torch
+    from dianoia_b200 import _lib
+    L = _lib.lib()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    nst = max(args.steps, 1) * 10
+    out = torch.empty(sms * 576, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    for _ in range(max(args.warmup, 3)):
+        _lib.check(L.dn_drain_probe(sms, nst, out.data_ptr(), stream.cuda_stream), "dn_drain_probe")
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(0) as clocks:
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            _lib.check(L.dn_drain_probe(sms, nst, out.data_ptr(), stream.cuda_stream), "dn_drain_probe")
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e-3)
+    t = min(times)
+    ck = clocks.summary() or {}
+    mhz = float(ck.get("sm_mhz") or 1965.0)
+    eb = sms * 128 * 64 * 4 * nst
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    int8 = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    res = {"metric": "tcgen05 GEMM drain ceiling", "sms": sms, "stages": nst, "seconds": t,
+           "element_blocks_per_clk_per_sm": eb / (t * mhz * 1e6 * sms), "sm_mhz": mhz,
+           "ceiling_tops": eb * 64 / t / 1e12, "int8_peak_tops": int8,
+           "ceiling_frac_of_int8_peak": eb * 64 / t / 1e12 / int8, "clocks": ck,
+           "what": "per block: tcgen05.ld 32x32b.x32, exact int->float (f32x2 add), rank-1 scale "
+                   "product (f32x2 mul), f32x2 fma; 16 drain warps per SM, no MMA, copy or barrier"}
+    print(json.dumps(res), flush=True)
 
 
 def run_configs_workload(args):

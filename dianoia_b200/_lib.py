@@ -80,6 +80,7 @@ SIGNATURES = {
     "dn_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_qa_allgather": (_i64, [_i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _i64, _p]),
     "dn_peer_wait": (_i64, [_p, _p, _i64, _p]),
+    "dn_drain_probe": (_i64, [_i64, _i64, _p, _p]),
     "dn_chain_create": (_i64, [_i64, _p, _i64, _p]),
     "dn_chain_create_sharded": (_i64, [_i64, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "dn_peer_alloc": (_i64, [_i64, _p, _p]),

@@ -637,6 +637,11 @@ int64_t dn_linear_qa_allgather(int64_t format, const void* qs, const void* scale
   return dn::launch_gemv_ex(g, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
 }
 
+int64_t dn_drain_probe(int64_t ctas, int64_t stages, float* out, void* stream) {
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_drain_probe(ctas, stages, out, static_cast<cudaStream_t>(stream));
+}
+
 int64_t dn_peer_wait(const int32_t* counter, int32_t* expect, int64_t count, void* stream) {
   if (counter == nullptr || expect == nullptr || count < 0 || count > INT32_MAX / 2) return DN_ERR_ARGS;
   DeviceState* d = device_state();

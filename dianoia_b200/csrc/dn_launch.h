@@ -258,6 +258,9 @@ int64_t launch_gemv(const LinearArgs& a, cudaStream_t stream, bool pdl);
 int64_t launch_generic(const LinearArgs& a, cudaStream_t stream);
 int64_t launch_gemm_tc(const LinearArgs& a, cudaStream_t stream);
 
+// The tensor-core GEMM's drain step alone, for measuring its ceiling (gemm_tc.cu).
+int64_t launch_drain_probe(int64_t ctas, int64_t nst, float* out, cudaStream_t stream);
+
 // Which path launch_linear would pick (0 gemv, 1 tensor-core gemm, 2 generic).
 int path_for(const LinearArgs& a);
 

@@ -722,7 +722,83 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
+// The drain step alone, for measuring the GEMM's own ceiling: the drain warps
+// of one CTA per SM run the GEMM's per-block step - TMEM load of a block's
+// 32 x 32 int32 tile, exact conversion, rank-1 scale product and f32x2
+// accumulate - over `nst` stages of four blocks, with no MMA, no TMA and no
+// barrier between them (the D slots hold the seed value). Each thread's sums
+// go to out[] so that nothing is optimized away.
+__global__ void __launch_bounds__(TcShape<false>::kThreads, 1)
+    drain_probe_kernel(int nst, float* out) {
+  __shared__ __align__(16) float sx_s[kBlocksPerStage * kTileTok];
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kBlocksPerStage * kTileTok; i += blockDim.x) sx_s[i] = 1.0f + 1e-3f * (float)i;
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  if (warp >= 2 && warp < 2 + kEpiWarps) {
+    const int quarter = warp & 3, sub = (warp - 2) >> 2, parity = sub & 1, col0 = (sub >> 1) * kEpiCols;
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
+#pragma unroll
+    for (int q = 0; q < kSlots; q++)
+#pragma unroll
+      for (int c = 0; c < kEpiCols; c += 32) tmem_fill32(tlane + (uint32_t)(q * kTileTok + c), kSeed);
+    tmem_wait_st();
+    uint64_t acc[kEpiCols / 2];
+#pragma unroll
+    for (int j = 0; j < kEpiCols / 2; j++) acc[j] = 0;
+    int32_t dn[kEpiCols];
+    const float sw = 0.01f + 1e-5f * (float)lane;
+    for (int k = 0; k < nst; k++) {
+      const int slot0 = (k & 1) * kBlocksPerStage;
+#pragma unroll
+      for (int q = parity; q < kBlocksPerStage; q += 2) {
+#pragma unroll
+        for (int c = 0; c < kEpiCols; c += 32)
+          tmem_ld32(tlane + (uint32_t)((slot0 + q) * kTileTok + c), *reinterpret_cast<int32_t(*)[32]>(dn + c));
+#pragma unroll
+        for (int c = 0; c < kEpiCols; c += 32) tmem_wait_ld_regs(*reinterpret_cast<int32_t(*)[32]>(dn + c));
+        const uint64_t sw2 = f2_pack(sw, sw);
+        const float* sxq = sx_s + q * kTileTok + col0;
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4) {
+          const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
+          acc[j / 2] = f2_fma(slot_to_f2<true>(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
+          acc[j / 2 + 1] = f2_fma(slot_to_f2<true>(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
+                                  acc[j / 2 + 1]);
+        }
+      }
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kEpiCols / 2; j++)
+      sum += __uint_as_float((uint32_t)acc[j]) + __uint_as_float((uint32_t)(acc[j] >> 32));
+    out[(int64_t)blockIdx.x * blockDim.x + tid] = sum;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 }  // namespace
+
+// The drain ceiling probe (see drain_probe_kernel): `ctas` CTAs, one per
+// SM, `nst` stages of four blocks each; out holds ctas x kThreads floats.
+// Each stage is 128 weight rows x 64 tokens x 4 blocks per CTA.
+int64_t launch_drain_probe(int64_t ctas, int64_t nst, float* out, cudaStream_t stream) {
+  if (ctas <= 0 || nst <= 0 || out == nullptr) return kErrArgs;
+  drain_probe_kernel<<<(unsigned)ctas, TcShape<false>::kThreads, 0, stream>>>((int)nst, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
 
 // The tensor-core path needs 16-byte aligned weights and quantized
 // activations (TMA), cols a multiple of 32, and the quantized activations

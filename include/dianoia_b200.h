@@ -497,6 +497,16 @@ int64_t dn_linear_noalloc(int64_t format, const void* qs, const void* scales, co
  * covers. No counterpart in the reference. */
 int64_t dn_linear_noalloc_status(int64_t clear);
 
+/* Measurement only: the tensor-core GEMM's drain step by itself - per block
+ * a TMEM load of the 128 x 64 int32 tile, the exact int -> float
+ * conversion, the rank-1 scale product and the f32x2 accumulate, the
+ * per-32-block work that exact reference semantics put on the CUDA cores
+ * (lab_native.c:456-466, 987-1002) - with no MMA, copy or barrier: `ctas`
+ * CTAs (one per SM) each run `stages` stages of 4 blocks of 128 x 64
+ * elements; out receives ctas x 576 floats. Timing it gives the element-
+ * blocks per clock an SM can drain, the GEMM's own ceiling. */
+int64_t dn_drain_probe(int64_t ctas, int64_t stages, float* out, void* stream);
+
 /* The calling thread's last error from a lab_* call (DN_OK if none), cleared
  * by reading. */
 int64_t dn_last_error(void);
