@@ -672,6 +672,9 @@ def main():
     ap.add_argument("--context", type=int, default=1024,
                     help="KV-cache position of the whole decode step (with attention)")
     ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--sharded", action="store_true",
+                    help="--workload configs: the row-sharded form (config 5 and the lm_head sweep), "
+                         "also on one GPU (the N = 1 point of the same measurement)")
     ap.add_argument("--config-steps", type=int, default=50,
                     help="launches per case of the configs key (0: leave it out)")
     ap.add_argument("--workload", choices=["stack", "gemv", "gemm", "configs", "neighbours", "cache", "drain"],
@@ -691,6 +694,10 @@ def main():
     if args.workload == "gemm":
         return run_gemm_workload(args)
     if args.workload == "configs":
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.sharded:
+            return run_configs_sharded(args, int(os.environ.get("RANK", "0")),
+                                       int(os.environ.get("WORLD_SIZE", "1")),
+                                       int(os.environ.get("LOCAL_RANK", "0")))
         return run_configs_workload(args)
     if args.workload == "drain":
         return run_drain_workload(args)
@@ -1329,6 +1336,109 @@ def run_drain_workload(args):
            "what": "per block: tcgen05.ld 32x32b.x32, exact int->float (f32x2 add), rank-1 scale "
                    "product (f32x2 mul), f32x2 fma; 16 drain warps per SM, no MMA, copy or barrier"}
     print(json.dumps(res), flush=True)
+
+
+# Config 5 and the lm_head M sweep at N GPUs (row-sharded weights, the
+# output blocks all-gathered): (case, fmt, rows, cols, n, vision weights).
+SHARDED_CASES = ([(f"vision_{nm}_m1024", "q8", r, c, 1024, True)
+                  for nm, r, c in [("qkv", 3456, 1152), ("o", 1152, 1152), ("fc1", 4304, 1152),
+                                   ("fc2", 1152, 4320)]]
+                 + [(f"lm_head_m{m}", "q8", VOCAB, HIDDEN, m, False) for m in (1, 2, 4, 8, 16, 32, 64)])
+
+
+def run_configs_sharded(args, rank, world, local_rank):
+    """Configs 5 and the lm_head sweep on N GPUs: each rank holds its row
+    slice of the weights (rows * p // N ..), runs dn_linear on the whole batch
+    of tokens, and an NCCL all-gather of the output column blocks rebuilds
+    Y[n, rows] on every rank (padded to the widest slice, then laid out
+    token-major by one copy). Both are inside the timed region; time is the
+    max over ranks. One JSON line per case from rank 0."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from dianoia_b200 import _lib
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    L = _lib.lib()
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    int8 = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    stream = torch.cuda.Stream(device=device)
+    for name, fmt, rows, cols, n, vision in SHARDED_CASES:
+        r0, r1 = row_split(rows, rank, world, False)
+        rr = r1 - r0
+        width = max(row_split(rows, p, world, False)[1] - row_split(rows, p, world, False)[0]
+                    for p in range(world))
+        blocks = cols // 32
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1000 + rank)
+        qs, sc = device_weights(torch, L, fmt, rr, cols, gen, vision)
+        xs = torch.randn(n * cols, device=device, generator=torch.Generator(device=device).manual_seed(7))
+        xq = torch.zeros(n * cols, dtype=torch.int8, device=device)
+        xsc = torch.zeros(n * blocks + 4, device=device)
+        ys = torch.zeros(n * width, device=device)  # [n, width]: this rank's block, padded
+        gathered = torch.empty(world * n * width, device=device)
+        full = torch.empty(n * rows, device=device)
+        spans = [row_split(rows, p, world, False) for p in range(world)]
+
+        def step():
+            rc = L.dn_linear(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
+                             xq.data_ptr(), xsc.data_ptr(), ys.data_ptr(), rr, cols, n, width, 1, -1, 0,
+                             stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(L.dn_error_string(rc).decode())
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, ys)
+                g = gathered.view(world, n, width)
+                fv = full.view(n, rows)
+                for p, (a, b) in enumerate(spans):
+                    fv[:, a:b].copy_(g[p, :, :b - a])
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        steps = max(args.steps, 1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / steps], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+        ops = 2.0 * n * rows * cols
+        wbytes = rows * blocks * 34
+        if rank == 0:
+            print(json.dumps({"case": name, "n_gpus": world, "fmt": fmt, "rows": rows, "cols": cols, "n": n,
+                              "rows_per_gpu": width, "us": us, "tops": ops / us / 1e6,
+                              "int8_frac_per_gpu": ops / us / 1e6 / (int8 * world),
+                              "weight_gbs": wbytes / us / 1e3,
+                              "hbm_frac_per_gpu": wbytes / us / 1e3 / (hbm * world),
+                              "includes": "dn_linear on each rank's row slice (activation quantize "
+                                          "included) + NCCL all-gather of the output blocks + "
+                                          "token-major layout copy" if world > 1 else "dn_linear",
+                              "weights": "bf16 N(0,0.02) -> lab_quantize_q8" if vision else "config distribution",
+                              "timing": f"{steps} launches, CUDA events, max over ranks; operands L2-resident "
+                                        "between launches (one copy per rank)"}), flush=True)
+        del qs, sc, xs, xq, xsc, ys, gathered, full
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_configs_workload(args):
