@@ -319,6 +319,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
         prefetch_tmap(&tsx);
       }
     }
+    // Launched as a programmatic dependent of the activation quantize: the
+    // CTA's setup above overlapped it; the quantized activations and their
+    // scales are read only after it completed.
+    pdl_wait();
     __syncwarp();
     int k = 0, s = 0;
     uint32_t eph = 1;  // parity of empty[s] to wait for, from the ring's second pass on
@@ -718,8 +722,19 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, tma_scales ? 1 : 0};
   const dim3 grid((unsigned)((a.rows + kTileRows - 1) / kTileRows),
                   (unsigned)((a.n + kTileTok - 1) / kTileTok), 1);
-  kern<<<grid, S::kThreads, smem, stream>>>(t, stages, tw, tx, tsw, tsx);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(S::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int nstages = stages;
+  void* params[] = {&t, &nstages, &tw, &tx, &tsw, &tsx};
+  return cudaLaunchKernelExC(&cfg, (const void*)kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
 // The drain step alone, for measuring the GEMM's own ceiling: the drain warps
