@@ -88,6 +88,7 @@ struct TcArgs {
   int64_t rows, cols, n, ldy;
   uint32_t* status;
   int tma_scales;  // scales arrive by TMA (tsw, tsx) rather than cp.async
+  int64_t row_tiles, tiles;  // the narrow kernel's tile walk
 };
 
 // ----------------------------------------------------------- tcgen05 PTX
@@ -737,6 +738,573 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
   return cudaLaunchKernelExC(&cfg, (const void*)kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
+// ------------------------------------------------------------ narrow tiles
+//
+// Few tokens (the lm_head M sweep, a short prompt): the 64-token tile leaves
+// TMEM room for two stages only, and at one handshake round trip per two
+// stages (~2 k cycles each) the kernel streams far below HBM speed however
+// little there is to compute. A narrow tile of TOK = 16 or 32 tokens leaves
+// room for 512 / TOK D slots = 8 or 4 stages in flight, so the round trip
+// hides behind the weight stream. The kernel is persistent (one CTA per SM
+// walks tiles blockIdx.x, + gridDim.x, ...; every ring runs on across
+// tiles) and its drain is stage-parallel: drain warp (quarter, sub) takes
+// the stages g with g % 4 == sub, all 4 blocks x TOK tokens of them, so the
+// four subs of a quarter work on different stages and meet only at a tile's
+// end. There each warp leaves its partial sums in shared memory, and the
+// producer warp, which otherwise waits for free stages, adds the four subs'
+// sums and writes the tile. Roles otherwise as in gemm_tc_kernel: warp 0
+// producer, warp 1 MMA issuer (and the activation-scale transpose), warps
+// 2-17 drain, warps 18-19 (Q4) nibble expansion.
+template <bool Q4, int TOK>
+struct NarrowShape {
+  static constexpr int kSlots = (int)kTmemCols / TOK;
+  static constexpr int kLookahead = kSlots / kBlocksPerStage;  // stages TMEM can hold: 8 or 4
+  static constexpr int kWarps = 2 + kEpiWarps + (Q4 ? kConvWarps : 0);
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kBBytes = TOK * kStageK;
+  static constexpr int kSxBytes = kBlocksPerStage * TOK * 4;
+  static constexpr int kRawOff = kABytes + kBBytes;
+  static constexpr int kSxOff = kRawOff + (Q4 ? kRawBytes : 0);
+  static constexpr int kSwOff = kSxOff + kSxBytes;
+  static constexpr int kSxbOff = kSwOff + kSwBytes;
+  static constexpr int kStageBytes = (kSxbOff + kSxBytes + 1023) / 1024 * 1024;
+  static constexpr int kXchgBytes = 4 * kTileRows * TOK * 4;  // each sub's sums of a tile
+  static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TOK >> 3) << 17) |
+                                     ((uint32_t)(kTileRows >> 4) << 24);
+  static_assert(kLookahead % 4 == 0, "each sub owns whole slot groups");
+};
+
+// 32 lanes x TOK consecutive 32-bit TMEM columns.
+template <int TOK>
+__device__ __forceinline__ void tmem_ld_tok(uint32_t taddr, int32_t (&v)[TOK]);
+template <>
+__device__ __forceinline__ void tmem_ld_tok<32>(uint32_t taddr, int32_t (&v)[32]) {
+  tmem_ld32(taddr, v);
+}
+template <>
+__device__ __forceinline__ void tmem_ld_tok<16>(uint32_t taddr, int32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+template <int TOK>
+__device__ __forceinline__ void tmem_wait_ld_tok(int32_t (&v)[TOK]);
+template <>
+__device__ __forceinline__ void tmem_wait_ld_tok<32>(int32_t (&v)[32]) {
+  tmem_wait_ld_regs(v);
+}
+template <>
+__device__ __forceinline__ void tmem_wait_ld_tok<16>(int32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
+        "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]),
+        "+r"(v[14]), "+r"(v[15])
+      :
+      : "memory");
+}
+// TMEM columns set to the seed: TOK of them for the calling warp's 32 lanes.
+template <int TOK>
+__device__ __forceinline__ void tmem_fill_tok(uint32_t taddr) {
+#pragma unroll
+  for (int c = 0; c < TOK; c += 8)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(
+                     taddr + (uint32_t)c),
+                 "r"(kSeed)
+                 : "memory");
+}
+// Non-blocking probe of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+template <bool Q4, int TOK>
+__global__ void __launch_bounds__(NarrowShape<Q4, TOK>::kThreads, 1)
+    gemm_narrow_kernel(const TcArgs a, const int stages, const int L, const __grid_constant__ CUtensorMap tw,
+                       const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tsw,
+                       const __grid_constant__ CUtensorMap tsx) {
+  using S = NarrowShape<Q4, TOK>;
+  // L: stages held in TMEM (slot groups of 4 D slots), 4 or 8; at most the
+  // ring's stage count, so a stage's `tfree` phase is waited for before
+  // the ring slot's next use can complete it again.
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
+  float* xchg = reinterpret_cast<float*>(smem + (int64_t)stages * S::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)stages * S::kStageBytes + S::kXchgBytes);
+  uint64_t* conv = full + stages;
+  uint64_t* empty = conv + stages;
+  uint64_t* dready = empty + stages;
+  uint64_t* tfree = dready + stages;
+  uint64_t* tinit = tfree + stages;
+  uint64_t* done = tinit + 1;
+  uint64_t* xbar = done + 1;
+  uint64_t* xfree = xbar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfree + 1);
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t blocks = a.cols / kBlock;
+  const int nst = (int)((blocks + kBlocksPerStage - 1) / kBlocksPerStage);
+  auto stage_a = [&](int s) { return smem + (int64_t)s * S::kStageBytes; };
+  auto stage_b = [&](int s) { return smem + (int64_t)s * S::kStageBytes + kABytes; };
+  auto stage_raw = [&](int s) { return smem + (int64_t)s * S::kStageBytes + S::kRawOff; };
+  auto stage_sx = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSxOff); };
+  auto stage_sw = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSwOff); };
+  auto stage_sxb = [&](int s) { return reinterpret_cast<float*>(smem + (int64_t)s * S::kStageBytes + S::kSxbOff); };
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; s++) {
+      mbar_init(&full[s], 1);                // TMA bytes
+      mbar_init(&conv[s], kConvWarps * 32);  // (Q4) the stage's weights expanded
+      // The stage's drain sub (4 warps) is done with its scales; the MMAs
+      // that read its operands completed before that sub saw `dready`.
+      mbar_init(&empty[s], 4 * 32);
+      // The stage's MMAs have completed and the MMA warp's lanes have written
+      // its block-major activation scales.
+      mbar_init(&dready[s], 1 + 32);
+      // The stage's drain sub has read (and, Q4, seeded again) its D slots.
+      mbar_init(&tfree[s], 4 * 32);
+    }
+    mbar_init(tinit, kEpiWarps * 32);
+    mbar_init(done, 1);
+    mbar_init(xbar, kEpiWarps * 32);  // every drain lane has left a tile's partial sums
+    mbar_init(xfree, 32);             // the producer has written that tile's outputs
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tw);
+      prefetch_tmap(&tx);
+      prefetch_tmap(&tsw);
+      prefetch_tmap(&tsx);
+    }
+    // A programmatic dependent of the activation quantize: only the copies
+    // below wait for it.
+    pdl_wait();
+    __syncwarp();
+    // Tile outputs: the oldest tile whose sums are not written yet.
+    int64_t ep_tile = blockIdx.x;
+    uint32_t ep_it = 0;
+    const bool vec_y = (a.ldy & 3) == 0 && ((uintptr_t)a.ys & 15) == 0;
+    auto finish_tile = [&]() {
+      // Every lane observes the completed phase itself (no wait: it is).
+      mbar_wait_bounded(xbar, ep_it & 1u, a.status, kStatusMmaTimeout);
+      const int64_t row0 = (ep_tile % a.row_tiles) * kTileRows;
+      const int64_t tok0 = (ep_tile / a.row_tiles) * TOK;
+      const int64_t r = row0 + 4 * lane;
+      // The four subs' sums, token-major: a lane's 4 rows are 16 bytes.
+      const float4* p = reinterpret_cast<const float4*>(xchg) + lane;
+      constexpr int kSub = TOK * kTileRows / 4;  // float4s per sub
+      for (int t = 0; t < TOK; t++) {
+        const int64_t tok = tok0 + t;
+        if (tok >= a.n) break;
+        const float4 u0 = p[t * (kTileRows / 4)], u1 = p[kSub + t * (kTileRows / 4)];
+        const float4 u2 = p[2 * kSub + t * (kTileRows / 4)], u3 = p[3 * kSub + t * (kTileRows / 4)];
+        const float4 y = make_float4(__fadd_rn(__fadd_rn(u0.x, u1.x), __fadd_rn(u2.x, u3.x)),
+                                     __fadd_rn(__fadd_rn(u0.y, u1.y), __fadd_rn(u2.y, u3.y)),
+                                     __fadd_rn(__fadd_rn(u0.z, u1.z), __fadd_rn(u2.z, u3.z)),
+                                     __fadd_rn(__fadd_rn(u0.w, u1.w), __fadd_rn(u2.w, u3.w)));
+        float* dst = a.ys + tok * a.ldy + r;
+        if (vec_y && r + 3 < a.rows) {
+          *reinterpret_cast<float4*>(dst) = y;
+        } else {
+          if (r < a.rows) dst[0] = y.x;
+          if (r + 1 < a.rows) dst[1] = y.y;
+          if (r + 2 < a.rows) dst[2] = y.z;
+          if (r + 3 < a.rows) dst[3] = y.w;
+        }
+      }
+      __syncwarp();
+      mbar_arrive(xfree);
+      ep_it++;
+      ep_tile += gridDim.x;
+    };
+    int64_t g = 0;
+    int s = 0;
+    uint32_t eph = 1;  // parity of empty[s] to wait for, from the ring's second pass on
+    bool stop = false;
+    for (int64_t tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x) {
+      const int64_t row0 = (tile % a.row_tiles) * kTileRows;
+      const int64_t tok0 = (tile / a.row_tiles) * TOK;
+      for (int k = 0; k < nst; k++, g++) {
+        if (g >= stages) {
+          // Wait for the stage to come free (sleeping in the wait, not
+          // spinning); meanwhile write any tile whose sums are complete - the
+          // drain needs that buffer back before it can finish its next tile.
+          // Lane 0 probes and the warp follows its decision.
+          bool got = false;
+          const uint64_t t_start = globaltimer_ns();
+          for (;;) {
+            int what = 0;  // 1: stage free, 2: give up, 3: a tile to write
+            if (lane == 0) {
+              if (abort_flag) {
+                what = 2;
+              } else if (mbar_try_wait_sleep(&empty[s], eph, 1000u)) {
+                what = 1;
+              } else if (ep_tile < tile && mbar_test(xbar, ep_it & 1u)) {
+                what = 3;
+              } else if (globaltimer_ns() - t_start > wait_limit_ns()) {
+                report(a.status, kStatusMmaTimeout);
+                what = 2;
+              }
+            }
+            what = __shfl_sync(0xffffffffu, what, 0);
+            if (what == 1) {
+              got = true;
+              break;
+            }
+            if (what == 2) break;
+            if (what == 3) finish_tile();
+          }
+          if (!__all_sync(0xffffffffu, got)) {
+            abort_flag = 1;
+            stop = true;
+            break;
+          }
+        }
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&full[s], (uint32_t)((Q4 ? kRawBytes : kABytes) + S::kBBytes + S::kSxBytes + kSwBytes));
+          if (Q4)
+            tma_load_2d(stage_raw(s), &tw, k * (kStageK / 2), (int32_t)row0, &full[s]);
+          else
+            tma_load_2d(stage_a(s), &tw, k * kStageK, (int32_t)row0, &full[s]);
+          tma_load_2d(stage_b(s), &tx, k * kStageK, (int32_t)tok0, &full[s]);
+          // Weight scales: Q8 the stage's 4 f32 per row; Q4 the 8 fp16 per
+          // row of the pair of stages holding this one, of which the drain
+          // reads its half. Activation scales token-major: TOK x 4.
+          tma_load_2d(stage_sw(s), &tsw, Q4 ? (k >> 1) * 2 * kBlocksPerStage : k * kBlocksPerStage,
+                      (int32_t)row0, &full[s]);
+          tma_load_2d(stage_sx(s), &tsx, k * kBlocksPerStage, (int32_t)tok0, &full[s]);
+        }
+        __syncwarp();
+        if (++s == stages) {
+          s = 0;
+          eph ^= 1u;
+        }
+      }
+    }
+    while (!stop && ep_tile < a.tiles) {
+      const bool got = !abort_flag && mbar_wait_bounded(xbar, ep_it & 1u, a.status, kStatusMmaTimeout);
+      if (!__all_sync(0xffffffffu, got)) {
+        abort_flag = 1;
+        break;
+      }
+      finish_tile();
+    }
+    if (abort_flag && lane == 0) {
+      // Let the copies already issued land before the CTA's memory goes.
+      for (int64_t j = g - 1; j >= 0 && j >= g - stages; j--)
+        mbar_wait_bounded(&full[j % stages], (uint32_t)(j / stages) & 1u, a.status, kStatusTmaTimeout);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    // Stage g's block q goes to D slot 4 * (g % L) + q.
+    const uint32_t smem0 = smem_u32(smem);
+    int s = 0, sl = 0;  // ring indices of stages g and g - L
+    uint32_t ph = 0, phl = 0;
+    int grp = 0;        // g % L
+    int64_t g = 0;
+    bool stop = false;
+    for (int64_t tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x) {
+      for (int k = 0; k < nst; k++, g++) {
+        bool ok = !abort_flag && mbar_wait_bounded(&full[s], ph, a.status, kStatusTmaTimeout);
+        if (Q4) ok = ok && mbar_wait_bounded(&conv[s], ph, a.status, kStatusTmaTimeout);
+        if (!__all_sync(0xffffffffu, ok)) {
+          abort_flag = 1;
+          stop = true;
+          break;
+        }
+        // Activation scales [TOK tokens][4 blocks] -> [4 blocks][TOK tokens],
+        // so a drain warp reads four tokens of one block in one 16-byte load.
+        if (lane < TOK) {
+          const float4 v = reinterpret_cast<const float4*>(stage_sx(s))[lane];
+          float* dst = stage_sxb(s);
+          dst[0 * TOK + lane] = v.x;
+          dst[1 * TOK + lane] = v.y;
+          dst[2 * TOK + lane] = v.z;
+          dst[3 * TOK + lane] = v.w;
+        }
+        mbar_arrive(&dready[s]);
+        if (g == 0) ok = ok && mbar_wait_bounded(tinit, 0, a.status, kStatusMmaTimeout);
+        if (g >= L) {
+          // The slot group held stage g - L's blocks: free (and seeded
+          // again) once that stage's drain sub has read them.
+          ok = ok && mbar_wait_bounded(&tfree[sl], phl, a.status, kStatusMmaTimeout);
+          if (++sl == stages) {
+            sl = 0;
+            phl ^= 1u;
+          }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+          abort_flag = 1;
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem0 + (uint32_t)s * (uint32_t)S::kStageBytes;
+        const uint64_t ad = sw128_desc(a_addr), bd = sw128_desc(a_addr + kABytes);
+        const int nq = (int)min64(kBlocksPerStage, blocks - (int64_t)k * kBlocksPerStage);
+        if (elect_one()) {
+          const uint32_t d0 = tmem + (uint32_t)(grp * kBlocksPerStage * TOK);
+#pragma unroll
+          for (int q = 0; q < kBlocksPerStage; q++) {
+            // Every slot holds the seed 0x4B400000; the MMA adds the dot.
+            if (q < nq)
+              mma_i8(d0 + (uint32_t)(q * TOK), ad + (uint64_t)(2 * q), bd + (uint64_t)(2 * q), S::kIdesc, 1u);
+          }
+          mma_commit(&dready[s]);  // the drain may read the stage's D slots
+        }
+        __syncwarp();
+        grp = grp + 1 == L ? 0 : grp + 1;
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    if (elect_one()) mma_commit(done);
+    __syncwarp();
+    mbar_wait_bounded(done, 0, a.status, kStatusMmaTimeout);
+  } else if (warp < 2 + kEpiWarps) {
+    // ------------------------------------------------------------ drain
+    const int quarter = warp & 3;               // TMEM lanes this warp may access
+    const int sub = (warp - 2) >> 2;            // 0 .. 3: the stages g with g % 4 == sub
+    const int row_local = quarter * 32 + lane;
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint64_t acc[TOK / 2];                      // f32 pairs: tokens 2i, 2i + 1
+    int32_t dn[TOK];
+    // Seed this warp's part of its slot groups (sub, sub + 4, ...).
+#pragma unroll
+    for (int gg = sub; gg < L; gg += 4)
+#pragma unroll
+      for (int q = 0; q < kBlocksPerStage; q++) tmem_fill_tok<TOK>(tlane + (uint32_t)((gg * kBlocksPerStage + q) * TOK));
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(tinit);
+    int st = 0, grp = 0, g4 = 0;  // ring index, g % L, g % 4
+    uint32_t sph = 0;
+    uint32_t it = 0;  // tiles done by this CTA
+    bool stop = false;
+    for (int64_t tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x, it++) {
+#pragma unroll
+      for (int j = 0; j < TOK / 2; j++) acc[j] = 0;
+      for (int k = 0; k < nst; k++) {
+        if (g4 == sub) {
+          bool got = !abort_flag && mbar_wait_bounded(&dready[st], sph, a.status, kStatusMmaTimeout);
+          if (!__all_sync(0xffffffffu, got)) {
+            abort_flag = 1;
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          // This row's weight scales of the stage, read per block (Q4: 8 fp16
+          // per row covering stages 2j and 2j + 1).
+          const float* sw32 = stage_sw(st) + row_local * kBlocksPerStage;
+          const uint16_t* sw16 = reinterpret_cast<const uint16_t*>(stage_sw(st)) + row_local * 2 * kBlocksPerStage +
+                                 (k & 1) * kBlocksPerStage;
+          const int nq = (int)min64(kBlocksPerStage, blocks - (int64_t)k * kBlocksPerStage);
+          const float* sxs = stage_sxb(st);
+          const uint32_t slots = tlane + (uint32_t)(grp * kBlocksPerStage * TOK);
+#pragma unroll
+          for (int q = 0; q < kBlocksPerStage; q++) {
+            if (q < nq) {
+              const uint32_t slot = slots + (uint32_t)(q * TOK);
+              tmem_ld_tok<TOK>(slot, dn);
+              tmem_wait_ld_tok<TOK>(dn);
+              tmem_fill_tok<TOK>(slot);  // seed for the slot's next block
+              if (q == nq - 1) {
+                // The whole slot group is in registers or done: back to the MMA.
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&tfree[st]);
+              }
+              const float sw = Q4 ? half_bits_to_float(sw16[q]) : sw32[q];
+              const uint64_t sw2 = f2_pack(sw, sw);
+              const float* sxq = sxs + q * TOK;
+#pragma unroll
+              for (int j = 0; j < TOK; j += 4) {
+                const float4 x4 = *reinterpret_cast<const float4*>(sxq + j);
+                // acc += f32(d) * f32(sw * sx), as the reference's per-block step.
+                acc[j / 2] = f2_fma(slot_to_f2<true>(dn[j], dn[j + 1]), f2_mul(sw2, f2_pack(x4.x, x4.y)), acc[j / 2]);
+                acc[j / 2 + 1] = f2_fma(slot_to_f2<true>(dn[j + 2], dn[j + 3]), f2_mul(sw2, f2_pack(x4.z, x4.w)),
+                                        acc[j / 2 + 1]);
+              }
+            }
+          }
+          mbar_arrive(&empty[st]);  // every lane: done with the stage's scales
+        }
+        grp = grp + 1 == L ? 0 : grp + 1;
+        g4 = (g4 + 1) & 3;
+        if (++st == stages) {
+          st = 0;
+          sph ^= 1u;
+        }
+      }
+      if (stop) break;
+      // This sub's partial sums of the tile, token-major (a warp's stores hit
+      // 32 banks), once the producer has written the previous tile's.
+      const bool got = it == 0 || (!abort_flag && mbar_wait_bounded(xfree, (it - 1) & 1u, a.status, kStatusMmaTimeout));
+      if (!__all_sync(0xffffffffu, got)) {
+        abort_flag = 1;
+        break;
+      }
+      float* x = xchg + (int64_t)sub * TOK * kTileRows + row_local;
+#pragma unroll
+      for (int j = 0; j < TOK / 2; j++) {
+        x[(2 * j) * kTileRows] = __uint_as_float((uint32_t)acc[j]);
+        x[(2 * j + 1) * kTileRows] = __uint_as_float((uint32_t)(acc[j] >> 32));
+      }
+      mbar_arrive(xbar);
+    }
+  } else {
+    // ------------------------------------------------------------ Q4 expansion
+    const int ct = tid - (2 + kEpiWarps) * 32;  // 0 .. 63
+    int s = 0;
+    uint32_t ph = 0;
+    bool stop = false;
+    for (int64_t tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x) {
+      for (int k = 0; k < nst; k++) {
+        if (!wait_tc(&full[s], ph, a.status, kStatusTmaTimeout, &abort_flag)) {
+          stop = true;
+          break;
+        }
+        const uint8_t* raw = stage_raw(s);
+        uint8_t* dst = stage_a(s);
+        // One (row, block) per task: 16 nibble bytes -> two swizzled 16-byte
+        // chunks of int8 (q - 8): low nibbles are weights 0..15 of the block,
+        // high nibbles weights 16..31 (GGUF order).
+        for (int task = ct; task < kTileRows * kBlocksPerStage; task += kConvWarps * 32) {
+          const int r = task >> 2, q = task & 3;
+          const uint4 v = *reinterpret_cast<const uint4*>(raw + r * (kStageK / 2) + q * 16);
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            // (n & 15) + 0x78, then ^ 0x80, is n - 8 as a two's-complement byte.
+            lo[i] = ((wv[i] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            hi[i] = (((wv[i] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+          }
+          uint8_t* line = dst + (r >> 3) * 1024 + (r & 7) * 128;
+          *reinterpret_cast<uint4*>(line + (((2 * q) ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(line + (((2 * q + 1) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
+        mbar_arrive(&conv[s]);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& c = counts[dev & 63];
+  if (c == 0 && cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) c = 0;
+  return c > 0 ? c : 148;
+}
+
+// The narrow kernel needs the scales by TMA (blocks a multiple of 4 for Q8,
+// 8 for Q4; 16-byte aligned scale arrays).
+template <bool Q4, int TOK>
+int64_t launch_narrow(const LinearArgs& a, cudaStream_t stream) {
+  using S = NarrowShape<Q4, TOK>;
+  const int64_t blocks = a.cols / kBlock;
+  if (blocks % (Q4 ? 8 : 4) != 0 || ((uintptr_t)a.scales & 15) != 0 || ((uintptr_t)a.xsc & 15) != 0)
+    return kErrUnsupported;
+  constexpr int kMaxStages = 12;
+  // Barrier rings (full, conv, empty, dready, tfree), tinit, done, xbar, xfree,
+  // the TMEM slot address.
+  const int64_t bar_bytes = 8 * (5 * kMaxStages + 4) + 16;
+  int stages = (int)((kMaxSmemTc - 1024 - S::kXchgBytes - bar_bytes) / S::kStageBytes);
+  stages = stages > kMaxStages ? kMaxStages : stages;
+  if (stages < 4) return kErrTooLarge;
+  // Stages in TMEM: all it holds when the ring has as many stages, else 4.
+  int lookahead = stages >= S::kLookahead ? S::kLookahead : 4;
+  const size_t smem = 1024 + (size_t)stages * S::kStageBytes + S::kXchgBytes + (size_t)bar_bytes;
+  CUtensorMap tw, tx, tsw, tsx;
+  if (Q4) {
+    if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)blocks * 16,
+                        (uint64_t)a.rows, (uint64_t)blocks * 16, kStageK / 2, kTileRows, false))
+      return kErrUnsupported;
+  } else {
+    if (!encode_tmap_2d(&tw, a.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)blocks * 32,
+                        (uint64_t)a.rows, (uint64_t)blocks * 32, kStageK, kTileRows, true))
+      return kErrUnsupported;
+  }
+  if (!encode_tmap_2d(&tx, a.xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)a.cols, (uint64_t)a.n,
+                      (uint64_t)a.cols, kStageK, TOK, true))
+    return kErrUnsupported;
+  const bool ok_w =
+      Q4 ? encode_tmap_2d(&tsw, a.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)blocks,
+                          (uint64_t)a.rows, (uint64_t)blocks * 2, 2 * kBlocksPerStage, kTileRows, false)
+         : encode_tmap_2d(&tsw, a.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)blocks,
+                          (uint64_t)a.rows, (uint64_t)blocks * 4, kBlocksPerStage, kTileRows, false);
+  if (!ok_w || !encode_tmap_2d(&tsx, a.xsc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)blocks,
+                               (uint64_t)a.n, (uint64_t)blocks * 4, kBlocksPerStage, TOK, false))
+    return kErrUnsupported;
+  auto kern = gemm_narrow_kernel<Q4, TOK>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemTc) != cudaSuccess)
+      return kErrCuda;
+    configured[dev & 63] = true;
+  }
+  const int64_t row_tiles = (a.rows + kTileRows - 1) / kTileRows;
+  const int64_t tiles = row_tiles * ((a.n + TOK - 1) / TOK);
+  TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, 1, row_tiles, tiles};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)min64(tiles, (int64_t)sm_count()), 1, 1);
+  cfg.blockDim = dim3(S::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int nstages = stages;
+  void* params[] = {&t, &nstages, &lookahead, &tw, &tx, &tsw, &tsx};
+  return cudaLaunchKernelExC(&cfg, (const void*)kern, params) == cudaSuccess ? kOk : kErrCuda;
+}
+
 // The drain step alone, for measuring the GEMM's own ceiling: the drain warps
 // of one CTA per SM run the GEMM's per-block step - TMEM load of a block's
 // 32 x 32 int32 tile, exact conversion, rank-1 scale product and f32x2
@@ -825,10 +1393,27 @@ bool gemm_tc_supported(const LinearArgs& a) {
          ((uintptr_t)a.xsc & 3) == 0;
 }
 
+// Up to this many tokens the narrow kernel runs (16-token tiles up to 16,
+// 32-token tiles above); DN_GEMM_NARROW overrides it (0: never).
+static int64_t gemm_narrow_max() {
+  static int64_t v = -1;
+  if (v < 0) {
+    const char* e = getenv("DN_GEMM_NARROW");
+    v = e != nullptr ? atoll(e) : 32;
+    if (v < 0) v = 0;
+  }
+  return v;
+}
+
 int64_t launch_gemm_tc(const LinearArgs& a, cudaStream_t stream) {
   if (!gemm_tc_supported(a)) return kErrUnsupported;
   if (a.rows <= 0 || a.n <= 0) return kOk;
   if (launch_quantize_q8(a.xs, a.xq, a.xsc, a.n, a.cols, stream) != cudaSuccess) return kErrCuda;
+  if (a.n <= gemm_narrow_max()) {
+    const int64_t rc = a.n <= 16 ? (a.q4 ? launch_narrow<true, 16>(a, stream) : launch_narrow<false, 16>(a, stream))
+                                 : (a.q4 ? launch_narrow<true, 32>(a, stream) : launch_narrow<false, 32>(a, stream));
+    if (rc != kErrUnsupported) return rc;
+  }
   return a.q4 ? launch_tc<true>(a, stream) : launch_tc<false>(a, stream);
 }
 
