@@ -338,6 +338,36 @@ def test_tensor_core_gemm_within_tolerance(cuda_lib, oracle, fmt, rows, cols, n)
     assert err < TOL, f"max relative error {err:.3e}"
 
 
+# The narrow-tile kernel (n <= 32: 16-token tiles up to 16 tokens, 32-token
+# tiles above): ragged rows and token counts, both formats, tiles across more
+# than one wave so the persistent CTAs walk several tiles and the rings run on
+# across tile boundaries; and K whose block count the kernel's scale boxes
+# cannot take (Q8: not a multiple of 4), which falls back to the wide kernel.
+NARROW_CASES = [("q8", 33000, 2048, 5), ("q8", 4097, 1024, 9), ("q8", 1000, 512, 16), ("q8", 20000, 1024, 17),
+                ("q8", 3000, 2048, 31), ("q8", 700, 544, 12), ("q4", 9000, 2048, 7), ("q4", 4100, 1024, 24)]
+
+
+@pytest.mark.parametrize("fmt,rows,cols,n", NARROW_CASES)
+def test_narrow_tiles_within_tolerance(cuda_lib, oracle, fmt, rows, cols, n):
+    rng = np.random.default_rng(rows * 3 + cols + n)
+    qs, sc = weights(fmt, rng, rows, cols)
+    xs = orc.activations(rng, n, cols)
+    ys, _, _ = dev_linear(cuda_lib, fmt, dev(qs), dev(sc), dev(xs), rows, cols, n, path=1)
+    assert not np.isnan(ys).any()
+    ref, mag = oracle.reference_f64(fmt, qs, sc, xs, rows, cols, n, 1)
+    err = orc.max_rel_err(ys, ref, mag)
+    assert err < TOL, f"max relative error {err:.3e}"
+
+
+def test_narrow_crossover_by_rows(cuda_lib):
+    """The tensor-core GEMM takes the lm_head from 5 tokens on (its narrow
+    tiles stream faster than the n-token GEMV there), other shapes from 16."""
+    assert cuda_lib.dn_linear_path(0, None, None, None, None, 151936, 2048, 4, 1) == 0
+    assert cuda_lib.dn_linear_path(0, None, None, None, None, 151936, 2048, 5, 1) == 1
+    assert cuda_lib.dn_linear_path(0, None, None, None, None, 6144, 2048, 8, 1) == 0
+    assert cuda_lib.dn_linear_path(0, None, None, None, None, 6144, 2048, 16, 1) == 1
+
+
 def test_auto_path_uses_tensor_cores_for_prefill(cuda_lib):
     assert cuda_lib.dn_linear_path(0, None, None, None, None, 6144, 2048, 512, 1) == 1
     assert cuda_lib.dn_linear_path(1, None, None, None, None, 6144, 2048, 1, 1) == 0
