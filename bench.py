@@ -510,6 +510,51 @@ class ShardedChain:
             self.base = None
 
 
+class DecodeStack:
+    """All projections of one token as ONE persistent kernel with one CTA per
+    SM and every projection's rows split over all SMs (dn_stack_run). Each
+    projection reads the f32 output of the one before it and quantizes it
+    itself; qkv reads x0 after the previous layer's down, as in the model.
+    Each op has its own f32 output buffer; the logits are stack.bufs
+    ["lm_head"]. One GPU."""
+
+    def __init__(self, torch, stack, L, device):
+        from dianoia_b200 import _lib
+        self.L = L
+        self.keep = []
+        ops, last = [], {}
+        for i, m in enumerate(stack.mats):
+            name = m["name"]
+            src = INPUT_OF[name]
+            if src is not None:
+                x, dep = last[src]
+            else:
+                x, dep = stack.x0.data_ptr(), (last["down"][1] if "down" in last else -1)
+            if name == "lm_head":
+                y = stack.bufs["lm_head"].data_ptr()
+            else:
+                buf = torch.zeros(m["rows"], dtype=torch.float32, device=device)
+                self.keep.append(buf)
+                y = buf.data_ptr()
+                last[name] = (y, i)
+            ops.append(_lib.StackOp(m["qs"].data_ptr(), m["scales"].data_ptr(), x, y,
+                                    m["rows"], m["cols"], dep))
+        arr = (_lib.StackOp * len(ops))(*ops)
+        self.handle = ctypes.c_void_p()
+        _lib.check(L.dn_stack_create(0, arr, len(ops), ctypes.byref(self.handle)), "dn_stack_create")
+
+    def run(self, stream_handle, flags=1):
+        rc = self.L.dn_stack_run(self.handle, flags, stream_handle)
+        if rc != 0:
+            raise RuntimeError(f"dn_stack_run failed: {self.L.dn_error_string(rc).decode()}")
+        return 1
+
+    def close(self):
+        if self.handle:
+            self.L.dn_stack_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+
 def run_step_chain(stack, qa, dchain, L, stream_handle, flags=1):
     """One token: quantize x0, then every projection in one chain kernel."""
     rc = L.dn_quantize_qa(stack.x0.data_ptr(), qa.xa0.data_ptr(), 1, HIDDEN,
@@ -654,8 +699,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--path", choices=["auto", "chain", "ops", "head"], default="auto",
-                    help="chain: one persistent kernel per token (on N > 1 GPUs with the "
+    ap.add_argument("--path", choices=["auto", "stack", "chain", "ops", "head"], default="auto",
+                    help="stack: one persistent kernel per token, one CTA per SM, every "
+                         "projection's rows split over all SMs (1 GPU); chain: one persistent kernel per token (on N > 1 GPUs with the "
                          "all-gather fused into it over NVLink); ops: one GEMV launch per "
                          "projection (N > 1: NCCL all-gather after each); head: the ops "
                          "launches with the decoder layers whole on every GPU and only the "
@@ -750,15 +796,21 @@ def main():
         dchain = (DecodeChain(torch, stack, chain, L, device) if world == 1
                   else ShardedChain(torch, stack, chain, L, device, dist))
     fused = FusedHead(torch, stack, L, dist) if path == "head" and world > 1 and args.gather == "fused" else None
+    if path == "stack" and world > 1:
+        raise SystemExit("--path stack runs on one GPU")
+    dstack = DecodeStack(torch, stack, L, device) if path == "stack" else None
 
     def one_step(handle):
+        if dstack is not None:
+            return dstack.run(handle)
         if dchain is not None:
             return run_step_chain(stack, chain, dchain, L, handle)
         return run_step(stack, chain, L, handle, gather, gather_qa, fused=fused)
 
     stream = torch.cuda.Stream(device=device)
     graph = None
-    launches_per_step = 2 if dchain is not None else len(stack.mats) + 1 + (1 if fused is not None else 0)
+    launches_per_step = (1 if dstack is not None else 2 if dchain is not None
+                         else len(stack.mats) + 1 + (1 if fused is not None else 0))
     with torch.cuda.stream(stream):
         for _ in range(2):
             one_step(stream.cuda_stream)
@@ -835,7 +887,7 @@ def main():
         dist.all_reduce(full_logits)
     checksum = float(full_logits.double().sum().item())
     chain_matches_ops = None
-    if dchain is not None and world == 1:
+    if (dchain is not None or dstack is not None) and world == 1:
         # The chain's logits equal the per-projection launches', bit for bit.
         chain_logits = stack.bufs["lm_head"].clone()
         with torch.cuda.stream(stream):
@@ -898,7 +950,9 @@ def main():
             "cpu_baseline": cpu_baseline,
             "configs": configs,
             "gpu_launches": launches_per_step * args.steps,
-            "gpu_launches_note": ("1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
+            "gpu_launches_note": ("1 decode-stack kernel (113 products, each quantizing its f32 input) per step"
+                                  if dstack is not None else
+                                  "1 activation quantize + 1 decode-chain kernel (113 fused GEMVs) per step"
                                   if dchain is not None else
                                   "1 activation quantize + 113 fused GEMVs per step"),
             "path": path,
@@ -912,6 +966,8 @@ def main():
     torch.cuda.synchronize()
     if dchain is not None:
         dchain.close()
+    if dstack is not None:
+        dstack.close()
     if fused is not None:
         fused.close()
     if world > 1:

@@ -90,6 +90,10 @@ SIGNATURES = {
     "dn_chain_run": (_i64, [_p, _i64, _p]),
     "dn_chain_reset": (_i64, [_p, _p]),
     "dn_chain_destroy": (_i64, [_p]),
+    "dn_stack_create": (_i64, [_i64, _p, _i64, _p]),
+    "dn_stack_run": (_i64, [_p, _i64, _p]),
+    "dn_stack_reset": (_i64, [_p, _p]),
+    "dn_stack_destroy": (_i64, [_p]),
     "dn_linear_noalloc": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "dn_linear_noalloc_status": (_i64, [_i64]),
     "dn_set_wait_limit_ns": (_i64, [_i64]),
@@ -112,6 +116,12 @@ DN_PEER_HANDLE_BYTES = 64
 class ChainOp(ctypes.Structure):
     """dn_chain_op (include/dianoia_b200.h)."""
     _fields_ = [("qs", _p), ("scales", _p), ("xa", _p), ("ys", _p), ("ya", _p),
+                ("rows", _i64), ("cols", _i64), ("dep", _i64)]
+
+
+class StackOp(ctypes.Structure):
+    """dn_stack_op (include/dianoia_b200.h)."""
+    _fields_ = [("qs", _p), ("scales", _p), ("x", _p), ("y", _p),
                 ("rows", _i64), ("cols", _i64), ("dep", _i64)]
 
 _lib = None

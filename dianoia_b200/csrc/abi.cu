@@ -742,6 +742,37 @@ int64_t dn_chain_destroy(void* chain) {
   return DN_OK;
 }
 
+int64_t dn_stack_create(int64_t format, const dn_stack_op* ops, int64_t nops, void** stack) {
+  if (stack == nullptr) return DN_ERR_ARGS;
+  *stack = nullptr;
+  if ((format != DN_Q8 && format != DN_Q4) || ops == nullptr || nops <= 0) return DN_ERR_ARGS;
+  if (format == DN_Q4) return DN_ERR_UNSUPPORTED;
+  if (device_state() == nullptr) return DN_ERR_NO_DEVICE;
+  static_assert(sizeof(dn_stack_op) == sizeof(dn::StackOpSpec), "op layouts differ");
+  dn::StackHost* h = nullptr;
+  const int64_t rc = dn::stack_create(reinterpret_cast<const dn::StackOpSpec*>(ops), nops, &h);
+  *stack = rc == DN_OK ? h : nullptr;
+  return rc;
+}
+
+int64_t dn_stack_run(void* stack, int64_t flags, void* stream) {
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  if (stack == nullptr) return DN_ERR_ARGS;
+  return dn::stack_launch(static_cast<dn::StackHost*>(stack), d->status_dev,
+                          static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
+}
+
+int64_t dn_stack_reset(void* stack, void* stream) {
+  if (stack == nullptr) return DN_ERR_ARGS;
+  return dn::stack_reset(static_cast<dn::StackHost*>(stack), static_cast<cudaStream_t>(stream));
+}
+
+int64_t dn_stack_destroy(void* stack) {
+  dn::stack_destroy(static_cast<dn::StackHost*>(stack));
+  return DN_OK;
+}
+
 int64_t dn_last_error(void) {
   const int64_t e = tl_last_error;
   tl_last_error = DN_OK;

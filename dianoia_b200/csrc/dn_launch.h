@@ -237,6 +237,23 @@ void chain_destroy(ChainHost* h);
 int64_t chain_launch(ChainHost* h, uint32_t* status, cudaStream_t stream, bool pdl);
 int64_t chain_reset(ChainHost* h, cudaStream_t stream);
 
+// Decode stacks (stack.cu): a token's one-token Q8_0 products on f32
+// activations run by one persistent kernel, each product's rows split evenly
+// over every SM.
+struct StackOpSpec {
+  const void* qs;      // Q8_0 weights [rows, cols], reference layout
+  const void* scales;  // f32 block scales [rows, cols / 32]
+  const float* x;      // f32 input [cols]
+  float* y;            // f32 output [rows]
+  int64_t rows, cols;
+  int64_t dep;         // index of an earlier op to wait for (its output may be x), or -1
+};
+struct StackHost;
+int64_t stack_create(const StackOpSpec* specs, int64_t nops, StackHost** out);
+void stack_destroy(StackHost* h);
+int64_t stack_launch(StackHost* h, uint32_t* status, cudaStream_t stream, bool pdl);
+int64_t stack_reset(StackHost* h, cudaStream_t stream);
+
 // GGUF Q4_0 / Q8_0 blocks (count of them, 2-byte aligned) -> values (4-byte
 // aligned) and scales, the engine's split layout (gguf.cu).
 cudaError_t launch_gguf_split(bool q4, const void* blocks, int64_t count, void* qs, void* scales,

@@ -472,6 +472,44 @@ int64_t dn_chain_run(void* chain, int64_t flags, void* stream);
 int64_t dn_chain_reset(void* chain, void* stream);
 int64_t dn_chain_destroy(void* chain);
 
+/* A decode stack: the one-token Q8_0 products of a decode step on f32
+ * activations (lab_gemm_q8 mode 1, n = 1, lab_native.c:553-579), run by ONE
+ * persistent kernel with one CTA per SM. Every product's rows are split
+ * evenly over all SMs; each SM's weights stream ahead through its
+ * shared-memory ring while earlier products compute, and a product whose
+ * `dep` is op j starts on every SM as soon as op j's last SM has stored its
+ * outputs (a counter in device memory, no kernel boundary). Op i reads f32
+ * `x` (cols values, 16-byte aligned; with dep = j it may lie inside op j's
+ * output `y`, e.g. the q rows of a fused qkv output) and writes f32 `y`
+ * (rows values). dep = -1: x was written before the launch (with
+ * DN_FLAG_PDL, read after the previous kernel completes); otherwise an
+ * earlier op, which then orders the two even when x is elsewhere. Each
+ * product quantizes its input itself (lab_quantize_q8), so results equal one
+ * lab_gemm_q8 (mode 1, n = 1) per op, bit for bit. Q8_0 only (format DN_Q8;
+ * DN_Q4 is DN_ERR_UNSUPPORTED), cols a multiple of 512 and at most 8192.
+ * Each output belongs to one op: it may not overlap another op's output or
+ * any weights, nor an input other than through a dep edge (DN_ERR_ARGS).
+ * No counterpart object in the reference: dianoia runs these products one
+ * dispatch each (lib/src/gpu.dart:1130-1190). */
+typedef struct dn_stack_op {
+  const void* qs;
+  const void* scales;
+  const float* x;
+  float* y;
+  int64_t rows, cols, dep;
+} dn_stack_op;
+/* Validates the ops, encodes their TMA descriptors and copies the op table
+ * and zeroed completion counters to device memory (the stack's only
+ * allocations); *stack receives a handle. */
+int64_t dn_stack_create(int64_t format, const dn_stack_op* ops, int64_t nops, void** stack);
+/* Runs every op once, in order, on `stream` (asynchronous; capturable in a
+ * CUDA graph). Runs of one stack must not overlap in time. */
+int64_t dn_stack_run(void* stack, int64_t flags, void* stream);
+/* Clears the completion counters (only needed after a run that reported a
+ * bounded-wait timeout in dn_device_status). */
+int64_t dn_stack_reset(void* stack, void* stream);
+int64_t dn_stack_destroy(void* stack);
+
 /* dn_linear in mode 1 with the automatic path, for callers that must not
  * allocate: an engine that reserves all of its device memory up front and
  * cannot have a library grow it, or code that may not call cudaMalloc and
