@@ -1302,6 +1302,87 @@ COMPACT_CASES = [("c1", "mlp_up_q4_gemv", "q4", 6144, 2048, 1, False),
                  ("c5", "lm_head_q8_m16", "q8", VOCAB, HIDDEN, 16, False)]
 
 
+# Products straight on GGUF blocks (dn_gguf_linear_qa, no split), one token.
+GGUF_CASES = [("c1", "mlp_up_q4_gguf", "q4", 6144, 2048),
+              ("c5", "lm_head_q8_gguf", "q8", VOCAB, HIDDEN)]
+
+
+def gguf_device_blocks(torch, fmt, rows, cols, gen):
+    """A matrix as a GGUF file stores it, on the device: per 32-block an fp16
+    scale (Q4_0 U[0.002, 0.02], Q8_0 U[0.001, 0.01], the configs' ranges) and
+    the 16 nibble bytes / 32 int8 (U[-127, 127])."""
+    nb = rows * (cols // 32)
+    size = 18 if fmt == "q4" else 34
+    raw = torch.empty((nb, size), dtype=torch.uint8, device="cuda")
+    if fmt == "q4":
+        raw[:, 2:] = torch.randint(0, 256, (nb, 16), dtype=torch.uint8, device="cuda", generator=gen)
+        lo, hi = 0.002, 0.02
+    else:
+        raw[:, 2:] = torch.randint(-127, 128, (nb, 32), dtype=torch.int8, device="cuda",
+                                   generator=gen).view(torch.uint8)
+        lo, hi = 0.001, 0.01
+    sc = torch.empty(nb, device="cuda").uniform_(lo, hi, generator=gen).half()
+    raw[:, :2] = sc.view(torch.uint8).view(nb, 2)
+    return raw
+
+
+def time_gguf(torch, L, oracle, fmt, rows, cols, steps, warmup):
+    """us per one-token product on GGUF blocks (the activation quantize to QA
+    blocks included, as in time_linear), blocks rotating through copies past
+    twice the L2; and its first CHECK_ROWS rows against the oracle on the
+    blocks split as the reference's loader splits them."""
+    q4 = fmt == "q4"
+    per_copy = rows * (cols // 32) * (18 if q4 else 34)
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    copies = max(1, -(-2 * l2 // per_copy))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(rows * 13 + cols)
+    raw0 = gguf_device_blocks(torch, fmt, rows, cols, gen)
+    sets = [raw0] + [raw0.clone() for _ in range(copies - 1)]
+    x = torch.randn(cols, device="cuda", generator=gen)
+    xa = torch.zeros(cols // 32 * 36, dtype=torch.uint8, device="cuda")
+    ys = torch.full((rows,), float("nan"), device="cuda")
+    stream = torch.cuda.Stream()
+
+    def launch(i, h):
+        rc = L.dn_quantize_qa(x.data_ptr(), xa.data_ptr(), 1, cols, cols // 32 * 36, h)
+        if rc == 0:
+            rc = L.dn_gguf_linear_qa(1 if q4 else 0, sets[i % copies].data_ptr(), xa.data_ptr(), ys.data_ptr(),
+                                     rows, cols, 1, h)
+        if rc != 0:
+            raise RuntimeError(L.dn_error_string(rc).decode())
+
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            launch(i, stream.cuda_stream)
+        torch.cuda.synchronize()
+        r = min(rows, CHECK_ROWS)
+        raw = raw0[:r * (cols // 32)].cpu().numpy()
+        if q4:
+            qs, sc = raw[:, 2:].ravel().copy(), raw[:, :2].ravel().copy().view(np.uint16)
+        else:
+            qs, sc = raw[:, 2:].ravel().copy(), raw[:, :2].copy().view(np.float16).astype(np.float32).ravel()
+        want, _, _ = oracle.gemm(fmt, qs, sc, x.cpu().numpy(), r, cols, 1, 1)
+        launch(0, stream.cuda_stream)
+        torch.cuda.synchronize()
+        ok = bool(np.array_equal(ys[:r].cpu().numpy().view(np.uint32), want.view(np.uint32)))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                launch(i, torch.cuda.current_stream().cuda_stream)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    del graph
+    if L.dn_device_status(1) != 0:
+        raise SystemExit("kernel bounded wait timed out")
+    return e0.elapsed_time(e1) * 1e3 / steps, ok, copies
+
+
 def run_configs_compact(args, torch, L):
     """Configs 1, 2, 4, 5 and the lm_head sweep in short: per case the GPU time
     per dn_linear launch (graph-replayed, operands past L2) as HBM GB/s and
@@ -1341,6 +1422,18 @@ def run_configs_compact(args, torch, L):
                "copies": copies}
         if ref is not None:
             cus = cpu_linear_us(ref, fmt, rows, cols, n, threads, budget_s=1.0)
+            res.update(cpu_reference_us=cus, cpu_threads=threads, gpu_speedup=cus / us)
+        out.append(res)
+    for cfg, name, fmt, rows, cols in GGUF_CASES:
+        us, ok, copies = time_gguf(torch, L, oracle, fmt, rows, cols, args.config_steps, 3)
+        alg_bytes = rows * cols // 32 * (18 if fmt == "q4" else 34) + 4 * (cols + rows)
+        res = {"config": cfg, "case": name, "fmt": fmt, "rows": rows, "cols": cols, "n": 1,
+               "path": "gguf gemv (the file's interleaved blocks, no split)", "us": us,
+               "gbs_algorithmic": alg_bytes / us / 1e3, "hbm_frac": alg_bytes / us / 1e3 / hbm,
+               "check": "bit-exact with the oracle on the blocks split as the reference's loader splits them",
+               "check_rows": min(rows, CHECK_ROWS), "check_ok": ok, "copies": copies}
+        if ref is not None:
+            cus = cpu_linear_us(ref, fmt, rows, cols, 1, threads, budget_s=1.0)
             res.update(cpu_reference_us=cus, cpu_threads=threads, gpu_speedup=cus / us)
         out.append(res)
     return {"cases": out, "peaks": {"hbm_gbs": hbm, "int8_tops": int8,

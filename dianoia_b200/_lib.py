@@ -73,6 +73,7 @@ SIGNATURES = {
     "dn_linear_path": (_i64, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64]),
     "dn_quantize_q8": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_gguf_split": (_i64, [_i64, _p, _i64, _p, _p, _p]),
+    "dn_gguf_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _i64, _i64, _p]),
     "dn_quantize_q4": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_quantize_qa": (_i64, [_p, _p, _i64, _i64, _i64, _p]),
     "dn_rms_norm": (_i64, [_p, _p, _p, _p, _i64, _i64, _i64, ctypes.c_double, _i64, _i64, _p]),

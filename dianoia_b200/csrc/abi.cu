@@ -537,6 +537,15 @@ int64_t dn_quantize_qa(const float* xs, uint8_t* xa, int64_t n, int64_t cols, in
              : DN_ERR_CUDA;
 }
 
+int64_t dn_gguf_linear_qa(int64_t format, const void* blocks, const uint8_t* xa, float* ys, int64_t rows,
+                          int64_t cols, int64_t flags, void* stream) {
+  if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  return dn::launch_gguf_gemv(format == DN_Q4, blocks, xa, ys, rows, cols, d->status_dev,
+                              static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
+}
+
 int64_t dn_gguf_split(int64_t format, const void* blocks, int64_t count, void* qs, void* scales,
                       void* stream) {
   if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;

@@ -259,6 +259,11 @@ int64_t stack_reset(StackHost* h, cudaStream_t stream);
 cudaError_t launch_gguf_split(bool q4, const void* blocks, int64_t count, void* qs, void* scales,
                               cudaStream_t stream);
 
+// One token times a matrix of GGUF Q4_0 / Q8_0 blocks, read as stored
+// (gguf_gemv.cu): QA input, f32 outputs.
+int64_t launch_gguf_gemv(bool q4, const void* blocks, const uint8_t* xa, float* ys, int64_t rows, int64_t cols,
+                         uint32_t* status, cudaStream_t stream, bool pdl);
+
 // Quantizes n rows of cols floats to Q8_0 (lab_quantize_q8 semantics).
 cudaError_t launch_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
                                cudaStream_t stream);

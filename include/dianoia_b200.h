@@ -346,6 +346,19 @@ int64_t dn_linear_path(int64_t format, const void* qs, const void* scales, const
 int64_t dn_gguf_split(int64_t format, const void* blocks, int64_t count, void* qs, void* scales,
                       void* stream);
 
+/* The one-token product straight on GGUF blocks, with no split: ys[r] for
+ * rows r = 0 .. rows - 1 of a matrix stored as the file stores it, `rows`
+ * rows of cols / 32 Q4_0 (18-byte) or Q8_0 (34-byte) blocks each, times one
+ * token of QA activations xa (cols / 32 blocks of 36 bytes, as
+ * dn_quantize_qa writes them; 4-byte aligned). The result equals lab_gemm_q4
+ * / lab_gemm_q8 (mode 1, n = 1, lab_native.c:553-579, 1059-1080) on the
+ * weights dianoia's loader would split (gguf.dart:206-215, 269-283), bit for
+ * bit. `blocks` 16-byte aligned; cols a multiple of 256 (Q8_0) or 512
+ * (Q4_0), else DN_ERR_ARGS; asynchronous on `stream`; DN_FLAG_PDL as for
+ * dn_linear. */
+int64_t dn_gguf_linear_qa(int64_t format, const void* blocks, const uint8_t* xa, float* ys, int64_t rows,
+                          int64_t cols, int64_t flags, void* stream);
+
 /* lab_quantize_q8 / lab_quantize_q4 on device memory, asynchronous. */
 int64_t dn_quantize_q8(const float* xs, int8_t* xq, float* xsc, int64_t n, int64_t cols,
                        void* stream);
