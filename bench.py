@@ -728,6 +728,8 @@ def main():
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
     ap.add_argument("--fmt", choices=["q8", "q4"], default="q8")
+    ap.add_argument("--gguf", action="store_true",
+                    help="--workload gemv: the product on GGUF blocks as the file stores them (dn_gguf_linear_qa)")
     ap.add_argument("--rows", type=int, default=VOCAB)
     ap.add_argument("--cols", type=int, default=HIDDEN)
     ap.add_argument("--n", type=int, default=1, help="tokens per product")
@@ -984,13 +986,19 @@ def run_gemv_workload(args):
     L = _lib.lib()
     rows, cols, n, q4 = args.rows, args.cols, args.n, args.fmt == "q4"
     blocks = cols // 32
-    wbytes = rows * blocks * (18 if q4 else 36)
+    gguf = args.gguf
+    if gguf and n != 1:
+        raise SystemExit("--gguf runs one token")
+    wbytes = rows * blocks * ((18 if q4 else 34) if gguf else (18 if q4 else 36))
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
     copies = max(1, -(-2 * l2 // wbytes))
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0)
     mats = []
     for _ in range(copies):
+        if gguf:
+            mats.append((gguf_device_blocks(torch, args.fmt, rows, cols, gen), None))
+            continue
         if q4:
             qs = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=gen)
             sc = torch.empty(rows * blocks, device="cuda").uniform_(0.002, 0.02, generator=gen)
@@ -1010,9 +1018,13 @@ def run_gemv_workload(args):
 
     def launch(i, handle):
         qs, sc = mats[i % copies]
-        rc = L.dn_linear_qa(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xa.data_ptr(),
-                            blocks * 36, ys.data_ptr(), rows, ya.data_ptr(), (rows // 32) * 36,
-                            rows, cols, n, 1, handle)
+        if gguf:
+            rc = L.dn_gguf_linear_qa(1 if q4 else 0, qs.data_ptr(), xa.data_ptr(), ys.data_ptr(), rows, cols, 1,
+                                     handle)
+        else:
+            rc = L.dn_linear_qa(1 if q4 else 0, qs.data_ptr(), sc.data_ptr(), xa.data_ptr(),
+                                blocks * 36, ys.data_ptr(), rows, ya.data_ptr(), (rows // 32) * 36,
+                                rows, cols, n, 1, handle)
         if rc != 0:
             raise RuntimeError(L.dn_error_string(rc).decode())
 
@@ -1048,7 +1060,8 @@ def run_gemv_workload(args):
     except OSError:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    res = {"metric": "quantized-linear GEMV HBM GB/s", "workload": f"{args.fmt} {rows}x{cols} n={n}",
+    res = {"metric": "quantized-linear GEMV HBM GB/s",
+           "workload": f"{args.fmt} {rows}x{cols} n={n}" + (" (GGUF blocks as stored)" if gguf else ""),
            "us_per_launch": us, "weight_bytes_ref_layout": wbytes,
            "gbs_ref_layout": wbytes / us / 1e3, "gbs_algorithmic": alg / us / 1e3,
            "roofline_frac": alg / us / 1e3 / peak, "peak_gbs": peak, "copies": copies,
