@@ -39,6 +39,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import re
 import os
 
 # The host's cores as this process may use them, taken before any OpenMP
@@ -727,6 +728,9 @@ def main():
                     default="stack",
                     help="stack: config 3 (the default bench line); gemv: one matrix "
                          "(configs 1, 2 and the lm_head M sweep; also the ncu case)")
+    ap.add_argument("--cases", default="",
+                    help="--workload configs on N > 1 GPUs (or --sharded): only the cases whose name matches "
+                         "this regular expression")
     ap.add_argument("--fmt", choices=["q8", "q4"], default="q8")
     ap.add_argument("--gguf", action="store_true",
                     help="--workload gemv: the product on GGUF blocks as the file stores them (dn_gguf_linear_qa)")
@@ -1508,6 +1512,49 @@ SHARDED_CASES = ([(f"vision_{nm}_m1024", "q8", r, c, 1024, True)
                  + [(f"lm_head_m{m}", "q8", VOCAB, HIDDEN, m, False) for m in (1, 2, 4, 8, 16, 32, 64)])
 
 
+class FusedRegion:
+    """`nbytes` of device memory on every rank that every other rank maps
+    (dn_peer_alloc / dn_peer_open, handles exchanged with the process group);
+    bases[p] is rank p's region as mapped here."""
+
+    def __init__(self, L, dist, rank, world, nbytes):
+        from dianoia_b200 import _lib
+        self.L, self.dist, self.world = L, dist, world
+        nbytes = (nbytes + 4095) // 4096 * 4096
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.DN_PEER_HANDLE_BYTES)()
+        _lib.check(L.dn_peer_alloc(nbytes, ctypes.byref(base), handle), "dn_peer_alloc")
+        self.base = base.value
+        handles = [bytes(handle)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle))
+        self.bases, self.opened = [], []
+        for p in range(world):
+            if p == rank:
+                self.bases.append(self.base)
+                continue
+            ptr = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * _lib.DN_PEER_HANDLE_BYTES).from_buffer_copy(handles[p])
+            _lib.check(L.dn_peer_open(h, ctypes.byref(ptr)), "dn_peer_open")
+            self.bases.append(ptr.value)
+            self.opened.append(ptr.value)
+        if world > 1:
+            dist.barrier()  # every region mapped everywhere before any rank stores into it
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()  # no rank still stores into another's region
+        for p in self.opened:
+            self.L.dn_peer_close(p)
+        self.opened = []
+        if self.world > 1:
+            self.dist.barrier()
+        if self.base:
+            self.L.dn_peer_free(self.base)
+            self.base = None
+
+
 def run_configs_sharded(args, rank, world, local_rank):
     """Configs 5 and the lm_head sweep on N GPUs: each rank holds its row
     slice of the weights (rows * p // N ..), runs dn_linear on the whole batch
@@ -1534,6 +1581,8 @@ def run_configs_sharded(args, rank, world, local_rank):
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     stream = torch.cuda.Stream(device=device)
     for name, fmt, rows, cols, n, vision in SHARDED_CASES:
+        if args.cases and not re.search(args.cases, name):
+            continue
         r0, r1 = row_split(rows, rank, world, False)
         rr = r1 - r0
         width = max(row_split(rows, p, world, False)[1] - row_split(rows, p, world, False)[0]
@@ -1545,12 +1594,34 @@ def run_configs_sharded(args, rank, world, local_rank):
         xs = torch.randn(n * cols, device=device, generator=torch.Generator(device=device).manual_seed(7))
         xq = torch.zeros(n * cols, dtype=torch.int8, device=device)
         xsc = torch.zeros(n * blocks + 4, device=device)
-        ys = torch.zeros(n * width, device=device)  # [n, width]: this rank's block, padded
-        gathered = torch.empty(world * n * width, device=device)
-        full = torch.empty(n * rows, device=device)
         spans = [row_split(rows, p, world, False) for p in range(world)]
+        fused = args.gather == "fused" and n > 32  # the tensor-core GEMM's wide kernel
+        if fused:
+            # Every rank's Y[n, rows] (then its counter and wait word) in peer
+            # memory; each rank's GEMM epilogue stores its column block into
+            # every copy over NVLink (dn_linear_allgather), then a bounded
+            # wait on this rank's counter for all ranks' tiles.
+            region = FusedRegion(L, dist, rank, world, 4 * n * rows + 256)
+            ys_arr = (ctypes.c_void_p * world)(*region.bases)
+            cnt_arr = (ctypes.c_void_p * world)(*[b + 4 * n * rows for b in region.bases])
+            counter = region.bases[rank] + 4 * n * rows
+            expect = counter + 4
+            tiles = world  # one count per rank's product
+        else:
+            ys = torch.zeros(n * width, device=device)  # [n, width]: this rank's block, padded
+            gathered = torch.empty(world * n * width, device=device)
+            full = torch.empty(n * rows, device=device)
 
         def step():
+            if fused:
+                rc = L.dn_linear_allgather(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
+                                           xq.data_ptr(), xsc.data_ptr(), rr, cols, n, r0, rows, ys_arr, cnt_arr,
+                                           world, stream.cuda_stream)
+                if rc == 0:
+                    rc = L.dn_peer_wait(counter, expect, tiles, stream.cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(L.dn_error_string(rc).decode())
+                return
             rc = L.dn_linear(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
                              xq.data_ptr(), xsc.data_ptr(), ys.data_ptr(), rr, cols, n, width, 1, -1, 0,
                              stream.cuda_stream)
@@ -1572,31 +1643,84 @@ def run_configs_sharded(args, rank, world, local_rank):
         torch.cuda.synchronize()
         steps = max(args.steps, 1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        graph = None
+        if fused:
+            # The fused steps replay from a CUDA graph (no collective inside:
+            # the ranks meet in the bounded counter waits).
+            with torch.cuda.stream(stream):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(steps):
+                        step()
+                graph.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             e0.record(stream)
-            for _ in range(steps):
-                step()
+            if graph is not None:
+                graph.replay()
+            else:
+                for _ in range(steps):
+                    step()
             e1.record(stream)
         torch.cuda.synchronize()
+        del graph
         t = torch.tensor([e0.elapsed_time(e1) * 1e3 / steps], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us = float(t.item())
         ops = 2.0 * n * rows * cols
         wbytes = rows * blocks * 34
+        check = None
+        if fused:
+            # Outside the timed region: every rank's copy of Y is the same,
+            # and this rank's own columns equal dn_linear on its slice.
+            torch.cuda.synchronize()
+            mine = torch.as_tensor(_DevArray(region.bases[rank], n * rows), device=device).view(n, rows)
+            own = torch.empty(n * rr, device=device)
+            rc = L.dn_linear(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(), xq.data_ptr(),
+                             xsc.data_ptr(), own.data_ptr(), rr, cols, n, rr, 1, -1, 0, stream.cuda_stream)
+            torch.cuda.synchronize()
+            own_ok = rc == 0 and bool(torch.equal(mine[:, r0:r1].contiguous().view(torch.int32),
+                                                  own.view(n, rr).view(torch.int32)))
+            sums = torch.tensor([float(mine.double().sum().item())], dtype=torch.float64, device=device)
+            allsums = [torch.zeros_like(sums) for _ in range(world)]
+            if world > 1:
+                dist.all_gather(allsums, sums)
+            else:
+                allsums = [sums]
+            flags = torch.tensor([1 if own_ok else 0], device=device)
+            if world > 1:
+                dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+            check = {"copies_identical": len({float(x.item()) for x in allsums}) == 1,
+                     "own_columns_equal_dn_linear_on_all_ranks": bool(flags.item() == 1)}
         if rank == 0:
             print(json.dumps({"case": name, "n_gpus": world, "fmt": fmt, "rows": rows, "cols": cols, "n": n,
                               "rows_per_gpu": width, "us": us, "tops": ops / us / 1e6,
                               "int8_frac_per_gpu": ops / us / 1e6 / (int8 * world),
                               "weight_gbs": wbytes / us / 1e3,
                               "hbm_frac_per_gpu": wbytes / us / 1e3 / (hbm * world),
-                              "includes": "dn_linear on each rank's row slice (activation quantize "
-                                          "included) + NCCL all-gather of the output blocks + "
-                                          "token-major layout copy" if world > 1 else "dn_linear",
+                              "includes": ("dn_linear_allgather on each rank's row slice (activation "
+                                           "quantize included; the output columns stored into every rank's "
+                                           "Y over NVLink inside the GEMM epilogue) + dn_peer_wait"
+                                           if fused else
+                                           "dn_linear on each rank's row slice (activation quantize "
+                                           "included) + NCCL all-gather of the output blocks + "
+                                           "token-major layout copy" if world > 1 else "dn_linear"),
+                              "check": check,
                               "weights": "bf16 N(0,0.02) -> lab_quantize_q8" if vision else "config distribution",
-                              "timing": f"{steps} launches, CUDA events, max over ranks; operands L2-resident "
-                                        "between launches (one copy per rank)"}), flush=True)
-        del qs, sc, xs, xq, xsc, ys, gathered, full
+                              "timing": f"{steps} steps" + (" replayed from a CUDA graph" if fused else
+                                                            " launched eagerly") +
+                                        ", CUDA events, max over ranks; operands L2-resident between "
+                                        "launches (one copy per rank)"}), flush=True)
+        torch.cuda.synchronize()
+        if fused:
+            region.close()
+        else:
+            del ys, gathered, full
+        del qs, sc, xs, xq, xsc
         torch.cuda.empty_cache()
     if world > 1:
         dist.barrier()

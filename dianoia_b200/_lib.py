@@ -79,6 +79,7 @@ SIGNATURES = {
     "dn_rms_norm": (_i64, [_p, _p, _p, _p, _i64, _i64, _i64, ctypes.c_double, _i64, _i64, _p]),
     "dn_swiglu": (_i64, [_p, _p, _p, _i64, _i64, _p]),
     "dn_linear_qa": (_i64, [_i64, _p, _p, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p]),
+    "dn_linear_allgather": (_i64, [_i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i64, _p]),
     "dn_linear_qa_allgather": (_i64, [_i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _i64, _p]),
     "dn_peer_wait": (_i64, [_p, _p, _i64, _p]),
     "dn_drain_probe": (_i64, [_i64, _i64, _p, _p]),

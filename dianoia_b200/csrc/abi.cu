@@ -617,6 +617,33 @@ int64_t dn_linear_qa(int64_t format, const void* qs, const void* scales, const u
   return dn::launch_gemv_ex(g, static_cast<cudaStream_t>(stream), (flags & DN_FLAG_PDL) != 0);
 }
 
+int64_t dn_linear_allgather(int64_t format, const void* qs, const void* scales, const float* xs, int8_t* xq,
+                            float* xsc, int64_t rows, int64_t cols, int64_t n, int64_t row0, int64_t total_rows,
+                            float* const* ys, int32_t* const* counters, int64_t world, void* stream) {
+  if (format != DN_Q8 && format != DN_Q4) return DN_ERR_ARGS;
+  if (rows < 0 || cols <= 0 || n < 0 || row0 < 0 || total_rows < row0 + rows || xs == nullptr || ys == nullptr ||
+      counters == nullptr || world < 1 || world > dn::kMaxGatherRanks)
+    return DN_ERR_ARGS;
+  DeviceState* d = device_state();
+  if (d == nullptr) return DN_ERR_NO_DEVICE;
+  dn::LinearArgs a{};
+  a.q4 = format == DN_Q4;
+  a.qs = qs;
+  a.scales = scales;
+  a.xs = xs;
+  a.xq = xq;
+  a.xsc = xsc;
+  a.ys = nullptr;
+  a.rows = rows;
+  a.cols = cols;
+  a.n = n;
+  a.ldy = total_rows;
+  a.mode = 1;
+  a.status = d->status_dev;
+  return dn::launch_gemm_tc_allgather(a, row0, ys, reinterpret_cast<int* const*>(counters), (int)world,
+                                      static_cast<cudaStream_t>(stream));
+}
+
 int64_t dn_linear_qa_allgather(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
                                int64_t rows, int64_t cols, int64_t row0, float* const* ys,
                                int32_t* const* counters, int64_t world, int64_t flags, void* stream) {

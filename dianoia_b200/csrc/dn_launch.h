@@ -280,6 +280,13 @@ int64_t launch_gemv(const LinearArgs& a, cudaStream_t stream, bool pdl);
 int64_t launch_generic(const LinearArgs& a, cudaStream_t stream);
 int64_t launch_gemm_tc(const LinearArgs& a, cudaStream_t stream);
 
+// The tensor-core GEMM on this GPU's row slice (rows row0 .. row0 + a.rows of
+// the whole output, a.ldy values per token) with the all-gather fused into
+// its epilogue: every value into every rank's copy ys[p], then, once the
+// GEMM is complete, one count in every rank's cnt[p] (gemm_tc.cu).
+int64_t launch_gemm_tc_allgather(const LinearArgs& a, int64_t row0, float* const* ys, int* const* cnt, int world,
+                                 cudaStream_t stream);
+
 // The tensor-core GEMM's drain step alone, for measuring its ceiling (gemm_tc.cu).
 int64_t launch_drain_probe(int64_t ctas, int64_t nst, float* out, cudaStream_t stream);
 

@@ -89,6 +89,14 @@ struct TcArgs {
   uint32_t* status;
   int tma_scales;  // scales arrive by TMA (tsw, tsx) rather than cp.async
   int64_t row_tiles, tiles;  // the narrow kernel's tile walk
+  // The all-gather of a row-sharded output fused into the epilogue (the wide
+  // kernel; gather_n > 0): this GPU's rows are rows gather_row0 .. + rows of
+  // the whole output, and each value goes to every rank's copy of it,
+  // gather_ys[p][t * ldy + gather_row0 + row] (plain stores, over NVLink for
+  // the peers); peer_signal_kernel then counts the product on every rank.
+  int gather_n;
+  int64_t gather_row0;
+  float* gather_ys[kMaxGatherRanks];
 };
 
 // ----------------------------------------------------------- tcgen05 PTX
@@ -621,8 +629,16 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           const int64_t t = tok0 + col0 + 2 * j;
           const float y0 = __fadd_rn(__uint_as_float((uint32_t)acc[j]), x[(2 * j) * 32 + lane]);
           const float y1 = __fadd_rn(__uint_as_float((uint32_t)(acc[j] >> 32)), x[(2 * j + 1) * 32 + lane]);
-          if (t < a.n) a.ys[t * a.ldy + row] = y0;
-          if (t + 1 < a.n) a.ys[(t + 1) * a.ldy + row] = y1;
+          if (a.gather_n > 0) {
+            for (int p = 0; p < a.gather_n; p++) {
+              float* g = a.gather_ys[p] + a.gather_row0 + row;
+              if (t < a.n) g[t * a.ldy] = y0;
+              if (t + 1 < a.n) g[(t + 1) * a.ldy] = y1;
+            }
+          } else {
+            if (t < a.n) a.ys[t * a.ldy + row] = y0;
+            if (t + 1 < a.n) a.ys[(t + 1) * a.ldy + row] = y1;
+          }
         }
       }
     }
@@ -672,8 +688,33 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
   }
 }
 
+// After the gathering GEMM (the previous kernel in the stream, complete, so
+// every store it made is ordered before this one): one system-scope fence
+// makes those stores visible to the peers, then one count on every rank's
+// counter (the waiting side acquires). One fence per product instead of one
+// per CTA: a fence per CTA measured +21 us on a 45 us GEMM. After a bounded
+// wait ran out anywhere (the status word is set) nothing is counted, so the
+// peers' waits run out too rather than read a partial output.
+struct PeerCounters {
+  int* p[kMaxGatherRanks];
+};
+__global__ void peer_signal_kernel(const PeerCounters c, int world, const uint32_t* status) {
+  if (status != nullptr && *reinterpret_cast<const volatile uint32_t*>(status) != 0) return;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int p = 0; p < world; p++)
+    asm volatile("red.relaxed.sys.global.add.s32 [%0], 1;" ::"l"(c.p[p]) : "memory");
+}
+
+// The fused all-gather's destinations (launch_tc; null: plain outputs).
+struct TcGather {
+  int world;
+  int64_t row0;
+  float* const* ys;
+  int* const* cnt;
+};
+
 template <bool Q4>
-int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
+int64_t launch_tc(const LinearArgs& a, cudaStream_t stream, const TcGather* gather = nullptr) {
   using S = TcShape<Q4>;
   const int64_t blocks = a.cols / kBlock;
   const int64_t bar_bytes = 8 * (4 * 16 + 2 * kSlots + 3) + 16;  // up to 16 stages
@@ -721,6 +762,11 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream) {
     configured[variant][dev & 63] = true;
   }
   TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, tma_scales ? 1 : 0};
+  if (gather != nullptr) {
+    t.gather_n = gather->world;
+    t.gather_row0 = gather->row0;
+    for (int p = 0; p < gather->world; p++) t.gather_ys[p] = gather->ys[p];
+  }
   const dim3 grid((unsigned)((a.rows + kTileRows - 1) / kTileRows),
                   (unsigned)((a.n + kTileTok - 1) / kTileTok), 1);
   cudaLaunchConfig_t cfg = {};
@@ -1415,6 +1461,24 @@ int64_t launch_gemm_tc(const LinearArgs& a, cudaStream_t stream) {
     if (rc != kErrUnsupported) return rc;
   }
   return a.q4 ? launch_tc<true>(a, stream) : launch_tc<false>(a, stream);
+}
+
+int64_t launch_gemm_tc_allgather(const LinearArgs& a, int64_t row0, float* const* ys, int* const* cnt, int world,
+                                 cudaStream_t stream) {
+  if (!gemm_tc_supported(a) || world < 1 || world > kMaxGatherRanks) return kErrArgs;
+  if (a.rows <= 0 || a.n <= 0) return kOk;
+  for (int p = 0; p < world; p++)
+    if (ys[p] == nullptr || cnt[p] == nullptr || ((uintptr_t)ys[p] & 3) != 0 || ((uintptr_t)cnt[p] & 3) != 0)
+      return kErrArgs;
+  if (launch_quantize_q8(a.xs, a.xq, a.xsc, a.n, a.cols, stream) != cudaSuccess) return kErrCuda;
+  const TcGather g{world, row0, ys, cnt};
+  const int64_t rc = a.q4 ? launch_tc<true>(a, stream, &g) : launch_tc<false>(a, stream, &g);
+  if (rc != kOk) return rc;
+  // The counters' addresses travel by value.
+  PeerCounters c{};
+  for (int p = 0; p < world; p++) c.p[p] = cnt[p];
+  peer_signal_kernel<<<1, 1, 0, stream>>>(c, world, a.status);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 }  // namespace dn

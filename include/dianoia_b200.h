@@ -440,6 +440,24 @@ int64_t dn_chain_create(int64_t format, const dn_chain_op* ops, int64_t nops, vo
 int64_t dn_linear_qa_allgather(int64_t format, const void* qs, const void* scales, const uint8_t* xa,
                                int64_t rows, int64_t cols, int64_t row0, float* const* ys,
                                int32_t* const* counters, int64_t world, int64_t flags, void* stream);
+/* The prefill / vision product (the tensor-core GEMM, mode 1 on f32 inputs
+ * xs [n, cols], xq / xsc its quantized-input scratch as for dn_linear) on N
+ * GPUs of one node with row-partitioned weights (north_star's sharding; the
+ * reference's row split, lab_native.c:550-579: a row's result does not
+ * depend on it): this GPU holds rows row0 .. row0 + rows of the total_rows
+ * of the whole matrix and stores every output value into every rank's copy
+ * of Y[n, total_rows], ys[p][t * total_rows + row0 + r] (ys[p]: rank p's
+ * buffer as mapped here - dn_peer_alloc / dn_peer_open memory - the local
+ * one included; plain stores over NVLink, no TMA on peer memory), inside the
+ * GEMM's epilogue. When the GEMM has completed, one thread makes the stores
+ * visible system-wide and adds one to every rank's counter (counters[p]), so
+ * a rank's copy is complete once its counter has grown by `world` (one per
+ * rank): dn_peer_wait. Nothing is counted after a bounded wait ran out (a
+ * set dn_device_status). Results equal dn_linear's tensor-core path on the
+ * whole matrix, value for value. */
+int64_t dn_linear_allgather(int64_t format, const void* qs, const void* scales, const float* xs, int8_t* xq,
+                            float* xsc, int64_t rows, int64_t cols, int64_t n, int64_t row0, int64_t total_rows,
+                            float* const* ys, int32_t* const* counters, int64_t world, void* stream);
 /* Waits on `stream` (one thread of the GPU, bounded: a timeout sets the
  * peer-timeout bit of dn_device_status) until *counter has grown by `count`
  * since the previous wait with the same `expect` word, a device int32 that
