@@ -556,6 +556,20 @@ void subtract(const std::vector<Range>& written, int64_t b, int64_t lo, int64_t 
   if (at < hi) add_range(out, b, at, hi);
 }
 
+// Removes bytes [lo, hi) of buffer b from the ranges v.
+void remove_range(std::vector<Range>& v, int64_t b, int64_t lo, int64_t hi) {
+  std::vector<Range> out;
+  for (const Range& r : v) {
+    if (r.buf != b || r.hi <= lo || hi <= r.lo) {
+      out.push_back(r);
+      continue;
+    }
+    if (r.lo < lo) out.push_back(Range{b, r.lo, lo});
+    if (hi < r.hi) out.push_back(Range{b, hi, r.hi});
+  }
+  v.swap(out);
+}
+
 // Records the command buffer's copies and products on g_stream.
 dn::LinearArgs linear_args(const Op& o, uint32_t* status) {
   const Buf &w = g_bufs[o.w], &x = g_bufs[o.x], &y = g_bufs[o.y];
@@ -823,7 +837,7 @@ Plan plan_ops(uint32_t* status) {
 float* f32_at(int64_t buf, int64_t off) { return reinterpret_cast<float*>(g_bufs[buf].dev + off); }
 
 bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloads,
-            const Plan& k, uint32_t* status) {
+            const Plan& k, uint32_t* status, int zc_op, float* zc_ys) {
   // With profiling, an event node after the uploads and after every launch
   // (external records: timestamps in the graph), and launches without
   // programmatic dependent launch, so that each one's share is its own.
@@ -912,7 +926,8 @@ bool record(const std::vector<Range>& uploads, const std::vector<Range>& downloa
       continue;
     }
     if (k.absorbed[i]) continue;  // the second product of a dual launch
-    const dn::LinearArgs a = linear_args(o, status);
+    dn::LinearArgs a = linear_args(o, status);
+    if ((int)i == zc_op) a.ys = zc_ys;  // straight into the pinned host mirror
     int64_t rc;
     if (k.xa_at[i] >= 0 || k.ya_at[i] >= 0 || k.glu[i] >= 0 || k.res[i] >= 0 || k.normin[i] >= 0 ||
         k.dual[i] >= 0 || k.grp[i] > 1) {
@@ -1091,8 +1106,32 @@ int64_t commit(int64_t wait) {
       }
     }
     cudaGraph_t graph = nullptr;
+    // The command buffer's last op, a plain product with a small output in a
+    // host-visible buffer (the logits of a decode step): its epilogue stores
+    // straight into the pinned host mirror (the device address of the mapped
+    // page-locked memory), so the output crosses PCIe while the product runs
+    // instead of in a copy after it. Nothing later in the command buffer reads
+    // it, and a later commit that reads the buffer copies the mirror in first.
+    int zc_op = -1;
+    float* zc_ys = nullptr;
+    if (!g_profiling && !g_ops.empty()) {
+      const int i = (int)g_ops.size() - 1;
+      const Op& o = g_ops[i];
+      const int64_t bytes = o.n * o.rows * 4;
+      void* d = nullptr;
+      if (o.kind == kMatmul && !plan.absorbed[i] && plan.grp[i] <= 1 && plan.dual[i] < 0 && plan.glu[i] < 0 &&
+          plan.res[i] < 0 && plan.ya_at[i] < 0 && g_bufs[o.y].host != nullptr && bytes <= (8 << 20)) {
+        if (cudaHostGetDevicePointer(&d, g_bufs[o.y].host + o.y_off, 0) == cudaSuccess && d != nullptr) {
+          zc_op = i;
+          zc_ys = static_cast<float*>(d);
+          remove_range(written, o.y, o.y_off, o.y_off + bytes);
+        } else {
+          cudaGetLastError();
+        }
+      }
+    }
     if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
-    const bool ok = record(uploads, written, plan, status);
+    const bool ok = record(uploads, written, plan, status, zc_op, zc_ys);
     const cudaError_t e = cudaStreamEndCapture(g_stream, &graph);
     if (!ok || e != cudaSuccess || graph == nullptr ||
         cudaGraphInstantiate(&g_exec, graph, 0) != cudaSuccess) {
