@@ -1595,7 +1595,10 @@ def run_configs_sharded(args, rank, world, local_rank):
         xq = torch.zeros(n * cols, dtype=torch.int8, device=device)
         xsc = torch.zeros(n * blocks + 4, device=device)
         spans = [row_split(rows, p, world, False) for p in range(world)]
-        fused = args.gather == "fused" and n > 32  # the tensor-core GEMM's wide kernel
+        # The fused gathers: one token on the GEMV (dn_linear_qa_allgather,
+        # its count one per 32-row tile), more on the tensor-core GEMM
+        # (dn_linear_allgather, one count per rank).
+        fused = args.gather == "fused"
         if fused:
             # Every rank's Y[n, rows] (then its counter and wait word) in peer
             # memory; each rank's GEMM epilogue stores its column block into
@@ -1606,13 +1609,25 @@ def run_configs_sharded(args, rank, world, local_rank):
             cnt_arr = (ctypes.c_void_p * world)(*[b + 4 * n * rows for b in region.bases])
             counter = region.bases[rank] + 4 * n * rows
             expect = counter + 4
-            tiles = world  # one count per rank's product
+            tiles = world if n > 1 else sum(-(-(b - a) // 32) for a, b in spans)
+            xa = torch.zeros(blocks * 36, dtype=torch.uint8, device=device) if n == 1 else None
         else:
             ys = torch.zeros(n * width, device=device)  # [n, width]: this rank's block, padded
             gathered = torch.empty(world * n * width, device=device)
             full = torch.empty(n * rows, device=device)
 
         def step():
+            if fused and n == 1:
+                rc = L.dn_quantize_qa(xs.data_ptr(), xa.data_ptr(), 1, cols, blocks * 36, stream.cuda_stream)
+                if rc == 0:
+                    rc = L.dn_linear_qa_allgather(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(),
+                                                  xa.data_ptr(), rr, cols, r0, ys_arr, cnt_arr, world, 1,
+                                                  stream.cuda_stream)
+                if rc == 0:
+                    rc = L.dn_peer_wait(counter, expect, tiles, stream.cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(L.dn_error_string(rc).decode())
+                return
             if fused:
                 rc = L.dn_linear_allgather(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(),
                                            xq.data_ptr(), xsc.data_ptr(), rr, cols, n, r0, rows, ys_arr, cnt_arr,
@@ -1683,8 +1698,15 @@ def run_configs_sharded(args, rank, world, local_rank):
             rc = L.dn_linear(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(), xs.data_ptr(), xq.data_ptr(),
                              xsc.data_ptr(), own.data_ptr(), rr, cols, n, rr, 1, -1, 0, stream.cuda_stream)
             torch.cuda.synchronize()
-            own_ok = rc == 0 and bool(torch.equal(mine[:, r0:r1].contiguous().view(torch.int32),
-                                                  own.view(n, rr).view(torch.int32)))
+            got = mine[:, r0:r1].contiguous()
+            same_path = n == 1 or L.dn_linear_path(1 if fmt == "q4" else 0, qs.data_ptr(), sc.data_ptr(),
+                                                   xs.data_ptr(), xq.data_ptr(), rr, cols, n, 1) == 1
+            if same_path:  # the same kernel: value for value
+                own_ok = rc == 0 and bool(torch.equal(got.view(torch.int32), own.view(n, rr).view(torch.int32)))
+            else:  # dn_linear picks the GEMV for these few tokens: the tensor-core bound
+                ref = own.view(n, rr).double()
+                own_ok = rc == 0 and bool(((got.double() - ref).abs().max() <=
+                                           1e-5 * ref.abs().max().clamp_min(1e-30)).item())
             sums = torch.tensor([float(mine.double().sum().item())], dtype=torch.float64, device=device)
             allsums = [torch.zeros_like(sums) for _ in range(world)]
             if world > 1:
@@ -1695,17 +1717,22 @@ def run_configs_sharded(args, rank, world, local_rank):
             if world > 1:
                 dist.all_reduce(flags, op=dist.ReduceOp.MIN)
             check = {"copies_identical": len({float(x.item()) for x in allsums}) == 1,
-                     "own_columns_equal_dn_linear_on_all_ranks": bool(flags.item() == 1)}
+                     "own_columns_match_dn_linear_on_all_ranks": bool(flags.item() == 1),
+                     "match": "bit for bit where dn_linear takes the same kernel, else within 1e-5 of the "
+                              "slice's largest output"}
         if rank == 0:
             print(json.dumps({"case": name, "n_gpus": world, "fmt": fmt, "rows": rows, "cols": cols, "n": n,
                               "rows_per_gpu": width, "us": us, "tops": ops / us / 1e6,
                               "int8_frac_per_gpu": ops / us / 1e6 / (int8 * world),
                               "weight_gbs": wbytes / us / 1e3,
                               "hbm_frac_per_gpu": wbytes / us / 1e3 / (hbm * world),
-                              "includes": ("dn_linear_allgather on each rank's row slice (activation "
+                              "includes": ("dn_quantize_qa + dn_linear_qa_allgather on each rank's row "
+                                           "slice (the GEMV's outputs stored into every rank's copy over "
+                                           "NVLink) + dn_peer_wait" if fused and n == 1 else
+                                           "dn_linear_allgather on each rank's row slice (activation "
                                            "quantize included; the output columns stored into every rank's "
-                                           "Y over NVLink inside the GEMM epilogue) + dn_peer_wait"
-                                           if fused else
+                                           "Y over NVLink inside the tensor-core GEMM's epilogue) + "
+                                           "dn_peer_wait" if fused else
                                            "dn_linear on each rank's row slice (activation quantize "
                                            "included) + NCCL all-gather of the output blocks + "
                                            "token-major layout copy" if world > 1 else "dn_linear"),

@@ -955,7 +955,8 @@ __global__ void __launch_bounds__(NarrowShape<Q4, TOK>::kThreads, 1)
     // Tile outputs: the oldest tile whose sums are not written yet.
     int64_t ep_tile = blockIdx.x;
     uint32_t ep_it = 0;
-    const bool vec_y = (a.ldy & 3) == 0 && ((uintptr_t)a.ys & 15) == 0;
+    bool vec_y = (a.ldy & 3) == 0 && (a.gather_n > 0 ? (a.gather_row0 & 3) == 0 : ((uintptr_t)a.ys & 15) == 0);
+    for (int p = 0; p < a.gather_n; p++) vec_y = vec_y && ((uintptr_t)a.gather_ys[p] & 15) == 0;
     auto finish_tile = [&]() {
       // Every lane observes the completed phase itself (no wait: it is).
       mbar_wait_bounded(xbar, ep_it & 1u, a.status, kStatusMmaTimeout);
@@ -974,14 +975,17 @@ __global__ void __launch_bounds__(NarrowShape<Q4, TOK>::kThreads, 1)
                                      __fadd_rn(__fadd_rn(u0.y, u1.y), __fadd_rn(u2.y, u3.y)),
                                      __fadd_rn(__fadd_rn(u0.z, u1.z), __fadd_rn(u2.z, u3.z)),
                                      __fadd_rn(__fadd_rn(u0.w, u1.w), __fadd_rn(u2.w, u3.w)));
-        float* dst = a.ys + tok * a.ldy + r;
-        if (vec_y && r + 3 < a.rows) {
-          *reinterpret_cast<float4*>(dst) = y;
-        } else {
-          if (r < a.rows) dst[0] = y.x;
-          if (r + 1 < a.rows) dst[1] = y.y;
-          if (r + 2 < a.rows) dst[2] = y.z;
-          if (r + 3 < a.rows) dst[3] = y.w;
+        // Into this GPU's output, or (the fused all-gather) into every rank's.
+        for (int p = 0; p < (a.gather_n > 0 ? a.gather_n : 1); p++) {
+          float* dst = a.gather_n > 0 ? a.gather_ys[p] + a.gather_row0 + tok * a.ldy + r : a.ys + tok * a.ldy + r;
+          if (vec_y && r + 3 < a.rows) {
+            *reinterpret_cast<float4*>(dst) = y;
+          } else {
+            if (r < a.rows) dst[0] = y.x;
+            if (r + 1 < a.rows) dst[1] = y.y;
+            if (r + 2 < a.rows) dst[2] = y.z;
+            if (r + 3 < a.rows) dst[3] = y.w;
+          }
         }
       }
       __syncwarp();
@@ -1288,7 +1292,7 @@ int sm_count() {
 // The narrow kernel needs the scales by TMA (blocks a multiple of 4 for Q8,
 // 8 for Q4; 16-byte aligned scale arrays).
 template <bool Q4, int TOK>
-int64_t launch_narrow(const LinearArgs& a, cudaStream_t stream) {
+int64_t launch_narrow(const LinearArgs& a, cudaStream_t stream, const TcGather* gather = nullptr) {
   using S = NarrowShape<Q4, TOK>;
   const int64_t blocks = a.cols / kBlock;
   if (blocks % (Q4 ? 8 : 4) != 0 || ((uintptr_t)a.scales & 15) != 0 || ((uintptr_t)a.xsc & 15) != 0)
@@ -1336,6 +1340,11 @@ int64_t launch_narrow(const LinearArgs& a, cudaStream_t stream) {
   const int64_t row_tiles = (a.rows + kTileRows - 1) / kTileRows;
   const int64_t tiles = row_tiles * ((a.n + TOK - 1) / TOK);
   TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, 1, row_tiles, tiles};
+  if (gather != nullptr) {
+    t.gather_n = gather->world;
+    t.gather_row0 = gather->row0;
+    for (int p = 0; p < gather->world; p++) t.gather_ys[p] = gather->ys[p];
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)min64(tiles, (int64_t)sm_count()), 1, 1);
   cfg.blockDim = dim3(S::kThreads, 1, 1);
@@ -1472,7 +1481,11 @@ int64_t launch_gemm_tc_allgather(const LinearArgs& a, int64_t row0, float* const
       return kErrArgs;
   if (launch_quantize_q8(a.xs, a.xq, a.xsc, a.n, a.cols, stream) != cudaSuccess) return kErrCuda;
   const TcGather g{world, row0, ys, cnt};
-  const int64_t rc = a.q4 ? launch_tc<true>(a, stream, &g) : launch_tc<false>(a, stream, &g);
+  int64_t rc = kErrUnsupported;
+  if (a.n <= gemm_narrow_max())  // the same kernel choice as launch_gemm_tc
+    rc = a.n <= 16 ? (a.q4 ? launch_narrow<true, 16>(a, stream, &g) : launch_narrow<false, 16>(a, stream, &g))
+                   : (a.q4 ? launch_narrow<true, 32>(a, stream, &g) : launch_narrow<false, 32>(a, stream, &g));
+  if (rc == kErrUnsupported) rc = a.q4 ? launch_tc<true>(a, stream, &g) : launch_tc<false>(a, stream, &g);
   if (rc != kOk) return rc;
   // The counters' addresses travel by value.
   PeerCounters c{};

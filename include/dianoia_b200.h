@@ -453,8 +453,11 @@ int64_t dn_linear_qa_allgather(int64_t format, const void* qs, const void* scale
  * visible system-wide and adds one to every rank's counter (counters[p]), so
  * a rank's copy is complete once its counter has grown by `world` (one per
  * rank): dn_peer_wait. Nothing is counted after a bounded wait ran out (a
- * set dn_device_status). Results equal dn_linear's tensor-core path on the
- * whole matrix, value for value. */
+ * set dn_device_status). The kernel is the one dn_linear's tensor-core path
+ * picks for n tokens (narrow tiles up to 32); its results equal that path's
+ * on the whole matrix value for value when cols / 128 is a multiple of 4
+ * (the narrow kernel's four partial sums then fall the same way on every
+ * slice), and lie within its 1e-5 bound otherwise. */
 int64_t dn_linear_allgather(int64_t format, const void* qs, const void* scales, const float* xs, int8_t* xq,
                             float* xsc, int64_t rows, int64_t cols, int64_t n, int64_t row0, int64_t total_rows,
                             float* const* ys, int32_t* const* counters, int64_t world, void* stream);

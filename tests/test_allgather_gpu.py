@@ -69,7 +69,8 @@ def test_allgather_arguments(cuda_lib):
 
 
 @pytest.mark.parametrize("fmt,rows,cols,n,world", [("q8", 1000, 1152, 100, 3), ("q4", 4096, 2048, 64, 2),
-                                                   ("q8", 3456, 1152, 1024, 4)])
+                                                   ("q8", 3456, 1152, 1024, 4), ("q8", 5000, 2048, 16, 3),
+                                                   ("q4", 4096, 2048, 32, 2)])
 def test_gemm_allgather_matches_whole_product(cuda_lib, oracle, fmt, rows, cols, n, world):
     """The tensor-core GEMM with the all-gather fused into its epilogue
     (dn_linear_allgather), the ranks' row slices run one after another on one
