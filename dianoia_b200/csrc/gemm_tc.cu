@@ -41,6 +41,8 @@
 // its copies and MMAs finish (bounded), frees its TMEM and returns.
 #include <string.h>
 
+#include <type_traits>
+
 #include "dn_common.cuh"
 #include "dn_launch.h"
 #include "dn_tmap.h"
@@ -89,15 +91,21 @@ struct TcArgs {
   uint32_t* status;
   int tma_scales;  // scales arrive by TMA (tsw, tsx) rather than cp.async
   int64_t row_tiles, tiles;  // the narrow kernel's tile walk
-  // The all-gather of a row-sharded output fused into the epilogue (the wide
-  // kernel; gather_n > 0): this GPU's rows are rows gather_row0 .. + rows of
-  // the whole output, and each value goes to every rank's copy of it,
-  // gather_ys[p][t * ldy + gather_row0 + row] (plain stores, over NVLink for
-  // the peers); peer_signal_kernel then counts the product on every rank.
+};
+
+// The kernels' arguments when the all-gather of a row-sharded output is
+// fused into the epilogue (a compile-time variant; the plain kernels take
+// TcArgs itself, unchanged): this GPU's rows are rows gather_row0 .. + rows
+// of the whole output, and each value goes to every rank's copy of it,
+// gather_ys[p][t * ldy + gather_row0 + row] (plain stores, over NVLink for
+// the peers); peer_signal_kernel then counts the product on every rank.
+struct TcGatherArgs : TcArgs {
   int gather_n;
   int64_t gather_row0;
   float* gather_ys[kMaxGatherRanks];
 };
+template <bool GATHER>
+using TcArgsOf = typename std::conditional<GATHER, TcGatherArgs, TcArgs>::type;
 
 // ----------------------------------------------------------- tcgen05 PTX
 
@@ -259,9 +267,9 @@ __device__ __forceinline__ bool wait_tc(uint64_t* bar, uint32_t parity, uint32_t
 
 // kPartial: all tokens in one partial tile (n < 64), and drain warps whose
 // token columns are all beyond n skip their work.
-template <bool Q4, bool kPartial>
+template <bool Q4, bool kPartial, bool GATHER = false>
 __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
-    gemm_tc_kernel(const TcArgs a, const int stages, const __grid_constant__ CUtensorMap tw,
+    gemm_tc_kernel(const TcArgsOf<GATHER> a, const int stages, const __grid_constant__ CUtensorMap tw,
                    const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tsw,
                    const __grid_constant__ CUtensorMap tsx) {
   using S = TcShape<Q4>;
@@ -629,7 +637,10 @@ __global__ void __launch_bounds__(TcShape<Q4>::kThreads, 1)
           const int64_t t = tok0 + col0 + 2 * j;
           const float y0 = __fadd_rn(__uint_as_float((uint32_t)acc[j]), x[(2 * j) * 32 + lane]);
           const float y1 = __fadd_rn(__uint_as_float((uint32_t)(acc[j] >> 32)), x[(2 * j + 1) * 32 + lane]);
-          if (a.gather_n > 0) {
+          if constexpr (GATHER) {
+            // (A compile-time variant: a run-time index into the argument
+            // struct would move the whole struct to local memory in the plain
+            // kernels too - measured 3-12 % slower.)
             for (int p = 0; p < a.gather_n; p++) {
               float* g = a.gather_ys[p] + a.gather_row0 + row;
               if (t < a.n) g[t * a.ldy] = y0;
@@ -750,18 +761,22 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream, const TcGather* gath
                                  (uint64_t)a.n, (uint64_t)blocks * 4, kBlocksPerStage, kTileTok, false))
       return kErrUnsupported;
   }
-  auto kern = a.n < kTileTok ? gemm_tc_kernel<Q4, true> : gemm_tc_kernel<Q4, false>;
-  static bool configured[2][64] = {};
+  const void* kern =
+      gather != nullptr
+          ? (a.n < kTileTok ? (const void*)gemm_tc_kernel<Q4, true, true> : (const void*)gemm_tc_kernel<Q4, false, true>)
+          : (a.n < kTileTok ? (const void*)gemm_tc_kernel<Q4, true> : (const void*)gemm_tc_kernel<Q4, false>);
+  static bool configured[4][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int variant = a.n < kTileTok ? 1 : 0;
+  const int variant = (a.n < kTileTok ? 1 : 0) + (gather != nullptr ? 2 : 0);
   if (!configured[variant][dev & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemTc) !=
         cudaSuccess)
       return kErrCuda;
     configured[variant][dev & 63] = true;
   }
-  TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, tma_scales ? 1 : 0};
+  TcGatherArgs t{};
+  static_cast<TcArgs&>(t) = TcArgs{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, tma_scales ? 1 : 0};
   if (gather != nullptr) {
     t.gather_n = gather->world;
     t.gather_row0 = gather->row0;
@@ -781,7 +796,7 @@ int64_t launch_tc(const LinearArgs& a, cudaStream_t stream, const TcGather* gath
   cfg.numAttrs = 1;
   int nstages = stages;
   void* params[] = {&t, &nstages, &tw, &tx, &tsw, &tsx};
-  return cudaLaunchKernelExC(&cfg, (const void*)kern, params) == cudaSuccess ? kOk : kErrCuda;
+  return cudaLaunchKernelExC(&cfg, kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
 // ------------------------------------------------------------ narrow tiles
@@ -877,9 +892,9 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-template <bool Q4, int TOK>
+template <bool Q4, int TOK, bool GATHER = false>
 __global__ void __launch_bounds__(NarrowShape<Q4, TOK>::kThreads, 1)
-    gemm_narrow_kernel(const TcArgs a, const int stages, const int L, const __grid_constant__ CUtensorMap tw,
+    gemm_narrow_kernel(const TcArgsOf<GATHER> a, const int stages, const int L, const __grid_constant__ CUtensorMap tw,
                        const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tsw,
                        const __grid_constant__ CUtensorMap tsx) {
   using S = NarrowShape<Q4, TOK>;
@@ -955,8 +970,13 @@ __global__ void __launch_bounds__(NarrowShape<Q4, TOK>::kThreads, 1)
     // Tile outputs: the oldest tile whose sums are not written yet.
     int64_t ep_tile = blockIdx.x;
     uint32_t ep_it = 0;
-    bool vec_y = (a.ldy & 3) == 0 && (a.gather_n > 0 ? (a.gather_row0 & 3) == 0 : ((uintptr_t)a.ys & 15) == 0);
-    for (int p = 0; p < a.gather_n; p++) vec_y = vec_y && ((uintptr_t)a.gather_ys[p] & 15) == 0;
+    bool vec_y = (a.ldy & 3) == 0;
+    if constexpr (GATHER) {
+      vec_y = vec_y && (a.gather_row0 & 3) == 0;
+      for (int p = 0; p < a.gather_n; p++) vec_y = vec_y && ((uintptr_t)a.gather_ys[p] & 15) == 0;
+    } else {
+      vec_y = vec_y && ((uintptr_t)a.ys & 15) == 0;
+    }
     auto finish_tile = [&]() {
       // Every lane observes the completed phase itself (no wait: it is).
       mbar_wait_bounded(xbar, ep_it & 1u, a.status, kStatusMmaTimeout);
@@ -975,9 +995,16 @@ __global__ void __launch_bounds__(NarrowShape<Q4, TOK>::kThreads, 1)
                                      __fadd_rn(__fadd_rn(u0.y, u1.y), __fadd_rn(u2.y, u3.y)),
                                      __fadd_rn(__fadd_rn(u0.z, u1.z), __fadd_rn(u2.z, u3.z)),
                                      __fadd_rn(__fadd_rn(u0.w, u1.w), __fadd_rn(u2.w, u3.w)));
-        // Into this GPU's output, or (the fused all-gather) into every rank's.
-        for (int p = 0; p < (a.gather_n > 0 ? a.gather_n : 1); p++) {
-          float* dst = a.gather_n > 0 ? a.gather_ys[p] + a.gather_row0 + tok * a.ldy + r : a.ys + tok * a.ldy + r;
+        // Into this GPU's output, or (the fused all-gather, a compile-time
+        // variant) into every rank's.
+        int ncopies = 1;
+        if constexpr (GATHER) ncopies = a.gather_n;
+        for (int p = 0; p < ncopies; p++) {
+          float* dst;
+          if constexpr (GATHER)
+            dst = a.gather_ys[p] + a.gather_row0 + tok * a.ldy + r;
+          else
+            dst = a.ys + tok * a.ldy + r;
           if (vec_y && r + 3 < a.rows) {
             *reinterpret_cast<float4*>(dst) = y;
           } else {
@@ -1328,18 +1355,21 @@ int64_t launch_narrow(const LinearArgs& a, cudaStream_t stream, const TcGather* 
   if (!ok_w || !encode_tmap_2d(&tsx, a.xsc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)blocks,
                                (uint64_t)a.n, (uint64_t)blocks * 4, kBlocksPerStage, TOK, false))
     return kErrUnsupported;
-  auto kern = gemm_narrow_kernel<Q4, TOK>;
-  static bool configured[64] = {};
+  const void* kern = gather != nullptr ? (const void*)gemm_narrow_kernel<Q4, TOK, true>
+                                       : (const void*)gemm_narrow_kernel<Q4, TOK>;
+  static bool configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!configured[dev & 63]) {
+  const int variant = gather != nullptr ? 1 : 0;
+  if (!configured[variant][dev & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemTc) != cudaSuccess)
       return kErrCuda;
-    configured[dev & 63] = true;
+    configured[variant][dev & 63] = true;
   }
   const int64_t row_tiles = (a.rows + kTileRows - 1) / kTileRows;
   const int64_t tiles = row_tiles * ((a.n + TOK - 1) / TOK);
-  TcArgs t{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, 1, row_tiles, tiles};
+  TcGatherArgs t{};
+  static_cast<TcArgs&>(t) = TcArgs{a.scales, a.xsc, a.ys, a.rows, a.cols, a.n, a.ldy, a.status, 1, row_tiles, tiles};
   if (gather != nullptr) {
     t.gather_n = gather->world;
     t.gather_row0 = gather->row0;
@@ -1357,7 +1387,7 @@ int64_t launch_narrow(const LinearArgs& a, cudaStream_t stream, const TcGather* 
   cfg.numAttrs = 1;
   int nstages = stages;
   void* params[] = {&t, &nstages, &lookahead, &tw, &tx, &tsw, &tsx};
-  return cudaLaunchKernelExC(&cfg, (const void*)kern, params) == cudaSuccess ? kOk : kErrCuda;
+  return cudaLaunchKernelExC(&cfg, kern, params) == cudaSuccess ? kOk : kErrCuda;
 }
 
 // The drain step alone, for measuring the GEMM's own ceiling: the drain warps
