@@ -1557,11 +1557,16 @@ class FusedRegion:
 
 def run_configs_sharded(args, rank, world, local_rank):
     """Configs 5 and the lm_head sweep on N GPUs: each rank holds its row
-    slice of the weights (rows * p // N ..), runs dn_linear on the whole batch
-    of tokens, and an NCCL all-gather of the output column blocks rebuilds
-    Y[n, rows] on every rank (padded to the widest slice, then laid out
-    token-major by one copy). Both are inside the timed region; time is the
-    max over ranks. One JSON line per case from rank 0."""
+    slice of the weights (rows * p // N ..) and computes its column block of
+    Y[n, rows] for the whole batch of tokens. By default the gather is fused
+    into the product: every rank's kernel stores its block into every rank's
+    Y over NVLink and counts it on the peers' counters (dn_linear_allgather,
+    or dn_linear_qa_allgather for one token), and each rank's step ends in a
+    bounded wait for all the blocks; the steps replay from a CUDA graph.
+    With --gather nccl, dn_linear on the slice is followed by an NCCL
+    all-gather of the column blocks (padded to the widest slice, then laid
+    out token-major by one copy). Everything is inside the timed region;
+    time is the max over ranks. One JSON line per case from rank 0."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
